@@ -1,0 +1,511 @@
+// bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), with the
+// epilogues of the recompute layers fused in:
+//   EPI_STORE  out = bf16(x W^T (+ bias))                      nn.Linear
+//   EPI_RESID  h   = bf16(h + bf16(x W^T))                      torch_engine.py:72-73
+//   EPI_SWIGLU out = bf16(silu(bf16(g)) * bf16(u))              Qwen2MLP gate/up
+//   EPI_QKV    q/k/v = bf16(x W^T + b), RoPE at positions on q,k (torch_engine.py:61-66),
+//              k/v written straight into the blended cache       (torch_engine.py:155-156)
+//
+// D = A B^T with A = x [M][K] and B = W [N][K], both K-major.  One persistent CTA
+// per SM, 6 warps:
+//   warp 0      TMA producer (one thread): A 128x64 and B 256x64 tiles, 128B swizzle,
+//               4-stage ring guarded by full/empty mbarriers;
+//   warp 1      TMEM owner + MMA issuer (one thread): tcgen05.mma kind::f16,
+//               M=128 N=256 K=16 per instruction, fp32 accumulators in TMEM;
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes
+//               32*(w%4)..+31 = tile rows), fused math, stores.
+// Two 256-column accumulators (all 512 TMEM columns) let the epilogue of one tile
+// overlap the main loop of the next.  Tiles are visited M-fastest so CTAs that
+// run together share the same weight tile through L2.
+//
+// Every mbarrier wait is bounded (ckv::mbar_wait); a wait that runs out sets
+// CKV_DEV_ERR_WAIT_TIMEOUT, the CTA drains what it issued and frees its TMEM.
+#include "ckv_common.cuh"
+
+CKV_DEFINE_ERR_WORD(gemm)
+
+namespace ckv {
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, UMMA_K = 16;
+constexpr int STAGES = 4;
+constexpr int kThreads = 192;
+constexpr uint32_t A_BYTES = BM * BK * 2;  // 16 KiB
+constexpr uint32_t B_BYTES = BN * BK * 2;  // 32 KiB
+constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr uint32_t TMEM_COLS = 2 * BN;     // 512: two accumulators
+constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN);
+
+enum Epi { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKV = 3 };
+
+struct EpiParams {
+  const uint16_t* bias;  // by absolute column of the full weight (STORE optional, QKV)
+  uint16_t* out;         // STORE out, RESID h, SWIGLU out
+  int64_t ldo;
+  const int32_t* positions;
+  const float2* rope;
+  int rope_max_pos;
+  int col_begin;
+  int n_q_heads, n_kv_heads;
+  uint16_t* q_out;
+  uint16_t* k_cache;
+  uint16_t* v_cache;
+  int n_ctx;
+  uint16_t* k_compact;
+  uint16_t* v_compact;
+};
+
+__device__ __forceinline__ void store8(uint16_t* dst, const float* v) {
+  uint4 w;
+  w.x = pack_bf2(v[0], v[1]);
+  w.y = pack_bf2(v[2], v[3]);
+  w.z = pack_bf2(v[4], v[5]);
+  w.w = pack_bf2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(dst) = w;
+}
+
+// ---- epilogues: one thread = one tile row; all lanes execute the TMEM loads.
+__device__ __forceinline__ void epi_store(uint32_t tacc, int row, int M, int n0, int N,
+                                          const EpiParams& ep) {
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    float v[32];
+    tmem_ld32(tacc + c, v);
+    if (row >= M) continue;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int col = n0 + c + g * 8;
+      if (col >= N) continue;
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        o[e] = v[g * 8 + e];
+        if (ep.bias) o[e] = __fadd_rn(o[e], bf2f(ep.bias[col + e]));
+      }
+      store8(ep.out + int64_t(row) * ep.ldo + col, o);
+    }
+  }
+}
+
+__device__ __forceinline__ void epi_resid(uint32_t tacc, int row, int M, int n0, int N,
+                                          const EpiParams& ep) {
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    float v[32];
+    tmem_ld32(tacc + c, v);
+    if (row >= M) continue;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int col = n0 + c + g * 8;
+      if (col >= N) continue;
+      uint16_t* hp = ep.out + int64_t(row) * ep.ldo + col;
+      const uint4 hv = *reinterpret_cast<const uint4*>(hp);
+      const uint32_t* hw = reinterpret_cast<const uint32_t*>(&hv);
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        o[2 * e] = __fadd_rn(lo_bf(hw[e]), bf16_round(v[g * 8 + 2 * e]));
+        o[2 * e + 1] = __fadd_rn(hi_bf(hw[e]), bf16_round(v[g * 8 + 2 * e + 1]));
+      }
+      store8(hp, o);
+    }
+  }
+}
+
+// Tile = 128 gate columns then the 128 matching up columns (interleaved weight).
+__device__ __forceinline__ void epi_swiglu(uint32_t tacc, int row, int M, int n0, int N,
+                                           const EpiParams& ep) {
+  const int out0 = n0 / 2;
+#pragma unroll 1
+  for (int c = 0; c < BN / 2; c += 32) {
+    float g[32], u[32];
+    tmem_ld32(tacc + c, g);
+    tmem_ld32(tacc + BN / 2 + c, u);
+    if (row >= M || n0 >= N) continue;
+    float o[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float gb = bf16_round(g[j]);
+      const float s = bf16_round(__fdiv_rn(gb, __fadd_rn(1.0f, expf(-gb))));
+      o[j] = __fmul_rn(s, bf16_round(u[j]));
+    }
+    uint16_t* dst = ep.out + int64_t(row) * ep.ldo + out0 + c;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) store8(dst + q * 8, o + q * 8);
+  }
+}
+
+template <int HD>
+__device__ __forceinline__ void epi_qkv(uint32_t tacc, int row, int M, int n0, int N,
+                                        const EpiParams& ep) {
+  constexpr int HALF = HD / 2;
+  const int Hq = ep.n_q_heads, Hk = ep.n_kv_heads;
+  int pos = 0;
+  bool ok = row < M;
+  if (ok) {
+    pos = ep.positions[row];
+    const bool bad = pos < 0 || pos >= ep.rope_max_pos || (ep.k_cache && pos >= ep.n_ctx);
+    if (bad) {
+      atomicOr(&g_err_word, CKV_DEV_ERR_POSITION_RANGE);
+      ok = false;
+    }
+  }
+#pragma unroll 1
+  for (int hh = 0; hh < BN / HD; ++hh) {
+    if (n0 + hh * HD >= N) break;  // warp-uniform
+    const int gcol = ep.col_begin + n0 + hh * HD;
+    const int head = gcol / HD;
+    const uint32_t tcol = tacc + hh * HD;
+    if (head < Hq + Hk) {
+      uint16_t* dst;
+      if (head < Hq) {
+        dst = ep.q_out + int64_t(row) * (Hq * HD) + head * HD;
+      } else if (ep.k_cache) {
+        dst = ep.k_cache + (int64_t(head - Hq) * ep.n_ctx + pos) * HD;
+      } else {
+        dst = ep.k_compact + int64_t(row) * (Hk * HD) + (head - Hq) * HD;
+      }
+      const float2* cs = ep.rope + int64_t(pos) * HALF;
+#pragma unroll 1
+      for (int c = 0; c < HALF; c += 32) {
+        float x1[32], x2[32];
+        tmem_ld32(tcol + c, x1);
+        tmem_ld32(tcol + HALF + c, x2);
+        if (!ok) continue;
+        float o1[32], o2[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float a = bf16_round(__fadd_rn(x1[j], bf2f(ep.bias[gcol + c + j])));
+          const float b = bf16_round(__fadd_rn(x2[j], bf2f(ep.bias[gcol + HALF + c + j])));
+          const float2 r = cs[c + j];
+          o1[j] = __fsub_rn(__fmul_rn(a, r.x), __fmul_rn(b, r.y));
+          o2[j] = __fadd_rn(__fmul_rn(a, r.y), __fmul_rn(b, r.x));
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          store8(dst + c + q * 8, o1 + q * 8);
+          store8(dst + HALF + c + q * 8, o2 + q * 8);
+        }
+      }
+    } else {
+      const int hv = head - Hq - Hk;
+      uint16_t* dst = ep.v_cache ? ep.v_cache + (int64_t(hv) * ep.n_ctx + pos) * HD
+                                 : ep.v_compact + int64_t(row) * (Hk * HD) + hv * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        float x[32];
+        tmem_ld32(tcol + c, x);
+        if (!ok) continue;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) x[j] = __fadd_rn(x[j], bf2f(ep.bias[gcol + c + j]));
+#pragma unroll
+        for (int q = 0; q < 4; ++q) store8(dst + c + q * 8, x + q * 8);
+      }
+    }
+  }
+}
+
+template <int EPI, int HD>
+__device__ __forceinline__ void run_epilogue(uint32_t tacc, int row, int M, int n0, int N,
+                                             const EpiParams& ep) {
+  if constexpr (EPI == EPI_STORE) epi_store(tacc, row, M, n0, N, ep);
+  else if constexpr (EPI == EPI_RESID) epi_resid(tacc, row, M, n0, N, ep);
+  else if constexpr (EPI == EPI_SWIGLU) epi_swiglu(tacc, row, M, n0, N, ep);
+  else epi_qkv<HD>(tacc, row, M, n0, N, ep);
+}
+
+// Bounded wait that ignores the abort flag (used only while draining).
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_ns() - t0 > kWaitLimitNs) break;
+}
+
+template <int EPI, int HD>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                int M, int N, int K, EpiParams ep) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_tiles = (M + BM - 1) / BM;
+  const int n_tiles = (N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int num_kb = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(drain, 1);
+    *abort = 0;
+    fence_barrier_init();
+    fence_async_smem();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int mt = tile % m_tiles, nt = tile / m_tiles;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort, &g_err_word)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[s], STAGE_BYTES);
+          tma_load_2d(sA + s * A_BYTES, &tmA, kb * BK, mt * BM, &full[s]);
+          tma_load_2d(sB + s * B_BYTES, &tmB, kb * BK, nt * BN, &full[s]);
+        }
+      }
+      if (!ok)  // let the copies already issued land before the CTA goes away
+        for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
+          drain_wait(&full[j % STAGES], (j / STAGES) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int it = 0, tcount = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++tcount) {
+        const int acc = tcount & 1;
+        const uint32_t use = tcount >> 1;
+        if (!mbar_wait(&tempty[acc], (use & 1) ^ 1, abort, &g_err_word)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, abort, &g_err_word)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * A_BYTES);
+          const uint32_t b0 = smem_u32(sB + s * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k) {
+            const uint64_t ad = umma_desc_sw128(a0 + k * UMMA_K * 2);
+            const uint64_t bd = umma_desc_sw128(b0 + k * UMMA_K * 2);
+            tc_mma_f16(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
+        }
+        if (ok) tc_commit(&tfull[acc]);
+      }
+      if (!ok) {  // wait for the MMAs already issued before TMEM is released
+        tc_commit(drain);
+        drain_wait(drain, 0);
+      }
+    }
+  } else {
+    const int sub = warp & 3;  // TMEM sub-partition this warp may access
+    int tcount = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tcount) {
+      const int acc = tcount & 1;
+      const uint32_t use = tcount >> 1;
+      if (!mbar_wait(&tfull[acc], use & 1, abort, &g_err_word)) break;
+      tc_fence_after();
+      const int mt = tile % m_tiles, nt = tile / m_tiles;
+      const int row = mt * BM + sub * 32 + lane;
+      const uint32_t tacc = tmem_base + (uint32_t(sub * 32) << 16) + acc * BN;
+      run_epilogue<EPI, HD>(tacc, row, M, nt * BN, N, ep);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// Row-major bf16 [rows][k] (row stride ld elements), box = box_rows x 64.
+int make_map(CUtensorMap* map, const void* ptr, int rows, int k, int64_t ld, int box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) {
+    set_error("cuTensorMapEncodeTiled unavailable (driver too old?)");
+    return CKV_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(ld) * 2};
+  cuuint32_t box[2] = {cuuint32_t(BK), cuuint32_t(box_rows)};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                   box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d) rows=%d k=%d ld=%lld", int(r), rows, k,
+              (long long)ld);
+    return CKV_ERR_CUDA;
+  }
+  return CKV_OK;
+}
+
+template <int EPI, int HD>
+int launch(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, int M, int N, int K,
+           const EpiParams& ep, cudaStream_t stream, const char* name) {
+  CKV_REQUIRE(a && b, "%s: null operand", name);
+  CKV_REQUIRE(M >= 0 && N > 0 && K > 0, "%s: bad sizes m=%d n=%d k=%d", name, M, N, K);
+  CKV_REQUIRE(aligned16(a) && aligned16(b), "%s: operands must be 16-byte aligned", name);
+  CKV_REQUIRE(K % 8 == 0 && lda % 8 == 0 && ldb % 8 == 0,
+              "%s: k and row strides must be multiples of 8", name);
+  CKV_REQUIRE(N % 16 == 0, "%s: n=%d must be a multiple of 16", name, N);
+  if (M == 0) return CKV_OK;
+  CUtensorMap ma, mb;
+  if (int rc = make_map(&ma, a, M, K, lda, BM)) return rc;
+  if (int rc = make_map(&mb, b, N, K, ldb, BN)) return rc;
+  auto kern = gemm_kernel<EPI, HD>;
+  if (int rc = set_smem_limit(reinterpret_cast<const void*>(kern), SMEM_BYTES)) return rc;
+  const int tiles = ceil_div(M, BM) * ceil_div(N, BN);
+  const int grid = std::min(tiles, num_sms());
+  kern<<<grid, kThreads, SMEM_BYTES, stream>>>(ma, mb, M, N, K, ep);
+  CKV_LAUNCH_CHECK(name);
+  return CKV_OK;
+}
+
+EpiParams zero_params() {
+  EpiParams ep;
+  memset(&ep, 0, sizeof(ep));
+  return ep;
+}
+
+}  // namespace
+}  // namespace ckv
+
+using namespace ckv;
+
+extern "C" {
+
+int ckv_linear(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* out, int m,
+               int n, int k, ckv_stream_t stream) {
+  CKV_REQUIRE(out && aligned16(out), "ckv_linear: output must be 16-byte aligned");
+  EpiParams ep = zero_params();
+  ep.bias = bias;
+  ep.out = out;
+  ep.ldo = n;
+  return launch<EPI_STORE, 128>(x, k, w, k, m, n, k, ep, as_stream(stream), "ckv_linear");
+}
+
+int ckv_linear_residual(const uint16_t* x, const uint16_t* w, uint16_t* h, int m, int n, int k,
+                        ckv_stream_t stream) {
+  CKV_REQUIRE(h && aligned16(h), "ckv_linear_residual: h must be 16-byte aligned");
+  EpiParams ep = zero_params();
+  ep.out = h;
+  ep.ldo = n;
+  return launch<EPI_RESID, 128>(x, k, w, k, m, n, k, ep, as_stream(stream),
+                                "ckv_linear_residual");
+}
+
+int ckv_linear_swiglu(const uint16_t* x, const uint16_t* w_gate_up, uint16_t* out, int m,
+                      int inter, int k, ckv_stream_t stream) {
+  CKV_REQUIRE(out && aligned16(out), "ckv_linear_swiglu: output must be 16-byte aligned");
+  CKV_REQUIRE(inter > 0 && inter % (BN / 2) == 0, "ckv_linear_swiglu: inter %% 128 != 0");
+  EpiParams ep = zero_params();
+  ep.out = out;
+  ep.ldo = inter;
+  return launch<EPI_SWIGLU, 128>(x, k, w_gate_up, k, m, 2 * inter, k, ep, as_stream(stream),
+                                 "ckv_linear_swiglu");
+}
+
+int ckv_qkv_rope(const uint16_t* x, const uint16_t* w_qkv, const uint16_t* b_qkv, int m, int k,
+                 int col_begin, int col_end, int n_q_heads, int n_kv_heads, int head_dim,
+                 const int32_t* positions, const float* rope_table, int rope_max_pos,
+                 uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache, int n_ctx,
+                 uint16_t* k_compact, uint16_t* v_compact, ckv_stream_t stream) {
+  CKV_REQUIRE(head_dim == 64 || head_dim == 128, "ckv_qkv_rope: head_dim %d (64 or 128)",
+              head_dim);
+  CKV_REQUIRE(b_qkv && positions && rope_table, "ckv_qkv_rope: null bias/positions/table");
+  const int total = (n_q_heads + 2 * n_kv_heads) * head_dim;
+  CKV_REQUIRE(0 <= col_begin && col_begin < col_end && col_end <= total,
+              "ckv_qkv_rope: column range [%d,%d) outside [0,%d)", col_begin, col_end, total);
+  CKV_REQUIRE(col_begin % head_dim == 0 && col_end % head_dim == 0,
+              "ckv_qkv_rope: column range must cover whole heads");
+  const bool has_q = col_begin < n_q_heads * head_dim;
+  const bool has_kv = col_end > n_q_heads * head_dim;
+  CKV_REQUIRE(!has_q || (q_out && aligned16(q_out)), "ckv_qkv_rope: q_out required");
+  if (has_kv) {
+    const bool cache = k_cache && v_cache;
+    const bool compact = k_compact && v_compact;
+    CKV_REQUIRE(cache != compact, "ckv_qkv_rope: give either k/v caches or compact k/v buffers");
+    CKV_REQUIRE(cache ? (aligned16(k_cache) && aligned16(v_cache) && n_ctx > 0)
+                      : (aligned16(k_compact) && aligned16(v_compact)),
+                "ckv_qkv_rope: k/v outputs must be 16-byte aligned");
+  }
+  CKV_REQUIRE(rope_max_pos > 0, "ckv_qkv_rope: empty rope table");
+  EpiParams ep = zero_params();
+  ep.bias = b_qkv;
+  ep.positions = positions;
+  ep.rope = reinterpret_cast<const float2*>(rope_table);
+  ep.rope_max_pos = rope_max_pos;
+  ep.col_begin = col_begin;
+  ep.n_q_heads = n_q_heads;
+  ep.n_kv_heads = n_kv_heads;
+  ep.q_out = q_out;
+  ep.k_cache = k_cache;
+  ep.v_cache = v_cache;
+  ep.n_ctx = n_ctx;
+  ep.k_compact = k_compact;
+  ep.v_compact = v_compact;
+  const uint16_t* wb = w_qkv + int64_t(col_begin) * k;
+  const int n = col_end - col_begin;
+  if (head_dim == 128)
+    return launch<EPI_QKV, 128>(x, k, wb, k, m, n, k, ep, as_stream(stream), "ckv_qkv_rope");
+  return launch<EPI_QKV, 64>(x, k, wb, k, m, n, k, ep, as_stream(stream), "ckv_qkv_rope");
+}
+
+}  // extern "C"

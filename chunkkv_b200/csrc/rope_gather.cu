@@ -1,0 +1,372 @@
+// Re-RoPE and the store <-> blended-cache copies (HBM-streaming kernels).
+//
+// Rotation arithmetic follows TorchEngine._rotate (torch_engine.py:46-51):
+// angle = fp32(delta * inv_freq[j]); out1 = x1*cos - x2*sin, out2 = x1*sin + x2*cos,
+// each product and sum rounded in fp32 (no FMA contraction), result rounded to
+// bf16.  Pairs are (j, j + rot/2) for j < rot/2 (half-split layout,
+// rerope.py:36-47); dims >= rot are copied unchanged.
+//
+// Work unit of the gather/scatter kernels: 16 tokens (one page block) of one
+// (layer, K|V, kv-head) — 16 * head_dim * 2 bytes, contiguous on both sides.
+#include "ckv_common.cuh"
+
+CKV_DEFINE_ERR_WORD(rope)
+
+namespace ckv {
+namespace {
+
+constexpr int kPage = CKV_PAGE_TOKENS;
+constexpr int kMaxHalf = 128;  // rot_dims <= 256
+
+struct uint4x2 {
+  uint4 a, b;
+};
+
+// Rotate 8 (x1, x2) pairs held as two 16-byte vectors.
+__device__ __forceinline__ void rotate8(uint4& v1, uint4& v2, const float2* cs) {
+  uint32_t* p1 = reinterpret_cast<uint32_t*>(&v1);
+  uint32_t* p2 = reinterpret_cast<uint32_t*>(&v2);
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    float a[2] = {lo_bf(p1[w]), hi_bf(p1[w])};
+    float b[2] = {lo_bf(p2[w]), hi_bf(p2[w])};
+    float o1[2], o2[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float c = cs[2 * w + e].x, s = cs[2 * w + e].y;
+      o1[e] = __fsub_rn(__fmul_rn(a[e], c), __fmul_rn(b[e], s));
+      o2[e] = __fadd_rn(__fmul_rn(a[e], s), __fmul_rn(b[e], c));
+    }
+    p1[w] = pack_bf2(o1[0], o1[1]);
+    p2[w] = pack_bf2(o2[0], o2[1]);
+  }
+}
+
+__device__ __forceinline__ float2 rope_cs(float pos_or_delta, float inv_freq) {
+  const float a = __fmul_rn(pos_or_delta, inv_freq);
+  return make_float2(cosf(a), sinf(a));
+}
+
+// Copy `rows` rows of head_dim bf16 from src to dst, rotating by the per-j
+// table cs (smem) when rotate != 0.  Executed by one warp.
+__device__ __forceinline__ void copy_rows_warp(const uint16_t* __restrict__ src, int64_t src_row_stride,
+                                               uint16_t* __restrict__ dst, int64_t dst_row_stride,
+                                               int rows, int head_dim, int rot, bool rotate,
+                                               const float2* cs, int lane) {
+  const int n_pair = rotate ? rot / 16 : 0;      // pair items (two 16 B vectors)
+  const int n_copy = (head_dim / 8) - 2 * n_pair;  // plain 16 B vectors
+  const int per_row = n_pair + n_copy;
+  const int total = rows * per_row;
+  for (int it = lane; it < total; it += 32) {
+    const int r = it / per_row;
+    const int item = it - r * per_row;
+    const uint16_t* s = src + r * src_row_stride;
+    uint16_t* d = dst + r * dst_row_stride;
+    if (item < n_pair) {
+      const int j = item * 8;
+      uint4 v1 = *reinterpret_cast<const uint4*>(s + j);
+      uint4 v2 = *reinterpret_cast<const uint4*>(s + j + rot / 2);
+      rotate8(v1, v2, cs + j);
+      *reinterpret_cast<uint4*>(d + j) = v1;
+      *reinterpret_cast<uint4*>(d + j + rot / 2) = v2;
+    } else {
+      const int c = item - n_pair;
+      // copy vectors: the dims past rot (or every dim when not rotating)
+      const int off = (rotate ? rot : 0) + c * 8;
+      *reinterpret_cast<uint4*>(d + off) = *reinterpret_cast<const uint4*>(s + off);
+    }
+  }
+}
+
+__global__ void rope_table_kernel(const float* __restrict__ inv_freq, int half, int max_pos,
+                                  float2* __restrict__ table) {
+  const int64_t n = int64_t(max_pos) * half;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int p = int(i / half), j = int(i - int64_t(p) * half);
+    table[i] = rope_cs(float(p), inv_freq[j]);
+  }
+}
+
+// dst[row] = rotate(src[row], cs(pos(row))) with pos = delta (shift) or positions[row % seq].
+__global__ void rope_rows_kernel(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst,
+                                 int64_t rows, int head_dim, int rot, int delta,
+                                 const int32_t* __restrict__ positions, int seq,
+                                 const float* __restrict__ inv_freq) {
+  const int n_pair = rot / 16;
+  const int n_copy = head_dim / 8 - 2 * n_pair;
+  const int per_row = n_pair + n_copy;
+  const int64_t total = rows * per_row;
+  for (int64_t it = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; it < total;
+       it += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = it / per_row;
+    const int item = int(it - r * per_row);
+    const uint16_t* s = src + r * head_dim;
+    uint16_t* d = dst + r * head_dim;
+    if (item < n_pair) {
+      const int j = item * 8;
+      const float p = positions ? float(positions[r % seq]) : float(delta);
+      float2 cs[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) cs[e] = rope_cs(p, inv_freq[j + e]);
+      uint4 v1 = *reinterpret_cast<const uint4*>(s + j);
+      uint4 v2 = *reinterpret_cast<const uint4*>(s + j + rot / 2);
+      rotate8(v1, v2, cs);
+      *reinterpret_cast<uint4*>(d + j) = v1;
+      *reinterpret_cast<uint4*>(d + j + rot / 2) = v2;
+    } else {
+      const int off = rot + (item - n_pair) * 8;
+      *reinterpret_cast<uint4*>(d + off) = *reinterpret_cast<const uint4*>(s + off);
+    }
+  }
+}
+
+// One CTA column (blockIdx.y) per chunk; warps stride over the chunk's units.
+// Unit u -> (block b, layer l, kv, head h), head fastest so consecutive warps
+// stream consecutive 4 KiB pieces of the same page.
+template <bool kPaged>
+__global__ void __launch_bounds__(256) blend_gather_kernel(
+    const uint16_t* __restrict__ pool, int64_t n_pages, const int32_t* __restrict__ page_table,
+    const uint64_t* __restrict__ k_ptrs, const uint64_t* __restrict__ v_ptrs,
+    const int32_t* __restrict__ chunk_meta, const float* __restrict__ inv_freq, int rot,
+    uint16_t* __restrict__ k_out, uint16_t* __restrict__ v_out, int layer_lo, int layer_hi,
+    int n_layers, int H, int D, int n_ctx) {
+  __shared__ float2 cs[kMaxHalf];
+  const int32_t* meta = chunk_meta + blockIdx.y * CKV_META_STRIDE;
+  const int table_off = meta[CKV_META_TABLE_OFFSET];
+  const int length = meta[CKV_META_LENGTH];
+  const int dst_start = meta[CKV_META_DST_START];
+  const int delta = meta[CKV_META_DELTA];
+  const int lb = max(layer_lo, meta[CKV_META_LAYER_BEGIN]);
+  const int le = min(layer_hi, meta[CKV_META_LAYER_END]);
+  const int src_off = meta[CKV_META_SRC_OFFSET];
+  const int64_t head_stride = meta[CKV_META_HEAD_STRIDE];
+  if (le <= lb || length <= 0) return;
+  const bool rotate = delta != 0;
+  if (rotate)
+    for (int j = threadIdx.x; j < rot / 2; j += blockDim.x) cs[j] = rope_cs(float(delta), inv_freq[j]);
+  __syncthreads();
+
+  const int nl = le - lb;
+  const int n_blocks = (length + kPage - 1) / kPage;
+  const int64_t n_units = int64_t(n_blocks) * nl * 2 * H;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int warps = blockDim.x / 32;
+  const int64_t layer_elems = int64_t(H) * n_ctx * D;
+  for (int64_t u = int64_t(blockIdx.x) * warps + warp; u < n_units; u += int64_t(gridDim.x) * warps) {
+    int64_t t = u;
+    const int h = int(t % H);
+    t /= H;
+    const int kv = int(t % 2);
+    t /= 2;
+    const int l = lb + int(t % nl);
+    const int b = int(t / nl);
+    const int r0 = b * kPage;
+    const int rows = min(kPage, length - r0);
+    const int dpos = dst_start + r0;
+    if (dpos < 0 || dpos + rows > n_ctx) {
+      if (lane == 0) atomicOr(&g_err_word, CKV_DEV_ERR_POSITION_RANGE);
+      continue;
+    }
+    uint16_t* dst = (kv ? v_out : k_out) + int64_t(l - layer_lo) * layer_elems +
+                    (int64_t(h) * n_ctx + dpos) * D;
+    const bool rot_this = rotate && kv == 0;
+    if (kPaged) {
+      // rows may straddle two pages when src_off is not page aligned: split
+      int done = 0;
+      while (done < rows) {
+        const int tok = src_off + r0 + done;
+        const int slot = tok / kPage, in_page = tok % kPage;
+        const int take = min(rows - done, kPage - in_page);
+        const int page = page_table[table_off + slot];
+        if (page < 0 || page >= n_pages) {
+          if (lane == 0) atomicOr(&g_err_word, CKV_DEV_ERR_PAGE_RANGE);
+        } else {
+          const uint16_t* src = pool + ((((int64_t(page) * n_layers + l) * 2 + kv) * H + h) * kPage + in_page) * D;
+          copy_rows_warp(src, D, dst + int64_t(done) * D, D, take, D, rot, rot_this, cs, lane);
+        }
+        done += take;
+      }
+    } else {
+      const uint64_t base = (kv ? v_ptrs : k_ptrs)[table_off + l];
+      if ((base & 15u) != 0 || (head_stride & 7) != 0) {  // would break 16-byte vector loads
+        if (lane == 0) atomicOr(&g_err_word, CKV_DEV_ERR_POSITION_RANGE);
+        continue;
+      }
+      const uint16_t* src = reinterpret_cast<const uint16_t*>(base) + h * head_stride +
+                            int64_t(src_off + r0) * D;
+      copy_rows_warp(src, D, dst, D, rows, D, rot, rot_this, cs, lane);
+    }
+  }
+}
+
+// Dense (H, >=length, D) per-layer sources -> pages.
+__global__ void __launch_bounds__(256) pages_write_kernel(
+    uint16_t* __restrict__ pool, int64_t n_pages, const int32_t* __restrict__ page_ids, int length,
+    const uint64_t* __restrict__ k_ptrs, const uint64_t* __restrict__ v_ptrs, int64_t head_stride,
+    int n_layers, int H, int D) {
+  const int n_blocks = (length + kPage - 1) / kPage;
+  const int64_t n_units = int64_t(n_blocks) * n_layers * 2 * H;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int warps = blockDim.x / 32;
+  for (int64_t u = int64_t(blockIdx.x) * warps + warp; u < n_units; u += int64_t(gridDim.x) * warps) {
+    int64_t t = u;
+    const int h = int(t % H);
+    t /= H;
+    const int kv = int(t % 2);
+    t /= 2;
+    const int l = int(t % n_layers);
+    const int b = int(t / n_layers);
+    const int page = page_ids[b];
+    if (page < 0 || page >= n_pages) {
+      if (lane == 0) atomicOr(&g_err_word, CKV_DEV_ERR_PAGE_RANGE);
+      continue;
+    }
+    const int r0 = b * kPage;
+    const int rows = min(kPage, length - r0);
+    const uint64_t base = (kv ? v_ptrs : k_ptrs)[l];
+    if ((base & 15u) != 0) {
+      if (lane == 0) atomicOr(&g_err_word, CKV_DEV_ERR_POSITION_RANGE);
+      continue;
+    }
+    const uint16_t* src = reinterpret_cast<const uint16_t*>(base) + h * head_stride + int64_t(r0) * D;
+    uint16_t* dst = pool + (((int64_t(page) * n_layers + l) * 2 + kv) * H + h) * kPage * D;
+    copy_rows_warp(src, D, dst, D, rows, D, 0, false, nullptr, lane);
+  }
+}
+
+int check_rot(int head_dim, int rot) {
+  CKV_REQUIRE(head_dim > 0 && head_dim % 8 == 0 && head_dim <= 2 * kMaxHalf,
+              "head_dim %d must be a positive multiple of 8 and <= %d", head_dim, 2 * kMaxHalf);
+  CKV_REQUIRE(rot > 0 && rot % 16 == 0 && rot <= head_dim,
+              "rot_dims %d must be a positive multiple of 16 and <= head_dim", rot);
+  return CKV_OK;
+}
+
+}  // namespace
+}  // namespace ckv
+
+using namespace ckv;
+
+extern "C" {
+
+int ckv_rope_table(const float* inv_freq, int half_dim, int max_pos, float* table,
+                   ckv_stream_t stream) {
+  CKV_REQUIRE(inv_freq && table, "ckv_rope_table: null pointer");
+  CKV_REQUIRE(half_dim > 0 && max_pos > 0, "ckv_rope_table: bad sizes");
+  const int64_t n = int64_t(half_dim) * max_pos;
+  const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, 8 * num_sms()));
+  rope_table_kernel<<<grid, 256, 0, as_stream(stream)>>>(inv_freq, half_dim, max_pos,
+                                                         reinterpret_cast<float2*>(table));
+  CKV_LAUNCH_CHECK("ckv_rope_table");
+  return CKV_OK;
+}
+
+int ckv_shift_keys(const uint16_t* src, uint16_t* dst, int64_t rows, int head_dim, int rot_dims,
+                   int delta, const float* inv_freq, ckv_stream_t stream) {
+  CKV_REQUIRE(src && dst && inv_freq, "ckv_shift_keys: null pointer");
+  CKV_REQUIRE(aligned16(src) && aligned16(dst), "ckv_shift_keys: pointers must be 16-byte aligned");
+  if (int rc = check_rot(head_dim, rot_dims)) return rc;
+  if (rows <= 0) return CKV_OK;
+  if (delta == 0) {
+    if (src != dst)
+      if (cudaMemcpyAsync(dst, src, rows * head_dim * 2, cudaMemcpyDeviceToDevice,
+                          as_stream(stream)) != cudaSuccess) {
+        set_error("ckv_shift_keys: copy failed");
+        return CKV_ERR_CUDA;
+      }
+    return CKV_OK;
+  }
+  const int64_t items = rows * (head_dim / 8 - rot_dims / 16);
+  const int grid = static_cast<int>(std::min<int64_t>((items + 255) / 256, 16 * num_sms()));
+  rope_rows_kernel<<<grid, 256, 0, as_stream(stream)>>>(src, dst, rows, head_dim, rot_dims, delta,
+                                                        nullptr, 1, inv_freq);
+  CKV_LAUNCH_CHECK("ckv_shift_keys");
+  return CKV_OK;
+}
+
+int ckv_apply_rope(const uint16_t* src, uint16_t* dst, int64_t batch_heads, int seq, int head_dim,
+                   int rot_dims, const int32_t* positions, const float* inv_freq,
+                   ckv_stream_t stream) {
+  CKV_REQUIRE(src && dst && inv_freq && positions, "ckv_apply_rope: null pointer");
+  CKV_REQUIRE(aligned16(src) && aligned16(dst), "ckv_apply_rope: pointers must be 16-byte aligned");
+  if (int rc = check_rot(head_dim, rot_dims)) return rc;
+  CKV_REQUIRE(seq >= 0 && batch_heads >= 0, "ckv_apply_rope: bad sizes");
+  const int64_t rows = batch_heads * seq;
+  if (rows == 0) return CKV_OK;
+  const int64_t items = rows * (head_dim / 8 - rot_dims / 16);
+  const int grid = static_cast<int>(std::min<int64_t>((items + 255) / 256, 16 * num_sms()));
+  rope_rows_kernel<<<grid, 256, 0, as_stream(stream)>>>(src, dst, rows, head_dim, rot_dims, 0,
+                                                        positions, seq, inv_freq);
+  CKV_LAUNCH_CHECK("ckv_apply_rope");
+  return CKV_OK;
+}
+
+static int gather_common(const int32_t* chunk_meta, int n_chunks, const float* inv_freq, int rot,
+                         uint16_t* k_out, uint16_t* v_out, int layer_lo, int layer_hi, int H, int D,
+                         int n_ctx) {
+  CKV_REQUIRE(chunk_meta && inv_freq && k_out && v_out, "blend_gather: null pointer");
+  CKV_REQUIRE(aligned16(k_out) && aligned16(v_out), "blend_gather: outputs must be 16-byte aligned");
+  if (int rc = check_rot(D, rot)) return rc;
+  CKV_REQUIRE(n_chunks >= 0 && n_chunks <= 65535, "blend_gather: n_chunks %d out of range", n_chunks);
+  CKV_REQUIRE(layer_lo >= 0 && layer_hi >= layer_lo, "blend_gather: bad layer range");
+  CKV_REQUIRE(H > 0 && n_ctx > 0, "blend_gather: bad sizes");
+  return CKV_OK;
+}
+
+int ckv_blend_gather_paged(const uint16_t* pool, int64_t n_pages, const int32_t* page_table,
+                           const int32_t* chunk_meta, int n_chunks, const float* inv_freq,
+                           int rot_dims, uint16_t* k_out, uint16_t* v_out, int layer_lo,
+                           int layer_hi, int n_layers, int n_kv_heads, int head_dim, int n_ctx,
+                           ckv_stream_t stream) {
+  if (int rc = gather_common(chunk_meta, n_chunks, inv_freq, rot_dims, k_out, v_out, layer_lo,
+                             layer_hi, n_kv_heads, head_dim, n_ctx))
+    return rc;
+  CKV_REQUIRE(pool && page_table && aligned16(pool), "ckv_blend_gather_paged: bad pool/page table");
+  CKV_REQUIRE(layer_hi <= n_layers, "ckv_blend_gather_paged: layer_hi > n_layers");
+  if (n_chunks == 0 || layer_hi == layer_lo) return CKV_OK;
+  const int gx = std::max(1, 4 * num_sms() / n_chunks);
+  blend_gather_kernel<true><<<dim3(gx, n_chunks), 256, 0, as_stream(stream)>>>(
+      pool, n_pages, page_table, nullptr, nullptr, chunk_meta, inv_freq, rot_dims, k_out, v_out,
+      layer_lo, layer_hi, n_layers, n_kv_heads, head_dim, n_ctx);
+  CKV_LAUNCH_CHECK("ckv_blend_gather_paged");
+  return CKV_OK;
+}
+
+int ckv_blend_gather_dense(const uint64_t* k_ptrs, const uint64_t* v_ptrs,
+                           const int32_t* chunk_meta, int n_chunks, const float* inv_freq,
+                           int rot_dims, uint16_t* k_out, uint16_t* v_out, int layer_lo,
+                           int layer_hi, int n_kv_heads, int head_dim, int n_ctx,
+                           ckv_stream_t stream) {
+  if (int rc = gather_common(chunk_meta, n_chunks, inv_freq, rot_dims, k_out, v_out, layer_lo,
+                             layer_hi, n_kv_heads, head_dim, n_ctx))
+    return rc;
+  CKV_REQUIRE(k_ptrs && v_ptrs, "ckv_blend_gather_dense: null pointer arrays");
+  if (n_chunks == 0 || layer_hi == layer_lo) return CKV_OK;
+  const int gx = std::max(1, 4 * num_sms() / n_chunks);
+  blend_gather_kernel<false><<<dim3(gx, n_chunks), 256, 0, as_stream(stream)>>>(
+      nullptr, 0, nullptr, k_ptrs, v_ptrs, chunk_meta, inv_freq, rot_dims, k_out, v_out, layer_lo,
+      layer_hi, /*n_layers=*/0, n_kv_heads, head_dim, n_ctx);
+  CKV_LAUNCH_CHECK("ckv_blend_gather_dense");
+  return CKV_OK;
+}
+
+int ckv_pages_write(uint16_t* pool, int64_t n_pages, const int32_t* page_ids, int length,
+                    const uint64_t* k_ptrs, const uint64_t* v_ptrs, int64_t head_stride,
+                    int n_layers, int n_kv_heads, int head_dim, ckv_stream_t stream) {
+  CKV_REQUIRE(pool && page_ids && k_ptrs && v_ptrs, "ckv_pages_write: null pointer");
+  CKV_REQUIRE(aligned16(pool), "ckv_pages_write: pool must be 16-byte aligned");
+  CKV_REQUIRE(head_dim > 0 && head_dim % 8 == 0, "ckv_pages_write: head_dim %% 8 != 0");
+  CKV_REQUIRE(n_layers > 0 && n_kv_heads > 0 && length >= 0, "ckv_pages_write: bad sizes");
+  CKV_REQUIRE(head_stride % 8 == 0, "ckv_pages_write: head_stride must keep 16-byte alignment");
+  if (length == 0) return CKV_OK;
+  const int64_t units = int64_t(ceil_div(length, kPage)) * n_layers * 2 * n_kv_heads;
+  const int grid = static_cast<int>(std::min<int64_t>((units + 7) / 8, 8 * num_sms()));
+  pages_write_kernel<<<grid, 256, 0, as_stream(stream)>>>(pool, n_pages, page_ids, length, k_ptrs,
+                                                          v_ptrs, head_stride, n_layers,
+                                                          n_kv_heads, head_dim);
+  CKV_LAUNCH_CHECK("ckv_pages_write");
+  return CKV_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,247 @@
+"""Torch-tensor front end of the C ABI: shape/dtype/device checks, then one call.
+
+Every op runs on the current CUDA stream and launches the library's own
+kernels; nothing here computes on the host.  Tensors are bf16 unless noted.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from chunkkv_b200 import _lib
+
+BF16 = torch.bfloat16
+PAGE_TOKENS = 16
+META_STRIDE = 8
+SEL_META_STRIDE = 4
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _cuda(*ts: torch.Tensor | None) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("chunkkv_b200 ops take CUDA tensors (there is no CPU path)")
+
+
+def _bf16(*ts: torch.Tensor | None) -> None:
+    for t in ts:
+        if t is not None and t.dtype != BF16:
+            raise ValueError(f"expected bfloat16, got {t.dtype}")
+
+
+def _contig(*ts: torch.Tensor | None) -> None:
+    for t in ts:
+        if t is not None and not t.is_contiguous():
+            raise ValueError("expected a contiguous tensor")
+
+
+# ------------------------------------------------------------------ re-RoPE
+def rope_table(inv_freq: torch.Tensor, max_pos: int) -> torch.Tensor:
+    """(cos, sin) of fp32(p * inv_freq[j]) for p < max_pos: float32 [max_pos, half, 2]."""
+    _cuda(inv_freq)
+    half = inv_freq.numel()
+    out = torch.empty((max_pos, half, 2), dtype=torch.float32, device=inv_freq.device)
+    _lib.call("ckv_rope_table", _ptr(inv_freq), half, max_pos, _ptr(out), _stream())
+    return out
+
+
+def shift_keys(keys: torch.Tensor, delta: int, inv_freq: torch.Tensor, rot_dims: int | None = None,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """Rotate post-RoPE keys (..., L, D) by `delta` positions (new tensor unless `out`)."""
+    _cuda(keys, inv_freq)
+    _bf16(keys)
+    _contig(keys)
+    D = keys.shape[-1]
+    rot = D if rot_dims is None else rot_dims
+    out = torch.empty_like(keys) if out is None else out
+    _lib.call("ckv_shift_keys", _ptr(keys), _ptr(out), keys.numel() // D, D, rot, int(delta),
+              _ptr(inv_freq), _stream())
+    return out
+
+
+def apply_rope(x: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor,
+               rot_dims: int | None = None) -> torch.Tensor:
+    """RoPE of x (..., L, D) at int positions (L,)."""
+    _cuda(x, positions, inv_freq)
+    _bf16(x)
+    _contig(x)
+    D, L = x.shape[-1], x.shape[-2]
+    pos = positions.to(torch.int32).contiguous()
+    if pos.numel() != L:
+        raise ValueError(f"positions has {pos.numel()} entries for sequence length {L}")
+    out = torch.empty_like(x)
+    rot = D if rot_dims is None else rot_dims
+    _lib.call("ckv_apply_rope", _ptr(x), _ptr(out), x.numel() // (D * L) if L else 0, L, D, rot,
+              _ptr(pos), _ptr(inv_freq), _stream())
+    return out
+
+
+# ---------------------------------------------------------- gather / scatter
+def blend_gather_paged(pool: torch.Tensor, page_table: torch.Tensor, chunk_meta: torch.Tensor,
+                       inv_freq: torch.Tensor, k_out: torch.Tensor, v_out: torch.Tensor,
+                       layer_lo: int, layer_hi: int, rot_dims: int | None = None) -> None:
+    """Moved cached chunks (paged) -> blended cache k_out/v_out [layers, H, N, D]."""
+    _cuda(pool, page_table, chunk_meta, inv_freq, k_out, v_out)
+    n_pages, n_layers, _, H, _, D = pool.shape
+    _lib.call("ckv_blend_gather_paged", _ptr(pool), n_pages, _ptr(page_table), _ptr(chunk_meta),
+              chunk_meta.shape[0], _ptr(inv_freq), D if rot_dims is None else rot_dims, _ptr(k_out),
+              _ptr(v_out), layer_lo, layer_hi, n_layers, H, D, k_out.shape[2], _stream())
+
+
+def blend_gather_dense(k_ptrs: torch.Tensor, v_ptrs: torch.Tensor, chunk_meta: torch.Tensor,
+                       inv_freq: torch.Tensor, k_out: torch.Tensor, v_out: torch.Tensor,
+                       layer_lo: int, layer_hi: int, rot_dims: int | None = None) -> None:
+    """Moved cached chunks (per-layer tensors, by address) -> blended cache."""
+    _cuda(k_ptrs, v_ptrs, chunk_meta, inv_freq, k_out, v_out)
+    H, D = k_out.shape[1], k_out.shape[3]
+    _lib.call("ckv_blend_gather_dense", _ptr(k_ptrs), _ptr(v_ptrs), _ptr(chunk_meta),
+              chunk_meta.shape[0], _ptr(inv_freq), D if rot_dims is None else rot_dims, _ptr(k_out),
+              _ptr(v_out), layer_lo, layer_hi, H, D, k_out.shape[2], _stream())
+
+
+def pages_write(pool: torch.Tensor, page_ids: torch.Tensor, length: int, k_ptrs: torch.Tensor,
+                v_ptrs: torch.Tensor, head_stride: int) -> None:
+    _cuda(pool, page_ids, k_ptrs, v_ptrs)
+    n_pages, n_layers, _, H, _, D = pool.shape
+    _lib.call("ckv_pages_write", _ptr(pool), n_pages, _ptr(page_ids), length, _ptr(k_ptrs),
+              _ptr(v_ptrs), head_stride, n_layers, H, D, _stream())
+
+
+# ------------------------------------------------------ deviation / selection
+def deviation_select(k_fresh: torch.Tensor, v_fresh: torch.Tensor, k_base: torch.Tensor,
+                     v_base: torch.Tensor, active: torch.Tensor, pos_flags: torch.Tensor,
+                     sel_meta: torch.Tensor, threshold: float | None, ws: "SelectWorkspace") -> None:
+    """Layer-1 deviation + pooled top-k into the workspace (no host sync)."""
+    _cuda(k_fresh, v_fresh, k_base, v_base, active, pos_flags, sel_meta)
+    H, n_ctx, D = k_base.shape
+    _lib.call("ckv_deviation_select", _ptr(k_fresh), _ptr(v_fresh), k_fresh.stride(0), _ptr(k_base),
+              _ptr(v_base), _ptr(active), active.numel(), _ptr(pos_flags), n_ctx, _ptr(sel_meta),
+              sel_meta.shape[0], int(threshold is not None), float(threshold or 0.0), H, D,
+              _ptr(ws.diff), _ptr(ws.norm), _ptr(ws.rel), _ptr(ws.keep_abs), _ptr(ws.sel),
+              _ptr(ws.counts), _ptr(ws.flags), _ptr(ws.counter), _stream())
+
+
+def select_from_scores(diff: torch.Tensor, norm: torch.Tensor, pos_flags: torch.Tensor,
+                       sel_meta: torch.Tensor, threshold: float | None,
+                       ws: "SelectWorkspace") -> None:
+    _cuda(diff, norm, pos_flags, sel_meta)
+    _lib.call("ckv_select_from_scores", _ptr(diff), _ptr(norm), _ptr(pos_flags), pos_flags.numel(),
+              _ptr(sel_meta), sel_meta.shape[0], int(threshold is not None), float(threshold or 0.0),
+              _ptr(ws.rel), _ptr(ws.keep_abs), _ptr(ws.sel), _ptr(ws.counts), _ptr(ws.flags),
+              _stream())
+
+
+class SelectWorkspace:
+    """Device buffers of one selection (sized for n_ctx positions, n_chunks chunks)."""
+
+    def __init__(self, n_ctx: int, n_chunks: int, device):
+        f32 = dict(dtype=torch.float32, device=device)
+        i32 = dict(dtype=torch.int32, device=device)
+        self.diff = torch.zeros(n_ctx, **f32)
+        self.norm = torch.zeros(n_ctx, **f32)
+        self.rel = torch.zeros(max(1, n_chunks), **f32)
+        self.keep_abs = torch.empty(n_ctx, **i32)
+        self.sel = torch.empty(n_ctx, **i32)
+        self.counts = torch.zeros(8, **i32)
+        self.flags = torch.zeros((n_ctx + 3) // 4 * 4, dtype=torch.uint8, device=device)
+        self.counter = torch.zeros(1, **i32)
+
+
+def apply_selection(ws: SelectWorkspace, max_rows: int, h_in, h_out, x_in, x_out, k_fresh, v_fresh,
+                    k_cache, v_cache) -> None:
+    H, n_ctx, D = k_cache.shape
+    _lib.call("ckv_apply_selection", _ptr(ws.sel), _ptr(ws.keep_abs), _ptr(ws.counts), max_rows,
+              _ptr(h_in), _ptr(h_out), _ptr(x_in), _ptr(x_out), h_in.shape[-1], _ptr(k_fresh),
+              _ptr(v_fresh), k_fresh.stride(0), _ptr(k_cache), _ptr(v_cache), H, D, n_ctx, _stream())
+
+
+# ------------------------------------------------------------ decoder pieces
+def embed(table: torch.Tensor, tokens: torch.Tensor, rows: torch.Tensor | None,
+          out: torch.Tensor) -> torch.Tensor:
+    _cuda(table, tokens, rows, out)
+    n = out.shape[0]
+    _lib.call("ckv_embed", _ptr(table), table.shape[0], table.shape[1], _ptr(tokens), _ptr(rows), n,
+              _ptr(out), _stream())
+    return out
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    _cuda(x, w)
+    _bf16(x, w)
+    out = torch.empty_like(x) if out is None else out
+    rows = x.numel() // x.shape[-1]
+    _lib.call("ckv_rmsnorm", _ptr(x), _ptr(w), _ptr(out), rows, x.shape[-1], float(eps), _stream())
+    return out
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    _cuda(x, w, bias)
+    _bf16(x, w, bias)
+    _contig(x, w)
+    m, k = x.numel() // x.shape[-1], x.shape[-1]
+    n = w.shape[0]
+    out = torch.empty((*x.shape[:-1], n), dtype=BF16, device=x.device) if out is None else out
+    _lib.call("ckv_linear", _ptr(x), _ptr(w), _ptr(bias), _ptr(out), m, n, k, _stream())
+    return out
+
+
+def linear_residual(x: torch.Tensor, w: torch.Tensor, h: torch.Tensor, m: int | None = None) -> torch.Tensor:
+    _cuda(x, w, h)
+    m = x.numel() // x.shape[-1] if m is None else m
+    _lib.call("ckv_linear_residual", _ptr(x), _ptr(w), _ptr(h), m, w.shape[0], x.shape[-1], _stream())
+    return h
+
+
+def linear_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor, m: int | None = None) -> torch.Tensor:
+    _cuda(x, w_gate_up, out)
+    m = x.numel() // x.shape[-1] if m is None else m
+    _lib.call("ckv_linear_swiglu", _ptr(x), _ptr(w_gate_up), _ptr(out), m, w_gate_up.shape[0] // 2,
+              x.shape[-1], _stream())
+    return out
+
+
+def qkv_rope(x, w_qkv, b_qkv, m, col_begin, col_end, n_q_heads, n_kv_heads, head_dim, positions,
+             rope_tab, q_out=None, k_cache=None, v_cache=None, k_compact=None, v_compact=None) -> None:
+    n_ctx = k_cache.shape[1] if k_cache is not None else 0
+    _lib.call("ckv_qkv_rope", _ptr(x), _ptr(w_qkv), _ptr(b_qkv), m, x.shape[-1], col_begin, col_end,
+              n_q_heads, n_kv_heads, head_dim, _ptr(positions), _ptr(rope_tab), rope_tab.shape[0],
+              _ptr(q_out), _ptr(k_cache), _ptr(v_cache), n_ctx, _ptr(k_compact), _ptr(v_compact),
+              _stream())
+
+
+def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, positions: torch.Tensor,
+              out: torch.Tensor, m: int | None = None, scale: float | None = None) -> torch.Tensor:
+    """q/out [m, Hq, D]; caches [H, n_ctx, D]; key j visible to row i iff j <= positions[i]."""
+    _cuda(q, k_cache, v_cache, positions, out)
+    H, n_ctx, D = k_cache.shape
+    m = q.shape[0] if m is None else m
+    Hq = q.shape[-2] if q.dim() == 3 else q.shape[-1] // D
+    scale = 1.0 / math.sqrt(D) if scale is None else scale
+    _lib.call("ckv_attention", _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(positions), _ptr(out), m, Hq,
+              H, D, n_ctx, float(scale), _stream())
+    return out
+
+
+def gemv(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    _cuda(x, w)
+    m, k = x.shape
+    out = torch.empty((m, w.shape[0]), dtype=BF16, device=x.device) if out is None else out
+    _lib.call("ckv_gemv", _ptr(x), _ptr(w), _ptr(out), m, w.shape[0], k, _stream())
+    return out
+
+
+def log_softmax(row: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    _cuda(row)
+    out = torch.empty(row.numel(), dtype=torch.float32, device=row.device) if out is None else out
+    _lib.call("ckv_log_softmax", _ptr(row), row.numel(), _ptr(out), _stream())
+    return out

@@ -1,0 +1,236 @@
+/*
+ * chunkkv_b200 — C ABI of the B200 (sm_100a) blend-prefill kernels.
+ *
+ * The reference (sarvanithin/chunkkv) is pure Python: its blend prefill is
+ * TorchEngine.prefill (src/chunkkv/engine/torch_engine.py:80-178) over torch
+ * library calls, and it has no FFI of its own.  Every entry point below
+ * replaces one step of that method (or of the re-RoPE helpers / the store
+ * insert); the reference line range each one stands in for is given beside it.
+ *
+ * Conventions shared by every entry point:
+ *   - all pointers are DEVICE pointers unless named *_host; bf16 tensors are
+ *     passed as uint16_t* (raw bf16 bit patterns), row-major, contiguous
+ *     unless a stride argument says otherwise;
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream); every call is
+ *     asynchronous on that stream and never synchronises the device;
+ *   - no entry point allocates device memory: callers pass every buffer;
+ *   - the return value is a ckv_status; on failure ckv_last_error() gives a
+ *     one-line message (thread-local) and nothing was launched.
+ * Faults detected on the device (a bounded wait that ran out, an index the
+ * kernel refused) are recorded in a device error word that
+ * ckv_get_device_error() reads and clears after a synchronisation.
+ */
+#ifndef CHUNKKV_B200_H
+#define CHUNKKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define CKV_API __attribute__((visibility("default")))
+#else
+#define CKV_API
+#endif
+
+typedef void* ckv_stream_t; /* cudaStream_t */
+
+typedef enum {
+  CKV_OK = 0,
+  CKV_ERR_ARG = 1,         /* bad shape / pointer / alignment (python: ValueError) */
+  CKV_ERR_CUDA = 2,        /* launch or runtime failure (python: RuntimeError) */
+  CKV_ERR_DEVICE = 3,      /* device-side error word set (python: RuntimeError) */
+  CKV_ERR_UNSUPPORTED = 4  /* shape the kernels do not cover (python: NotImplementedError) */
+} ckv_status;
+
+/* Device-side error bits reported by ckv_get_device_error(). */
+#define CKV_DEV_ERR_WAIT_TIMEOUT   0x1u  /* an mbarrier wait ran past its limit */
+#define CKV_DEV_ERR_PAGE_RANGE     0x2u  /* a page id outside [0, n_pages) was skipped */
+#define CKV_DEV_ERR_SELECT_UNCOMPUTED 0x4u /* selection kept a position never computed
+                                              (torch_engine.py:151 assert) */
+#define CKV_DEV_ERR_POSITION_RANGE 0x8u  /* a position outside [0, n_ctx) was skipped */
+
+/* ---- library -------------------------------------------------------------- */
+CKV_API const char* ckv_version(void);
+CKV_API const char* ckv_last_error(void);
+/* Reads and clears the device error word of the current device (synchronises
+ * the device first).  *code receives the OR of CKV_DEV_ERR_* bits. */
+CKV_API int ckv_get_device_error(uint32_t* code);
+
+/* ---- re-RoPE (scheduler/rerope.py:16-61; torch_engine.py:33,46-59) -------- */
+
+/* table[p][j] = (cos, sin)(fp32(p) * inv_freq[j]) for p < max_pos, j < half_dim.
+ * Angles exactly as torch_engine.py:54 forms them (fp32 product, fp32 cos/sin). */
+CKV_API int ckv_rope_table(const float* inv_freq, int half_dim, int max_pos, float* table,
+                   ckv_stream_t stream);
+
+/* Re-RoPE of post-RoPE keys by a whole-tensor shift `delta`
+ * (TorchEngine.shift_keys, torch_engine.py:56-59; rerope.shift_keys, rerope.py:56-61).
+ * src/dst: [rows][head_dim] bf16 (any (B,H,L) flattening); rotary pairs are
+ * (j, j + rot_dims/2) for j < rot_dims/2; dims >= rot_dims are copied.
+ * delta == 0 copies.  src == dst is allowed. */
+CKV_API int ckv_shift_keys(const uint16_t* src, uint16_t* dst, int64_t rows, int head_dim,
+                   int rot_dims, int delta, const float* inv_freq, ckv_stream_t stream);
+
+/* RoPE at explicit positions (rerope.apply_rope, rerope.py:50-53;
+ * TorchEngine._rope, torch_engine.py:53-54).  src/dst: [batch_heads][seq][head_dim];
+ * positions: [seq] int32. */
+CKV_API int ckv_apply_rope(const uint16_t* src, uint16_t* dst, int64_t batch_heads, int seq,
+                   int head_dim, int rot_dims, const int32_t* positions,
+                   const float* inv_freq, ckv_stream_t stream);
+
+/* ---- gather of moved chunks into the blended cache -------------------------
+ * Replaces base_kv (torch_engine.py:96-103) for ALL layers in one launch:
+ * for every chunk c and layer l in [max(layer_lo, meta.layer_begin), min(layer_hi, meta.layer_end)),
+ *   k_out[l - layer_lo][h][dst_start + t][:] = shift(K_c[l][h][src_off + t][:], delta)
+ *   v_out[l - layer_lo][h][dst_start + t][:] = V_c[l][h][src_off + t][:]
+ * k_out/v_out: [layer_hi - layer_lo][n_kv_heads][n_ctx][head_dim].
+ * chunk_meta: [n_chunks][CKV_META_STRIDE] int32 (CKV_META_* fields below).
+ *
+ * Paged source: page pool [n_pages][n_layers][2 (K,V)][n_kv_heads][CKV_PAGE_TOKENS][head_dim],
+ * the chunk's pages listed at page_table[meta.table_offset ...]. */
+#define CKV_PAGE_TOKENS 16
+#define CKV_META_STRIDE 8
+#define CKV_META_TABLE_OFFSET 0 /* first page-table slot (paged) / first pointer slot (dense) */
+#define CKV_META_LENGTH 1       /* tokens to copy */
+#define CKV_META_DST_START 2    /* destination position (Placement.start) */
+#define CKV_META_DELTA 3        /* Placement.start - ChunkKV.start */
+#define CKV_META_LAYER_BEGIN 4  /* first layer to copy (1 skips a layer 0 that is recomputed) */
+#define CKV_META_LAYER_END 5    /* one past the last layer to copy */
+#define CKV_META_SRC_OFFSET 6   /* first token of the chunk to copy */
+#define CKV_META_HEAD_STRIDE 7  /* dense source only: elements between heads */
+
+CKV_API int ckv_blend_gather_paged(const uint16_t* pool, int64_t n_pages, const int32_t* page_table,
+                           const int32_t* chunk_meta, int n_chunks, const float* inv_freq,
+                           int rot_dims, uint16_t* k_out, uint16_t* v_out, int layer_lo,
+                           int layer_hi, int n_layers, int n_kv_heads, int head_dim, int n_ctx,
+                           ckv_stream_t stream);
+
+/* Dense source: k_ptrs/v_ptrs are device arrays of device addresses,
+ * [n_chunks * n_layers] (slot meta.table_offset + l), each pointing at a
+ * (H, len, D) tensor with head stride meta.head_stride and token stride head_dim
+ * (what ChunkKV.keys[l] holds, torch_engine.py:101-102). */
+CKV_API int ckv_blend_gather_dense(const uint64_t* k_ptrs, const uint64_t* v_ptrs,
+                           const int32_t* chunk_meta, int n_chunks, const float* inv_freq,
+                           int rot_dims, uint16_t* k_out, uint16_t* v_out, int layer_lo,
+                           int layer_hi, int n_kv_heads, int head_dim, int n_ctx,
+                           ckv_stream_t stream);
+
+/* ---- store insert (PrefillResult.chunk base.py:55-60 + KVStore.put kvstore.py:47-58) --
+ * Writes `length` tokens of every layer into pages page_ids[0 .. ceil(length/16)).
+ * k_ptrs/v_ptrs: device arrays [n_layers] of device addresses of (H, >=length, D)
+ * sources with head stride head_stride (elements) and token stride head_dim. */
+CKV_API int ckv_pages_write(uint16_t* pool, int64_t n_pages, const int32_t* page_ids, int length,
+                    const uint64_t* k_ptrs, const uint64_t* v_ptrs, int64_t head_stride,
+                    int n_layers, int n_kv_heads, int head_dim, ckv_stream_t stream);
+
+/* ---- layer-1 deviation + pooled top-k (torch_engine.py:117-153) ------------
+ * Fused: per active token diff = sum (bf16(k - K))^2 + sum (bf16(v - V))^2,
+ * norm = sum k^2 + sum v^2 (fp32), then in the last CTA to finish: per-chunk
+ * rel = sum diff / sum norm, escalation, budget capped at the eligible count,
+ * top-`budget` by diff (ties: lower position first), compaction.
+ *   k_fresh/v_fresh: [n_act][n_kv_heads*head_dim] rows at stride fresh_row_stride
+ *   k_base/v_base  : [n_kv_heads][n_ctx][head_dim] (layer-1 blended cache before the write)
+ *   active         : [n_act] ascending positions computed at layer 1
+ *   pos_flags      : [n_ctx] bit0 cached, bit1 sink, bit2 exact
+ *   sel_meta       : [n_chunks][4] start, length, budget (-1: ratio <= 0, not pooled), exact
+ * Outputs: diff/norm [n_ctx] (positions not in `active` untouched), rel [n_chunks],
+ *   keep_abs [n_ctx] ascending kept positions, sel [n_ctx] their index in `active`,
+ *   counts [8]: n_sel, selected_cached, budget_final, n_eligible, escalated_mask_lo,
+ *   status (0 ok), n_keep_fresh, reserved.
+ * The threshold is compared in double, as the reference compares the Python float
+ * rel (torch_engine.py:132-134).
+ * Scratch: flags [n_ctx rounded up to a multiple of 4] bytes, 4-byte aligned;
+ * counter: one uint32 that must be zero before the first call (the kernel leaves
+ * it zero).  Calls that share a counter must not overlap on the GPU. */
+#define CKV_SEL_META_STRIDE 4
+CKV_API int ckv_deviation_select(const uint16_t* k_fresh, const uint16_t* v_fresh,
+                         int64_t fresh_row_stride, const uint16_t* k_base,
+                         const uint16_t* v_base, const int32_t* active, int n_act,
+                         const uint8_t* pos_flags, int n_ctx, const int32_t* sel_meta,
+                         int n_chunks, int has_threshold, double escalate_threshold,
+                         int n_kv_heads, int head_dim, float* diff, float* norm, float* rel,
+                         int32_t* keep_abs, int32_t* sel, int32_t* counts, uint8_t* flags,
+                         uint32_t* counter, ckv_stream_t stream);
+
+/* Selection only, from given fp32 scores (torch_engine.py:125-153): the same
+ * device code as the second phase of ckv_deviation_select, one CTA.  `active`
+ * is implied: every non-exact position, ascending. */
+CKV_API int ckv_select_from_scores(const float* diff, const float* norm, const uint8_t* pos_flags,
+                           int n_ctx, const int32_t* sel_meta, int n_chunks,
+                           int has_threshold, double escalate_threshold, float* rel,
+                           int32_t* keep_abs, int32_t* sel, int32_t* counts, uint8_t* flags,
+                           ckv_stream_t stream);
+
+/* Shrink to the selection (torch_engine.py:152-156): for i < counts[0]
+ *   h_out[i] = h_in[sel[i]], x_out[i] = x_in[sel[i]]  (rows of `hidden`)
+ *   k_cache[h][keep_abs[i]] = k_fresh[sel[i]][h], same for v.
+ * Rows at or beyond counts[0] (up to max_rows) are left untouched. */
+CKV_API int ckv_apply_selection(const int32_t* sel, const int32_t* keep_abs, const int32_t* counts,
+                        int max_rows, const uint16_t* h_in, uint16_t* h_out,
+                        const uint16_t* x_in, uint16_t* x_out, int hidden,
+                        const uint16_t* k_fresh, const uint16_t* v_fresh,
+                        int64_t fresh_row_stride, uint16_t* k_cache, uint16_t* v_cache,
+                        int n_kv_heads, int head_dim, int n_ctx, ckv_stream_t stream);
+
+/* ---- decoder pieces of the recompute (torch_engine.py:61-76, 105-107, 112-165) -- */
+
+/* out[i] = table[tokens[rows[i]]] (embed_tokens, torch_engine.py:105-107). */
+CKV_API int ckv_embed(const uint16_t* table, int vocab, int hidden, const int32_t* tokens,
+              const int32_t* rows, int n_rows, uint16_t* out, ckv_stream_t stream);
+
+/* Qwen2RMSNorm: y = w * bf16(x * rsqrt(mean(x^2) + eps)) (fp32 inside). */
+CKV_API int ckv_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows, int hidden,
+                float eps, ckv_stream_t stream);
+
+/* out = bf16(x @ w^T (+ bias)); x [m][k], w [n][k] (nn.Linear), out [m][n].
+ * tcgen05/TMEM GEMM; k % 8 == 0, n % 16 == 0, 16-byte aligned rows. */
+CKV_API int ckv_linear(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* out,
+               int m, int n, int k, ckv_stream_t stream);
+
+/* h = bf16(h + bf16(x @ w^T)) in place (o_proj / down_proj + residual,
+ * torch_engine.py:72-73). */
+CKV_API int ckv_linear_residual(const uint16_t* x, const uint16_t* w, uint16_t* h, int m, int n, int k,
+                        ckv_stream_t stream);
+
+/* out = bf16(silu(bf16(x@Wg^T)) * bf16(x@Wu^T)) (Qwen2MLP gate/up).  w_gate_up
+ * interleaves the two weights in blocks of 128 rows: rows [256b, 256b+128) are
+ * gate rows [128b, 128b+128), rows [256b+128, 256b+256) the matching up rows.
+ * out [m][inter]; inter % 128 == 0. */
+CKV_API int ckv_linear_swiglu(const uint16_t* x, const uint16_t* w_gate_up, uint16_t* out, int m,
+                      int inter, int k, ckv_stream_t stream);
+
+/* QKV projection + bias + RoPE at `positions` (TorchEngine._qkv, torch_engine.py:61-66)
+ * for output columns [col_begin, col_end) of w_qkv ([Hq*D + 2*H*D][k], q|k|v rows).
+ * q heads -> q_out [m][Hq*D]; k/v heads -> scattered into k_cache/v_cache
+ * [H][n_ctx][D] at positions[i] (torch_engine.py:155-156) when those are non-NULL,
+ * else into k_compact/v_compact [m][H*D].  rope_table from ckv_rope_table with
+ * rope_max_pos > every position. */
+CKV_API int ckv_qkv_rope(const uint16_t* x, const uint16_t* w_qkv, const uint16_t* b_qkv, int m, int k,
+                 int col_begin, int col_end, int n_q_heads, int n_kv_heads, int head_dim,
+                 const int32_t* positions, const float* rope_table, int rope_max_pos,
+                 uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache, int n_ctx,
+                 uint16_t* k_compact, uint16_t* v_compact, ckv_stream_t stream);
+
+/* Attention of m query tokens over the blended cache with the reference's
+ * position mask key j visible iff j <= positions[i] (torch_engine.py:68-70,157),
+ * GQA n_q_heads / n_kv_heads.  q/out [m][Hq][D]; caches [H][n_ctx][D]. */
+CKV_API int ckv_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                  const int32_t* positions, uint16_t* out, int m, int n_q_heads,
+                  int n_kv_heads, int head_dim, int n_ctx, float scale, ckv_stream_t stream);
+
+/* Small-m projection (lm_head on the logit rows, torch_engine.py:75-76,165):
+ * out [m][n] = bf16(x [m][k] @ w[n][k]^T), m <= 8. */
+CKV_API int ckv_gemv(const uint16_t* x, const uint16_t* w, uint16_t* out, int m, int n, int k,
+             ckv_stream_t stream);
+
+/* log_softmax of one bf16 row into fp32 (TorchEngine.last_logprobs, torch_engine.py:200-201). */
+CKV_API int ckv_log_softmax(const uint16_t* logits, int n, float* out, ckv_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CHUNKKV_B200_H */
