@@ -1,0 +1,423 @@
+#!/usr/bin/env python
+"""Blend-prefill benchmark (Qwen2.5-7B shape on one B200).
+
+Workload per step: one blend prefill of a request made of 10 cached chunks x 512
+tokens served in a seeded random permutation plus a 128-token query (N = 5248),
+15 % recompute + 4 sink tokens per chunk, through TorchEngine.prefill.  Weights
+are random-init bf16 (seed 0); chunk K/V come from a full prefill of the chunks
+in their original order, stored in the paged HBM store (untimed setup).
+
+    python bench.py [--gpus N --steps K --warmup W]            # this engine
+    python bench.py --impl reference [...]                      # CPU reference arm
+
+Under torchrun each rank serves its own request stream on its own GPU (data
+parallel by request, no collective on the data path); times are the max over
+ranks.  One JSON line is printed by rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import random
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+METRIC = "blend-prefill tokens/s (Qwen2.5-7B shape, 10x512 shuffled cached chunks + 128-token query)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--ratio", type=float, default=0.15)
+    ap.add_argument("--n-sink", type=int, default=4)
+    ap.add_argument("--shape", default="qwen2.5-7b")
+    ap.add_argument("--chunks", type=int, default=10)
+    ap.add_argument("--chunk-len", type=int, default=512)
+    ap.add_argument("--query-len", type=int, default=128)
+    ap.add_argument("--cpu-layers", type=int, default=3, help="layers the CPU sample executes")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--extra-ratios", default="0.30,0.50", help="also time these ratios (TTFT only)")
+    return ap.parse_args()
+
+
+def peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured"
+        except Exception:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def make_request(vocab: int, n_chunks: int, chunk_len: int, query_len: int, seed: int):
+    rng = random.Random(seed)
+    chunks = [[rng.randrange(vocab) for _ in range(chunk_len)] for _ in range(n_chunks)]
+    query = [rng.randrange(vocab) for _ in range(query_len)]
+    order = list(range(n_chunks))
+    while order == sorted(order):
+        rng.shuffle(order)
+    return chunks, order, query
+
+
+def max_over_ranks(x: float, device="cpu") -> float:
+    """Timing reduction of the data-parallel run: the slowest rank's time (no data exchange)."""
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return float(x)
+    t = torch.tensor([float(x)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def request_seed(rank: int) -> int:
+    """Each rank serves its own request stream (data parallel by request)."""
+    return 1000 + rank
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clock and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "200"], stdout=self.file,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        return False
+
+    def summary(self) -> dict:
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append((float(f[1]), float(f[2]), float(f[3]), f[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for _, _, _, r in rows for n, v in zip(names, r) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "power_w_max": max(r[2] for r in rows), "samples": len(rows), "reasons": reasons}
+
+
+# -------------------------------------------------------------- CPU sample
+class CpuSample:
+    """The reference algorithm (oracle port of torch_engine.py) on the host cores.
+
+    Bounded sample: the same request on a truncated model of `cpu_layers` layers
+    (layer 0 on every token, layer 1 with the deviation and selection, then one
+    recompute layer); the time of layers 2..L-1 is extrapolated from the
+    measured layer-2 time.  fp32 (the host has no fast bf16 matmul path).
+    Weight values are a tiled random block (timing only)."""
+
+    def __init__(self, args, shape):
+        import torch
+
+        from chunkkv_b200.engine.base import BlendConfig, ChunkKV, Placement
+        from chunkkv_b200.engine.weights import param_shapes
+        from oracle.blend_oracle import OracleEngine
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.shape = shape
+        self.nl = nl = max(3, args.cpu_layers)
+        small = shape.truncated(nl)
+        g = torch.Generator().manual_seed(0)
+        block = torch.randn(1 << 20, generator=g) * 0.02
+
+        def fill(*shp, scale=1.0):
+            n = 1
+            for x in shp:
+                n *= x
+            reps_ = (n + block.numel() - 1) // block.numel()
+            return (block.repeat(reps_)[:n] * scale).view(*shp).clone()
+
+        sd = {}
+        for name, shp in param_shapes(small):
+            if name.endswith("norm.weight"):
+                sd[name] = torch.ones(shp)
+            else:
+                sd[name] = fill(*shp, scale=50.0 if "embed" in name else 1.0)
+        self.eng = OracleEngine(small, sd, dtype=torch.float32)
+        chunks, order, query = make_request(shape.vocab, args.chunks, args.chunk_len, args.query_len, 0)
+        H, D = shape.n_kv, shape.head_dim
+        tokens, pl = [], []
+        for c in order:
+            ck = ChunkKV([fill(1, H, args.chunk_len, D, scale=50.0) for _ in range(nl)],
+                         [fill(1, H, args.chunk_len, D, scale=50.0) for _ in range(nl)], c * args.chunk_len)
+            pl.append(Placement(ck, len(tokens)))
+            tokens += chunks[c]
+        self.tokens, self.pl = tokens + query, pl
+        self.cfg = BlendConfig(recompute_ratio=args.ratio, n_sink=args.n_sink)
+        self.threads = torch.get_num_threads()
+
+    def run_once(self) -> float:
+        """Estimated full-depth TTFT in seconds."""
+        t0 = time.perf_counter()
+        res = self.eng.prefill(self.tokens, self.pl, self.cfg)
+        self.eng.last_logprobs(res)
+        total = time.perf_counter() - t0
+        lt = res.layer_times
+        return (total - sum(lt)) + lt[0] + lt[1] + (self.shape.n_layers - 2) * lt[2]
+
+    def describe(self, reps: int) -> str:
+        return (f"oracle port of TorchEngine.prefill on the host CPU, fp32, same request shape "
+                f"(N={len(self.tokens)}, 15% recompute); {self.nl} of {self.shape.n_layers} layers executed, "
+                f"layers 2..{self.shape.n_layers - 1} extrapolated from the measured layer-2 time; "
+                f"median of {reps}")
+
+
+def cpu_sample(args, shape, reps: int = 2) -> dict:
+    s = CpuSample(args, shape)
+    t = statistics.median(s.run_once() for _ in range(reps))
+    return {"value": round(len(s.tokens) / t, 2), "unit": "tokens/s", "cores": s.threads, "kind": "port",
+            "ttft_ms": round(t * 1e3, 1), "sample": s.describe(reps)}
+
+
+# ------------------------------------------------------------------ ours
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from chunkkv_b200 import _lib, ops
+    from chunkkv_b200.engine.base import BlendConfig, Placement
+    from chunkkv_b200.engine.torch_engine import TorchEngine
+    from chunkkv_b200.engine.weights import SHAPES, random_packed
+    from chunkkv_b200.store.keys import LookupKey
+    from chunkkv_b200.store.kvstore import Entry, KVStore
+    from chunkkv_b200.types import TrustLevel
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and world > 1:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    shape = SHAPES[args.shape]
+    weights = random_packed(shape, seed=0, device=dev)
+    eng = TorchEngine.from_packed(weights)
+    chunks, order, query = make_request(shape.vocab, args.chunks, args.chunk_len, args.query_len,
+                                        request_seed(rank))
+    # untimed setup: the chunks' K/V from a prefill in the original order, into the paged store
+    first = eng.prefill(sum(chunks, []))
+    store = KVStore(budget_bytes=2 * args.chunks * args.chunk_len * shape.kv_bytes_per_token)
+    paged = []
+    for i in range(args.chunks):
+        key = LookupKey.build(chunks[i], shape.name, None)
+        store.put(key, Entry(first.chunk(i * args.chunk_len, (i + 1) * args.chunk_len), "bench", f"c{i}",
+                             TrustLevel.SYSTEM))
+        paged.append(store.get(key)[0].kv)
+    del first
+    torch.cuda.empty_cache()
+    tokens, pl = [], []
+    for c in order:
+        pl.append(Placement(paged[c], len(tokens)))
+        tokens += chunks[c]
+    tokens += query
+    N = len(tokens)
+    cfg = BlendConfig(recompute_ratio=args.ratio, n_sink=args.n_sink)
+
+    def step(c=cfg):
+        return eng.prefill(tokens, pl, c)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    _lib.check_device()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- device-timed region: K prefills, inputs resident in HBM
+    stream = torch.cuda.current_stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    barrier()
+    torch.cuda.synchronize()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    phys = int(vis.split(",")[local]) if vis and vis.split(",")[local].strip().isdigit() else local
+    with ClockSampler(phys) as clk, \
+            ops.LaunchTimer() as timer:
+        ev[0].record(stream)
+        for i in range(args.steps):
+            res = step()
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    step_ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
+    total_ms = max_over_ranks(ev[0].elapsed_time(ev[-1]), dev)
+    kern = timer.summary()
+    launches = sum(d["launches"] for d in kern.values())
+    stats = res.stats
+
+    # ---- e2e: the public API with host buffers (token list in, log-probs out)
+    barrier()
+    torch.cuda.synchronize()
+    wall = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        r = eng.prefill(tokens, pl, cfg)
+        lp = eng.last_logprobs(r)
+        wall.append(time.perf_counter() - t0)
+    e2e_total = max_over_ranks(sum(wall), dev)
+    h2d = eng.last_h2d_bytes
+    d2h = eng.last_d2h_bytes + lp.nbytes
+
+    extra = {}
+    for rs in [float(x) for x in args.extra_ratios.split(",") if x]:
+        c2 = BlendConfig(recompute_ratio=rs, n_sink=args.n_sink)
+        step(c2)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = max(3, args.steps // 4)
+        e0.record()
+        for _ in range(n):
+            step(c2)
+        e1.record()
+        torch.cuda.synchronize()
+        extra[f"{rs:.2f}"] = round(e0.elapsed_time(e1) / n, 3)
+
+    _lib.check_device()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    pk, pk_kind = peaks()
+    gemm_names = ("ckv_linear", "ckv_linear_residual", "ckv_linear_swiglu", "ckv_qkv_rope")
+    g_ms = sum(kern[n]["ms"] for n in gemm_names if n in kern)
+    g_fl = sum(kern[n]["flops"] for n in gemm_names if n in kern)
+    g_n = sum(kern[n]["launches"] for n in gemm_names if n in kern)
+    busy = sum(d["ms"] for d in kern.values())
+    achieved = g_fl / (g_ms * 1e-3) / 1e12 if g_ms else 0.0
+    roof = {"kernel": "tcgen05 GEMMs (qkv+rope, o_proj+residual, gate/up+swiglu, down+residual)",
+            "bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops_sustained"],
+            "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops_sustained"], 4),
+            "peak_source": f"{pk_kind} bf16_tflops_sustained", "traffic": None,
+            "flops_per_launch": round(g_fl / max(g_n, 1)), "ms_per_launch": round(g_ms / max(g_n, 1), 4)}
+    kernels = {}
+    for name, d in sorted(kern.items(), key=lambda kv: -kv[1]["ms"]):
+        e = {"launches": d["launches"], "ms": round(d["ms"], 3), "share": round(d["ms"] / busy, 4) if busy else 0}
+        if d["flops"] and name != "ckv_gemv":
+            tf = d["flops"] / (d["ms"] * 1e-3) / 1e12
+            e.update(tflops=round(tf, 1), frac_tensor=round(tf / pk["bf16_tflops_sustained"], 4))
+        if d["bytes"]:
+            gb = d["bytes"] / (d["ms"] * 1e-3) / 1e9
+            e.update(gbs=round(gb, 1), frac_hbm=round(gb / pk["hbm_gbs"], 4),
+                     bytes_per_launch=round(d["bytes"] / d["launches"]))
+        kernels[name] = e
+    ms_step = total_ms / args.steps
+    out = {
+        "metric": METRIC, "value": round(N * args.steps * world / (total_ms * 1e-3), 1), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: random-init bf16 weights (seed 0), uniform random token ids",
+        "config": {"workload": "BASELINE config 3: shuffled multi-chunk blend prefill, 1 request per step per GPU",
+                   "model": f"{args.shape} architecture, random init", "tokens": N,
+                   "cached_tokens": args.chunks * args.chunk_len, "chunks": f"{args.chunks}x{args.chunk_len}",
+                   "query_tokens": args.query_len, "recompute_ratio": args.ratio, "n_sink": args.n_sink,
+                   "global_batch": world, "seq_len": N, "parallelism": f"dp{world} (request replicas)",
+                   "l2": "inputs larger than L2 every step (15.2 GB weights, 0.6 GB cached K/V pages)"},
+        "ttft_ms_p50": round(statistics.median(step_ms), 3), "ttft_ms_p95": round(sorted(step_ms)[
+            min(len(step_ms) - 1, int(0.95 * len(step_ms)))], 3),
+        "ttft_ms_by_ratio": {f"{args.ratio:.2f}": round(statistics.median(step_ms), 3), **extra},
+        "selected_tokens": int(len(res.selected)), "recomputed_cached_tokens": stats["recomputed_cached_tokens"],
+        "prefill_token_equiv": stats["prefill_token_equiv"],
+        "e2e": {"value": round(N * args.steps * world / e2e_total, 1), "unit": "tokens/s",
+                "ttft_ms_p50": round(statistics.median(wall) * 1e3, 3),
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                "api": "TorchEngine.prefill(list[int], placements from the paged store) + last_logprobs"},
+        "roofline": roof, "kernels": kernels, "gpu_launches": int(launches),
+        "gpu_busy_ms_per_step": round(busy / args.steps, 3),
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_sample(args, shape)
+    print(json.dumps(out), flush=True)
+
+
+def run_reference(args):
+    """CPU reference arm: the oracle port of the reference path on the host cores."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    from chunkkv_b200.engine.weights import SHAPES
+
+    shape = SHAPES[args.shape]
+    s = CpuSample(args, shape)
+    for _ in range(args.warmup):
+        s.run_once()
+    t0 = time.perf_counter()
+    ttft = [s.run_once() for _ in range(args.steps)]
+    wall = time.perf_counter() - t0
+    v = len(s.tokens) / statistics.median(ttft)
+    cb = {"value": round(v, 2), "unit": "tokens/s", "cores": s.threads, "kind": "port",
+          "ttft_ms": round(statistics.median(ttft) * 1e3, 1), "sample": s.describe(args.steps)}
+    out = {"impl": "reference", "metric": METRIC, "value": round(v, 2), "unit": "tokens/s",
+           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": round(1e3 * wall / args.steps, 1), "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": "BASELINE config 3 request on the host CPU (bounded sample, see cpu_baseline)",
+                      "model": f"{args.shape} architecture", "tokens": len(s.tokens)},
+           "cpu_baseline": cb,
+           "e2e": {"value": round(v, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -117,7 +117,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int i = tid; i < BC * CH; i += kThreads) {
       const int r = i / CH, ch = i - r * CH;
       const int j = j0 + r;
-      const bool valid = j < n_ctx;
+      // keys past the block's last position are never visible: zero them instead of
+      // reading rows the caller may not have written (0 * garbage could be NaN)
+      const bool valid = j <= max_pos;
       const int64_t off = int64_t(valid ? j : 0) * HD + ch * 8;
       cp_async16(smem_u32(sK + buf * BC * HD + swz<HD>(r, ch)), kbase + off, valid);
       cp_async16(smem_u32(sV + buf * BC * HD + swz<HD>(r, ch)), vbase + off, valid);

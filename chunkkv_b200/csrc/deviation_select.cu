@@ -295,14 +295,18 @@ __global__ void __launch_bounds__(kThreads) deviation_select_kernel(
       if (lane == 0) atomicOr(&g_err_word, CKV_DEV_ERR_POSITION_RANGE);
       continue;
     }
+    // the reference compares against a zero-initialised cache (torch_engine.py:97) that
+    // only moved chunks fill, so a position no chunk covers compares against zeros
+    const bool cached = (sa.pos_flags[p] & kInCached) != 0;
     float dk = 0.f, dv = 0.f, nk = 0.f, nv = 0.f;
     for (int v = lane; v < vecs; v += 32) {
       const int e0 = v * 8, h = e0 / D, d = e0 - h * D;
       const int64_t boff = (int64_t(h) * n_ctx + p) * D + d;
       const uint4 kf = *reinterpret_cast<const uint4*>(k_fresh + i * fstride + e0);
       const uint4 vf = *reinterpret_cast<const uint4*>(v_fresh + i * fstride + e0);
-      const uint4 kb = *reinterpret_cast<const uint4*>(k_base + boff);
-      const uint4 vb = *reinterpret_cast<const uint4*>(v_base + boff);
+      const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+      const uint4 kb = cached ? *reinterpret_cast<const uint4*>(k_base + boff) : zero;
+      const uint4 vb = cached ? *reinterpret_cast<const uint4*>(v_base + boff) : zero;
       const uint32_t* pkf = reinterpret_cast<const uint32_t*>(&kf);
       const uint32_t* pvf = reinterpret_cast<const uint32_t*>(&vf);
       const uint32_t* pkb = reinterpret_cast<const uint32_t*>(&kb);

@@ -105,7 +105,7 @@ __global__ void apply_selection_kernel(const int32_t* __restrict__ sel,
   for (int i = warp; i < n_sel; i += nw) {
     const int src = sel[i];
     const int pos = keep_abs[i];
-    if (pos < 0 || pos >= n_ctx || src < 0) {
+    if (pos < 0 || pos >= n_ctx || src < 0 || src >= max_rows) {
       if (lane == 0) atomicOr(&g_err_word, CKV_DEV_ERR_POSITION_RANGE);
       continue;
     }

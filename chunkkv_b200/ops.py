@@ -18,6 +18,52 @@ META_STRIDE = 8
 SEL_META_STRIDE = 4
 
 
+class LaunchTimer:
+    """Records a CUDA-event pair around every kernel launch made through this module
+    while installed (``with LaunchTimer() as t: ...``), with the launch's algorithmic
+    work (FLOPs and HBM bytes) for roofline accounting."""
+
+    def __init__(self):
+        self.records: list[tuple[str, float, float, torch.cuda.Event, torch.cuda.Event]] = []
+
+    def __enter__(self):
+        global _TIMER
+        self._prev, _TIMER = _TIMER, self
+        return self
+
+    def __exit__(self, *exc):
+        global _TIMER
+        _TIMER = self._prev
+        return False
+
+    def summary(self) -> dict[str, dict]:
+        """Per entry point: launches, total ms, FLOPs and bytes (events must have completed)."""
+        out: dict[str, dict] = {}
+        for name, flops, nbytes, e0, e1 in self.records:
+            d = out.setdefault(name, {"launches": 0, "ms": 0.0, "flops": 0.0, "bytes": 0.0})
+            d["launches"] += 1
+            d["ms"] += e0.elapsed_time(e1)
+            d["flops"] += flops
+            d["bytes"] += nbytes
+        return out
+
+
+_TIMER: LaunchTimer | None = None
+
+
+def _run(name: str, *args, flops: float = 0.0, nbytes: float = 0.0) -> None:
+    t = _TIMER
+    if t is None:
+        _lib.call(name, *args)
+        return
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    _lib.call(name, *args)
+    e1.record()
+    t.records.append((name, float(flops), float(nbytes), e0, e1))
+
+
 def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
@@ -50,7 +96,7 @@ def rope_table(inv_freq: torch.Tensor, max_pos: int) -> torch.Tensor:
     _cuda(inv_freq)
     half = inv_freq.numel()
     out = torch.empty((max_pos, half, 2), dtype=torch.float32, device=inv_freq.device)
-    _lib.call("ckv_rope_table", _ptr(inv_freq), half, max_pos, _ptr(out), _stream())
+    _run("ckv_rope_table", _ptr(inv_freq), half, max_pos, _ptr(out), _stream())
     return out
 
 
@@ -63,7 +109,7 @@ def shift_keys(keys: torch.Tensor, delta: int, inv_freq: torch.Tensor, rot_dims:
     D = keys.shape[-1]
     rot = D if rot_dims is None else rot_dims
     out = torch.empty_like(keys) if out is None else out
-    _lib.call("ckv_shift_keys", _ptr(keys), _ptr(out), keys.numel() // D, D, rot, int(delta),
+    _run("ckv_shift_keys", _ptr(keys), _ptr(out), keys.numel() // D, D, rot, int(delta),
               _ptr(inv_freq), _stream())
     return out
 
@@ -80,7 +126,7 @@ def apply_rope(x: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor,
         raise ValueError(f"positions has {pos.numel()} entries for sequence length {L}")
     out = torch.empty_like(x)
     rot = D if rot_dims is None else rot_dims
-    _lib.call("ckv_apply_rope", _ptr(x), _ptr(out), x.numel() // (D * L) if L else 0, L, D, rot,
+    _run("ckv_apply_rope", _ptr(x), _ptr(out), x.numel() // (D * L) if L else 0, L, D, rot,
               _ptr(pos), _ptr(inv_freq), _stream())
     return out
 
@@ -88,31 +134,33 @@ def apply_rope(x: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor,
 # ---------------------------------------------------------- gather / scatter
 def blend_gather_paged(pool: torch.Tensor, page_table: torch.Tensor, chunk_meta: torch.Tensor,
                        inv_freq: torch.Tensor, k_out: torch.Tensor, v_out: torch.Tensor,
-                       layer_lo: int, layer_hi: int, rot_dims: int | None = None) -> None:
+                       layer_lo: int, layer_hi: int, rot_dims: int | None = None,
+                       nbytes: float = 0.0) -> None:
     """Moved cached chunks (paged) -> blended cache k_out/v_out [layers, H, N, D]."""
     _cuda(pool, page_table, chunk_meta, inv_freq, k_out, v_out)
     n_pages, n_layers, _, H, _, D = pool.shape
-    _lib.call("ckv_blend_gather_paged", _ptr(pool), n_pages, _ptr(page_table), _ptr(chunk_meta),
+    _run("ckv_blend_gather_paged", _ptr(pool), n_pages, _ptr(page_table), _ptr(chunk_meta),
               chunk_meta.shape[0], _ptr(inv_freq), D if rot_dims is None else rot_dims, _ptr(k_out),
-              _ptr(v_out), layer_lo, layer_hi, n_layers, H, D, k_out.shape[2], _stream())
+              _ptr(v_out), layer_lo, layer_hi, n_layers, H, D, k_out.shape[2], _stream(), nbytes=nbytes)
 
 
 def blend_gather_dense(k_ptrs: torch.Tensor, v_ptrs: torch.Tensor, chunk_meta: torch.Tensor,
                        inv_freq: torch.Tensor, k_out: torch.Tensor, v_out: torch.Tensor,
-                       layer_lo: int, layer_hi: int, rot_dims: int | None = None) -> None:
+                       layer_lo: int, layer_hi: int, rot_dims: int | None = None,
+                       nbytes: float = 0.0) -> None:
     """Moved cached chunks (per-layer tensors, by address) -> blended cache."""
     _cuda(k_ptrs, v_ptrs, chunk_meta, inv_freq, k_out, v_out)
     H, D = k_out.shape[1], k_out.shape[3]
-    _lib.call("ckv_blend_gather_dense", _ptr(k_ptrs), _ptr(v_ptrs), _ptr(chunk_meta),
+    _run("ckv_blend_gather_dense", _ptr(k_ptrs), _ptr(v_ptrs), _ptr(chunk_meta),
               chunk_meta.shape[0], _ptr(inv_freq), D if rot_dims is None else rot_dims, _ptr(k_out),
-              _ptr(v_out), layer_lo, layer_hi, H, D, k_out.shape[2], _stream())
+              _ptr(v_out), layer_lo, layer_hi, H, D, k_out.shape[2], _stream(), nbytes=nbytes)
 
 
 def pages_write(pool: torch.Tensor, page_ids: torch.Tensor, length: int, k_ptrs: torch.Tensor,
                 v_ptrs: torch.Tensor, head_stride: int) -> None:
     _cuda(pool, page_ids, k_ptrs, v_ptrs)
     n_pages, n_layers, _, H, _, D = pool.shape
-    _lib.call("ckv_pages_write", _ptr(pool), n_pages, _ptr(page_ids), length, _ptr(k_ptrs),
+    _run("ckv_pages_write", _ptr(pool), n_pages, _ptr(page_ids), length, _ptr(k_ptrs),
               _ptr(v_ptrs), head_stride, n_layers, H, D, _stream())
 
 
@@ -123,7 +171,7 @@ def deviation_select(k_fresh: torch.Tensor, v_fresh: torch.Tensor, k_base: torch
     """Layer-1 deviation + pooled top-k into the workspace (no host sync)."""
     _cuda(k_fresh, v_fresh, k_base, v_base, active, pos_flags, sel_meta)
     H, n_ctx, D = k_base.shape
-    _lib.call("ckv_deviation_select", _ptr(k_fresh), _ptr(v_fresh), k_fresh.stride(0), _ptr(k_base),
+    _run("ckv_deviation_select", _ptr(k_fresh), _ptr(v_fresh), k_fresh.stride(0), _ptr(k_base),
               _ptr(v_base), _ptr(active), active.numel(), _ptr(pos_flags), n_ctx, _ptr(sel_meta),
               sel_meta.shape[0], int(threshold is not None), float(threshold or 0.0), H, D,
               _ptr(ws.diff), _ptr(ws.norm), _ptr(ws.rel), _ptr(ws.keep_abs), _ptr(ws.sel),
@@ -134,7 +182,7 @@ def select_from_scores(diff: torch.Tensor, norm: torch.Tensor, pos_flags: torch.
                        sel_meta: torch.Tensor, threshold: float | None,
                        ws: "SelectWorkspace") -> None:
     _cuda(diff, norm, pos_flags, sel_meta)
-    _lib.call("ckv_select_from_scores", _ptr(diff), _ptr(norm), _ptr(pos_flags), pos_flags.numel(),
+    _run("ckv_select_from_scores", _ptr(diff), _ptr(norm), _ptr(pos_flags), pos_flags.numel(),
               _ptr(sel_meta), sel_meta.shape[0], int(threshold is not None), float(threshold or 0.0),
               _ptr(ws.rel), _ptr(ws.keep_abs), _ptr(ws.sel), _ptr(ws.counts), _ptr(ws.flags),
               _stream())
@@ -159,7 +207,7 @@ class SelectWorkspace:
 def apply_selection(ws: SelectWorkspace, max_rows: int, h_in, h_out, x_in, x_out, k_fresh, v_fresh,
                     k_cache, v_cache) -> None:
     H, n_ctx, D = k_cache.shape
-    _lib.call("ckv_apply_selection", _ptr(ws.sel), _ptr(ws.keep_abs), _ptr(ws.counts), max_rows,
+    _run("ckv_apply_selection", _ptr(ws.sel), _ptr(ws.keep_abs), _ptr(ws.counts), max_rows,
               _ptr(h_in), _ptr(h_out), _ptr(x_in), _ptr(x_out), h_in.shape[-1], _ptr(k_fresh),
               _ptr(v_fresh), k_fresh.stride(0), _ptr(k_cache), _ptr(v_cache), H, D, n_ctx, _stream())
 
@@ -169,7 +217,7 @@ def embed(table: torch.Tensor, tokens: torch.Tensor, rows: torch.Tensor | None,
           out: torch.Tensor) -> torch.Tensor:
     _cuda(table, tokens, rows, out)
     n = out.shape[0]
-    _lib.call("ckv_embed", _ptr(table), table.shape[0], table.shape[1], _ptr(tokens), _ptr(rows), n,
+    _run("ckv_embed", _ptr(table), table.shape[0], table.shape[1], _ptr(tokens), _ptr(rows), n,
               _ptr(out), _stream())
     return out
 
@@ -179,7 +227,7 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | No
     _bf16(x, w)
     out = torch.empty_like(x) if out is None else out
     rows = x.numel() // x.shape[-1]
-    _lib.call("ckv_rmsnorm", _ptr(x), _ptr(w), _ptr(out), rows, x.shape[-1], float(eps), _stream())
+    _run("ckv_rmsnorm", _ptr(x), _ptr(w), _ptr(out), rows, x.shape[-1], float(eps), _stream())
     return out
 
 
@@ -191,44 +239,46 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
     m, k = x.numel() // x.shape[-1], x.shape[-1]
     n = w.shape[0]
     out = torch.empty((*x.shape[:-1], n), dtype=BF16, device=x.device) if out is None else out
-    _lib.call("ckv_linear", _ptr(x), _ptr(w), _ptr(bias), _ptr(out), m, n, k, _stream())
+    _run("ckv_linear", _ptr(x), _ptr(w), _ptr(bias), _ptr(out), m, n, k, _stream(), flops=2.0 * m * n * k)
     return out
 
 
 def linear_residual(x: torch.Tensor, w: torch.Tensor, h: torch.Tensor, m: int | None = None) -> torch.Tensor:
     _cuda(x, w, h)
     m = x.numel() // x.shape[-1] if m is None else m
-    _lib.call("ckv_linear_residual", _ptr(x), _ptr(w), _ptr(h), m, w.shape[0], x.shape[-1], _stream())
+    _run("ckv_linear_residual", _ptr(x), _ptr(w), _ptr(h), m, w.shape[0], x.shape[-1], _stream(),
+         flops=2.0 * m * w.shape[0] * x.shape[-1])
     return h
 
 
 def linear_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor, m: int | None = None) -> torch.Tensor:
     _cuda(x, w_gate_up, out)
     m = x.numel() // x.shape[-1] if m is None else m
-    _lib.call("ckv_linear_swiglu", _ptr(x), _ptr(w_gate_up), _ptr(out), m, w_gate_up.shape[0] // 2,
-              x.shape[-1], _stream())
+    _run("ckv_linear_swiglu", _ptr(x), _ptr(w_gate_up), _ptr(out), m, w_gate_up.shape[0] // 2,
+         x.shape[-1], _stream(), flops=2.0 * m * w_gate_up.shape[0] * x.shape[-1])
     return out
 
 
 def qkv_rope(x, w_qkv, b_qkv, m, col_begin, col_end, n_q_heads, n_kv_heads, head_dim, positions,
              rope_tab, q_out=None, k_cache=None, v_cache=None, k_compact=None, v_compact=None) -> None:
     n_ctx = k_cache.shape[1] if k_cache is not None else 0
-    _lib.call("ckv_qkv_rope", _ptr(x), _ptr(w_qkv), _ptr(b_qkv), m, x.shape[-1], col_begin, col_end,
+    _run("ckv_qkv_rope", _ptr(x), _ptr(w_qkv), _ptr(b_qkv), m, x.shape[-1], col_begin, col_end,
               n_q_heads, n_kv_heads, head_dim, _ptr(positions), _ptr(rope_tab), rope_tab.shape[0],
               _ptr(q_out), _ptr(k_cache), _ptr(v_cache), n_ctx, _ptr(k_compact), _ptr(v_compact),
-              _stream())
+              _stream(), flops=2.0 * m * (col_end - col_begin) * x.shape[-1])
 
 
 def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, positions: torch.Tensor,
-              out: torch.Tensor, m: int | None = None, scale: float | None = None) -> torch.Tensor:
+              out: torch.Tensor, m: int | None = None, scale: float | None = None,
+              flops: float = 0.0) -> torch.Tensor:
     """q/out [m, Hq, D]; caches [H, n_ctx, D]; key j visible to row i iff j <= positions[i]."""
     _cuda(q, k_cache, v_cache, positions, out)
     H, n_ctx, D = k_cache.shape
     m = q.shape[0] if m is None else m
     Hq = q.shape[-2] if q.dim() == 3 else q.shape[-1] // D
     scale = 1.0 / math.sqrt(D) if scale is None else scale
-    _lib.call("ckv_attention", _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(positions), _ptr(out), m, Hq,
-              H, D, n_ctx, float(scale), _stream())
+    _run("ckv_attention", _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(positions), _ptr(out), m, Hq,
+              H, D, n_ctx, float(scale), _stream(), flops=flops)
     return out
 
 
@@ -236,12 +286,13 @@ def gemv(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> t
     _cuda(x, w)
     m, k = x.shape
     out = torch.empty((m, w.shape[0]), dtype=BF16, device=x.device) if out is None else out
-    _lib.call("ckv_gemv", _ptr(x), _ptr(w), _ptr(out), m, w.shape[0], k, _stream())
+    _run("ckv_gemv", _ptr(x), _ptr(w), _ptr(out), m, w.shape[0], k, _stream(),
+         flops=2.0 * m * w.shape[0] * k, nbytes=2.0 * w.shape[0] * k)
     return out
 
 
 def log_softmax(row: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     _cuda(row)
     out = torch.empty(row.numel(), dtype=torch.float32, device=row.device) if out is None else out
-    _lib.call("ckv_log_softmax", _ptr(row), row.numel(), _ptr(out), _stream())
+    _run("ckv_log_softmax", _ptr(row), row.numel(), _ptr(out), _stream())
     return out

@@ -1,0 +1,447 @@
+"""Each CUDA kernel against a plain torch statement of the same op (run on the GPU
+in fp32 where the op is floating point), or against the oracle for the selection.
+
+Tolerances: bf16 outputs must match within max |err| / max |ref| <= 1e-2 (the
+north-star bf16 tolerance); ops whose reference rounding points we reproduce
+exactly are also checked for (near-)bitwise agreement.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+from chunkkv_b200 import _lib, ops  # noqa: E402
+
+DEV = "cuda"
+BF = torch.bfloat16
+
+
+def rel_err(a: torch.Tensor, b: torch.Tensor) -> float:
+    a, b = a.float(), b.float()
+    return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+
+
+def inv_freq(D, theta=1e6, device=DEV):
+    return theta ** (-torch.arange(0, D, 2, device=device, dtype=torch.float32) / D)
+
+
+def torch_rotate(x, angles):
+    """TorchEngine._rotate (torch_engine.py:46-51) restated."""
+    cos, sin = angles.cos(), angles.sin()
+    half = x.shape[-1] // 2
+    x32 = x.float()
+    x1, x2 = x32[..., :half], x32[..., half:]
+    return torch.cat([x1 * cos - x2 * sin, x1 * sin + x2 * cos], dim=-1).to(x.dtype)
+
+
+@pytest.fixture(autouse=True)
+def _device_error_free():
+    yield
+    _lib.check_device()
+
+
+# ------------------------------------------------------------------ re-RoPE
+@pytest.mark.parametrize("D", [64, 128])
+def test_rope_table_matches_torch(D):
+    inv = inv_freq(D)
+    tab = ops.rope_table(inv, 5000)
+    ang = torch.arange(5000, device=DEV).float()[:, None] * inv[None, :]
+    assert torch.equal(tab[..., 0], ang.cos()) or (tab[..., 0] - ang.cos()).abs().max() < 1e-6
+    assert (tab[..., 1] - ang.sin()).abs().max() < 1e-6
+
+
+@pytest.mark.parametrize("D,delta", [(64, 37), (128, -4096), (128, 4095), (64, 16384)])
+def test_shift_keys_matches_reference_rotation(D, delta):
+    g = torch.Generator(device=DEV).manual_seed(1)
+    k = torch.randn((1, 4, 300, D), generator=g, device=DEV).to(BF)
+    inv = inv_freq(D)
+    ref = torch_rotate(k, (delta * inv)[None, :].expand(k.shape[-2], -1))
+    out = ops.shift_keys(k, delta, inv)
+    assert rel_err(out, ref) <= 1e-2
+    # same rounding points as the reference: at most a last-bit difference from cos/sin
+    assert (out.float() != ref.float()).float().mean() < 1e-3
+
+
+def test_shift_round_trip_and_compose():
+    """rerope tests (test_rerope.py:20-27): shift(rope(x,5),37) == rope(x,42); +-37 round trip."""
+    from chunkkv_b200.scheduler.rerope import RopeSpec, apply_rope, shift_keys
+
+    spec = RopeSpec(dims=64, base=1e6)
+    x = torch.randn((1, 2, 10, 64), device=DEV).to(BF)
+    at5 = apply_rope(x, torch.arange(5, 15, device=DEV), spec)
+    at42 = apply_rope(x, torch.arange(42, 52, device=DEV), spec)
+    assert rel_err(shift_keys(at5, 37, spec), at42) <= 1e-2
+    back = shift_keys(shift_keys(at5, 37, spec), -37, spec)
+    assert rel_err(back, at5) <= 1e-2
+    assert shift_keys(at5, 0, spec) is at5
+
+
+def test_apply_rope_matches_reference_rope():
+    D = 128
+    x = torch.randn((2, 3, 77, D), device=DEV).to(BF)
+    pos = torch.randperm(9000, device=DEV)[:77].sort().values
+    inv = inv_freq(D)
+    ref = torch_rotate(x, pos.float()[:, None] * inv[None, :])
+    out = ops.apply_rope(x, pos, inv)
+    assert rel_err(out, ref) <= 1e-2
+    assert (out.float() != ref.float()).float().mean() < 1e-3
+
+
+def test_partial_rotary_dims_copy_tail():
+    D, rot = 128, 64
+    x = torch.randn((1, 2, 40, D), device=DEV).to(BF)
+    inv = 1e6 ** (-torch.arange(0, rot // 2, device=DEV, dtype=torch.float32) * 2.0 / rot)
+    out = ops.shift_keys(x, 11, inv, rot_dims=rot)
+    ref = torch_rotate(x[..., :rot], (11 * inv)[None, :].expand(40, -1))
+    assert rel_err(out[..., :rot], ref) <= 1e-2
+    assert torch.equal(out[..., rot:], x[..., rot:])
+
+
+# ---------------------------------------------------------- gather / pages
+def _make_pool(L, H, D, n_pages, seed=0):
+    from chunkkv_b200.store.pages import PagePool
+
+    pool = PagePool(L, H, D, n_pages, DEV)
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    pool.pages.copy_(torch.randn(pool.pages.shape, generator=g, device=DEV).to(BF))
+    return pool
+
+
+def _chunk_dense(pool, ids, length, src_off=0):
+    """Per-layer dense K/V of a paged chunk, read with torch indexing."""
+    pg = pool.pages[torch.as_tensor(ids, device=DEV).long()]      # [n, L, 2, H, 16, D]
+    t = pg.permute(1, 2, 3, 0, 4, 5).reshape(pool.n_layers, 2, pool.n_kv_heads, -1, pool.head_dim)
+    return t[:, 0, :, src_off:src_off + length], t[:, 1, :, src_off:src_off + length]
+
+
+@pytest.mark.parametrize("L,H,D", [(3, 4, 128), (4, 2, 64)])
+def test_blend_gather_paged(L, H, D):
+    pool = _make_pool(L, H, D, 64)
+    rng = np.random.default_rng(0)
+    N = 700
+    chunks = [  # (length, dst_start, src_start, layer_begin, src_offset)
+        (100, 10, 400, 1, 0), (37, 150, 0, 0, 5), (256, 200, 1000, 1, 0), (16, 600, 600, 0, 0)]
+    table, meta = [], []
+    for length, dst, src, lb, off in chunks:
+        n = (length + off + 15) // 16
+        ids = rng.choice(64, size=n, replace=False).astype(np.int32)
+        meta.append([len(table), length, dst, dst - src, lb, L, off, 0])
+        table.extend(ids.tolist())
+    inv = inv_freq(D)
+    k_out = torch.zeros((L, H, N, D), dtype=BF, device=DEV)
+    v_out = torch.zeros_like(k_out)
+    ops.blend_gather_paged(pool.pages, torch.tensor(table, dtype=torch.int32, device=DEV),
+                           torch.tensor(meta, dtype=torch.int32, device=DEV), inv, k_out, v_out, 0, L)
+    k_ref = torch.zeros_like(k_out)
+    v_ref = torch.zeros_like(v_out)
+    for (length, dst, src, lb, off), m in zip(chunks, meta):
+        ids = table[m[0]:m[0] + (length + off + 15) // 16]
+        kd, vd = _chunk_dense(pool, ids, length, off)
+        delta = dst - src
+        for li in range(lb, L):
+            kk = kd[li] if delta == 0 else torch_rotate(kd[li], (delta * inv)[None, :].expand(length, -1))
+            k_ref[li, :, dst:dst + length] = kk
+            v_ref[li, :, dst:dst + length] = vd[li]
+    assert torch.equal(v_out, v_ref)
+    assert rel_err(k_out, k_ref) <= 1e-2
+    assert (k_out.float() != k_ref.float()).float().mean() < 1e-3
+
+
+def test_blend_gather_dense_and_pages_roundtrip():
+    L, H, D, length = 3, 4, 128, 77
+    from chunkkv_b200.store.pages import PagedChunkKV, PagePool
+
+    pool = PagePool(L, H, D, 16, DEV)
+    ks = [torch.randn((1, H, length, D), device=DEV).to(BF) for _ in range(L)]
+    vs = [torch.randn((1, H, length, D), device=DEV).to(BF) for _ in range(L)]
+    ids = pool.alloc((length + 15) // 16)
+    pool.write(ids, length, ks, vs)
+    c = PagedChunkKV(pool, ids, length, start=0)
+    for li in range(L):
+        assert torch.equal(c.keys[li], ks[li]) and torch.equal(c.values[li], vs[li])
+    # dense gather of the same chunk with a shift
+    N, dst, delta = 200, 50, 50
+    inv = inv_freq(D)
+    kp = torch.tensor([k.data_ptr() for k in ks], dtype=torch.uint64, device=DEV)
+    vp = torch.tensor([v.data_ptr() for v in vs], dtype=torch.uint64, device=DEV)
+    meta = torch.tensor([[0, length, dst, delta, 0, L, 0, ks[0].stride(1)]], dtype=torch.int32, device=DEV)
+    k_out = torch.zeros((L, H, N, D), dtype=BF, device=DEV)
+    v_out = torch.zeros_like(k_out)
+    ops.blend_gather_dense(kp, vp, meta, inv, k_out, v_out, 0, L)
+    for li in range(L):
+        ref = torch_rotate(ks[li][0], (delta * inv)[None, :].expand(length, -1))
+        assert rel_err(k_out[li, :, dst:dst + length], ref) <= 1e-2
+        assert torch.equal(v_out[li, :, dst:dst + length], vs[li][0])
+
+
+def test_page_id_out_of_range_is_reported_not_faulted():
+    pool = _make_pool(2, 2, 64, 4)
+    meta = torch.tensor([[0, 16, 0, 0, 0, 2, 0, 0]], dtype=torch.int32, device=DEV)
+    table = torch.tensor([99], dtype=torch.int32, device=DEV)  # outside the pool: skipped by the kernel
+    k = torch.zeros((2, 2, 16, 64), dtype=BF, device=DEV)
+    ops.blend_gather_paged(pool.pages, table, meta, inv_freq(64), k, k.clone(), 0, 2)
+    assert _lib.device_error() & 0x2
+
+
+# --------------------------------------------------------------- selection
+def _sel_meta(place, chunk_len, cfg):
+    rows = []
+    for p in place:
+        ratio = cfg.recompute_ratio if p["ratio"] is None else p["ratio"]
+        rows.append([p["start"], chunk_len, int(round(ratio * chunk_len)) if ratio > 0 else -1, int(p["exact"])])
+    return torch.tensor(rows, dtype=torch.int32, device=DEV).reshape(-1, 4)
+
+
+@pytest.mark.parametrize("name", ["tiny_fp32", "tiny_escalate", "tiny_exact_overflow", "tiny7_fp32",
+                                  "cfg1_0p5b"])
+def test_select_from_reference_scores_is_bit_exact(name):
+    """Given the reference's own fp32 layer-1 scores, the kernel keeps exactly its tokens."""
+    from chunkkv_b200.engine.base import plan_arrays
+    from helpers import scenario
+    from scenarios import SCENARIOS
+
+    s = scenario(name)
+    a = s.arrays
+    L = SCENARIOS[name].chunk_len
+    N = len(s.tokens)
+
+    class C:
+        length = L
+
+    class P:
+        def __init__(self, p):
+            self.start, self.ratio, self.exact, self.chunk = p["start"], p["ratio"], p["exact"], C()
+
+    plan = plan_arrays(N, [P(p) for p in s.place], s.config.n_sink)
+    ws = ops.SelectWorkspace(N, len(s.place), DEV)
+    ops.select_from_scores(torch.from_numpy(a["diff"]).to(DEV), torch.from_numpy(a["norm"]).to(DEV),
+                           torch.from_numpy(plan.pos_flags()).to(DEV), _sel_meta(s.place, L, s.config),
+                           s.config.escalate_threshold, ws)
+    counts = ws.counts.cpu().numpy()
+    n_sel = counts[0]
+    np.testing.assert_array_equal(ws.keep_abs[:n_sel].cpu().numpy(), a["keep_abs"])
+    assert counts[2] == s.meta["budget"]
+    assert counts[1] == s.meta["stats"]["recomputed_cached_tokens"]
+    rel = ws.rel[:len(s.place)].cpu().numpy()
+    ref_rel = [c["rel_dev"] for c in s.meta["stats"]["chunks"]]
+    np.testing.assert_allclose(rel[[not p["exact"] for p in s.place]], ref_rel, rtol=1e-5)
+    # sel = index of each kept position among the non-exact (layer-1 active) positions
+    active = np.flatnonzero(~plan.exact)
+    np.testing.assert_array_equal(active[ws.sel[:n_sel].cpu().numpy()], a["keep_abs"])
+
+
+def test_select_ties_lower_position_first_and_microbench_shape():
+    """Config-2 shape: 8 x 256 chunks, exact-zero deviation on 80 % of tokens."""
+    from chunkkv_b200.engine.base import BlendConfig
+    from oracle.blend_oracle import select
+
+    g = torch.Generator().manual_seed(2)
+    N, n_ch, cl = 2048, 8, 256
+    diff = torch.zeros(N)
+    noisy = torch.rand(N, generator=g) < 0.2
+    diff[noisy] = torch.rand(int(noisy.sum()), generator=g) + 0.01
+    diff[100:104] = 0.5  # an exact tie straddling the threshold region
+    norm = torch.rand(N, generator=g) + 1.0
+    cfg = BlendConfig(recompute_ratio=0.15, n_sink=4)
+
+    class C:
+        length = cl
+
+    class P:
+        def __init__(self, s):
+            self.start, self.ratio, self.exact, self.chunk = s, None, False, C()
+
+    pl = [P(i * cl) for i in range(n_ch)]
+    cached = torch.ones(N, dtype=torch.bool)
+    sink = torch.zeros(N, dtype=torch.bool)
+    for p in pl:
+        sink[p.start:p.start + 4] = True
+    ref = select(diff, norm, cached, sink, pl, cfg)
+    flags = (cached.to(torch.uint8) | (sink.to(torch.uint8) << 1)).to(DEV)
+    meta = torch.tensor([[p.start, cl, 38, 0] for p in pl], dtype=torch.int32, device=DEV)
+    ws = ops.SelectWorkspace(N, n_ch, DEV)
+    ops.select_from_scores(diff.to(DEV), norm.to(DEV), flags, meta, None, ws)
+    n_sel = int(ws.counts[0])
+    assert n_sel == 304 + 32
+    np.testing.assert_array_equal(ws.keep_abs[:n_sel].cpu().numpy(), ref["keep_abs"].numpy())
+
+
+def test_deviation_select_fused_matches_formula_and_selection():
+    from oracle.blend_oracle import select
+    from chunkkv_b200.engine.base import BlendConfig
+
+    H, D, N, n_ch, cl = 4, 128, 2048 + 64, 8, 256
+    g = torch.Generator(device=DEV).manual_seed(3)
+    Kb = torch.randn((H, N, D), generator=g, device=DEV).to(BF)
+    Vb = torch.randn((H, N, D), generator=g, device=DEV).to(BF)
+    active = torch.arange(N, dtype=torch.int32, device=DEV)
+    kf = Kb.permute(1, 0, 2).reshape(N, H * D).clone()
+    vf = Vb.permute(1, 0, 2).reshape(N, H * D).clone()
+    noisy = torch.rand(N, generator=g, device=DEV) < 0.2
+    kf[noisy] = (kf[noisy].float() + 0.05 * torch.randn(kf[noisy].shape, generator=g, device=DEV)).to(BF)
+    vf[noisy] = (vf[noisy].float() + 0.05 * torch.randn(vf[noisy].shape, generator=g, device=DEV)).to(BF)
+    # fresh query tail (not cached)
+    cached = torch.zeros(N, dtype=torch.bool)
+    cached[:n_ch * cl] = True
+    sink = torch.zeros(N, dtype=torch.bool)
+    for c in range(n_ch):
+        sink[c * cl:c * cl + 4] = True
+    flags = (cached.to(torch.uint8) | (sink.to(torch.uint8) << 1)).to(DEV)
+    meta = torch.tensor([[c * cl, cl, 38, 0] for c in range(n_ch)], dtype=torch.int32, device=DEV)
+    ws = ops.SelectWorkspace(N, n_ch, DEV)
+    ops.deviation_select(kf, vf, Kb, Vb, active, flags, meta, None, ws)
+    # formula of torch_engine.py:118-120 on the same data
+    kr = kf.view(N, H, D).permute(1, 0, 2)
+    vr = vf.view(N, H, D).permute(1, 0, 2)
+    d_ref = ((kr - Kb).float() ** 2).sum(dim=(0, 2)) + ((vr - Vb).float() ** 2).sum(dim=(0, 2))
+    n_ref = (kr.float() ** 2).sum(dim=(0, 2)) + (vr.float() ** 2).sum(dim=(0, 2))
+    torch.testing.assert_close(ws.diff[:N], d_ref, rtol=1e-4, atol=1e-6)
+    torch.testing.assert_close(ws.norm[:N], n_ref, rtol=1e-4, atol=1e-4)
+    # selection is exact given the kernel's own scores
+
+    class C:
+        length = cl
+
+    class P:
+        def __init__(self, s):
+            self.start, self.ratio, self.exact, self.chunk = s, None, False, C()
+
+    ref = select(ws.diff[:N].cpu(), ws.norm[:N].cpu(), cached, sink, [P(c * cl) for c in range(n_ch)],
+                 BlendConfig(recompute_ratio=0.15, n_sink=4))
+    n_sel = int(ws.counts[0])
+    np.testing.assert_array_equal(ws.keep_abs[:n_sel].cpu().numpy(), ref["keep_abs"].numpy())
+    # the ticket counter is back at zero: a second launch works the same
+    ops.deviation_select(kf, vf, Kb, Vb, active, flags, meta, None, ws)
+    assert int(ws.counts[0]) == n_sel and int(ws.counter[0]) == 0
+
+
+# ------------------------------------------------------------------- GEMMs
+GEMM_SHAPES = [(1, 256, 256), (100, 896, 896), (938, 4608, 3584), (1000, 512, 1152), (257, 3584, 18944)]
+
+
+@pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
+def test_linear_matches_fp32(m, n, k):
+    g = torch.Generator(device=DEV).manual_seed(m + n)
+    x = torch.randn((m, k), generator=g, device=DEV).to(BF)
+    w = (torch.randn((n, k), generator=g, device=DEV) * 0.02).to(BF)
+    b = (torch.randn(n, generator=g, device=DEV) * 0.02).to(BF)
+    out = ops.linear(x, w, b)
+    ref = x.float() @ w.float().T + b.float()
+    assert rel_err(out, ref) <= 1e-2
+    out_nb = ops.linear(x, w)
+    assert rel_err(out_nb, x.float() @ w.float().T) <= 1e-2
+
+
+def test_linear_many_tiles_persistent_loop():
+    """More tiles than SMs: every tile of the persistent schedule is written."""
+    m, n, k = 4096, 4096, 512
+    x = torch.randn((m, k), device=DEV).to(BF)
+    w = (torch.randn((n, k), device=DEV) * 0.05).to(BF)
+    out = ops.linear(x, w)
+    assert rel_err(out, x.float() @ w.float().T) <= 1e-2
+
+
+def test_linear_residual_and_swiglu():
+    from chunkkv_b200.engine.weights import interleave_gate_up
+
+    m, hid, inter = 333, 896, 1024
+    x = torch.randn((m, hid), device=DEV).to(BF)
+    w = (torch.randn((hid, inter), device=DEV) * 0.02).to(BF)
+    a = torch.randn((m, inter), device=DEV).to(BF)
+    h = torch.randn((m, hid), device=DEV).to(BF)
+    ref = (h.float() + (a.float() @ w.float().T).to(BF).float())
+    ops.linear_residual(a, w, h)
+    assert rel_err(h, ref) <= 1e-2
+    wg = (torch.randn((inter, hid), device=DEV) * 0.02).to(BF)
+    wu = (torch.randn((inter, hid), device=DEV) * 0.02).to(BF)
+    out = torch.empty((m, inter), dtype=BF, device=DEV)
+    ops.linear_swiglu(x, interleave_gate_up(wg, wu), out)
+    gg = (x.float() @ wg.float().T).to(BF)
+    uu = (x.float() @ wu.float().T).to(BF)
+    ref2 = (F.silu(gg) * uu).float()
+    assert rel_err(out, ref2) <= 1e-2
+
+
+@pytest.mark.parametrize("Hq,H,D,hid", [(28, 4, 128, 512), (14, 2, 64, 896), (4, 2, 64, 256)])
+def test_qkv_rope_scatter_and_compact(Hq, H, D, hid):
+    m, N = 300, 1000
+    g = torch.Generator(device=DEV).manual_seed(Hq)
+    x = torch.randn((m, hid), generator=g, device=DEV).to(BF)
+    cols = (Hq + 2 * H) * D
+    w = (torch.randn((cols, hid), generator=g, device=DEV) * 0.05).to(BF)
+    b = (torch.randn(cols, generator=g, device=DEV) * 0.05).to(BF)
+    pos = torch.randperm(N, generator=g, device=DEV)[:m].sort().values.to(torch.int32)
+    inv = inv_freq(D)
+    tab = ops.rope_table(inv, 4096)
+    q = torch.empty((m, Hq * D), dtype=BF, device=DEV)
+    Kc = torch.zeros((H, N, D), dtype=BF, device=DEV)
+    Vc = torch.zeros_like(Kc)
+    ops.qkv_rope(x, w, b, m, 0, cols, Hq, H, D, pos, tab, q_out=q, k_cache=Kc, v_cache=Vc)
+    y = (x.float() @ w.float().T + b.float()).to(BF)
+    qr = y[:, :Hq * D].view(m, Hq, D).transpose(0, 1)
+    kr = y[:, Hq * D:(Hq + H) * D].view(m, H, D).transpose(0, 1)
+    vr = y[:, (Hq + H) * D:].view(m, H, D).transpose(0, 1)
+    ang = pos.float()[:, None] * inv[None, :]
+    q_ref = torch_rotate(qr, ang).transpose(0, 1).reshape(m, Hq * D)
+    k_ref = torch_rotate(kr, ang)
+    assert rel_err(q, q_ref) <= 1e-2
+    assert rel_err(Kc[:, pos.long()], k_ref) <= 1e-2
+    assert rel_err(Vc[:, pos.long()], vr) <= 1e-2
+    # compact k/v for the K/V columns only (the layer-1 deviation input)
+    kc = torch.empty((m, H * D), dtype=BF, device=DEV)
+    vc = torch.empty_like(kc)
+    ops.qkv_rope(x, w, b, m, Hq * D, cols, Hq, H, D, pos, tab, k_compact=kc, v_compact=vc)
+    assert rel_err(kc.view(m, H, D).transpose(0, 1), k_ref) <= 1e-2
+    assert rel_err(vc.view(m, H, D).transpose(0, 1), vr) <= 1e-2
+
+
+# --------------------------------------------------------------- attention
+@pytest.mark.parametrize("Hq,H,D,N,m", [(28, 4, 128, 1500, 300), (14, 2, 64, 700, 700), (4, 2, 64, 100, 37),
+                                        (7, 1, 128, 4100, 1)])
+def test_attention_matches_masked_sdpa(Hq, H, D, N, m):
+    g = torch.Generator(device=DEV).manual_seed(N)
+    q = torch.randn((m, Hq, D), generator=g, device=DEV).to(BF)
+    K = torch.randn((H, N, D), generator=g, device=DEV).to(BF)
+    V = torch.randn((H, N, D), generator=g, device=DEV).to(BF)
+    if m == N:
+        pos = torch.arange(N, device=DEV, dtype=torch.int32)
+    else:
+        pos = torch.randperm(N, generator=g, device=DEV)[:m].sort().values.to(torch.int32)
+    out = torch.empty_like(q)
+    ops.attention(q, K, V, pos, out)
+    mask = pos.long()[:, None] >= torch.arange(N, device=DEV)[None, :]
+    ref = F.scaled_dot_product_attention(q.float().transpose(0, 1)[None], K.float()[None], V.float()[None],
+                                         attn_mask=mask, enable_gqa=True)[0].transpose(0, 1)
+    assert rel_err(out, ref) <= 1e-2
+
+
+# ------------------------------------------------------------- elementwise
+def test_rmsnorm_embed_gemv_log_softmax():
+    hid, vocab = 896, 5000
+    x = torch.randn((77, hid), device=DEV).to(BF)
+    w = (1 + 0.1 * torch.randn(hid, device=DEV)).to(BF)
+    y = ops.rmsnorm(x, w, 1e-6)
+    x32 = x.float()
+    ref = w * (x32 * torch.rsqrt(x32.pow(2).mean(-1, keepdim=True) + 1e-6)).to(BF)
+    assert rel_err(y, ref) <= 1e-2
+    assert (y != ref).float().mean() < 0.01
+    E = torch.randn((vocab, hid), device=DEV).to(BF)
+    toks = torch.randint(0, vocab, (200,), device=DEV, dtype=torch.int32)
+    rows = torch.randperm(200, device=DEV)[:50].sort().values.to(torch.int32)
+    out = torch.empty((50, hid), dtype=BF, device=DEV)
+    ops.embed(E, toks, rows, out)
+    assert torch.equal(out, E[toks[rows.long()].long()])
+    for mm in (1, 3, 8):
+        xx = x[:mm].contiguous()
+        lo = ops.gemv(xx, E)
+        assert rel_err(lo, xx.float() @ E.float().T) <= 1e-2
+    row = (torch.randn(vocab, device=DEV) * 5).to(BF)
+    lp = ops.log_softmax(row)
+    torch.testing.assert_close(lp, torch.log_softmax(row.float(), -1), rtol=1e-5, atol=1e-5)
