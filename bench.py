@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--cpu-layers", type=int, default=3, help="layers the CPU sample executes")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--extra-ratios", default="0.30,0.50", help="also time these ratios (TTFT only)")
+    ap.add_argument("--kernel-case", choices=["swiglu", "oproj", "qkv", "attention", "gather", "deviation"],
+                    help="time one kernel at its 7B-bench shape (for ncu captures) instead of the prefill")
     return ap.parse_args()
 
 
@@ -411,8 +413,87 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+def run_kernel_case(args):
+    """One kernel at the shape it has in the 7B bench (layers >= 2: 938 active tokens),
+    launched `steps` times after `warmup` launches; prints ms per launch.  Operands
+    are larger than L2 where the real launch's are (weights, cache pages)."""
+    import torch
+
+    from chunkkv_b200 import ops
+    from chunkkv_b200.engine.weights import SHAPES, interleave_gate_up
+
+    shape = SHAPES[args.shape]
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    bf = torch.bfloat16
+    M, N = 938, args.chunks * args.chunk_len + args.query_len
+    hid, H, Hq, D = shape.hidden, shape.n_kv, shape.n_heads, shape.head_dim
+
+    def rnd(*s, scale=0.02):
+        return (torch.randn(s, generator=g, device=dev) * scale).to(bf)
+
+    x = rnd(M, hid, scale=1.0)
+    pos = torch.randperm(N, generator=g, device=dev)[:M].sort().values.to(torch.int32)
+    if args.kernel_case == "swiglu":
+        w, out = rnd(2 * shape.inter, hid), torch.empty((M, shape.inter), dtype=bf, device=dev)
+        fn = lambda: ops.linear_swiglu(x, w, out)  # noqa: E731
+    elif args.kernel_case == "oproj":
+        a, w, h = rnd(M, Hq * D, scale=1.0), rnd(hid, Hq * D), rnd(M, hid, scale=1.0)
+        fn = lambda: ops.linear_residual(a, w, h)  # noqa: E731
+    elif args.kernel_case == "qkv":
+        cols = (Hq + 2 * H) * D
+        w, b = rnd(cols, hid), rnd(cols)
+        q = torch.empty((M, Hq * D), dtype=bf, device=dev)
+        kc = torch.empty((H, N, D), dtype=bf, device=dev)
+        vc = torch.empty_like(kc)
+        inv = shape.rope_theta ** (-torch.arange(0, D, 2, device=dev, dtype=torch.float32) / D)
+        tab = ops.rope_table(inv, 8192)
+        fn = lambda: ops.qkv_rope(x, w, b, M, 0, cols, Hq, H, D, pos, tab, q_out=q, k_cache=kc, v_cache=vc)  # noqa: E731
+    elif args.kernel_case == "attention":
+        q = rnd(M, Hq, D, scale=1.0)
+        kc, vc = rnd(H, N, D, scale=1.0), rnd(H, N, D, scale=1.0)
+        out = torch.empty_like(q)
+        fn = lambda: ops.attention(q, kc, vc, pos, out)  # noqa: E731
+    elif args.kernel_case == "deviation":
+        kf, vf = rnd(N, H * D, scale=1.0), rnd(N, H * D, scale=1.0)
+        Kb, Vb = rnd(H, N, D, scale=1.0), rnd(H, N, D, scale=1.0)
+        act = torch.arange(N, dtype=torch.int32, device=dev)
+        flags = torch.ones(N, dtype=torch.uint8, device=dev)
+        meta = torch.tensor([[c * args.chunk_len, args.chunk_len, 77, 0] for c in range(args.chunks)],
+                            dtype=torch.int32, device=dev)
+        ws = ops.SelectWorkspace(N, args.chunks, dev)
+        fn = lambda: ops.deviation_select(kf, vf, Kb, Vb, act, flags, meta, None, ws)  # noqa: E731
+    else:  # gather: 10 chunks x 512 tokens x 27 layers from the page pool
+        from chunkkv_b200.store.pages import PagePool
+
+        L = shape.n_layers
+        n_pages = args.chunks * args.chunk_len // 16
+        pool = PagePool(L, H, D, n_pages, dev)
+        pool.pages.view(-1)[:] = 1
+        table = torch.arange(n_pages, dtype=torch.int32, device=dev)
+        meta = torch.tensor([[c * args.chunk_len // 16, args.chunk_len, c * args.chunk_len, 1000, 1, L, 0, 0]
+                             for c in range(args.chunks)], dtype=torch.int32, device=dev)
+        inv = shape.rope_theta ** (-torch.arange(0, D, 2, device=dev, dtype=torch.float32) / D)
+        kall = torch.empty((L, H, N, D), dtype=bf, device=dev)
+        vall = torch.empty_like(kall)
+        fn = lambda: ops.blend_gather_paged(pool.pages, table, meta, inv, kall, vall, 0, L)  # noqa: E731
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel_case": args.kernel_case, "ms_per_launch": e0.elapsed_time(e1) / args.steps}))
+
+
 def main():
     args = parse()
+    if args.kernel_case:
+        run_kernel_case(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -24,6 +24,15 @@ from chunkkv_b200.types import TrustLevel
 _ids = itertools.count()
 
 
+def entry_bytes(entry) -> int:
+    """K/V bytes of an entry, counted like the reference (kvstore.py:29-31) but without
+    reading paged K/V back; works for this module's Entry and the reference's."""
+    kv = entry.kv
+    if isinstance(kv, PagedChunkKV):
+        return kv.nbytes
+    return sum(k.nbytes + v.nbytes for k, v in zip(kv.keys, kv.values))
+
+
 @dataclass
 class Entry:
     kv: object  # ChunkKV (per-layer tensors) until stored, then PagedChunkKV
@@ -35,10 +44,7 @@ class Entry:
 
     @property
     def nbytes(self) -> int:
-        kv = self.kv
-        if isinstance(kv, PagedChunkKV):
-            return kv.nbytes
-        return sum(k.nbytes + v.nbytes for k, v in zip(kv.keys, kv.values))
+        return entry_bytes(self)
 
 
 class KVStore:
@@ -67,7 +73,7 @@ class KVStore:
         self._store_pages(entry, protect=key)
         entries = self._data.setdefault(key, entries)
         entries.append(entry)
-        self.bytes += entry.nbytes
+        self.bytes += entry_bytes(entry)
         while len(entries) > self.max_variants:
             self._drop(entries.pop(0))
         self._data.move_to_end(key)
@@ -107,7 +113,7 @@ class KVStore:
         entry.kv = PagedChunkKV(pool, ids, length, kv.start)
 
     def _drop(self, e: Entry) -> None:
-        self.bytes -= e.nbytes
+        self.bytes -= entry_bytes(e)
         if isinstance(e.kv, PagedChunkKV) and e.kv.pool is self.pool:
             self.pool.release(e.kv.page_ids)
 

@@ -297,10 +297,13 @@ def test_deviation_select_fused_matches_formula_and_selection():
     meta = torch.tensor([[c * cl, cl, 38, 0] for c in range(n_ch)], dtype=torch.int32, device=DEV)
     ws = ops.SelectWorkspace(N, n_ch, DEV)
     ops.deviation_select(kf, vf, Kb, Vb, active, flags, meta, None, ws)
-    # formula of torch_engine.py:118-120 on the same data
+    # formula of torch_engine.py:118-120 on the same data; the reference's base cache is
+    # zero wherever no chunk was placed (torch_engine.py:97), i.e. at the fresh query tail
     kr = kf.view(N, H, D).permute(1, 0, 2)
     vr = vf.view(N, H, D).permute(1, 0, 2)
-    d_ref = ((kr - Kb).float() ** 2).sum(dim=(0, 2)) + ((vr - Vb).float() ** 2).sum(dim=(0, 2))
+    cm = cached.to(DEV)[None, :, None]
+    Kz, Vz = torch.where(cm, Kb, torch.zeros_like(Kb)), torch.where(cm, Vb, torch.zeros_like(Vb))
+    d_ref = ((kr - Kz).float() ** 2).sum(dim=(0, 2)) + ((vr - Vz).float() ** 2).sum(dim=(0, 2))
     n_ref = (kr.float() ** 2).sum(dim=(0, 2)) + (vr.float() ** 2).sum(dim=(0, 2))
     torch.testing.assert_close(ws.diff[:N], d_ref, rtol=1e-4, atol=1e-6)
     torch.testing.assert_close(ws.norm[:N], n_ref, rtol=1e-4, atol=1e-4)
