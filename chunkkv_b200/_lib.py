@@ -34,6 +34,8 @@ SIGNATURES: dict[str, list] = {
     "ckv_pages_write": [_p, _i64, _p, _i32, _p, _p, _i64, _i32, _i32, _i32, _p],
     "ckv_deviation_select": [_p, _p, _i64, _p, _p, _p, _i32, _p, _i32, _p, _i32, _i32, _f64, _i32, _i32,
                              _p, _p, _p, _p, _p, _p, _p, _p, _p],
+    "ckv_deviation_select_noalloc": [_p, _p, _i64, _p, _p, _p, _i32, _p, _i32, _p, _i32, _i32, _f64, _i32,
+                                     _i32, _p, _p, _p, _p, _p, _p, _p],
     "ckv_select_from_scores": [_p, _p, _p, _i32, _p, _i32, _i32, _f64, _p, _p, _p, _p, _p, _p],
     "ckv_apply_selection": [_p, _p, _p, _i32, _p, _p, _p, _p, _i32, _p, _p, _i64, _p, _p, _i32, _i32,
                             _i32, _p],

@@ -412,3 +412,93 @@ int ckv_select_from_scores(const float* diff, const float* norm, const uint8_t* 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of ckv_deviation_select.
+//
+// Some callers cannot hand this library any memory beyond the tensors they
+// already own: a serving loop whose device memory is entirely carved up by its
+// own arena or caching allocator (a cudaMalloc there would synchronise the GPU
+// or break its memory accounting), or a plain C/FFI host that has the input and
+// output buffers but no allocator to make the selection's two scratch buffers
+// with.  For them the scratch lives here, in one file-scope device array that
+// every GPU which loads the library keeps until the process exits:
+//   bytes [0, 4)                      the last-CTA ticket counter
+//   bytes [256, 256 + CKV_NOALLOC_MAX_CTX)  one flag byte per position
+// Its device address is looked up once per device (cudaGetSymbolAddress, on the
+// first call made while that device is current).  Every call shares the array:
+// the counter is cleared with an async memset on the caller's stream before
+// each launch and the flags are rewritten in full, but two calls that overlap
+// on the GPU (different streams, no ordering between them) race on it.
+namespace ckv {
+namespace {
+
+constexpr int kNoAllocFlagsOffset = 256;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocFlagsOffset + CKV_NOALLOC_MAX_CTX];
+
+constexpr int kNoAllocMaxDevices = 64;
+
+// Device address of g_noalloc_scratch on the current device (looked up once per device).
+int noalloc_scratch(unsigned char** out) {
+  static unsigned char* addr[kNoAllocMaxDevices] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) {
+    set_error("ckv_deviation_select_noalloc: no usable current device (%s)", cudaGetErrorString(e));
+    return CKV_ERR_CUDA;
+  }
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error("ckv_deviation_select_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      return CKV_ERR_CUDA;
+    }
+    addr[dev] = static_cast<unsigned char*>(p);
+  }
+  *out = addr[dev];
+  return CKV_OK;
+}
+
+}  // namespace
+}  // namespace ckv
+
+extern "C" int ckv_deviation_select_noalloc(
+    const uint16_t* k_fresh, const uint16_t* v_fresh, int64_t fresh_row_stride,
+    const uint16_t* k_base, const uint16_t* v_base, const int32_t* active, int n_act,
+    const uint8_t* pos_flags, int n_ctx, const int32_t* sel_meta, int n_chunks, int has_threshold,
+    double escalate_threshold, int n_kv_heads, int head_dim, float* diff, float* norm, float* rel,
+    int32_t* keep_abs, int32_t* sel, int32_t* counts, ckv_stream_t stream) {
+  CKV_REQUIRE(n_ctx > 0 && n_ctx <= CKV_NOALLOC_MAX_CTX,
+              "ckv_deviation_select_noalloc: n_ctx %d outside 1..%d (the size of its built-in "
+              "scratch); use ckv_deviation_select with caller-provided scratch",
+              n_ctx, CKV_NOALLOC_MAX_CTX);
+  unsigned char* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  uint32_t* counter = reinterpret_cast<uint32_t*>(scratch);
+  uint8_t* flags = scratch + kNoAllocFlagsOffset;
+  if (int rc = check_select(pos_flags, n_ctx, sel_meta, n_chunks, rel, keep_abs, sel, counts, flags))
+    return rc;
+  CKV_REQUIRE(k_fresh && v_fresh && k_base && v_base && active && diff && norm,
+              "ckv_deviation_select_noalloc: null pointer");
+  CKV_REQUIRE(aligned16(k_fresh) && aligned16(v_fresh) && aligned16(k_base) && aligned16(v_base),
+              "ckv_deviation_select_noalloc: K/V must be 16-byte aligned");
+  CKV_REQUIRE(head_dim % 8 == 0 && fresh_row_stride % 8 == 0 && n_kv_heads > 0,
+              "ckv_deviation_select_noalloc: head_dim and row stride must be multiples of 8");
+  CKV_REQUIRE(n_act > 0 && n_act <= n_ctx, "ckv_deviation_select_noalloc: n_act %d out of range",
+              n_act);
+  // the ticket counter must start at zero; a memset is a copy, not an allocation
+  cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(uint32_t), as_stream(stream));
+  if (e != cudaSuccess) {
+    set_error("ckv_deviation_select_noalloc: clearing the counter failed: %s", cudaGetErrorString(e));
+    return CKV_ERR_CUDA;
+  }
+  SelectArgs sa{diff, norm, pos_flags, n_ctx, sel_meta, n_chunks, has_threshold,
+                escalate_threshold, rel, keep_abs, sel, counts, flags};
+  const int grid = std::min(ceil_div(n_act, kWarps), 2 * num_sms());
+  deviation_select_kernel<<<grid, kThreads, 0, as_stream(stream)>>>(
+      k_fresh, v_fresh, fresh_row_stride, k_base, v_base, active, n_act, n_kv_heads, head_dim,
+      diff, norm, counter, sa);
+  CKV_LAUNCH_CHECK("ckv_deviation_select_noalloc");
+  return CKV_OK;
+}

@@ -156,6 +156,25 @@ CKV_API int ckv_deviation_select(const uint16_t* k_fresh, const uint16_t* v_fres
                          int32_t* keep_abs, int32_t* sel, int32_t* counts, uint8_t* flags,
                          uint32_t* counter, ckv_stream_t stream);
 
+/* Allocation-free variant of ckv_deviation_select — no counterpart in the
+ * reference.  For callers that can pass their inputs and outputs but cannot
+ * provide (allocate) the selection's scratch: its flag bytes and ticket counter
+ * live in a static device array inside the library, held by every GPU that
+ * loads it until process exit.  Same arguments and results as
+ * ckv_deviation_select without `flags` and `counter`; n_ctx must be at most
+ * CKV_NOALLOC_MAX_CTX (else CKV_ERR_ARG).  The first call on a device looks up
+ * the array's device address; make that first call before any stream capture.
+ * Calls share the array: calls that overlap on the GPU race. */
+#define CKV_NOALLOC_MAX_CTX 65536
+CKV_API int ckv_deviation_select_noalloc(const uint16_t* k_fresh, const uint16_t* v_fresh,
+                                         int64_t fresh_row_stride, const uint16_t* k_base,
+                                         const uint16_t* v_base, const int32_t* active, int n_act,
+                                         const uint8_t* pos_flags, int n_ctx,
+                                         const int32_t* sel_meta, int n_chunks, int has_threshold,
+                                         double escalate_threshold, int n_kv_heads, int head_dim,
+                                         float* diff, float* norm, float* rel, int32_t* keep_abs,
+                                         int32_t* sel, int32_t* counts, ckv_stream_t stream);
+
 /* Selection only, from given fp32 scores (torch_engine.py:125-153): the same
  * device code as the second phase of ckv_deviation_select, one CTA.  `active`
  * is implied: every non-exact position, ascending. */
