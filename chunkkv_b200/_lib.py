@@ -46,11 +46,12 @@ SIGNATURES: dict[str, list] = {
     "ckv_linear_swiglu": [_p, _p, _p, _i32, _i32, _i32, _p],
     "ckv_qkv_rope": [_p, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _p, _p, _i32, _p, _p, _p,
                      _i32, _p, _p, _p],
-    "ckv_attention": [_p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _i32, _f32, _p],
+    "ckv_attention_workspace_size": [_i32, _i32, _i32, _i32, _i32],
+    "ckv_attention": [_p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _i32, _f32, _p, _i64, _p],
     "ckv_gemv": [_p, _p, _p, _i32, _i32, _i32, _p],
     "ckv_log_softmax": [_p, _i32, _p, _p],
 }
-_RESTYPES = {"ckv_version": C.c_char_p, "ckv_last_error": C.c_char_p}
+_RESTYPES = {"ckv_version": C.c_char_p, "ckv_last_error": C.c_char_p, "ckv_attention_workspace_size": C.c_int64}
 
 CKV_OK, CKV_ERR_ARG, CKV_ERR_CUDA, CKV_ERR_DEVICE, CKV_ERR_UNSUPPORTED = range(5)
 DEV_ERR_BITS = {

@@ -1,0 +1,565 @@
+// Attention of the recomputed tokens over the blended cache on tcgen05/TMEM
+// (torch_engine.py:68-70 with the mask of torch_engine.py:157).
+//
+// Query row (token t, head g) sees key j iff j <= positions[t].  GQA: the G =
+// Hq/Hk heads sharing a KV head are packed as consecutive rows; a Q tile holds
+// T = floor(128/G) tokens x G heads (126 rows at G = 7) and a CTA holds two Q
+// tiles of one KV head, so every K/V tile it loads serves 2T tokens x G heads.
+// Per key tile j (128 keys) and Q tile w in {0, 1}:
+//   S_w = Q_w K_j^T   tcgen05.mma (A = Q_w, B = K tile, both K-major in smem), fp32
+//                     into TMEM columns [128w, 128w+128)
+//   softmax           warpgroup w, one thread per row (= TMEM lane): the S row in one
+//                     128-column TMEM load, position mask, online max/sum in fp32 with
+//                     ex2 (scale folded in); O_w is rescaled in TMEM only when the
+//                     running max grows by more than 2^8 (lazy: O and l always share
+//                     the same max, so the result is exact)
+//   P_w (bf16)        stored back over S_w in TMEM (two values per column)
+//   O_w += P_w V_j    tcgen05.mma with A read from TMEM, B = V tile read MN-major (the
+//                     cache stores V as [key][d], d contiguous), fp32 in TMEM
+// The two Q tiles ping-pong: while warpgroup 0 runs the softmax of tile j the tensor
+// core runs P_1 V_{j-1} and S_1(j), and the other way round.  tcgen05.mma ops of
+// one thread execute in issue order, so S_w(j+1) may be issued right after
+// P_w(j) V_j, which reads the same TMEM columns.  K and V stages are released
+// separately (K after both S, V after both P.V).
+// Warps: 0 = TMA producer, 1 = MMA issuer + TMEM owner, 2..5 and 6..9 = softmax /
+// correction / epilogue of Q tiles 0 and 1.  Every wait is bounded (ckv_common.cuh).
+#include "ckv_common.cuh"
+
+CKV_DEFINE_ERR_WORD(attention_tc)
+
+namespace ckv {
+namespace {
+
+constexpr int BM = 128;  // rows per Q tile (packed token x head)
+constexpr int NQ = 2;    // Q tiles per CTA
+constexpr int BN = 128;  // keys per tile
+constexpr int KS = 2;    // K stages
+constexpr int VS = 2;    // V stages
+constexpr int kThreads = 64 + NQ * 128;
+constexpr uint32_t TMEM_COLS = 512;  // S/P of tile w at [128w, 128w+128), O of tile w at 256+128w
+constexpr uint32_t O_COL = 256;
+constexpr uint32_t ATOM_BYTES = 128 * 128;  // one [128 rows][64 bf16] swizzle-128 atom
+constexpr float kRescaleThreshold = 8.0f;   // log2 units
+
+template <int HD>
+struct Cfg {
+  static constexpr int ATOMS = HD / 64;
+  static constexpr uint32_t Q_BYTES = BM * HD * 2;
+  static constexpr uint32_t KV_TILE = BN * HD * 2;
+  // at least 120 KiB so two CTAs never share an SM: each allocates all 512 TMEM columns
+  static constexpr uint32_t SMEM_NEED = 1024 + NQ * Q_BYTES + (KS + VS) * KV_TILE + 256;
+  static constexpr uint32_t SMEM = SMEM_NEED > 120 * 1024 ? SMEM_NEED : 120 * 1024;
+  static constexpr uint32_t IDESC_S = umma_idesc_bf16(BM, BN);
+  static constexpr uint32_t IDESC_PV = umma_idesc_bf16(BM, HD) | (1u << 16);  // B MN-major
+};
+
+// byte offset of 16-byte chunk `ch` (of a 64-element atom row) of row r, swizzle-128
+__device__ __forceinline__ uint32_t sw128(int r, int ch) {
+  return uint32_t(r) * 128u + uint32_t((ch ^ (r & 7)) << 4);
+}
+
+// all lanes wait; the warp agrees on the outcome so collective TMEM ops stay converged
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  const bool ok = mbar_wait(bar, parity, abort, &g_err_word);
+  return __all_sync(0xffffffffu, ok);
+}
+
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_ns() - t0 > kWaitLimitNs) break;
+}
+
+// 10 warps: two of the four SM sub-partitions hold three warps, so the register
+// file allows at most 16384 / (3 * 32) = 170 registers per thread.
+template <int HD>
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                        const uint16_t* __restrict__ q, const int32_t* __restrict__ positions,
+                        uint16_t* __restrict__ out, int M, int Hq, int Hk, int n_ctx, float scale_log2,
+                        int tps, int max_splits, float* __restrict__ part_o, float2* __restrict__ part_ml) {
+  using C = Cfg<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sQ = smem;                      // [NQ][Q_BYTES]
+  uint8_t* sK = sQ + NQ * C::Q_BYTES;      // [KS][KV_TILE]
+  uint8_t* sV = sK + KS * C::KV_TILE;      // [VS][KV_TILE]
+  uint64_t* k_full = reinterpret_cast<uint64_t*>(sV + VS * C::KV_TILE);
+  uint64_t* k_empty = k_full + KS;
+  uint64_t* v_full = k_empty + KS;
+  uint64_t* v_empty = v_full + VS;
+  uint64_t* s_full = v_empty + VS;  // [NQ]
+  uint64_t* p_full = s_full + NQ;   // [NQ]
+  uint64_t* o_done = p_full + NQ;   // [NQ]
+  uint64_t* q_ready = o_done + NQ;
+  uint64_t* o_full = q_ready + 1;
+  uint64_t* drain = o_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* s_maxpos = reinterpret_cast<int*>(tmem_slot + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = Hq / Hk;
+  const int T = BM / G;  // tokens per Q tile
+  const int hk = blockIdx.y;
+  const int rb = gridDim.x - 1 - blockIdx.x;  // late (long) blocks first
+  const int t0 = rb * NQ * T;
+  const int n_tok = min(NQ * T, M - t0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < KS; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < VS; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int w = 0; w < NQ; ++w) {
+      mbar_init(&s_full[w], 1);
+      mbar_init(&p_full[w], 128);
+      mbar_init(&o_done[w], 1);
+    }
+    mbar_init(q_ready, NQ * 128);
+    mbar_init(o_full, 1);
+    mbar_init(drain, 1);
+    *abort = 0;
+    *s_maxpos = 0;
+    fence_barrier_init();
+    fence_async_smem();
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n_tok; i += kThreads) {
+    int p = positions[t0 + i];
+    if (p < 0 || p >= n_ctx) {
+      atomicOr(&g_err_word, CKV_DEV_ERR_POSITION_RANGE);
+      p = p < 0 ? 0 : n_ctx - 1;
+    }
+    atomicMax(s_maxpos, p);
+  }
+  __syncthreads();
+  // key tiles 0..max position, cut into splits of `tps` tiles (blockIdx.z = split)
+  const int n_kt_all = (*s_maxpos + BN) / BN;
+  const int n_split = (n_kt_all + tps - 1) / tps;
+  const int split = blockIdx.z;
+  if (split >= n_split) return;  // whole CTA leaves before touching TMEM
+  const int kt0 = split * tps;
+  const int n_kt = min(tps, n_kt_all - kt0);  // tiles of this CTA: kt0 .. kt0 + n_kt - 1
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int nk = 0, nv = 0;  // tiles whose K / V load was issued
+      for (int j = 0; j < n_kt; ++j) {
+        const int sk = j % KS, sv = j % VS;
+        if (!mbar_wait(&k_empty[sk], ((j / KS) & 1) ^ 1, abort, &g_err_word)) break;
+        mbar_expect_tx(&k_full[sk], C::KV_TILE);
+#pragma unroll
+        for (int a = 0; a < C::ATOMS; ++a)
+          tma_load_3d(sK + sk * C::KV_TILE + a * ATOM_BYTES, &tmK, a * 64, (kt0 + j) * BN, hk, &k_full[sk]);
+        ++nk;
+        if (!mbar_wait(&v_empty[sv], ((j / VS) & 1) ^ 1, abort, &g_err_word)) break;
+        mbar_expect_tx(&v_full[sv], C::KV_TILE);
+#pragma unroll
+        for (int a = 0; a < C::ATOMS; ++a)
+          tma_load_3d(sV + sv * C::KV_TILE + a * ATOM_BYTES, &tmV, a * 64, (kt0 + j) * BN, hk, &v_full[sv]);
+        ++nv;
+      }
+      if (nv < n_kt) {  // aborted: let the copies already issued land
+        for (int i = (nk > KS ? nk - KS : 0); i < nk; ++i) drain_wait(&k_full[i % KS], (i / KS) & 1);
+        for (int i = (nv > VS ? nv - VS : 0); i < nv; ++i) drain_wait(&v_full[i % VS], (i / VS) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(q_ready, 0, abort, &g_err_word);
+      auto issue_s = [&](int w, int j) {
+        const uint32_t q0 = smem_u32(sQ + w * C::Q_BYTES);
+        const uint32_t k0 = smem_u32(sK + (j % KS) * C::KV_TILE);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
+          tc_mma_f16(tmem + w * BN, umma_desc_sw128(q0 + off), umma_desc_sw128(k0 + off), C::IDESC_S,
+                     kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&s_full[w]);
+      };
+      auto issue_pv = [&](int w, int j) {
+        const uint32_t v0 = smem_u32(sV + (j % VS) * C::KV_TILE);
+        const uint32_t pbuf = tmem + w * BN;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          tc_mma_f16_ts(tmem + O_COL + w * 128, pbuf + kk * 8, umma_desc_sw128_mn(v0 + kk * 16 * 128, ATOM_BYTES),
+                        C::IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&o_done[w]);
+      };
+      if (ok && mbar_wait(&k_full[0], 0, abort, &g_err_word)) {
+        tc_fence_after();
+        for (int w = 0; w < NQ; ++w) issue_s(w, 0);
+        tc_commit(&k_empty[0]);
+      } else {
+        ok = false;
+      }
+      for (int j = 0; j < n_kt && ok; ++j) {
+        const int nxt = j + 1;
+        for (int w = 0; w < NQ && ok; ++w) {
+          if (!mbar_wait(&p_full[w], j & 1, abort, &g_err_word) ||
+              (w == 0 && !mbar_wait(&v_full[j % VS], (j / VS) & 1, abort, &g_err_word))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(w, j);
+          if (w == NQ - 1) tc_commit(&v_empty[j % VS]);
+          if (nxt < n_kt) {
+            if (w == 0 && !mbar_wait(&k_full[nxt % KS], (nxt / KS) & 1, abort, &g_err_word)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(w, nxt);
+            if (w == NQ - 1) tc_commit(&k_empty[nxt % KS]);
+          }
+        }
+      }
+      if (ok) {
+        tc_commit(o_full);
+      } else {
+        tc_commit(drain);
+        drain_wait(drain, 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------- softmax / correction / epilogue
+    const int w = (warp - 2) >> 2;   // Q tile of this warpgroup
+    const int sub = warp & 3;        // TMEM sub-partition (lanes 32*sub .. +31)
+    const int r = sub * 32 + lane;   // row in the Q tile == TMEM lane
+    const int tr = r / G, g = r - (r / G) * G;
+    const int tt = w * T + tr;       // token index in the CTA
+    const bool valid = r < T * G && tt < n_tok;
+    const int tok = t0 + (valid ? tt : 0);
+    int pos = 0;
+    if (valid) pos = min(max(positions[tok], 0), n_ctx - 1);
+    const uint16_t* qrow = q + (int64_t(tok) * Hq + hk * G + g) * HD;
+    uint8_t* myQ = sQ + w * C::Q_BYTES;
+#pragma unroll
+    for (int c = 0; c < HD / 8; ++c) {
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (valid) v = *reinterpret_cast<const uint4*>(qrow + c * 8);
+      *reinterpret_cast<uint4*>(myQ + (c >> 3) * ATOM_BYTES + sw128(r, c & 7)) = v;
+    }
+    fence_async_smem();
+    mbar_arrive(q_ready);
+
+    const uint32_t lane_base = tmem + (uint32_t(sub * 32) << 16);
+    const uint32_t sbuf = lane_base + w * BN;
+    const uint32_t obuf = lane_base + O_COL + w * 128;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kt; ++j) {
+      if (!warp_wait(&s_full[w], j & 1, abort)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t u[BN];
+      tmem_ld128w(sbuf, u);
+      const int lim = pos - (kt0 + j) * BN;  // keys at index > lim are masked
+      // row max of the raw scores (scale > 0 commutes with max), 8 independent chains
+      float mx8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
+      if (__all_sync(0xffffffffu, lim >= BN - 1)) {  // whole tile visible to the warp
+#pragma unroll
+        for (int e = 0; e < BN; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(u[e]));
+      } else {
+#pragma unroll
+        for (int e = 0; e < BN; ++e) {
+          const float x = e <= lim ? __uint_as_float(u[e]) : -INFINITY;
+          u[e] = __float_as_uint(x);
+          mx8[e & 7] = fmaxf(mx8[e & 7], x);
+        }
+      }
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      const float m_new = fmaxf(m, mx * scale_log2);
+      const bool need = j > 0 && m_new > m + kRescaleThreshold;
+      if (__any_sync(0xffffffffu, need)) {
+        // O may be touched only after P(j-1) V(j-1) has landed
+        if (!warp_wait(&o_done[w], (j - 1) & 1, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float corr = need ? ex2_approx(m - m_new) : 1.0f;
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 32) {
+          float o[32];
+          tmem_ld32(obuf + c, o);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] *= corr;
+          tmem_st32(obuf + c, o);
+        }
+        l *= corr;
+      }
+      if (j == 0 || need) m = m_new;
+      // P = 2^(s*scale - m): one FFMA + ex2 per element; masked scores are -inf -> 0.
+      // A row that has seen no visible key yet (possible in a later key split) keeps
+      // m = -inf; a finite base keeps its P at exactly 0 instead of NaN.
+      const float neg_m = m == -INFINITY ? 0.f : -m;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int e = 0; e < BN; e += 2) {  // packs in place: u[e/2] is already consumed
+        const float p0 = ex2_approx(fmaf(__uint_as_float(u[e]), scale_log2, neg_m));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(u[e + 1]), scale_log2, neg_m));
+        rs4[(e >> 1) & 3] += p0 + p1;
+        u[e >> 1] = pack_bf2(p0, p1);
+      }
+      tmem_st64w(sbuf, *reinterpret_cast<uint32_t(*)[64]>(u));
+      l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+      tc_fence_before();
+      mbar_arrive(&p_full[w]);
+    }
+    if (ok && n_split > 1 && warp_wait(o_full, 0, abort)) {
+      // one slice of the keys: unnormalised O with its (max, sum), merged by the combine kernel
+      tc_fence_after();
+      const int64_t prow = (int64_t((rb * Hk + hk) * max_splits + split)) * (NQ * BM) + w * BM + r;
+      float* po = part_o + prow * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        float o[32];
+        tmem_ld32(obuf + c, o);
+        if (valid) {
+#pragma unroll
+          for (int qd = 0; qd < 8; ++qd)
+            *reinterpret_cast<float4*>(po + c + 4 * qd) = make_float4(o[4 * qd], o[4 * qd + 1], o[4 * qd + 2], o[4 * qd + 3]);
+        }
+      }
+      if (valid) part_ml[prow] = make_float2(m, l);
+    } else if (ok && warp_wait(o_full, 0, abort)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.0f / l : 0.f;
+      uint16_t* orow = out + (int64_t(tok) * Hq + hk * G + g) * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        float o[32];
+        tmem_ld32(obuf + c, o);
+        if (valid) {
+#pragma unroll
+          for (int qd = 0; qd < 4; ++qd) {
+            uint4 v;
+            v.x = pack_bf2(o[8 * qd + 0] * inv, o[8 * qd + 1] * inv);
+            v.y = pack_bf2(o[8 * qd + 2] * inv, o[8 * qd + 3] * inv);
+            v.z = pack_bf2(o[8 * qd + 4] * inv, o[8 * qd + 5] * inv);
+            v.w = pack_bf2(o[8 * qd + 6] * inv, o[8 * qd + 7] * inv);
+            *reinterpret_cast<uint4*>(orow + c + 8 * qd) = v;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// Merge the key splits of the row blocks that were split: O = sum_s 2^(m_s - M) O_s /
+// sum_s 2^(m_s - M) l_s with M = max_s m_s (all in the log2 domain of the kernel).
+// One warp per packed row; lane s reads split s's (m, l), each lane then sums its
+// HD/32 columns over the splits.  Rows of unsplit blocks were written directly.
+constexpr int kCombineWarps = 8;
+template <int HD>
+__global__ void __launch_bounds__(kCombineWarps * 32) attention_combine_kernel(
+    const int32_t* __restrict__ positions, uint16_t* __restrict__ out, int M, int Hq, int Hk, int n_ctx,
+    int tps, int max_splits, const float* __restrict__ part_o, const float2* __restrict__ part_ml) {
+  const int G = Hq / Hk;
+  const int T = BM / G;
+  constexpr int kChunks = NQ * BM / kCombineWarps;  // CTAs per (row block, KV head)
+  const int rb = blockIdx.x / kChunks, chunk = blockIdx.x - rb * kChunks, hk = blockIdx.y;
+  const int t0 = rb * NQ * T;
+  const int n_tok = min(NQ * T, M - t0);
+  __shared__ int s_max;
+  if (threadIdx.x == 0) s_max = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < n_tok; i += blockDim.x)
+    atomicMax(&s_max, min(max(positions[t0 + i], 0), n_ctx - 1));
+  __syncthreads();
+  const int n_split = ((s_max + BN) / BN + tps - 1) / tps;
+  if (n_split <= 1) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pr = chunk * kCombineWarps + warp;
+  const int w = pr / BM, r = pr - w * BM;
+  const int tr = r / G, g = r - tr * G, tt = w * T + tr;
+  if (r >= T * G || tt >= n_tok) return;
+  const int64_t stride = NQ * BM;
+  const int64_t base = int64_t((rb * Hk + hk) * max_splits) * stride + pr;
+  const float2 ml = lane < n_split ? part_ml[base + lane * stride] : make_float2(-INFINITY, 0.f);
+  float mmax = ml.x;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, o));
+  const float wgt = lane < n_split ? exp2f(ml.x - mmax) : 0.f;
+  float L = wgt * ml.y;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  float acc[HD / 32];
+#pragma unroll
+  for (int i = 0; i < HD / 32; ++i) acc[i] = 0.f;
+#pragma unroll 4
+  for (int sp = 0; sp < n_split; ++sp) {
+    const float ws = __shfl_sync(0xffffffffu, wgt, sp);
+    const float* po = part_o + (base + sp * stride) * HD + lane;
+#pragma unroll
+    for (int i = 0; i < HD / 32; ++i) acc[i] = fmaf(ws, po[32 * i], acc[i]);
+  }
+  const float inv = L > 0.f ? 1.0f / L : 0.f;
+  uint16_t* orow = out + (int64_t(t0 + tt) * Hq + hk * G + g) * HD;
+#pragma unroll
+  for (int i = 0; i < HD / 32; ++i) orow[lane + 32 * i] = f2bf(acc[i] * inv);
+}
+
+// Key-split plan: split only when the unsplit grid leaves SMs idle.
+struct SplitPlan {
+  int tps, max_splits, blocks;
+  int64_t bytes;
+};
+SplitPlan plan_splits(int M, int Hq, int Hk, int HD, int n_ctx) {
+  const int T = BM / (Hq / Hk);
+  SplitPlan p;
+  p.blocks = ceil_div(M, NQ * T);
+  const int max_kt = ceil_div(n_ctx, BN);
+  const int ctas = p.blocks * Hk;
+  const int sms = num_sms();
+  if (ctas >= sms || max_kt <= 4) {
+    p.tps = max_kt;
+    p.max_splits = 1;
+    p.bytes = 0;
+    return p;
+  }
+  const int want = ceil_div(2 * sms, ctas);         // splits per block for about two waves
+  p.tps = std::max(std::max(4, ceil_div(max_kt, want)), ceil_div(max_kt, 32));
+  p.max_splits = ceil_div(max_kt, p.tps);  // <= 32: the combine gives each split one lane
+  p.bytes = int64_t(ctas) * p.max_splits * NQ * BM * (int64_t(HD) * 4 + 8);
+  return p;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// [H][n_ctx][HD] bf16 cache as a 3-D map, box = 64 x 128 keys x 1 head (keys past n_ctx read 0)
+int make_cache_map(CUtensorMap* map, const void* ptr, int H, int n_ctx, int HD) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) {
+    set_error("cuTensorMapEncodeTiled unavailable");
+    return CKV_ERR_CUDA;
+  }
+  cuuint64_t dims[3] = {cuuint64_t(HD), cuuint64_t(n_ctx), cuuint64_t(H)};
+  cuuint64_t strides[2] = {cuuint64_t(HD) * 2, cuuint64_t(n_ctx) * HD * 2};
+  cuuint32_t box[3] = {64, BN, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled (cache) failed (%d)", int(r));
+    return CKV_ERR_CUDA;
+  }
+  return CKV_OK;
+}
+
+template <int HD>
+int launch(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* positions, uint16_t* out,
+           int M, int Hq, int Hk, int n_ctx, float scale, void* workspace, int64_t ws_bytes,
+           cudaStream_t stream) {
+  CUtensorMap mk, mv;
+  if (int rc = make_cache_map(&mk, kc, Hk, n_ctx, HD)) return rc;
+  if (int rc = make_cache_map(&mv, vc, Hk, n_ctx, HD)) return rc;
+  auto kern = attention_tc_kernel<HD>;
+  if (int rc = set_smem_limit(reinterpret_cast<const void*>(kern), Cfg<HD>::SMEM)) return rc;
+  SplitPlan p = plan_splits(M, Hq, Hk, HD, n_ctx);
+  if (p.max_splits > 1 && (workspace == nullptr || ws_bytes < p.bytes)) {  // no room: one split
+    p.tps = ceil_div(n_ctx, BN);
+    p.max_splits = 1;
+  }
+  float* part_o = static_cast<float*>(workspace);
+  float2* part_ml = p.max_splits > 1
+                        ? reinterpret_cast<float2*>(part_o + int64_t(p.blocks) * Hk * p.max_splits * NQ * BM * HD)
+                        : nullptr;
+  const float sl2 = scale * 1.4426950408889634f;
+  kern<<<dim3(p.blocks, Hk, p.max_splits), kThreads, Cfg<HD>::SMEM, stream>>>(
+      mk, mv, q, positions, out, M, Hq, Hk, n_ctx, sl2, p.tps, p.max_splits, part_o, part_ml);
+  CKV_LAUNCH_CHECK("ckv_attention");
+  if (p.max_splits > 1) {
+    attention_combine_kernel<HD><<<dim3(p.blocks * (NQ * BM / kCombineWarps), Hk), kCombineWarps * 32, 0, stream>>>(
+        positions, out, M, Hq, Hk, n_ctx, p.tps, p.max_splits, part_o, part_ml);
+    CKV_LAUNCH_CHECK("ckv_attention(combine)");
+  }
+  return CKV_OK;
+}
+
+}  // namespace
+}  // namespace ckv
+
+using namespace ckv;
+
+extern "C" int64_t ckv_attention_workspace_size(int m, int n_q_heads, int n_kv_heads, int head_dim,
+                                                int n_ctx) {
+  if (m <= 0 || n_kv_heads <= 0 || n_q_heads % n_kv_heads != 0 || n_ctx <= 0 ||
+      (head_dim != 64 && head_dim != 128) || n_q_heads / n_kv_heads > BM)
+    return 0;
+  return plan_splits(m, n_q_heads, n_kv_heads, head_dim, n_ctx).bytes;
+}
+
+extern "C" int ckv_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                             const int32_t* positions, uint16_t* out, int m, int n_q_heads, int n_kv_heads,
+                             int head_dim, int n_ctx, float scale, void* workspace,
+                             int64_t workspace_bytes, ckv_stream_t stream) {
+  CKV_REQUIRE(q && k_cache && v_cache && positions && out, "ckv_attention: null pointer");
+  CKV_REQUIRE(aligned16(q) && aligned16(k_cache) && aligned16(v_cache) && aligned16(out),
+              "ckv_attention: tensors must be 16-byte aligned");
+  CKV_REQUIRE(n_kv_heads > 0 && n_q_heads % n_kv_heads == 0,
+              "ckv_attention: n_q_heads %d not a multiple of n_kv_heads %d", n_q_heads, n_kv_heads);
+  CKV_REQUIRE(n_q_heads / n_kv_heads <= BM, "ckv_attention: more than %d query heads per KV head", BM);
+  CKV_REQUIRE(n_kv_heads <= 65535 && n_ctx > 0 && m >= 0, "ckv_attention: bad sizes");
+  if (m == 0) return CKV_OK;
+  CKV_REQUIRE(workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 15u) == 0,
+              "ckv_attention: workspace must be 16-byte aligned");
+  if (head_dim == 128)
+    return launch<128>(q, k_cache, v_cache, positions, out, m, n_q_heads, n_kv_heads, n_ctx, scale,
+                       workspace, workspace_bytes, as_stream(stream));
+  if (head_dim == 64)
+    return launch<64>(q, k_cache, v_cache, positions, out, m, n_q_heads, n_kv_heads, n_ctx, scale,
+                      workspace, workspace_bytes, as_stream(stream));
+  set_error("ckv_attention: head_dim %d (64 or 128)", head_dim);
+  return CKV_ERR_UNSUPPORTED;
+}

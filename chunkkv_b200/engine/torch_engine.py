@@ -120,6 +120,7 @@ class TorchEngine:
         self._up = _Staging()
         self._down = _Staging()
         self._ws: ops.SelectWorkspace | None = None
+        self._attn_ws: torch.Tensor | None = None
         self.last_h2d_bytes = 0
         self.last_d2h_bytes = 0
         _lib.load()  # fail loudly now if the CUDA library is missing
@@ -148,6 +149,16 @@ class TorchEngine:
         if ws is None or ws.diff.numel() < n or ws.rel.numel() < n_chunks:
             ws = self._ws = ops.SelectWorkspace(max(n, 1024), max(n_chunks, 64), self.device)
         return ws
+
+    def _attn_workspace(self, m: int, n_ctx: int) -> torch.Tensor | None:
+        """Key-split scratch of the attention kernel, grown on demand and reused."""
+        s = self.shape
+        need = ops.attention_workspace_bytes(m, s.n_heads, s.n_kv, s.head_dim, n_ctx)
+        if need == 0:
+            return None
+        if self._attn_ws is None or self._attn_ws.numel() < need:
+            self._attn_ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        return self._attn_ws
 
     def shift_keys(self, keys: torch.Tensor, delta: int) -> torch.Tensor:
         """Re-RoPE post-RoPE keys (1, H, L, D) by `delta` (torch_engine.py:56-59)."""
@@ -306,7 +317,8 @@ class TorchEngine:
                              k_cache=K_all[li], v_cache=V_all[li])
             if M == 0:
                 break
-            ops.attention(q, K_all[li], V_all[li], active, attn, m=M, flops=attn_flops)
+            ops.attention(q, K_all[li], V_all[li], active, attn, m=M, flops=attn_flops,
+                          workspace=self._attn_workspace(M, N))
             ops.linear_residual(attn, lw.w_o, h, m=M)
             ops.rmsnorm(h[:M], lw.ln2, s.rms_eps, out=x[:M])
             ops.linear_swiglu(x, lw.w_gu, act, m=M)
@@ -375,7 +387,7 @@ class TorchEngine:
                 # the cache slice of this layer as [H, cap, D] (positions < cap)
                 ops.qkv_rope(x, lw.w_qkv, lw.b_qkv, 1, 0, qkv_cols, Hq, H, D, posd, rope_tab, q_out=q,
                              k_cache=K[li], v_cache=V[li])
-                ops.attention(q, K[li], V[li], posd, attn, m=1)
+                ops.attention(q, K[li], V[li], posd, attn, m=1, workspace=self._attn_workspace(1, cap))
                 ops.linear_residual(attn, lw.w_o, h, m=1)
                 ops.rmsnorm(h, lw.ln2, s.rms_eps, out=x)
                 ops.linear_swiglu(x, lw.w_gu, act, m=1)

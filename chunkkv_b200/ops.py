@@ -268,17 +268,28 @@ def qkv_rope(x, w_qkv, b_qkv, m, col_begin, col_end, n_q_heads, n_kv_heads, head
               _stream(), flops=2.0 * m * (col_end - col_begin) * x.shape[-1])
 
 
+def attention_workspace_bytes(m: int, n_q_heads: int, n_kv_heads: int, head_dim: int, n_ctx: int) -> int:
+    """Bytes of workspace that let ckv_attention split long rows along the keys (0: never)."""
+    return int(_lib.load().ckv_attention_workspace_size(m, n_q_heads, n_kv_heads, head_dim, n_ctx))
+
+
 def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, positions: torch.Tensor,
               out: torch.Tensor, m: int | None = None, scale: float | None = None,
-              flops: float = 0.0) -> torch.Tensor:
-    """q/out [m, Hq, D]; caches [H, n_ctx, D]; key j visible to row i iff j <= positions[i]."""
+              flops: float = 0.0, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """q/out [m, Hq, D]; caches [H, n_ctx, D]; key j visible to row i iff j <= positions[i].
+    Without `workspace` a scratch buffer is taken from torch's allocator when the
+    shape benefits from splitting the keys."""
     _cuda(q, k_cache, v_cache, positions, out)
     H, n_ctx, D = k_cache.shape
     m = q.shape[0] if m is None else m
     Hq = q.shape[-2] if q.dim() == 3 else q.shape[-1] // D
     scale = 1.0 / math.sqrt(D) if scale is None else scale
+    if workspace is None:
+        need = attention_workspace_bytes(m, Hq, H, D, n_ctx)
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device) if need else None
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
     _run("ckv_attention", _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(positions), _ptr(out), m, Hq,
-              H, D, n_ctx, float(scale), _stream(), flops=flops)
+         H, D, n_ctx, float(scale), _ptr(workspace), ws_bytes, _stream(), flops=flops)
     return out
 
 

@@ -236,10 +236,17 @@ CKV_API int ckv_qkv_rope(const uint16_t* x, const uint16_t* w_qkv, const uint16_
 
 /* Attention of m query tokens over the blended cache with the reference's
  * position mask key j visible iff j <= positions[i] (torch_engine.py:68-70,157),
- * GQA n_q_heads / n_kv_heads.  q/out [m][Hq][D]; caches [H][n_ctx][D]. */
+ * GQA n_q_heads / n_kv_heads (at most 128 query heads per KV head).
+ * q/out [m][Hq][D]; caches [H][n_ctx][D]; head_dim 64 or 128.  tcgen05/TMEM kernel.
+ * `workspace` (16-byte aligned, may be NULL) lets long rows be split along the keys
+ * when the unsplit grid would leave SMs idle; ckv_attention_workspace_size() gives
+ * the bytes that enables it (0: never split for this shape). */
+CKV_API int64_t ckv_attention_workspace_size(int m, int n_q_heads, int n_kv_heads, int head_dim,
+                                             int n_ctx);
 CKV_API int ckv_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
-                  const int32_t* positions, uint16_t* out, int m, int n_q_heads,
-                  int n_kv_heads, int head_dim, int n_ctx, float scale, ckv_stream_t stream);
+                          const int32_t* positions, uint16_t* out, int m, int n_q_heads,
+                          int n_kv_heads, int head_dim, int n_ctx, float scale, void* workspace,
+                          int64_t workspace_bytes, ckv_stream_t stream);
 
 /* Small-m projection (lm_head on the logit rows, torch_engine.py:75-76,165):
  * out [m][n] = bf16(x [m][k] @ w[n][k]^T), m <= 8. */

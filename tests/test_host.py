@@ -36,7 +36,7 @@ def test_status_codes_map_to_reference_exceptions():
         _lib.call("ckv_rmsnorm", None, None, None, 1, 8, 1e-6, None)
     assert "null" in _lib.last_error()
     with pytest.raises(NotImplementedError):
-        _lib.call("ckv_attention", 16, 16, 16, 16, 16, 1, 1, 1, 96, 8, 1.0, None)
+        _lib.call("ckv_attention", 16, 16, 16, 16, 16, 1, 1, 1, 96, 8, 1.0, None, 0, None)
 
 
 def test_ops_refuse_cpu_tensors():
