@@ -58,6 +58,10 @@ def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | N
             print(" ".join(cmd), file=sys.stderr)
         subprocess.run(cmd, check=True)
         relink = True
+    manifest = BUILD / "objects.txt"
+    names = "\n".join(o.name for o in objs)
+    if not manifest.exists() or manifest.read_text() != names:
+        relink = True  # an object was added or removed
     if relink or any(o.stat().st_mtime > LIB.stat().st_mtime for o in objs):
         tmp = LIB.with_suffix(".so.tmp")
         cmd = [nvcc, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-cudart", "static",
@@ -66,6 +70,7 @@ def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | N
             print(" ".join(cmd), file=sys.stderr)
         subprocess.run(cmd, check=True)
         os.replace(tmp, LIB)
+        manifest.write_text(names)
     return LIB
 
 

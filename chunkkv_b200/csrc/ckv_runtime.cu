@@ -58,7 +58,6 @@ int set_smem_limit(const void* kernel, int bytes) {
 uint32_t read_clear_err_rope();
 uint32_t read_clear_err_select();
 uint32_t read_clear_err_gemm();
-uint32_t read_clear_err_attention();
 uint32_t read_clear_err_attention_tc();
 uint32_t read_clear_err_elementwise();
 
@@ -81,7 +80,7 @@ int ckv_get_device_error(uint32_t* code) {
     return CKV_ERR_CUDA;
   }
   *code = ckv::read_clear_err_rope() | ckv::read_clear_err_select() | ckv::read_clear_err_gemm() |
-          ckv::read_clear_err_attention() | ckv::read_clear_err_attention_tc() |
+          ckv::read_clear_err_attention_tc() |
           ckv::read_clear_err_elementwise();
   return CKV_OK;
 }
