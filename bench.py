@@ -38,7 +38,7 @@ METRIC = "blend-prefill tokens/s (Qwen2.5-7B shape, 10x512 shuffled cached chunk
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ratio", type=float, default=0.15)
@@ -286,8 +286,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
     phys = int(vis.split(",")[local]) if vis and vis.split(",")[local].strip().isdigit() else local
-    with ClockSampler(phys) as clk, \
-            ops.LaunchTimer() as timer:
+    with ClockSampler(phys) as clk:
         ev[0].record(stream)
         for i in range(args.steps):
             res = step()
@@ -296,20 +295,31 @@ def run_ours(args):
     barrier()
     step_ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
     total_ms = max_over_ranks(ev[0].elapsed_time(ev[-1]), dev)
-    kern = timer.summary()
-    launches = sum(d["launches"] for d in kern.values())
     stats = res.stats
 
-    # ---- e2e: the public API with host buffers (token list in, log-probs out)
+    # ---- the same K steps again with an event pair around every launch: per-kernel
+    # times for the roofline and the launch count (not part of the timed value)
+    with ops.LaunchTimer() as timer:
+        for i in range(args.steps):
+            step()
+        torch.cuda.synchronize()
+    kern = timer.summary()
+    launches = sum(d["kernels"] for d in kern.values())
+
+    # ---- e2e: the public API with host buffers (token list in, log-probs out),
+    # timed by device events that bracket the host work, H2D, kernels and D2H
     barrier()
     torch.cuda.synchronize()
-    wall = []
+    e2e_ms = []
     for _ in range(args.steps):
-        t0 = time.perf_counter()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
         r = eng.prefill(tokens, pl, cfg)
-        lp = eng.last_logprobs(r)
-        wall.append(time.perf_counter() - t0)
-    e2e_total = max_over_ranks(sum(wall), dev)
+        lp = eng.last_logprobs(r)  # blocking D2H of the log-probs
+        e1.record(stream)
+        e1.synchronize()
+        e2e_ms.append(e0.elapsed_time(e1))
+    e2e_total = max_over_ranks(sum(e2e_ms), dev) * 1e-3
     h2d = eng.last_h2d_bytes
     d2h = eng.last_d2h_bytes + lp.nbytes
 
@@ -337,17 +347,17 @@ def run_ours(args):
     gemm_names = ("ckv_linear", "ckv_linear_residual", "ckv_linear_swiglu", "ckv_qkv_rope")
     g_ms = sum(kern[n]["ms"] for n in gemm_names if n in kern)
     g_fl = sum(kern[n]["flops"] for n in gemm_names if n in kern)
-    g_n = sum(kern[n]["launches"] for n in gemm_names if n in kern)
     busy = sum(d["ms"] for d in kern.values())
-    achieved = g_fl / (g_ms * 1e-3) / 1e12 if g_ms else 0.0
-    roof = {"kernel": "tcgen05 GEMMs (qkv+rope, o_proj+residual, gate/up+swiglu, down+residual)",
-            "bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops_sustained"],
-            "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops_sustained"], 4),
-            "peak_source": f"{pk_kind} bf16_tflops_sustained", "traffic": None,
-            "flops_per_launch": round(g_fl / max(g_n, 1)), "ms_per_launch": round(g_ms / max(g_n, 1), 4)}
+    roof = dominant_roofline(timer, pk, pk_kind, shape)
+    roof["gemm_family"] = {"kernels": "qkv+rope, o_proj+residual, gate/up+swiglu, down+residual",
+                           "achieved": round(g_fl / (g_ms * 1e-3) / 1e12, 1) if g_ms else 0.0,
+                           "frac": round(g_fl / (g_ms * 1e-3) / 1e12 / pk["bf16_tflops_sustained"], 4)
+                           if g_ms else 0.0,
+                           "share_of_busy": round(g_ms / busy, 4) if busy else 0.0}
     kernels = {}
     for name, d in sorted(kern.items(), key=lambda kv: -kv[1]["ms"]):
-        e = {"launches": d["launches"], "ms": round(d["ms"], 3), "share": round(d["ms"] / busy, 4) if busy else 0}
+        e = {"launches": d["launches"], "kernels": d["kernels"], "ms": round(d["ms"], 3),
+             "share": round(d["ms"] / busy, 4) if busy else 0}
         if d["flops"] and name != "ckv_gemv":
             tf = d["flops"] / (d["ms"] * 1e-3) / 1e12
             e.update(tflops=round(tf, 1), frac_tensor=round(tf / pk["bf16_tflops_sustained"], 4))
@@ -374,7 +384,7 @@ def run_ours(args):
         "selected_tokens": int(len(res.selected)), "recomputed_cached_tokens": stats["recomputed_cached_tokens"],
         "prefill_token_equiv": stats["prefill_token_equiv"],
         "e2e": {"value": round(N * args.steps * world / e2e_total, 1), "unit": "tokens/s",
-                "ttft_ms_p50": round(statistics.median(wall) * 1e3, 3),
+                "ttft_ms_p50": round(statistics.median(e2e_ms), 3),
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                 "api": "TorchEngine.prefill(list[int], placements from the paged store) + last_logprobs"},
         "roofline": roof, "kernels": kernels, "gpu_launches": int(launches),
@@ -384,6 +394,38 @@ def run_ours(args):
     if world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_sample(args, shape)
     print(json.dumps(out), flush=True)
+
+
+# DRAM bytes (read + write) of one ckv_linear_swiglu launch at the selected-row shape
+# (M = 938, N = 2 x 18944, K = 3584), from one ncu capture of
+# `bench.py --kernel-case swiglu`; the summary and the command are in
+# profiles/gemm_swiglu_7b_m938.md.  Algorithmic bytes of that launch: the 271.6 MB
+# weight, the 6.7 MB activation read and the 35.5 MB output write.
+SWIGLU_M938_TRAFFIC = 305.3e6
+
+
+def dominant_roofline(timer, pk, pk_kind, shape):
+    """Roofline of the step's dominant kernel, the gate/up GEMM with the SwiGLU
+    epilogue, over its launches at the selected-row shape (every layer after the
+    first); achieved = algorithmic FLOPs per launch / mean CUDA-event duration."""
+    groups: dict[float, list[float]] = {}
+    for name, flops, _nb, e0, e1 in timer.records:
+        if name == "ckv_linear_swiglu":
+            groups.setdefault(flops, []).append(e0.elapsed_time(e1))
+    if not groups:
+        return {"bound": "tensor", "achieved": 0.0, "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                "frac": 0.0, "traffic": None}
+    flops, times = max(groups.items(), key=lambda kv: len(kv[1]))
+    ms = statistics.mean(times)
+    achieved = flops / (ms * 1e-3) / 1e12
+    m_rows = round(flops / (4.0 * shape.inter * shape.hidden))
+    return {"kernel": "ckv_linear_swiglu (tcgen05 gate/up GEMM + SwiGLU epilogue), layers >= 1",
+            "bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops_sustained"],
+            "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops_sustained"], 4),
+            "peak_source": f"{pk_kind} bf16_tflops_sustained", "launches": len(times), "rows": m_rows,
+            "flops_per_launch": round(flops), "ms_per_launch": round(ms, 4),
+            "traffic": SWIGLU_M938_TRAFFIC if (m_rows == 938 and shape.name == "qwen2.5-7b") else None,
+            "traffic_note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at M = 938"}
 
 
 def run_reference(args):

@@ -39,20 +39,30 @@ __global__ void embed_kernel(const uint16_t* __restrict__ table, int vocab, int 
 }
 
 // Qwen2RMSNorm: y = w * bf16(x * rsqrt(mean(x^2) + eps)), fp32 inside.
-__global__ void __launch_bounds__(256) rmsnorm_kernel(const uint16_t* __restrict__ x,
-                                                      const uint16_t* __restrict__ w,
-                                                      uint16_t* __restrict__ y, int hidden,
-                                                      float eps) {
-  __shared__ float s_red[8];
+// One 128-thread CTA per row; each thread keeps its (at most kRmsVec) 16-byte vectors
+// of the row in registers between the reduction and the write, so x is read once.
+constexpr int kRmsThreads = 128;
+constexpr int kRmsVec = 5;  // hidden <= 128 * 8 * 5 = 5120
+__global__ void __launch_bounds__(kRmsThreads) rmsnorm_kernel(const uint16_t* __restrict__ x,
+                                                              const uint16_t* __restrict__ w,
+                                                              uint16_t* __restrict__ y, int hidden,
+                                                              float eps) {
+  __shared__ float s_red[kRmsThreads / 32];
   const int row = blockIdx.x;
   const uint4* xr = reinterpret_cast<const uint4*>(x + int64_t(row) * hidden);
   const uint4* wr = reinterpret_cast<const uint4*>(w);
   uint4* yr = reinterpret_cast<uint4*>(y + int64_t(row) * hidden);
   const int vecs = hidden / 8;
+  uint4 v[kRmsVec];
+#pragma unroll
+  for (int i = 0; i < kRmsVec; ++i) {
+    const int c = threadIdx.x + kRmsThreads * i;
+    v[i] = c < vecs ? __ldcs(xr + c) : make_uint4(0u, 0u, 0u, 0u);
+  }
   float ss = 0.f;
-  for (int v = threadIdx.x; v < vecs; v += blockDim.x) {
-    const uint4 a = xr[v];
-    const uint32_t* p = reinterpret_cast<const uint32_t*>(&a);
+#pragma unroll
+  for (int i = 0; i < kRmsVec; ++i) {
+    const uint32_t* p = reinterpret_cast<const uint32_t*>(&v[i]);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float f0 = lo_bf(p[e]), f1 = hi_bf(p[e]);
@@ -63,28 +73,25 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const uint16_t* __restrict
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = ss;
   __syncthreads();
-  if (threadIdx.x < 32) {
-    float t = threadIdx.x < (blockDim.x >> 5) ? s_red[threadIdx.x] : 0.f;
-    t = warp_sum(t);
-    if (threadIdx.x == 0) s_red[0] = t;
-  }
-  __syncthreads();
-  const float var = __fmul_rn(s_red[0], 1.0f / float(hidden));
-  const float r = rsqrtf(__fadd_rn(var, eps));
-  for (int v = threadIdx.x; v < vecs; v += blockDim.x) {
-    const uint4 a = xr[v];
-    const uint4 g = wr[v];
-    const uint32_t* p = reinterpret_cast<const uint32_t*>(&a);
-    const uint32_t* q = reinterpret_cast<const uint32_t*>(&g);
-    uint4 o;
-    uint32_t* po = reinterpret_cast<uint32_t*>(&o);
+  const float tot = (s_red[0] + s_red[1]) + (s_red[2] + s_red[3]);
+  const float r = rsqrtf(__fadd_rn(__fmul_rn(tot, 1.0f / float(hidden)), eps));
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float n0 = bf16_round(__fmul_rn(lo_bf(p[e]), r));
-      const float n1 = bf16_round(__fmul_rn(hi_bf(p[e]), r));
-      po[e] = pack_bf2(__fmul_rn(lo_bf(q[e]), n0), __fmul_rn(hi_bf(q[e]), n1));
+  for (int i = 0; i < kRmsVec; ++i) {
+    const int c = threadIdx.x + kRmsThreads * i;
+    if (c < vecs) {
+      const uint4 g = __ldg(wr + c);
+      const uint32_t* p = reinterpret_cast<const uint32_t*>(&v[i]);
+      const uint32_t* q = reinterpret_cast<const uint32_t*>(&g);
+      uint4 o;
+      uint32_t* po = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float n0 = bf16_round(__fmul_rn(lo_bf(p[e]), r));
+        const float n1 = bf16_round(__fmul_rn(hi_bf(p[e]), r));
+        po[e] = pack_bf2(__fmul_rn(lo_bf(q[e]), n0), __fmul_rn(hi_bf(q[e]), n1));
+      }
+      yr[c] = o;
     }
-    yr[v] = o;
   }
 }
 
@@ -219,8 +226,10 @@ int ckv_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows, int
   CKV_REQUIRE(x && w && y, "ckv_rmsnorm: null pointer");
   CKV_REQUIRE(hidden > 0 && hidden % 8 == 0 && aligned16(x) && aligned16(w) && aligned16(y),
               "ckv_rmsnorm: hidden must be a multiple of 8 and rows 16-byte aligned");
+  CKV_REQUIRE(hidden <= kRmsThreads * 8 * kRmsVec, "ckv_rmsnorm: hidden %d above %d", hidden,
+              kRmsThreads * 8 * kRmsVec);
   if (rows <= 0) return CKV_OK;
-  rmsnorm_kernel<<<rows, 256, 0, as_stream(stream)>>>(x, w, y, hidden, eps);
+  rmsnorm_kernel<<<rows, kRmsThreads, 0, as_stream(stream)>>>(x, w, y, hidden, eps);
   CKV_LAUNCH_CHECK("ckv_rmsnorm");
   return CKV_OK;
 }

@@ -27,15 +27,22 @@ CKV_DEFINE_ERR_WORD(gemm)
 namespace ckv {
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, UMMA_K = 16;
+constexpr int BM = 128, BK = 64, UMMA_K = 16;
 constexpr int STAGES = 4;
 constexpr int kThreads = 192;
 constexpr uint32_t A_BYTES = BM * BK * 2;  // 16 KiB
-constexpr uint32_t B_BYTES = BN * BK * 2;  // 32 KiB
-constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr uint32_t TMEM_COLS = 2 * BN;     // 512: two accumulators
-constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
-constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN);
+constexpr uint32_t TMEM_COLS = 512;        // two accumulators of up to 256 columns
+
+// N-tile width: 256, or 224 when that fills the SMs better (e.g. 3584 columns at
+// M = 938: 128 tiles of 224 instead of 112 of 256 on 148 SMs).
+template <int BN>
+struct GCfg {
+  static_assert(BN % 32 == 0 && BN <= 256, "BN");
+  static constexpr uint32_t B_BYTES = BN * BK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+  static constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN);
+};
 
 enum Epi { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKV = 3 };
 
@@ -66,6 +73,7 @@ __device__ __forceinline__ void store8(uint16_t* dst, const float* v) {
 }
 
 // ---- epilogues: one thread = one tile row; all lanes execute the TMEM loads.
+template <int BN>
 __device__ __forceinline__ void epi_store(uint32_t tacc, int row, int M, int n0, int N,
                                           const EpiParams& ep) {
 #pragma unroll 1
@@ -88,6 +96,7 @@ __device__ __forceinline__ void epi_store(uint32_t tacc, int row, int M, int n0,
   }
 }
 
+template <int BN>
 __device__ __forceinline__ void epi_resid(uint32_t tacc, int row, int M, int n0, int N,
                                           const EpiParams& ep) {
 #pragma unroll 1
@@ -114,6 +123,7 @@ __device__ __forceinline__ void epi_resid(uint32_t tacc, int row, int M, int n0,
 }
 
 // Tile = 128 gate columns then the 128 matching up columns (interleaved weight).
+template <int BN>
 __device__ __forceinline__ void epi_swiglu(uint32_t tacc, int row, int M, int n0, int N,
                                            const EpiParams& ep) {
   const int out0 = n0 / 2;
@@ -136,7 +146,7 @@ __device__ __forceinline__ void epi_swiglu(uint32_t tacc, int row, int M, int n0
   }
 }
 
-template <int HD>
+template <int BN, int HD>
 __device__ __forceinline__ void epi_qkv(uint32_t tacc, int row, int M, int n0, int N,
                                         const EpiParams& ep) {
   constexpr int HALF = HD / 2;
@@ -173,14 +183,20 @@ __device__ __forceinline__ void epi_qkv(uint32_t tacc, int row, int M, int n0, i
         tmem_ld32(tcol + c, x1);
         tmem_ld32(tcol + HALF + c, x2);
         if (!ok) continue;
+        // (cos, sin) of the 32 rotary pairs of this chunk: 16 x 16-byte loads of the row
+        float4 t[16];
+        const float4* cs4 = reinterpret_cast<const float4*>(cs + c);
+#pragma unroll
+        for (int q4 = 0; q4 < 16; ++q4) t[q4] = __ldg(cs4 + q4);
         float o1[32], o2[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const float a = bf16_round(__fadd_rn(x1[j], bf2f(ep.bias[gcol + c + j])));
           const float b = bf16_round(__fadd_rn(x2[j], bf2f(ep.bias[gcol + HALF + c + j])));
-          const float2 r = cs[c + j];
-          o1[j] = __fsub_rn(__fmul_rn(a, r.x), __fmul_rn(b, r.y));
-          o2[j] = __fadd_rn(__fmul_rn(a, r.y), __fmul_rn(b, r.x));
+          const float rc = (j & 1) ? t[j >> 1].z : t[j >> 1].x;
+          const float rs = (j & 1) ? t[j >> 1].w : t[j >> 1].y;
+          o1[j] = __fsub_rn(__fmul_rn(a, rc), __fmul_rn(b, rs));
+          o2[j] = __fadd_rn(__fmul_rn(a, rs), __fmul_rn(b, rc));
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -206,13 +222,13 @@ __device__ __forceinline__ void epi_qkv(uint32_t tacc, int row, int M, int n0, i
   }
 }
 
-template <int EPI, int HD>
+template <int EPI, int HD, int BN>
 __device__ __forceinline__ void run_epilogue(uint32_t tacc, int row, int M, int n0, int N,
                                              const EpiParams& ep) {
-  if constexpr (EPI == EPI_STORE) epi_store(tacc, row, M, n0, N, ep);
-  else if constexpr (EPI == EPI_RESID) epi_resid(tacc, row, M, n0, N, ep);
-  else if constexpr (EPI == EPI_SWIGLU) epi_swiglu(tacc, row, M, n0, N, ep);
-  else epi_qkv<HD>(tacc, row, M, n0, N, ep);
+  if constexpr (EPI == EPI_STORE) epi_store<BN>(tacc, row, M, n0, N, ep);
+  else if constexpr (EPI == EPI_RESID) epi_resid<BN>(tacc, row, M, n0, N, ep);
+  else if constexpr (EPI == EPI_SWIGLU) epi_swiglu<BN>(tacc, row, M, n0, N, ep);
+  else epi_qkv<BN, HD>(tacc, row, M, n0, N, ep);
 }
 
 // Bounded wait that ignores the abort flag (used only while draining).
@@ -222,10 +238,12 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
     if (global_ns() - t0 > kWaitLimitNs) break;
 }
 
-template <int EPI, int HD>
+template <int EPI, int HD, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 int M, int N, int K, EpiParams ep) {
+  using C = GCfg<BN>;
+  constexpr uint32_t B_BYTES = C::B_BYTES, STAGE_BYTES = C::STAGE_BYTES, IDESC = C::IDESC;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -338,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int mt = tile % m_tiles, nt = tile / m_tiles;
       const int row = mt * BM + sub * 32 + lane;
       const uint32_t tacc = tmem_base + (uint32_t(sub * 32) << 16) + acc * BN;
-      run_epilogue<EPI, HD>(tacc, row, M, nt * BN, N, ep);
+      run_epilogue<EPI, HD, BN>(tacc, row, M, nt * BN, N, ep);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -396,9 +414,9 @@ int make_map(CUtensorMap* map, const void* ptr, int rows, int k, int64_t ld, int
   return CKV_OK;
 }
 
-template <int EPI, int HD>
-int launch(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, int M, int N, int K,
-           const EpiParams& ep, cudaStream_t stream, const char* name) {
+template <int EPI, int HD, int BN>
+int launch_bn(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, int M, int N, int K,
+              const EpiParams& ep, cudaStream_t stream, const char* name) {
   CKV_REQUIRE(a && b, "%s: null operand", name);
   CKV_REQUIRE(M >= 0 && N > 0 && K > 0, "%s: bad sizes m=%d n=%d k=%d", name, M, N, K);
   CKV_REQUIRE(aligned16(a) && aligned16(b), "%s: operands must be 16-byte aligned", name);
@@ -409,13 +427,31 @@ int launch(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, int M
   CUtensorMap ma, mb;
   if (int rc = make_map(&ma, a, M, K, lda, BM)) return rc;
   if (int rc = make_map(&mb, b, N, K, ldb, BN)) return rc;
-  auto kern = gemm_kernel<EPI, HD>;
-  if (int rc = set_smem_limit(reinterpret_cast<const void*>(kern), SMEM_BYTES)) return rc;
+  auto kern = gemm_kernel<EPI, HD, BN>;
+  if (int rc = set_smem_limit(reinterpret_cast<const void*>(kern), GCfg<BN>::SMEM_BYTES)) return rc;
   const int tiles = ceil_div(M, BM) * ceil_div(N, BN);
   const int grid = std::min(tiles, num_sms());
-  kern<<<grid, kThreads, SMEM_BYTES, stream>>>(ma, mb, M, N, K, ep);
+  kern<<<grid, kThreads, GCfg<BN>::SMEM_BYTES, stream>>>(ma, mb, M, N, K, ep);
   CKV_LAUNCH_CHECK(name);
   return CKV_OK;
+}
+
+// Makespan of whole tiles, in column units: waves x tile width.
+int64_t makespan(int M, int N, int bn) {
+  const int tiles = ceil_div(M, BM) * ceil_div(N, bn);
+  return int64_t(ceil_div(tiles, num_sms())) * bn;
+}
+
+// SwiGLU (interleaved 128-column blocks) and QKV (whole heads) tiles stay 256 wide;
+// the plain and residual epilogues take 224 when it finishes sooner.
+template <int EPI, int HD>
+int launch(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, int M, int N, int K,
+           const EpiParams& ep, cudaStream_t stream, const char* name) {
+  if constexpr (EPI == EPI_STORE || EPI == EPI_RESID) {
+    if (M > 0 && makespan(M, N, 224) < makespan(M, N, 256))
+      return launch_bn<EPI, HD, 224>(a, lda, b, ldb, M, N, K, ep, stream, name);
+  }
+  return launch_bn<EPI, HD, 256>(a, lda, b, ldb, M, N, K, ep, stream, name);
 }
 
 EpiParams zero_params() {
@@ -454,7 +490,7 @@ int ckv_linear_residual(const uint16_t* x, const uint16_t* w, uint16_t* h, int m
 int ckv_linear_swiglu(const uint16_t* x, const uint16_t* w_gate_up, uint16_t* out, int m,
                       int inter, int k, ckv_stream_t stream) {
   CKV_REQUIRE(out && aligned16(out), "ckv_linear_swiglu: output must be 16-byte aligned");
-  CKV_REQUIRE(inter > 0 && inter % (BN / 2) == 0, "ckv_linear_swiglu: inter %% 128 != 0");
+  CKV_REQUIRE(inter > 0 && inter % 128 == 0, "ckv_linear_swiglu: inter %% 128 != 0");
   EpiParams ep = zero_params();
   ep.out = out;
   ep.ldo = inter;

@@ -25,6 +25,7 @@ class LaunchTimer:
 
     def __init__(self):
         self.records: list[tuple[str, float, float, torch.cuda.Event, torch.cuda.Event]] = []
+        self.kernels: dict[str, int] = {}  # device kernels launched per entry point
 
     def __enter__(self):
         global _TIMER
@@ -45,13 +46,15 @@ class LaunchTimer:
             d["ms"] += e0.elapsed_time(e1)
             d["flops"] += flops
             d["bytes"] += nbytes
+        for name, d in out.items():
+            d["kernels"] = self.kernels.get(name, d["launches"])
         return out
 
 
 _TIMER: LaunchTimer | None = None
 
 
-def _run(name: str, *args, flops: float = 0.0, nbytes: float = 0.0) -> None:
+def _run(name: str, *args, flops: float = 0.0, nbytes: float = 0.0, kernels: int = 1) -> None:
     t = _TIMER
     if t is None:
         _lib.call(name, *args)
@@ -62,6 +65,7 @@ def _run(name: str, *args, flops: float = 0.0, nbytes: float = 0.0) -> None:
     _lib.call(name, *args)
     e1.record()
     t.records.append((name, float(flops), float(nbytes), e0, e1))
+    t.kernels[name] = t.kernels.get(name, 0) + kernels
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -284,12 +288,14 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos
     m = q.shape[0] if m is None else m
     Hq = q.shape[-2] if q.dim() == 3 else q.shape[-1] // D
     scale = 1.0 / math.sqrt(D) if scale is None else scale
+    need = attention_workspace_bytes(m, Hq, H, D, n_ctx)
     if workspace is None:
-        need = attention_workspace_bytes(m, Hq, H, D, n_ctx)
         workspace = torch.empty(need, dtype=torch.uint8, device=q.device) if need else None
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    split = 0 < need <= ws_bytes  # split-KV: the attention kernel plus its combine kernel
     _run("ckv_attention", _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(positions), _ptr(out), m, Hq,
-         H, D, n_ctx, float(scale), _ptr(workspace), ws_bytes, _stream(), flops=flops)
+         H, D, n_ctx, float(scale), _ptr(workspace), ws_bytes, _stream(), flops=flops,
+         kernels=2 if split else 1)
     return out
 
 

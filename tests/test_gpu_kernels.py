@@ -351,6 +351,21 @@ def test_linear_many_tiles_persistent_loop():
     assert rel_err(out, x.float() @ w.float().T) <= 1e-2
 
 
+@pytest.mark.parametrize("m,n", [(938, 3584), (938, 3648), (1024, 896)])
+def test_linear_residual_narrow_tiles(m, n):
+    """Shapes whose makespan is shorter with 224-column tiles (incl. a ragged last tile)."""
+    k = 1152
+    g = torch.Generator(device=DEV).manual_seed(m * n)
+    a = torch.randn((m, k), generator=g, device=DEV).to(BF)
+    w = (torch.randn((n, k), generator=g, device=DEV) * 0.02).to(BF)
+    h = torch.randn((m, n), generator=g, device=DEV).to(BF)
+    ref = h.float() + (a.float() @ w.float().T).to(BF).float()
+    ops.linear_residual(a, w, h)
+    assert rel_err(h, ref) <= 1e-2
+    out = ops.linear(a, w)
+    assert rel_err(out, a.float() @ w.float().T) <= 1e-2
+
+
 def test_linear_residual_and_swiglu():
     from chunkkv_b200.engine.weights import interleave_gate_up
 
@@ -426,8 +441,8 @@ def test_attention_matches_masked_sdpa(Hq, H, D, N, m):
 
 
 # ------------------------------------------------------------- elementwise
-def test_rmsnorm_embed_gemv_log_softmax():
-    hid, vocab = 896, 5000
+@pytest.mark.parametrize("hid", [64, 896, 3584, 5120])
+def test_rmsnorm_matches_reference_formula(hid):
     x = torch.randn((77, hid), device=DEV).to(BF)
     w = (1 + 0.1 * torch.randn(hid, device=DEV)).to(BF)
     y = ops.rmsnorm(x, w, 1e-6)
@@ -435,6 +450,11 @@ def test_rmsnorm_embed_gemv_log_softmax():
     ref = w * (x32 * torch.rsqrt(x32.pow(2).mean(-1, keepdim=True) + 1e-6)).to(BF)
     assert rel_err(y, ref) <= 1e-2
     assert (y != ref).float().mean() < 0.01
+
+
+def test_rmsnorm_embed_gemv_log_softmax():
+    hid, vocab = 896, 5000
+    x = torch.randn((77, hid), device=DEV).to(BF)
     E = torch.randn((vocab, hid), device=DEV).to(BF)
     toks = torch.randint(0, vocab, (200,), device=DEV, dtype=torch.int32)
     rows = torch.randperm(200, device=DEV)[:50].sort().values.to(torch.int32)

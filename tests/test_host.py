@@ -35,6 +35,10 @@ def test_status_codes_map_to_reference_exceptions():
     with pytest.raises(ValueError):
         _lib.call("ckv_rmsnorm", None, None, None, 1, 8, 1e-6, None)
     assert "null" in _lib.last_error()
+    # hidden above the one-CTA-per-row limit is refused before any launch
+    with pytest.raises(ValueError):
+        _lib.call("ckv_rmsnorm", 16, 16, 16, 1, 5128, 1e-6, None)
+    assert "5120" in _lib.last_error()
     with pytest.raises(NotImplementedError):
         _lib.call("ckv_attention", 16, 16, 16, 16, 16, 1, 1, 1, 96, 8, 1.0, None, 0, None)
 
