@@ -43,8 +43,13 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ratio", type=float, default=0.15)
     ap.add_argument("--n-sink", type=int, default=4)
-    ap.add_argument("--shape", default="qwen2.5-7b")
-    ap.add_argument("--chunks", type=int, default=10)
+    ap.add_argument("--workload", choices=["dp", "tp", "replay"], default="dp",
+                    help="dp: config 3 (7B, one request per GPU); tp: config 5 (32B split over the GPUs "
+                         "by KV head, 64x512 chunks; defaults --shape qwen2.5-32b --chunks 64 --steps 10); "
+                         "replay: config 4 (256 requests over a 16x256 chunk pool, split over the GPUs)")
+    ap.add_argument("--requests", type=int, default=256, help="replay: total requests over all GPUs")
+    ap.add_argument("--shape", default=None)
+    ap.add_argument("--chunks", type=int, default=None)
     ap.add_argument("--chunk-len", type=int, default=512)
     ap.add_argument("--query-len", type=int, default=128)
     ap.add_argument("--cpu-layers", type=int, default=3, help="layers the CPU sample executes")
@@ -52,7 +57,20 @@ def parse():
     ap.add_argument("--extra-ratios", default="0.30,0.50", help="also time these ratios (TTFT only)")
     ap.add_argument("--kernel-case", choices=["swiglu", "oproj", "qkv", "attention", "gather", "deviation"],
                     help="time one kernel at its 7B-bench shape (for ncu captures) instead of the prefill")
-    return ap.parse_args()
+    args = ap.parse_args()
+    tp = args.workload == "tp"
+    if args.shape is None:
+        args.shape = "qwen2.5-32b" if tp else "qwen2.5-7b"
+    if args.chunks is None:
+        args.chunks = 64 if tp else 10
+    if tp and "--steps" not in sys.argv:
+        args.steps = 10
+    if args.workload == "replay":
+        if "--ratio" not in sys.argv:
+            args.ratio = 0.30
+        if "--n-sink" not in sys.argv:
+            args.n_sink = 2  # ChunkReuseRuntime's BlendConfig default (base.py:39)
+    return args
 
 
 def peaks() -> tuple[dict, str]:
@@ -428,6 +446,319 @@ def dominant_roofline(timer, pk, pk_kind, shape):
             "traffic_note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at M = 938"}
 
 
+def tp_order(n_chunks: int, chunk_len: int, max_shift: int, seed: int) -> list[int]:
+    """Seeded order of the chunks for the TP workload: shuffled within blocks of
+    max_shift // chunk_len chunks, so every chunk moves by at most max_shift tokens."""
+    rng = random.Random(seed)
+    blk = max(2, max_shift // chunk_len)
+    order = []
+    for b in range(0, n_chunks, blk):
+        part = list(range(b, min(b + blk, n_chunks)))
+        rng.shuffle(part)
+        order += part
+    return order
+
+
+def run_tp(args):
+    """Config 5: one request split over all ranks by KV head (tensor parallel, NCCL
+    all-reduce after o_proj and down_proj and of the layer-1 scores)."""
+    import torch
+    import torch.distributed as dist
+
+    from chunkkv_b200 import _lib, ops
+    from chunkkv_b200.engine.base import BlendConfig, Placement
+    from chunkkv_b200.engine.torch_engine import TorchEngine
+    from chunkkv_b200.engine.tp import TensorParallel
+    from chunkkv_b200.engine.weights import SHAPES, random_packed
+    from chunkkv_b200.store.keys import LookupKey
+    from chunkkv_b200.store.kvstore import Entry, KVStore
+    from chunkkv_b200.types import TrustLevel
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    tp = None
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+        tp = TensorParallel()
+    shape = SHAPES[args.shape]
+    weights = random_packed(shape, seed=0, device=dev, tp_rank=rank, tp_size=world)
+    eng = TorchEngine.from_packed(weights, tp=tp)
+    loc = weights.shape
+    # every rank serves the same request (its heads of it)
+    chunks, _, query = make_request(shape.vocab, args.chunks, args.chunk_len, args.query_len, request_seed(0))
+    order = tp_order(args.chunks, args.chunk_len, 16384, request_seed(0))
+    first = eng.prefill(sum(chunks, []))
+    store = KVStore(budget_bytes=2 * args.chunks * args.chunk_len * loc.kv_bytes_per_token)
+    paged = []
+    for i in range(args.chunks):
+        key = LookupKey.build(chunks[i], shape.name, None)
+        store.put(key, Entry(first.chunk(i * args.chunk_len, (i + 1) * args.chunk_len), "bench", f"c{i}",
+                             TrustLevel.SYSTEM))
+        paged.append(store.get(key)[0].kv)
+    del first
+    torch.cuda.empty_cache()
+    tokens, pl = [], []
+    for c in order:
+        pl.append(Placement(paged[c], len(tokens)))
+        tokens += chunks[c]
+    tokens += query
+    N = len(tokens)
+    max_delta = max(abs(p.start - p.chunk.start) for p in pl)
+    cfg = BlendConfig(recompute_ratio=args.ratio, n_sink=args.n_sink)
+
+    def step():
+        return eng.prefill(tokens, pl, cfg)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    _lib.check_device()
+    stream = torch.cuda.current_stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    barrier()
+    torch.cuda.synchronize()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    phys = int(vis.split(",")[local]) if vis and vis.split(",")[local].strip().isdigit() else local
+    with ClockSampler(phys) as clk:
+        ev[0].record(stream)
+        for i in range(args.steps):
+            res = step()
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    step_ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
+    total_ms = max_over_ranks(ev[0].elapsed_time(ev[-1]), dev)
+    with ops.LaunchTimer() as timer:
+        for i in range(args.steps):
+            step()
+        torch.cuda.synchronize()
+    kern = timer.summary()
+    barrier()
+    torch.cuda.synchronize()
+    e2e_ms = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        r = eng.prefill(tokens, pl, cfg)
+        lp = eng.last_logprobs(r)
+        e1.record(stream)
+        e1.synchronize()
+        e2e_ms.append(e0.elapsed_time(e1))
+    e2e_total = max_over_ranks(sum(e2e_ms), dev) * 1e-3
+    _lib.check_device()
+    barrier()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    pk, pk_kind = peaks()
+    busy = sum(d["ms"] for d in kern.values())
+    kernels = {}
+    for name, d in sorted(kern.items(), key=lambda kv: -kv[1]["ms"]):
+        e = {"launches": d["launches"], "kernels": d["kernels"], "ms": round(d["ms"], 3),
+             "share": round(d["ms"] / busy, 4) if busy else 0}
+        if d["flops"] and name != "ckv_gemv":
+            tf = d["flops"] / (d["ms"] * 1e-3) / 1e12
+            e.update(tflops=round(tf, 1), frac_tensor=round(tf / pk["bf16_tflops_sustained"], 4))
+        if d["bytes"]:
+            gb = d["bytes"] / (d["ms"] * 1e-3) / 1e9
+            if name == "nccl_all_reduce":
+                e.update(bus_gbs=round(gb, 1), frac_nvlink=round(gb / 770.0, 4),
+                         bus_bytes_per_launch=round(d["bytes"] / d["launches"]))
+            else:
+                e.update(gbs=round(gb, 1), frac_hbm=round(gb / pk["hbm_gbs"], 4),
+                         bytes_per_launch=round(d["bytes"] / d["launches"]))
+        kernels[name] = e
+    gemm_names = ("ckv_linear", "ckv_linear_residual", "ckv_linear_swiglu", "ckv_qkv_rope")
+    g_ms = sum(kern[n]["ms"] for n in gemm_names if n in kern)
+    g_fl = sum(kern[n]["flops"] for n in gemm_names if n in kern)
+    g_tf = g_fl / (g_ms * 1e-3) / 1e12 if g_ms else 0.0
+    out = {
+        "metric": f"blend-prefill tokens/s ({args.shape} shape, tensor parallel over {world} GPU(s), "
+                  f"{args.chunks}x{args.chunk_len} shuffled cached chunks + {args.query_len}-token query)",
+        "value": round(N * args.steps / (total_ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: random-init bf16 weights (seed 0, sharded per rank), uniform random token ids",
+        "config": {"workload": "BASELINE config 5: one shuffled 32k-token blend prefill split by KV head",
+                   "model": f"{args.shape} architecture, random init", "tokens": N,
+                   "cached_tokens": args.chunks * args.chunk_len, "chunks": f"{args.chunks}x{args.chunk_len}",
+                   "max_abs_delta": max_delta, "query_tokens": args.query_len, "recompute_ratio": args.ratio,
+                   "n_sink": args.n_sink, "parallelism": f"tp{world} (KV heads {loc.n_kv} per rank)",
+                   "l2": "inputs larger than L2 every step (weights and cached K/V pages)"},
+        "ttft_ms_p50": round(statistics.median(step_ms), 3),
+        "selected_tokens": int(len(res.selected)), "recomputed_cached_tokens": res.stats["recomputed_cached_tokens"],
+        "e2e": {"value": round(N * args.steps / e2e_total, 1), "unit": "tokens/s",
+                "ttft_ms_p50": round(statistics.median(e2e_ms), 3),
+                "h2d_bytes_per_step": int(eng.last_h2d_bytes),
+                "d2h_bytes_per_step": int(eng.last_d2h_bytes + lp.nbytes)},
+        "roofline": {"kernel": "tcgen05 GEMMs (all four entry points)", "bound": "tensor",
+                     "achieved": round(g_tf, 1), "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                     "frac": round(g_tf / pk["bf16_tflops_sustained"], 4),
+                     "peak_source": f"{pk_kind} bf16_tflops_sustained", "traffic": None},
+        "kernels": kernels, "gpu_launches": int(sum(d["kernels"] for d in kern.values())),
+        "gpu_busy_ms_per_step": round(busy / args.steps, 3), "clocks": clk.summary(),
+        "cpu_baseline": None,
+        "cpu_baseline_note": "infeasible on the host at 32B x 32k tokens",
+    }
+    print(json.dumps(out), flush=True)
+
+
+def replay_requests(n_req: int, vocab: int, seed: int = 7):
+    """Config 4 request stream: a pool of 16 chunks x 256 tokens; each request is a
+    distinct 200-token prefix, 6-12 pool chunks sampled without replacement in random
+    order, and a 16-token query (the last position must be computed for its logits)."""
+    rng = random.Random(seed)
+    pool = [[rng.randrange(vocab) for _ in range(256)] for _ in range(16)]
+    reqs = []
+    for _ in range(n_req):
+        prefix = [rng.randrange(vocab) for _ in range(200)]
+        picks = rng.sample(range(16), rng.randint(6, 12))
+        query = [rng.randrange(vocab) for _ in range(16)]
+        reqs.append((prefix, picks, query))
+    return pool, reqs
+
+
+def lpt_assign(sizes: list[int], world: int) -> list[list[int]]:
+    """Longest-processing-time assignment of requests (by token count) to ranks."""
+    loads = [0] * world
+    out: list[list[int]] = [[] for _ in range(world)]
+    for i in sorted(range(len(sizes)), key=lambda i: -sizes[i]):
+        r = min(range(world), key=lambda r: loads[r])
+        out[r].append(i)
+        loads[r] += sizes[i]
+    return [sorted(o) for o in out]
+
+
+def run_replay(args):
+    """Config 4: requests over a shared chunk pool, data parallel over the GPUs (each
+    rank warms its own pool copy in its own paged store and serves its LPT share).
+    Per request, like ChunkReuseRuntime.prefill (runtime.py:50-93) with every reusable
+    segment blended: store lookups -> blend prefill -> first-token log-probs -> the
+    request's chunk segments written back to the store as new variants."""
+    import torch
+    import torch.distributed as dist
+
+    from chunkkv_b200 import _lib
+    from chunkkv_b200.engine.base import BlendConfig, Placement
+    from chunkkv_b200.engine.torch_engine import TorchEngine
+    from chunkkv_b200.engine.weights import SHAPES, random_packed
+    from chunkkv_b200.store.keys import LookupKey, token_hash
+    from chunkkv_b200.store.kvstore import Entry, KVStore
+    from chunkkv_b200.types import TrustLevel
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    shape = SHAPES[args.shape]
+    eng = TorchEngine.from_packed(random_packed(shape, seed=0, device=dev))
+    pool, reqs = replay_requests(args.requests, shape.vocab)
+    store = KVStore(budget_bytes=40 << 30, pool_bytes=40 << 30, device=dev)
+    warm = eng.prefill(sum(pool, []))
+    keys = [LookupKey.build(c, shape.name, None) for c in pool]
+    for i, k in enumerate(keys):
+        store.put(k, Entry(warm.chunk(i * 256, (i + 1) * 256), "pool", token_hash([]), TrustLevel.SYSTEM))
+    del warm
+    sizes = [200 + 256 * len(p) + 16 for _, p, _ in reqs]
+    mine = lpt_assign(sizes, world)[rank]
+    cfg = BlendConfig(recompute_ratio=args.ratio, n_sink=args.n_sink)
+
+    def serve(i):
+        prefix, picks, query = reqs[i]
+        tokens, pl, segs = list(prefix), [], []
+        for c in picks:
+            entry = store.get(keys[c])[0]
+            pl.append(Placement(entry.kv, len(tokens)))
+            segs.append((c, len(tokens)))
+            tokens += pool[c]
+        tokens += query
+        res = eng.prefill(tokens, pl, cfg)
+        lp = eng.last_logprobs(res)
+        for c, st in segs:
+            store.put(keys[c], Entry(res.chunk(st, st + 256), f"req{i}", token_hash(tokens[:st]),
+                                     TrustLevel.SYSTEM))
+        return len(tokens), lp
+
+    for i in mine[:max(1, args.warmup)]:
+        serve(i)
+    torch.cuda.synchronize()
+    _lib.check_device()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    phys = int(vis.split(",")[local]) if vis and vis.split(",")[local].strip().isdigit() else local
+    ttft, toks = [], 0
+    with ClockSampler(phys) as clk:
+        t_all0 = torch.cuda.Event(enable_timing=True)
+        t_all0.record(stream)
+        for i in mine:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            n, _ = serve(i)
+            e1.record(stream)
+            e1.synchronize()
+            ttft.append(e0.elapsed_time(e1))
+            toks += n
+        t_all1 = torch.cuda.Event(enable_timing=True)
+        t_all1.record(stream)
+        torch.cuda.synchronize()
+    my_ms = t_all0.elapsed_time(t_all1)
+    _lib.check_device()
+    total_ms = max_over_ranks(my_ms, dev)
+    all_ttft, all_toks = [ttft], [toks]
+    if world > 1:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, (ttft, toks))
+        all_ttft = [g[0] for g in gathered]
+        all_toks = [g[1] for g in gathered]
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    flat = sorted(x for t in all_ttft for x in t)
+    out = {
+        "metric": "config-4 replay requests/s (Qwen2.5-7B shape, 16x256 chunk pool, 6-12 chunks per request)",
+        "value": round(args.requests / (total_ms * 1e-3), 2), "unit": "requests/s", "n_gpus": world,
+        "steps": args.requests, "warmup": max(1, args.warmup), "ms_per_step": round(total_ms / max(1, len(mine)), 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: random-init bf16 weights (seed 0), seeded random prefixes, pool chunks and queries",
+        "config": {"workload": "BASELINE config 4: DP replay; per request store lookups, blend prefill, "
+                               "log-probs and write-back of the chunk segments (direct placements, no gate)",
+                   "model": f"{args.shape} architecture, random init", "requests": args.requests,
+                   "pool": "16x256", "prefix_tokens": 200, "query_tokens": 16, "recompute_ratio": args.ratio,
+                   "n_sink": args.n_sink, "store_bytes_per_gpu": 40 << 30,
+                   "parallelism": f"dp{world} (requests assigned LPT by token count)"},
+        "tokens_per_s": round(sum(all_toks) / (total_ms * 1e-3), 1),
+        "ttft_ms_p50": round(statistics.median(flat), 3),
+        "ttft_ms_p95": round(flat[min(len(flat) - 1, int(0.95 * len(flat)))], 3),
+        "requests_per_gpu": [len(t) for t in all_ttft],
+        "e2e": {"value": round(args.requests / (total_ms * 1e-3), 2), "unit": "requests/s",
+                "h2d_bytes_per_step": int(eng.last_h2d_bytes), "d2h_bytes_per_step": int(eng.last_d2h_bytes),
+                "note": "the timed loop is the public API end to end (host token lists in, log-probs out)"},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(out), flush=True)
+
+
 def run_reference(args):
     """CPU reference arm: the oracle port of the reference path on the host cores."""
     if int(os.environ.get("RANK", "0")) != 0:
@@ -538,6 +869,10 @@ def main():
         return
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "tp":
+        run_tp(args)
+    elif args.workload == "replay":
+        run_replay(args)
     else:
         run_ours(args)
 

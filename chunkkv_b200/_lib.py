@@ -36,11 +36,13 @@ SIGNATURES: dict[str, list] = {
                              _p, _p, _p, _p, _p, _p, _p, _p, _p],
     "ckv_deviation_select_noalloc": [_p, _p, _i64, _p, _p, _p, _i32, _p, _i32, _p, _i32, _i32, _f64, _i32,
                                      _i32, _p, _p, _p, _p, _p, _p, _p],
+    "ckv_deviation_scores": [_p, _p, _i64, _p, _p, _p, _i32, _p, _i32, _i32, _i32, _p, _p, _p],
     "ckv_select_from_scores": [_p, _p, _p, _i32, _p, _i32, _i32, _f64, _p, _p, _p, _p, _p, _p],
     "ckv_apply_selection": [_p, _p, _p, _i32, _p, _p, _p, _p, _i32, _p, _p, _i64, _p, _p, _i32, _i32,
                             _i32, _p],
     "ckv_embed": [_p, _i32, _i32, _p, _p, _i32, _p, _p],
     "ckv_rmsnorm": [_p, _p, _p, _i32, _i32, _f32, _p],
+    "ckv_add_rmsnorm": [_p, _p, _p, _p, _i32, _i32, _f32, _p],
     "ckv_linear": [_p, _p, _p, _p, _i32, _i32, _i32, _p],
     "ckv_linear_residual": [_p, _p, _p, _i32, _i32, _i32, _p],
     "ckv_linear_swiglu": [_p, _p, _p, _i32, _i32, _i32, _p],

@@ -280,15 +280,14 @@ __device__ void select_phase(const SelectArgs& a) {
   }
 }
 
-__global__ void __launch_bounds__(kThreads) deviation_select_kernel(
+// Phase 1: one warp per active token; writes diff[p], norm[p] for p = active[i].
+__device__ __forceinline__ void deviation_rows(
     const uint16_t* __restrict__ k_fresh, const uint16_t* __restrict__ v_fresh, int64_t fstride,
     const uint16_t* __restrict__ k_base, const uint16_t* __restrict__ v_base,
-    const int32_t* __restrict__ active, int n_act, int H, int D, float* diff, float* norm,
-    unsigned* counter, SelectArgs sa) {
-  __shared__ int s_last;
+    const int32_t* __restrict__ active, int n_act, int H, int D, const uint8_t* __restrict__ pos_flags,
+    int n_ctx, float* diff, float* norm) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int vecs = (H * D) / 8;
-  const int n_ctx = sa.n_ctx;
   for (int i = blockIdx.x * kWarps + warp; i < n_act; i += gridDim.x * kWarps) {
     const int p = active[i];
     if (p < 0 || p >= n_ctx) {
@@ -297,7 +296,7 @@ __global__ void __launch_bounds__(kThreads) deviation_select_kernel(
     }
     // the reference compares against a zero-initialised cache (torch_engine.py:97) that
     // only moved chunks fill, so a position no chunk covers compares against zeros
-    const bool cached = (sa.pos_flags[p] & kInCached) != 0;
+    const bool cached = (pos_flags[p] & kInCached) != 0;
     float dk = 0.f, dv = 0.f, nk = 0.f, nv = 0.f;
     for (int v = lane; v < vecs; v += 32) {
       const int e0 = v * 8, h = e0 / D, d = e0 - h * D;
@@ -337,6 +336,25 @@ __global__ void __launch_bounds__(kThreads) deviation_select_kernel(
       norm[p] = nk + nv;
     }
   }
+}
+
+__global__ void __launch_bounds__(kThreads) deviation_scores_kernel(
+    const uint16_t* __restrict__ k_fresh, const uint16_t* __restrict__ v_fresh, int64_t fstride,
+    const uint16_t* __restrict__ k_base, const uint16_t* __restrict__ v_base,
+    const int32_t* __restrict__ active, int n_act, int H, int D, const uint8_t* __restrict__ pos_flags,
+    int n_ctx, float* diff, float* norm) {
+  deviation_rows(k_fresh, v_fresh, fstride, k_base, v_base, active, n_act, H, D, pos_flags, n_ctx,
+                 diff, norm);
+}
+
+__global__ void __launch_bounds__(kThreads) deviation_select_kernel(
+    const uint16_t* __restrict__ k_fresh, const uint16_t* __restrict__ v_fresh, int64_t fstride,
+    const uint16_t* __restrict__ k_base, const uint16_t* __restrict__ v_base,
+    const int32_t* __restrict__ active, int n_act, int H, int D, float* diff, float* norm,
+    unsigned* counter, SelectArgs sa) {
+  __shared__ int s_last;
+  deviation_rows(k_fresh, v_fresh, fstride, k_base, v_base, active, n_act, H, D, sa.pos_flags,
+                 sa.n_ctx, diff, norm);
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -394,6 +412,28 @@ int ckv_deviation_select(const uint16_t* k_fresh, const uint16_t* v_fresh,
       k_fresh, v_fresh, fresh_row_stride, k_base, v_base, active, n_act, n_kv_heads, head_dim,
       diff, norm, counter, sa);
   CKV_LAUNCH_CHECK("ckv_deviation_select");
+  return CKV_OK;
+}
+
+int ckv_deviation_scores(const uint16_t* k_fresh, const uint16_t* v_fresh,
+                         int64_t fresh_row_stride, const uint16_t* k_base, const uint16_t* v_base,
+                         const int32_t* active, int n_act, const uint8_t* pos_flags, int n_ctx,
+                         int n_kv_heads, int head_dim, float* diff, float* norm,
+                         ckv_stream_t stream) {
+  CKV_REQUIRE(k_fresh && v_fresh && k_base && v_base && active && pos_flags && diff && norm,
+              "ckv_deviation_scores: null pointer");
+  CKV_REQUIRE(aligned16(k_fresh) && aligned16(v_fresh) && aligned16(k_base) && aligned16(v_base),
+              "ckv_deviation_scores: K/V must be 16-byte aligned");
+  CKV_REQUIRE(head_dim % 8 == 0 && fresh_row_stride % 8 == 0 && n_kv_heads > 0,
+              "ckv_deviation_scores: head_dim and row stride must be multiples of 8");
+  CKV_REQUIRE(n_ctx > 0 && n_act >= 0 && n_act <= n_ctx, "ckv_deviation_scores: n_act %d out of range",
+              n_act);
+  if (n_act == 0) return CKV_OK;
+  const int grid = std::min(ceil_div(n_act, kWarps), 2 * num_sms());
+  deviation_scores_kernel<<<grid, kThreads, 0, as_stream(stream)>>>(
+      k_fresh, v_fresh, fresh_row_stride, k_base, v_base, active, n_act, n_kv_heads, head_dim,
+      pos_flags, n_ctx, diff, norm);
+  CKV_LAUNCH_CHECK("ckv_deviation_scores");
   return CKV_OK;
 }
 

@@ -41,15 +41,19 @@ __global__ void embed_kernel(const uint16_t* __restrict__ table, int vocab, int 
 // Qwen2RMSNorm: y = w * bf16(x * rsqrt(mean(x^2) + eps)), fp32 inside.
 // One 128-thread CTA per row; each thread keeps its (at most kRmsVec) 16-byte vectors
 // of the row in registers between the reduction and the write, so x is read once.
+// kAdd: first h = bf16(h + delta) (the residual add of a row-parallel projection whose
+// partial sums were all-reduced), written back to h, then y = RMSNorm(h).
 constexpr int kRmsThreads = 128;
 constexpr int kRmsVec = 5;  // hidden <= 128 * 8 * 5 = 5120
-__global__ void __launch_bounds__(kRmsThreads) rmsnorm_kernel(const uint16_t* __restrict__ x,
+template <bool kAdd>
+__global__ void __launch_bounds__(kRmsThreads) rmsnorm_kernel(uint16_t* __restrict__ x,
+                                                              const uint16_t* __restrict__ delta,
                                                               const uint16_t* __restrict__ w,
                                                               uint16_t* __restrict__ y, int hidden,
                                                               float eps) {
   __shared__ float s_red[kRmsThreads / 32];
   const int row = blockIdx.x;
-  const uint4* xr = reinterpret_cast<const uint4*>(x + int64_t(row) * hidden);
+  uint4* xr = reinterpret_cast<uint4*>(x + int64_t(row) * hidden);
   const uint4* wr = reinterpret_cast<const uint4*>(w);
   uint4* yr = reinterpret_cast<uint4*>(y + int64_t(row) * hidden);
   const int vecs = hidden / 8;
@@ -58,6 +62,22 @@ __global__ void __launch_bounds__(kRmsThreads) rmsnorm_kernel(const uint16_t* __
   for (int i = 0; i < kRmsVec; ++i) {
     const int c = threadIdx.x + kRmsThreads * i;
     v[i] = c < vecs ? __ldcs(xr + c) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  if constexpr (kAdd) {
+    const uint4* dr = reinterpret_cast<const uint4*>(delta + int64_t(row) * hidden);
+#pragma unroll
+    for (int i = 0; i < kRmsVec; ++i) {
+      const int c = threadIdx.x + kRmsThreads * i;
+      if (c < vecs) {
+        const uint4 dv = __ldcs(dr + c);
+        uint32_t* p = reinterpret_cast<uint32_t*>(&v[i]);
+        const uint32_t* q = reinterpret_cast<const uint32_t*>(&dv);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          p[e] = pack_bf2(__fadd_rn(lo_bf(p[e]), lo_bf(q[e])), __fadd_rn(hi_bf(p[e]), hi_bf(q[e])));
+        xr[c] = v[i];
+      }
+    }
   }
   float ss = 0.f;
 #pragma unroll
@@ -229,8 +249,24 @@ int ckv_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows, int
   CKV_REQUIRE(hidden <= kRmsThreads * 8 * kRmsVec, "ckv_rmsnorm: hidden %d above %d", hidden,
               kRmsThreads * 8 * kRmsVec);
   if (rows <= 0) return CKV_OK;
-  rmsnorm_kernel<<<rows, kRmsThreads, 0, as_stream(stream)>>>(x, w, y, hidden, eps);
+  rmsnorm_kernel<false><<<rows, kRmsThreads, 0, as_stream(stream)>>>(const_cast<uint16_t*>(x),
+                                                                      nullptr, w, y, hidden, eps);
   CKV_LAUNCH_CHECK("ckv_rmsnorm");
+  return CKV_OK;
+}
+
+int ckv_add_rmsnorm(uint16_t* h, const uint16_t* delta, const uint16_t* w, uint16_t* y, int rows,
+                    int hidden, float eps, ckv_stream_t stream) {
+  CKV_REQUIRE(h && delta && w && y, "ckv_add_rmsnorm: null pointer");
+  CKV_REQUIRE(hidden > 0 && hidden % 8 == 0 && aligned16(h) && aligned16(delta) && aligned16(w) &&
+                  aligned16(y),
+              "ckv_add_rmsnorm: hidden must be a multiple of 8 and rows 16-byte aligned");
+  CKV_REQUIRE(hidden <= kRmsThreads * 8 * kRmsVec, "ckv_add_rmsnorm: hidden %d above %d", hidden,
+              kRmsThreads * 8 * kRmsVec);
+  CKV_REQUIRE(y != h && y != delta, "ckv_add_rmsnorm: y must not alias h or delta");
+  if (rows <= 0) return CKV_OK;
+  rmsnorm_kernel<true><<<rows, kRmsThreads, 0, as_stream(stream)>>>(h, delta, w, y, hidden, eps);
+  CKV_LAUNCH_CHECK("ckv_add_rmsnorm");
   return CKV_OK;
 }
 

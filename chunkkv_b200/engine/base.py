@@ -29,6 +29,55 @@ class ChunkKV:
         return self.keys[0].shape[2]
 
 
+class CacheChunkKV:
+    """ChunkKV of a CUDA-engine result: positions [start, end) of its blended cache
+    (two [L, H, N, D] tensors).  `keys` / `values` are the reference's per-layer
+    (1, H, len, D) tensors, copied out on first access so that a chunk kept by the
+    caller stops pinning the request's cache (base.py:53 of the reference copies
+    eagerly).  Until then the chunk is a view: this package's KVStore writes its
+    pages, and the engine gathers, straight from the cache without the L x 2 copies."""
+
+    def __init__(self, cache, start: int, end: int, copy: Callable[[Any], Any]):
+        self._cache = cache
+        self.start = start
+        self._end = end
+        self._copy = copy
+        self._kv: tuple[list[Any], list[Any]] | None = None
+
+    @property
+    def length(self) -> int:
+        return self._end - self.start
+
+    @property
+    def viewable(self) -> bool:
+        return self._cache is not None
+
+    @property
+    def n_layers(self) -> int:
+        return self._cache[0].shape[0] if self._cache is not None else len(self._kv[0])
+
+    def view(self, li: int, kv: int):
+        """(H, len, D) view of layer `li` (kv 0: K, 1: V) in the cache."""
+        return self._cache[kv][li, :, self.start:self._end]
+
+    def _materialise(self):
+        if self._kv is None:
+            K, V = self._cache
+            L = K.shape[0]
+            self._kv = ([self._copy(K[li, None, :, self.start:self._end]) for li in range(L)],
+                        [self._copy(V[li, None, :, self.start:self._end]) for li in range(L)])
+            self._cache = None
+        return self._kv
+
+    @property
+    def keys(self) -> list[Any]:
+        return self._materialise()[0]
+
+    @property
+    def values(self) -> list[Any]:
+        return self._materialise()[1]
+
+
 @dataclass
 class Placement:
     """A cached chunk served at a new offset `start` of the request."""
@@ -63,6 +112,8 @@ class PrefillResult:
     selected: Any = None   # ascending positions recomputed at layers >= 1 (int32)
 
     def chunk(self, start: int, end: int) -> ChunkKV:
+        if self.cache is not None:
+            return CacheChunkKV(self.cache, start, end, self.copy)
         return ChunkKV(
             keys=[self.copy(k[:, :, start:end, :]) for k in self.keys],
             values=[self.copy(v[:, :, start:end, :]) for v in self.values],

@@ -28,60 +28,25 @@ import numpy as np
 import torch
 
 from chunkkv_b200 import _lib, ops
-from chunkkv_b200.engine.base import (BlendConfig, ChunkKV, Placement, PrefillResult,  # noqa: F401
-                                      plan_arrays, plan_positions)
+from chunkkv_b200.engine.base import (BlendConfig, CacheChunkKV, ChunkKV, Placement,  # noqa: F401
+                                      PrefillResult, plan_arrays, plan_positions)
+from chunkkv_b200.engine.staging import Staging as _Staging
+from chunkkv_b200.engine.staging import pack_upload as _pack_upload
 from chunkkv_b200.engine.weights import PackedQwen2, Qwen2Shape, pack
-
-_ALIGN = 16
-
-
-class _Staging:
-    """One pinned host buffer per direction, reused across calls; an event guards reuse."""
-
-    def __init__(self):
-        self.host: torch.Tensor | None = None
-        self.event: torch.cuda.Event | None = None
-
-    def get(self, nbytes: int) -> torch.Tensor:
-        if self.event is not None:
-            self.event.synchronize()
-        if self.host is None or self.host.numel() < nbytes:
-            self.host = torch.empty(max(nbytes, 1 << 16) * 2, dtype=torch.uint8, pin_memory=True)
-        return self.host[:nbytes]
-
-    def mark(self) -> None:
-        if self.event is None:
-            self.event = torch.cuda.Event()
-        self.event.record()
-
-
-def _pack_upload(parts: list[tuple[str, np.ndarray]], staging: _Staging, device):
-    """Copy several small host arrays to the device in ONE transfer; returns views + bytes."""
-    offs, off = [], 0
-    for _, a in parts:
-        off = (off + _ALIGN - 1) // _ALIGN * _ALIGN
-        offs.append(off)
-        off += a.nbytes
-    total = max(off, _ALIGN)
-    host = staging.get(total)
-    hview = host.numpy()
-    for (_, a), o in zip(parts, offs):
-        hview[o:o + a.nbytes] = np.frombuffer(np.ascontiguousarray(a).tobytes(), dtype=np.uint8)
-    dev = torch.empty(total, dtype=torch.uint8, device=device)
-    dev.copy_(host, non_blocking=True)
-    staging.mark()
-    out = {}
-    for (name, a), o in zip(parts, offs):
-        out[name] = dev[o:o + a.nbytes].view(getattr(torch, a.dtype.name)).view(a.shape)
-    return out, total
 
 
 class TorchEngine:
     """Blend-prefill engine over Qwen2-family weights, running on this package's CUDA kernels."""
 
-    def __init__(self, model, tokenizer=None, *, weights: PackedQwen2 | None = None, device=None):
+    def __init__(self, model, tokenizer=None, *, weights: PackedQwen2 | None = None, device=None,
+                 tp=None):
+        """`tp`: an `engine.tp.TensorParallel` group to split the model by KV head over
+        its ranks (one process per GPU); the engine then holds and returns only this
+        rank's KV heads, and `n_kv` / `layers` describe the local shard."""
         self.model = model
         self.tokenizer = tokenizer
+        self.tp = tp if (tp is not None and tp.size > 1) else None
+        tp_rank, tp_size = (tp.rank, tp.size) if self.tp else (0, 1)
         if weights is None:
             if model is None:
                 raise ValueError("pass an HF model or packed weights")
@@ -101,7 +66,10 @@ class TorchEngine:
             if shape.tied:
                 sd.setdefault("lm_head.weight", sd["model.embed_tokens.weight"])
             dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-            weights = pack(shape, sd, device=dev)
+            weights = pack(shape, sd, device=dev, tp_rank=tp_rank, tp_size=tp_size)
+        if (weights.tp_rank, weights.tp_size) != (tp_rank, tp_size):
+            raise ValueError(f"weights are shard {weights.tp_rank}/{weights.tp_size}, "
+                             f"the engine's group is rank {tp_rank} of {tp_size}")
         self.w = weights
         self.shape = s = weights.shape
         self.device = weights.device
@@ -117,7 +85,7 @@ class TorchEngine:
         tok_eos = getattr(tokenizer, "eos_token_id", None)
         self.eos = eos_set | ({tok_eos} if tok_eos is not None else set())
         self._rope_tab: torch.Tensor | None = None
-        self._up = _Staging()
+        self._up = _Staging(slots=4)
         self._down = _Staging()
         self._ws: ops.SelectWorkspace | None = None
         self._attn_ws: torch.Tensor | None = None
@@ -133,8 +101,8 @@ class TorchEngine:
         return cls(model, AutoTokenizer.from_pretrained(repo))
 
     @classmethod
-    def from_packed(cls, weights: PackedQwen2, tokenizer=None) -> "TorchEngine":
-        return cls(None, tokenizer, weights=weights)
+    def from_packed(cls, weights: PackedQwen2, tokenizer=None, tp=None) -> "TorchEngine":
+        return cls(None, tokenizer, weights=weights, tp=tp)
 
     # -- helpers -----------------------------------------------------------
     def rope_table(self, n: int) -> torch.Tensor:
@@ -168,11 +136,38 @@ class TorchEngine:
         return ops.shift_keys(k, delta, self.inv_freq)
 
     def _chunk_tensors(self, chunk, li: int, kv: int) -> torch.Tensor:
+        if isinstance(chunk, CacheChunkKV) and chunk.viewable:
+            t = chunk.view(li, kv)[None]
+            if t.device == self.device and t.dtype == torch.bfloat16:
+                return t
         t = (chunk.keys if kv == 0 else chunk.values)[li]
         if not (t.is_cuda and t.dtype == torch.bfloat16 and t.stride(-1) == 1 and t.stride(-2) == t.shape[-1]
                 and t.data_ptr() % 16 == 0 and t.stride(1) % 8 == 0):
             t = t.to(device=self.device, dtype=torch.bfloat16).contiguous()
         return t
+
+    def _block_tail(self, li: int, attn, h, x, act, part, M: int) -> bool:
+        """o_proj + residual, post-attention RMSNorm, SwiGLU MLP + residual of layer `li`
+        (torch_engine.py:68-76) over rows [0, M).  Tensor parallel: o_proj and down_proj
+        are row-parallel, so their partial rows are summed over the ranks and the
+        residual add is fused with the next RMSNorm (the next layer's input norm, or
+        the final norm after the last layer); returns True when x then holds it."""
+        s, lw, tp = self.shape, self.w.layers[li], self.tp
+        if tp is None:
+            ops.linear_residual(attn, lw.w_o, h, m=M)
+            ops.rmsnorm(h[:M], lw.ln2, s.rms_eps, out=x[:M])
+            ops.linear_swiglu(x, lw.w_gu, act, m=M)
+            ops.linear_residual(act, lw.w_down, h, m=M)
+            return False
+        ops.linear(attn[:M], lw.w_o, out=part[:M])
+        tp.all_reduce_(part[:M])
+        ops.add_rmsnorm(h[:M], part[:M], lw.ln2, s.rms_eps, out=x[:M])
+        ops.linear_swiglu(x, lw.w_gu, act, m=M)
+        ops.linear(act[:M], lw.w_down, out=part[:M])
+        tp.all_reduce_(part[:M])
+        nxt = self.w.layers[li + 1].ln1 if li + 1 < s.n_layers else self.w.norm
+        ops.add_rmsnorm(h[:M], part[:M], nxt, s.rms_eps, out=x[:M])
+        return True
 
     # -- main entry ----------------------------------------------------------
     @torch.inference_mode()
@@ -261,6 +256,9 @@ class TorchEngine:
         q = torch.empty((max(M0, 1), Hq * D), **bf)
         attn = torch.empty_like(q)
         act = torch.empty((max(M0, 1), s.inter), **bf)
+        tp = self.tp
+        part = torch.empty_like(h) if tp else None  # this rank's partial o_proj / down_proj rows
+        x_ready = False  # x already holds RMSNorm(h) for this layer (fused into the last add)
         if M0:
             ops.embed(self.w.embed, d["tokens"], d["active0"], h[:M0])
         active = d["active0"]
@@ -274,15 +272,25 @@ class TorchEngine:
             lw = self.w.layers[li]
             if M == 0:
                 break
-            ops.rmsnorm(h[:M], lw.ln1, s.rms_eps, out=x[:M])
+            if not x_ready:
+                ops.rmsnorm(h[:M], lw.ln1, s.rms_eps, out=x[:M])
+            x_ready = False
             if li == 1 and do_select:
                 ws = self._workspace(N, len(placements))
                 kc = torch.empty((M, H * D), **bf)
                 vc = torch.empty((M, H * D), **bf)
                 ops.qkv_rope(x, lw.w_qkv, lw.b_qkv, M, Hq * D, qkv_cols, Hq, H, D, active, rope_tab,
                              k_compact=kc, v_compact=vc)
-                ops.deviation_select(kc, vc, K_all[1], V_all[1], active, d["pos_flags"], d["sel_meta"],
-                                     config.escalate_threshold, ws)
+                if tp:
+                    # each rank scores its own KV heads; the sum over ranks is the
+                    # reference's sum over all heads (torch_engine.py:118-124)
+                    ops.deviation_scores(kc, vc, K_all[1], V_all[1], active, d["pos_flags"], ws)
+                    tp.all_reduce_(ws.scores)
+                    ops.select_from_scores(ws.diff, ws.norm, d["pos_flags"], d["sel_meta"],
+                                           config.escalate_threshold, ws)
+                else:
+                    ops.deviation_select(kc, vc, K_all[1], V_all[1], active, d["pos_flags"], d["sel_meta"],
+                                         config.escalate_threshold, ws)
                 h2, x2 = torch.empty_like(h), torch.empty_like(x)
                 ops.apply_selection(ws, M, h, h2, x, x2, kc, vc, K_all[1], V_all[1])
                 # the one host sync: selection size, chunk deviations, kept positions
@@ -319,17 +327,15 @@ class TorchEngine:
                 break
             ops.attention(q, K_all[li], V_all[li], active, attn, m=M, flops=attn_flops,
                           workspace=self._attn_workspace(M, N))
-            ops.linear_residual(attn, lw.w_o, h, m=M)
-            ops.rmsnorm(h[:M], lw.ln2, s.rms_eps, out=x[:M])
-            ops.linear_swiglu(x, lw.w_gu, act, m=M)
-            ops.linear_residual(act, lw.w_down, h, m=M)
+            x_ready = self._block_tail(li, attn, h, x, act, part, M)
 
         r0 = int(np.searchsorted(active_host, logits_from, side="left"))
         n_log = M - r0
         if n_log != N - logits_from:
             raise ValueError("logits requested for positions that were not recomputed")
         if n_log > 0:
-            xf = ops.rmsnorm(h[r0:M], self.w.norm, s.rms_eps)
+            # after the last layer a tensor-parallel run already holds norm(h) in x
+            xf = x[r0:M] if (x_ready and li == L - 1) else ops.rmsnorm(h[r0:M], self.w.norm, s.rms_eps)
             logits = ops.gemv(xf, self.w.lm_head) if n_log <= 8 else ops.linear(xf, self.w.lm_head)
         else:
             logits = torch.empty((0, s.vocab), **bf)
@@ -371,6 +377,7 @@ class TorchEngine:
         q = torch.empty((1, Hq * D), **bf)
         attn = torch.empty_like(q)
         act = torch.empty((1, s.inter), **bf)
+        part = torch.empty_like(h) if self.tp else None
         tok = torch.empty(1, dtype=torch.int32, device=dev)
         posd = torch.empty(1, dtype=torch.int32, device=dev)
         rope_tab = self.rope_table(cap)
@@ -381,19 +388,18 @@ class TorchEngine:
             posd.fill_(pos)
             ops.embed(self.w.embed, tok, None, h)
             Kc, Vc = K[:, :, :pos + 1], V[:, :, :pos + 1]
+            x_ready = False
             for li in range(L):
                 lw = self.w.layers[li]
-                ops.rmsnorm(h, lw.ln1, s.rms_eps, out=x)
+                if not x_ready:
+                    ops.rmsnorm(h, lw.ln1, s.rms_eps, out=x)
                 # the cache slice of this layer as [H, cap, D] (positions < cap)
                 ops.qkv_rope(x, lw.w_qkv, lw.b_qkv, 1, 0, qkv_cols, Hq, H, D, posd, rope_tab, q_out=q,
                              k_cache=K[li], v_cache=V[li])
                 ops.attention(q, K[li], V[li], posd, attn, m=1, workspace=self._attn_workspace(1, cap))
-                ops.linear_residual(attn, lw.w_o, h, m=1)
-                ops.rmsnorm(h, lw.ln2, s.rms_eps, out=x)
-                ops.linear_swiglu(x, lw.w_gu, act, m=1)
-                ops.linear_residual(act, lw.w_down, h, m=1)
+                x_ready = self._block_tail(li, attn, h, x, act, part, 1)
             del Kc, Vc
-            xf = ops.rmsnorm(h, self.w.norm, s.rms_eps)
+            xf = x if x_ready else ops.rmsnorm(h, self.w.norm, s.rms_eps)
             nxt = int(ops.gemv(xf, self.w.lm_head).float().argmax().item())
             pos += 1
         return out

@@ -8,6 +8,13 @@ packed for this engine.  Packing (one-time, at load):
   w_gu   [2*inter, hidden]        gate/up interleaved in 128-row blocks
                                   (block b = gate rows 128b.. then up rows 128b..)
   w_down [hidden, inter]
+
+Tensor parallel (`tp_size` > 1, rank `tp_rank`): rank r keeps KV heads
+[r*H/T, (r+1)*H/T) with their query heads, the same slice of q/k/v rows and
+of the o_proj columns, and intermediate rows [r*I/T, (r+1)*I/T) of gate/up with
+the matching down_proj columns (column-parallel QKV and gate/up, row-parallel
+o_proj and down_proj).  Embedding, norms and lm_head are replicated.  The
+packed `shape` of a rank is its local shape (`tp_local`).
 """
 
 from __future__ import annotations
@@ -35,6 +42,18 @@ class Qwen2Shape:
 
     def truncated(self, n_layers: int) -> "Qwen2Shape":
         return replace(self, name=f"{self.name}-L{n_layers}", n_layers=n_layers)
+
+    def tp_local(self, tp_size: int) -> "Qwen2Shape":
+        """The shape one of `tp_size` tensor-parallel ranks computes: its share of the
+        query/KV heads and of the intermediate size; hidden, vocab, layers unchanged."""
+        if tp_size == 1:
+            return self
+        if self.n_kv % tp_size or self.inter % tp_size or (self.inter // tp_size) % GU_BLOCK:
+            raise NotImplementedError(
+                f"{self.name}: {self.n_kv} KV heads / intermediate {self.inter} do not split {tp_size} ways "
+                f"(need whole KV heads and {GU_BLOCK}-row gate/up blocks per rank)")
+        return replace(self, name=f"{self.name}-tp{tp_size}", n_heads=self.n_heads // tp_size,
+                       n_kv=self.n_kv // tp_size, inter=self.inter // tp_size)
 
     def hf_config(self):
         from transformers import Qwen2Config
@@ -151,11 +170,13 @@ class LayerWeights:
 
 @dataclass
 class PackedQwen2:
-    shape: Qwen2Shape
+    shape: Qwen2Shape  # the local shape of this rank when tensor parallel
     embed: torch.Tensor
     layers: list[LayerWeights]
     norm: torch.Tensor
     lm_head: torch.Tensor
+    tp_rank: int = 0
+    tp_size: int = 1
 
     @property
     def device(self) -> torch.device:
@@ -177,48 +198,68 @@ def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     return torch.stack([g, u], dim=1).reshape(2 * inter, hidden).contiguous()
 
 
-def pack(shape: Qwen2Shape, sd: dict[str, torch.Tensor], device="cuda") -> PackedQwen2:
-    """Pack HF-named weights into the engine layout as contiguous bf16 on `device`."""
-    def get(name):
-        return sd[name].to(device=device, dtype=torch.bfloat16).contiguous()
+def pack(shape: Qwen2Shape, sd: dict[str, torch.Tensor], device="cuda", tp_rank: int = 0,
+         tp_size: int = 1) -> PackedQwen2:
+    """Pack HF-named weights into the engine layout as contiguous bf16 on `device`;
+    with tp_size > 1, only rank `tp_rank`'s shard (module docstring)."""
+    loc = shape.tp_local(tp_size)
+    D, r = shape.head_dim, tp_rank
+    qs = slice(r * loc.n_heads * D, (r + 1) * loc.n_heads * D)
+    ks = slice(r * loc.n_kv * D, (r + 1) * loc.n_kv * D)
+    fs = slice(r * loc.inter, (r + 1) * loc.inter)
+
+    def get(name, rows=slice(None), cols=slice(None)):
+        t = sd[name]
+        t = t[rows] if t.dim() == 1 else t[rows, cols]
+        return t.to(device=device, dtype=torch.bfloat16).contiguous()
 
     layers = []
     for i in range(shape.n_layers):
         p = f"model.layers.{i}."
-        w_qkv = torch.cat([get(p + "self_attn.q_proj.weight"), get(p + "self_attn.k_proj.weight"),
-                           get(p + "self_attn.v_proj.weight")], 0).contiguous()
-        b_qkv = torch.cat([get(p + "self_attn.q_proj.bias"), get(p + "self_attn.k_proj.bias"),
-                           get(p + "self_attn.v_proj.bias")], 0).contiguous()
+        w_qkv = torch.cat([get(p + "self_attn.q_proj.weight", qs), get(p + "self_attn.k_proj.weight", ks),
+                           get(p + "self_attn.v_proj.weight", ks)], 0).contiguous()
+        b_qkv = torch.cat([get(p + "self_attn.q_proj.bias", qs), get(p + "self_attn.k_proj.bias", ks),
+                           get(p + "self_attn.v_proj.bias", ks)], 0).contiguous()
         layers.append(LayerWeights(
             ln1=get(p + "input_layernorm.weight"), w_qkv=w_qkv, b_qkv=b_qkv,
-            w_o=get(p + "self_attn.o_proj.weight"), ln2=get(p + "post_attention_layernorm.weight"),
-            w_gu=interleave_gate_up(get(p + "mlp.gate_proj.weight"), get(p + "mlp.up_proj.weight")),
-            w_down=get(p + "mlp.down_proj.weight")))
+            w_o=get(p + "self_attn.o_proj.weight", slice(None), qs),
+            ln2=get(p + "post_attention_layernorm.weight"),
+            w_gu=interleave_gate_up(get(p + "mlp.gate_proj.weight", fs), get(p + "mlp.up_proj.weight", fs)),
+            w_down=get(p + "mlp.down_proj.weight", slice(None), fs)))
     embed = get("model.embed_tokens.weight")
     lm = embed if shape.tied else get("lm_head.weight")
-    return PackedQwen2(shape, embed, layers, get("model.norm.weight"), lm)
+    return PackedQwen2(loc, embed, layers, get("model.norm.weight"), lm, tp_rank, tp_size)
 
 
-def random_packed(shape: Qwen2Shape, seed: int = 0, device="cuda", std: float = 0.02) -> PackedQwen2:
+def random_packed(shape: Qwen2Shape, seed: int = 0, device="cuda", std: float = 0.02,
+                  tp_rank: int = 0, tp_size: int = 1) -> PackedQwen2:
     """Random weights generated directly on the device, already packed (for large shapes:
     no host copy).  Same distributions as random_state_dict but a different stream of
-    values (device generator), so not comparable with a CPU-generated state dict."""
+    values (device generator), so not comparable with a CPU-generated state dict.
+    With tp_size > 1 each rank draws only its shard, from a generator seeded by
+    (seed, rank); the replicated embedding, norms and lm_head come from `seed`
+    alone, so they are identical on every rank."""
     gen = torch.Generator(device=device).manual_seed(seed)
+    rep = gen
+    if tp_size > 1:
+        rep = torch.Generator(device=device).manual_seed(seed)
+        gen = torch.Generator(device=device).manual_seed(seed * 1009 + 1 + tp_rank)
+    loc = shape.tp_local(tp_size)
     bf = torch.bfloat16
 
-    def randn(*shp, s=std):
-        return (torch.randn(shp, generator=gen, device=device, dtype=torch.float32) * s).to(bf)
+    def randn(*shp, s=std, g=None):
+        return (torch.randn(shp, generator=g or gen, device=device, dtype=torch.float32) * s).to(bf)
 
     def norm_w(n):
-        return (1.0 + (torch.rand(n, generator=gen, device=device) * 2 - 1) * 0.1).to(bf)
+        return (1.0 + (torch.rand(n, generator=rep, device=device) * 2 - 1) * 0.1).to(bf)
 
-    D, H, Hq, hid = shape.head_dim, shape.n_kv, shape.n_heads, shape.hidden
+    D, H, Hq, hid = loc.head_dim, loc.n_kv, loc.n_heads, loc.hidden
     qkv = (Hq + 2 * H) * D
     layers = []
     for _ in range(shape.n_layers):
         layers.append(LayerWeights(
             ln1=norm_w(hid), w_qkv=randn(qkv, hid), b_qkv=randn(qkv), w_o=randn(hid, Hq * D),
-            ln2=norm_w(hid), w_gu=randn(2 * shape.inter, hid), w_down=randn(hid, shape.inter)))
-    embed = randn(shape.vocab, hid, s=1.0)
-    lm = embed if shape.tied else randn(shape.vocab, hid)
-    return PackedQwen2(shape, embed, layers, norm_w(hid), lm)
+            ln2=norm_w(hid), w_gu=randn(2 * loc.inter, hid), w_down=randn(hid, loc.inter)))
+    embed = randn(shape.vocab, hid, s=1.0, g=rep)
+    lm = embed if shape.tied else randn(shape.vocab, hid, g=rep)
+    return PackedQwen2(loc, embed, layers, norm_w(hid), lm, tp_rank, tp_size)

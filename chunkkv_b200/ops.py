@@ -182,6 +182,17 @@ def deviation_select(k_fresh: torch.Tensor, v_fresh: torch.Tensor, k_base: torch
               _ptr(ws.counts), _ptr(ws.flags), _ptr(ws.counter), _stream())
 
 
+def deviation_scores(k_fresh: torch.Tensor, v_fresh: torch.Tensor, k_base: torch.Tensor,
+                     v_base: torch.Tensor, active: torch.Tensor, pos_flags: torch.Tensor,
+                     ws: "SelectWorkspace") -> None:
+    """Layer-1 diff/norm of the given KV heads into ws.diff / ws.norm (no selection)."""
+    _cuda(k_fresh, v_fresh, k_base, v_base, active, pos_flags)
+    H, n_ctx, D = k_base.shape
+    _run("ckv_deviation_scores", _ptr(k_fresh), _ptr(v_fresh), k_fresh.stride(0), _ptr(k_base),
+         _ptr(v_base), _ptr(active), active.numel(), _ptr(pos_flags), n_ctx, H, D, _ptr(ws.diff),
+         _ptr(ws.norm), _stream())
+
+
 def select_from_scores(diff: torch.Tensor, norm: torch.Tensor, pos_flags: torch.Tensor,
                        sel_meta: torch.Tensor, threshold: float | None,
                        ws: "SelectWorkspace") -> None:
@@ -198,8 +209,9 @@ class SelectWorkspace:
     def __init__(self, n_ctx: int, n_chunks: int, device):
         f32 = dict(dtype=torch.float32, device=device)
         i32 = dict(dtype=torch.int32, device=device)
-        self.diff = torch.zeros(n_ctx, **f32)
-        self.norm = torch.zeros(n_ctx, **f32)
+        self.scores = torch.zeros((2, n_ctx), **f32)  # one buffer, so ranks can sum both at once
+        self.diff = self.scores[0]
+        self.norm = self.scores[1]
         self.rel = torch.zeros(max(1, n_chunks), **f32)
         self.keep_abs = torch.empty(n_ctx, **i32)
         self.sel = torch.empty(n_ctx, **i32)
@@ -232,6 +244,17 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | No
     out = torch.empty_like(x) if out is None else out
     rows = x.numel() // x.shape[-1]
     _run("ckv_rmsnorm", _ptr(x), _ptr(w), _ptr(out), rows, x.shape[-1], float(eps), _stream())
+    return out
+
+
+def add_rmsnorm(h: torch.Tensor, delta: torch.Tensor, w: torch.Tensor, eps: float,
+                out: torch.Tensor) -> torch.Tensor:
+    """h = bf16(h + delta) in place, then out = RMSNorm(h)."""
+    _cuda(h, delta, w, out)
+    _bf16(h, delta, w, out)
+    rows = h.numel() // h.shape[-1]
+    _run("ckv_add_rmsnorm", _ptr(h), _ptr(delta), _ptr(w), _ptr(out), rows, h.shape[-1], float(eps),
+         _stream())
     return out
 
 

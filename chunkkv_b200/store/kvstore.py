@@ -17,6 +17,7 @@ import itertools
 from collections import OrderedDict
 from dataclasses import dataclass, field
 
+from chunkkv_b200.engine.base import CacheChunkKV
 from chunkkv_b200.store.keys import LookupKey
 from chunkkv_b200.store.pages import PAGE_TOKENS, PagedChunkKV, PagePool
 from chunkkv_b200.types import TrustLevel
@@ -84,8 +85,10 @@ class KVStore:
 
     # -- paging ------------------------------------------------------------------
     def _ensure_pool(self, kv) -> PagePool:
-        L = len(kv.keys)
-        k0 = kv.keys[0]
+        if isinstance(kv, CacheChunkKV) and kv.viewable:
+            L, k0 = kv.n_layers, kv.view(0, 0)
+        else:
+            L, k0 = len(kv.keys), kv.keys[0]
         H, D = k0.shape[-3], k0.shape[-1]
         if self.pool is None:
             nbytes = self._pool_bytes or (self.budget + self.budget // 8)
@@ -109,7 +112,12 @@ class KVStore:
             if not self._evict_one(protect):
                 raise MemoryError("page pool exhausted")
             ids = pool.alloc(need)
-        pool.write(ids, length, list(kv.keys), list(kv.values))
+        if isinstance(kv, CacheChunkKV) and kv.viewable:
+            # straight from the engine result's cache: no per-layer copies
+            L = pool.n_layers
+            pool.write(ids, length, [kv.view(li, 0) for li in range(L)], [kv.view(li, 1) for li in range(L)])
+        else:
+            pool.write(ids, length, list(kv.keys), list(kv.values))
         entry.kv = PagedChunkKV(pool, ids, length, kv.start)
 
     def _drop(self, e: Entry) -> None:

@@ -15,6 +15,7 @@ import numpy as np
 import torch
 
 from chunkkv_b200 import ops
+from chunkkv_b200.engine.staging import Staging, pack_upload
 
 PAGE_TOKENS = ops.PAGE_TOKENS
 
@@ -27,6 +28,7 @@ class PagePool:
         self.pages = torch.empty((n_pages, n_layers, 2, n_kv_heads, PAGE_TOKENS, head_dim),
                                  dtype=torch.bfloat16, device=device)
         self._free = list(range(n_pages - 1, -1, -1))
+        self._stage = Staging(slots=64)  # page-pointer uploads, one slot per write in flight
 
     @classmethod
     def for_bytes(cls, n_layers, n_kv_heads, head_dim, nbytes: int, device="cuda") -> "PagePool":
@@ -72,12 +74,13 @@ class PagePool:
             ks = [k.contiguous() for k in ks]
             vs = [v.contiguous() for v in vs]
             stride = ks[0].stride(-3)
-        kp = torch.tensor([k.data_ptr() for k in ks], dtype=torch.uint64).to(dev, non_blocking=True)
-        vp = torch.tensor([v.data_ptr() for v in vs], dtype=torch.uint64).to(dev, non_blocking=True)
-        ids = torch.from_numpy(page_ids).to(dev, non_blocking=True)
-        ops.pages_write(self.pages, ids, length, kp, vp, stride)
-        # keep the sources alive until the copy has run
-        torch.cuda.current_stream().synchronize()
+        d, _ = pack_upload([("kp", np.asarray([k.data_ptr() for k in ks], dtype=np.uint64)),
+                            ("vp", np.asarray([v.data_ptr() for v in vs], dtype=np.uint64)),
+                            ("ids", np.asarray(page_ids, dtype=np.int32))], self._stage, dev)
+        ops.pages_write(self.pages, d["ids"], length, d["kp"], d["vp"], stride)
+        # No host sync: device temporaries made by _as_source are freed into torch's
+        # stream-ordered allocator, so no later work on this stream can reuse them
+        # before the copy has run.
 
 
 def _as_source(t: torch.Tensor, dev) -> torch.Tensor:

@@ -175,6 +175,17 @@ CKV_API int ckv_deviation_select_noalloc(const uint16_t* k_fresh, const uint16_t
                                          float* diff, float* norm, float* rel, int32_t* keep_abs,
                                          int32_t* sel, int32_t* counts, ckv_stream_t stream);
 
+/* Deviation scores only (torch_engine.py:118-124), the first phase of
+ * ckv_deviation_select: diff/norm [n_ctx] at the positions in `active`, summed
+ * over the n_kv_heads heads given.  A tensor-parallel rank scores its own KV
+ * heads; the sum of the ranks' scores (an all-reduce) then feeds
+ * ckv_select_from_scores on every rank. */
+CKV_API int ckv_deviation_scores(const uint16_t* k_fresh, const uint16_t* v_fresh,
+                                 int64_t fresh_row_stride, const uint16_t* k_base,
+                                 const uint16_t* v_base, const int32_t* active, int n_act,
+                                 const uint8_t* pos_flags, int n_ctx, int n_kv_heads, int head_dim,
+                                 float* diff, float* norm, ckv_stream_t stream);
+
 /* Selection only, from given fp32 scores (torch_engine.py:125-153): the same
  * device code as the second phase of ckv_deviation_select, one CTA.  `active`
  * is implied: every non-exact position, ascending. */
@@ -204,6 +215,13 @@ CKV_API int ckv_embed(const uint16_t* table, int vocab, int hidden, const int32_
 /* Qwen2RMSNorm: y = w * bf16(x * rsqrt(mean(x^2) + eps)) (fp32 inside). */
 CKV_API int ckv_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows, int hidden,
                 float eps, ckv_stream_t stream);
+
+/* Residual add then RMSNorm, for a row-parallel projection whose partial sums
+ * were all-reduced (tensor parallel; torch_engine.py:70-76 residual adds):
+ *   h = bf16(h + delta); y = w * bf16(h * rsqrt(mean(h^2) + eps)).
+ * h is updated in place; y must not alias h or delta.  hidden <= 5120. */
+CKV_API int ckv_add_rmsnorm(uint16_t* h, const uint16_t* delta, const uint16_t* w, uint16_t* y,
+                            int rows, int hidden, float eps, ckv_stream_t stream);
 
 /* out = bf16(x @ w^T (+ bias)); x [m][k], w [n][k] (nn.Linear), out [m][n].
  * tcgen05/TMEM GEMM; k % 8 == 0, n % 16 == 0, 16-byte aligned rows. */

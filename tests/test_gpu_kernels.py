@@ -323,6 +323,25 @@ def test_deviation_select_fused_matches_formula_and_selection():
     # the ticket counter is back at zero: a second launch works the same
     ops.deviation_select(kf, vf, Kb, Vb, active, flags, meta, None, ws)
     assert int(ws.counts[0]) == n_sel and int(ws.counter[0]) == 0
+    # scores only, per head group (tensor-parallel ranks): the group sums are the fused
+    # kernel's scores, and the selection from them is the fused kernel's selection
+    parts = []
+    for hs in (slice(0, 2), slice(2, 4)):
+        w2 = ops.SelectWorkspace(N, n_ch, DEV)
+        cols = slice(hs.start * D, hs.stop * D)
+        ops.deviation_scores(kf[:, cols].contiguous(), vf[:, cols].contiguous(), Kb[hs].contiguous(),
+                             Vb[hs].contiguous(), active, flags, w2)
+        parts.append(w2.scores.clone())
+    tot = parts[0] + parts[1]
+    torch.testing.assert_close(tot[0, :N], ws.diff[:N], rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(tot[1, :N], ws.norm[:N], rtol=1e-5, atol=1e-4)
+    w3 = ops.SelectWorkspace(N, n_ch, DEV)
+    w3.scores.copy_(tot)
+    ops.select_from_scores(w3.diff[:N], w3.norm[:N], flags, meta, None, w3)
+    ref3 = select(w3.diff[:N].cpu(), w3.norm[:N].cpu(), cached, sink, [P(c * cl) for c in range(n_ch)],
+                  BlendConfig(recompute_ratio=0.15, n_sink=4))
+    n3 = int(w3.counts[0])
+    np.testing.assert_array_equal(w3.keep_abs[:n3].cpu().numpy(), ref3["keep_abs"].numpy())
 
 
 # ------------------------------------------------------------------- GEMMs
@@ -387,7 +406,8 @@ def test_linear_residual_and_swiglu():
     assert rel_err(out, ref2) <= 1e-2
 
 
-@pytest.mark.parametrize("Hq,H,D,hid", [(28, 4, 128, 512), (14, 2, 64, 896), (4, 2, 64, 256)])
+@pytest.mark.parametrize("Hq,H,D,hid", [(28, 4, 128, 512), (14, 2, 64, 896), (4, 2, 64, 256),
+                                        (5, 1, 128, 5120)])
 def test_qkv_rope_scatter_and_compact(Hq, H, D, hid):
     m, N = 300, 1000
     g = torch.Generator(device=DEV).manual_seed(Hq)
@@ -450,6 +470,18 @@ def test_rmsnorm_matches_reference_formula(hid):
     ref = w * (x32 * torch.rsqrt(x32.pow(2).mean(-1, keepdim=True) + 1e-6)).to(BF)
     assert rel_err(y, ref) <= 1e-2
     assert (y != ref).float().mean() < 0.01
+
+
+@pytest.mark.parametrize("hid", [896, 5120])
+def test_add_rmsnorm_is_residual_add_then_rmsnorm(hid):
+    h = torch.randn((53, hid), device=DEV).to(BF)
+    dlt = torch.randn((53, hid), device=DEV).to(BF)
+    w = (1 + 0.1 * torch.randn(hid, device=DEV)).to(BF)
+    h_ref = h + dlt  # bf16 add: fp32 sum rounded once
+    x = torch.empty_like(h)
+    ops.add_rmsnorm(h, dlt, w, 1e-6, x)
+    assert torch.equal(h, h_ref)
+    assert torch.equal(x, ops.rmsnorm(h_ref, w, 1e-6))
 
 
 def test_rmsnorm_embed_gemv_log_softmax():

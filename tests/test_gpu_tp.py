@@ -1,0 +1,143 @@
+"""Tensor-parallel blend prefill on 2 GPUs (NCCL), against the reference fixtures and
+against the same engine on one GPU.
+
+Each rank holds one of the two KV heads of the `tiny` shape with its query heads
+and half of the MLP.  Checked per scenario, on every rank:
+  - stats (token counts, recomputed count, prefill_token_equiv, escalations) equal
+    the reference fixture's, and the first-token logit KL against it is <= 1e-3;
+  - selection bit-exact given the scores: the all-reduced layer-1 scores fed to the
+    oracle's selection give exactly the kept positions of the engine;
+  - every rank ends with the same selection and bit-identical logits (replicated
+    state stays in step);
+  - rank r's blended K/V equal head r of a one-GPU run within bf16 tolerance.
+Needs 2 GPUs; skipped otherwise.  NVLS is off (NCCL_NVLS_ENABLE=0).
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = Path(__file__).resolve().parent.parent
+TINY = ["tiny_fp32", "tiny_bf16", "tiny_escalate", "tiny_exact_overflow"]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    sys.path.insert(0, str(ROOT))
+    sys.path.insert(0, str(ROOT / "tests"))
+    sys.path.insert(0, str(ROOT / "tests" / "golden"))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from chunkkv_b200 import _lib
+        from chunkkv_b200.engine.tp import TensorParallel
+        from chunkkv_b200.engine.torch_engine import TorchEngine
+        from chunkkv_b200.engine.weights import pack
+        from helpers import kl, run_blend, scenario
+        from oracle.blend_oracle import select
+
+        tp = TensorParallel()
+        out = {}
+        for name in TINY:
+            s = scenario(name)
+            eng = TorchEngine.from_packed(pack(s.shape, s.sd, device=dev, tp_rank=rank, tp_size=world), tp=tp)
+            _, _, pl, res = run_blend(eng, s)
+            torch.cuda.synchronize()
+            N = len(s.tokens)
+            cached = torch.zeros(N, dtype=torch.bool)
+            sink = torch.zeros(N, dtype=torch.bool)
+            for p in pl:
+                cached[p.start:p.start + p.chunk.length] = True
+                if not p.exact:
+                    sink[p.start:min(p.start + p.chunk.length, p.start + s.config.n_sink)] = True
+            ws = eng._ws
+            sel = res.selected.cpu().numpy()
+            ref_sel = select(ws.diff[:N].cpu(), ws.norm[:N].cpu(), cached, sink, pl, s.config)["keep_abs"].numpy()
+            single = TorchEngine.from_packed(pack(s.shape, s.sd, device=dev))
+            _, _, _, res1 = run_blend(single, s)
+            K1, V1 = res1.cache
+            K2, V2 = res.cache
+            hs = slice(rank * K2.shape[1], (rank + 1) * K2.shape[1])
+
+            def rel(a, b):
+                a, b = a.float(), b.float()
+                return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+
+            # positions both runs recomputed or both moved (near-tied selections may differ)
+            same = np.ones(N, bool)
+            diff_sel = np.setxor1d(sel, res1.selected.cpu().numpy())
+            same[diff_sel] = False
+            same_t = torch.from_numpy(same).to(dev)
+            out[name] = {
+                "stats": {k: res.stats[k] for k in ("tokens", "cached_tokens", "recomputed_cached_tokens",
+                                                    "prefill_token_equiv")},
+                "escalated": [c["escalated"] for c in res.stats["chunks"]],
+                "kl_ref": kl(s.arrays["logits"][-1].astype(np.float32), res.logits[-1].float().cpu().numpy()),
+                "kl_single": kl(res1.logits[-1].float().cpu().numpy(), res.logits[-1].float().cpu().numpy()),
+                "sel_exact": bool(np.array_equal(ref_sel, sel)),
+                "selected": sel.tolist(),
+                "logits": res.logits[-1].float().cpu().numpy(),
+                "kv_rel": max(rel(K2[:, :, same_t], K1[:, hs][:, :, same_t]),
+                              rel(V2[:, :, same_t], V1[:, hs][:, :, same_t])),
+            }
+            del eng, single
+        _lib.check_device()
+        q.put((rank, out))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, f"{type(e).__name__}: {e}"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tensor_parallel_2gpu_matches_reference_and_single_gpu(golden):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, o = q.get(timeout=600)
+        res[r] = o
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    for r in (0, 1):
+        assert isinstance(res[r], dict), res[r]
+    for name in TINY:
+        meta, _ = golden(name)
+        for r in (0, 1):
+            o = res[r][name]
+            for k, v in o["stats"].items():
+                assert v == meta["stats"][k], (name, r, k)
+            assert o["escalated"] == [c["escalated"] for c in meta["stats"]["chunks"]], (name, r)
+            assert o["kl_ref"] <= 1e-3 and o["kl_single"] <= 1e-3, (name, r, o["kl_ref"], o["kl_single"])
+            assert o["sel_exact"], (name, r)
+            assert o["kv_rel"] <= 1e-2, (name, r, o["kv_rel"])
+        assert res[0][name]["selected"] == res[1][name]["selected"], name
+        assert np.array_equal(res[0][name]["logits"], res[1][name]["logits"]), name
