@@ -180,6 +180,36 @@ def test_paged_store_placements_equal_dense():
     assert torch.equal(out.cache[0], dense.cache[0]) and torch.equal(out.cache[1], dense.cache[1])
 
 
+def test_result_chunks_are_views_until_read_then_copies():
+    """PrefillResult.chunk: the store writes pages from the cache view; reading keys
+    gives (1, H, len, D) copies that no longer depend on the request's cache."""
+    from chunkkv_b200.engine.base import CacheChunkKV
+    from chunkkv_b200.store.keys import LookupKey
+    from chunkkv_b200.store.kvstore import Entry, KVStore
+    from chunkkv_b200.types import TrustLevel
+
+    s = scenario("tiny_bf16")
+    eng = engine_for(s)
+    res = eng.prefill(s.first_tokens[0])
+    K, V = res.cache
+    stored = res.chunk(5, 70)
+    assert isinstance(stored, CacheChunkKV) and stored.length == 65 and stored.start == 5
+    store = KVStore(budget_bytes=64 << 20)
+    key = LookupKey.build([1, 2, 3], "m", None)
+    store.put(key, Entry(stored, "ctx", "p", TrustLevel.SYSTEM))
+    paged = store.get(key)[0].kv
+    kept = res.chunk(5, 70)
+    ks, vs = kept.keys, kept.values
+    assert not kept.viewable and len(ks) == s.shape.n_layers
+    for li in range(s.shape.n_layers):
+        assert ks[li].shape == (1, s.shape.n_kv, 65, s.shape.head_dim) and ks[li].is_contiguous()
+        assert torch.equal(ks[li][0], K[li, :, 5:70]) and torch.equal(vs[li][0], V[li, :, 5:70])
+        assert torch.equal(paged.keys[li], ks[li]) and torch.equal(paged.values[li], vs[li])
+    with torch.inference_mode():
+        K.zero_()
+    assert ks[0].abs().sum() > 0  # the copy is detached from the cache
+
+
 def test_logits_for_unrecomputed_positions_raise():
     s = scenario("tiny_fp32")
     eng = engine_for(s)
