@@ -21,8 +21,13 @@
 // one thread execute in issue order, so S_w(j+1) may be issued right after
 // P_w(j) V_j, which reads the same TMEM columns.  K and V stages are released
 // separately (K after both S, V after both P.V).
-// Warps: 0 = TMA producer, 1 = MMA issuer + TMEM owner, 2..5 and 6..9 = softmax /
-// correction / epilogue of Q tiles 0 and 1.  Every wait is bounded (ckv_common.cuh).
+// Warps: 0..3 and 4..7 = softmax / correction / epilogue of Q tiles 0 and 1,
+// 8 = TMA producer, 9 = MMA issuer + TMEM owner.  A softmax thread reads its S row
+// from TMEM twice, 64 columns at a time (row max, then exponentials), so it never
+// holds more than half a row.  The exponentials are split between the MUFU unit
+// (ex2.approx, 16 results per clock per SM: alone as slow as the tensor core) and a
+// polynomial on the FMA pipe (one pair in four).  Every wait is bounded
+// (ckv_common.cuh).
 #include "ckv_common.cuh"
 
 CKV_DEFINE_ERR_WORD(attention_tc)
@@ -35,11 +40,13 @@ constexpr int NQ = 2;    // Q tiles per CTA
 constexpr int BN = 128;  // keys per tile
 constexpr int KS = 2;    // K stages
 constexpr int VS = 2;    // V stages
-constexpr int kThreads = 64 + NQ * 128;
+constexpr int kThreads = NQ * 128 + 64;  // two softmax warpgroups + producer + MMA warps
+constexpr int kWarpTma = 8, kWarpMma = 9;
 constexpr uint32_t TMEM_COLS = 512;  // S/P of tile w at [128w, 128w+128), O of tile w at 256+128w
 constexpr uint32_t O_COL = 256;
 constexpr uint32_t ATOM_BYTES = 128 * 128;  // one [128 rows][64 bf16] swizzle-128 atom
 constexpr float kRescaleThreshold = 8.0f;   // log2 units
+constexpr int kPolyOf4 = 1;                 // exponential pairs in four on the FMA pipe
 
 template <int HD>
 struct Cfg {
@@ -70,6 +77,31 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
     if (global_ns() - t0 > kWaitLimitNs) break;
 }
 
+// 2^x for a pair, on the FMA pipe: x = n + f with n = round(x), f in [-0.5, 0.5];
+// 2^f by a degree-3 polynomial fitted here to 2^f on [-0.5, 0.5] (relative error
+// 7.5e-5, under 4 % of a bf16 rounding step); 2^n added to the exponent bits.  The
+// rounding uses the float add of 1.5 * 2^23.  x <= 8 on this path; x is clamped at
+// -126 so 2^n stays in range (the result is then below 2^-125, as good as 0).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const float2 magic = make_float2(12582912.f, 12582912.f);
+  const float2 t = __fadd2_rn(x, magic);
+  const float2 n = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = __fadd2_rn(x, make_float2(-n.x, -n.y));
+  float2 p = __ffma2_rn(make_float2(0.05517132f, 0.05517132f), f, make_float2(0.24261054f, 0.24261054f));
+  p = __ffma2_rn(p, f, make_float2(0.69326097f, 0.69326097f));
+  p = __ffma2_rn(p, f, make_float2(0.99992812f, 0.99992812f));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // 10 warps: two of the four SM sub-partitions hold three warps, so the register
 // file allows at most 16384 / (3 * 32) = 170 registers per thread.
 template <int HD>
@@ -95,7 +127,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* q_ready = o_done + NQ;
   uint64_t* o_full = q_ready + 1;
   uint64_t* drain = o_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* turn = drain + 1;  // [NQ]: softmax warpgroup w may run its next tile
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(turn + NQ);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* s_maxpos = reinterpret_cast<int*>(tmem_slot + 2);
 
@@ -120,6 +153,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s_full[w], 1);
       mbar_init(&p_full[w], 128);
       mbar_init(&o_done[w], 1);
+      mbar_init(&turn[w], 128);
     }
     mbar_init(q_ready, NQ * 128);
     mbar_init(o_full, 1);
@@ -150,13 +184,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
   }
-  if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+  if (warp == kWarpMma) tmem_alloc(tmem_slot, TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp == kWarpTma) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
       int nk = 0, nv = 0;  // tiles whose K / V load was issued
@@ -180,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = (nv > VS ? nv - VS : 0); i < nv; ++i) drain_wait(&v_full[i % VS], (i / VS) & 1);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == kWarpMma) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       bool ok = mbar_wait(q_ready, 0, abort, &g_err_word);
@@ -240,16 +274,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         drain_wait(drain, 0);
       }
     }
-  } else {
+  } else if (warp < kWarpTma) {
     // ------------------------------------------------- softmax / correction / epilogue
-    const int w = (warp - 2) >> 2;   // Q tile of this warpgroup
+    const int w = warp >> 2;         // Q tile of this warpgroup
     const int sub = warp & 3;        // TMEM sub-partition (lanes 32*sub .. +31)
     const int r = sub * 32 + lane;   // row in the Q tile == TMEM lane
     const int tr = r / G, g = r - (r / G) * G;
     const int tt = w * T + tr;       // token index in the CTA
     const bool valid = r < T * G && tt < n_tok;
     const int tok = t0 + (valid ? tt : 0);
-    int pos = 0;
+    // padding rows see every key: they never force the masked path on their warp
+    int pos = n_ctx - 1;
     if (valid) pos = min(max(positions[tok], 0), n_ctx - 1);
     const uint16_t* qrow = q + (int64_t(tok) * Hq + hk * G + g) * HD;
     uint8_t* myQ = sQ + w * C::Q_BYTES;
@@ -272,27 +307,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = false;
         break;
       }
+      // the two warpgroups take turns (0, 1, 0, 1, ...): each runs its softmax alone on
+      // the SM sub-partitions while the tensor core works on the other Q tile
+      if ((w == 1 || j > 0) && !warp_wait(&turn[w], (w == 0 ? j - 1 : j) & 1, abort)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
-      uint32_t u[BN];
-      tmem_ld128w(sbuf, u);
       const int lim = pos - (kt0 + j) * BN;  // keys at index > lim are masked
-      // row max of the raw scores (scale > 0 commutes with max), 8 independent chains
+      const bool full = __all_sync(0xffffffffu, lim >= BN - 1);  // whole tile visible to the warp
+      // pass 1: row max of the raw scores (scale > 0 commutes with max), 64 columns at a
+      // time, 8 chains of 3-input max
       float mx8[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
-      if (__all_sync(0xffffffffu, lim >= BN - 1)) {  // whole tile visible to the warp
+      for (int c = 0; c < 8; ++c) mx8[c] = -INFINITY;
 #pragma unroll
-        for (int e = 0; e < BN; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(u[e]));
-      } else {
+      for (int h = 0; h < BN / 64; ++h) {
+        uint32_t u[64];
+        tmem_ld64w(sbuf + 64 * h, u);
+        if (!full) {
 #pragma unroll
-        for (int e = 0; e < BN; ++e) {
-          const float x = e <= lim ? __uint_as_float(u[e]) : -INFINITY;
-          u[e] = __float_as_uint(x);
-          mx8[e & 7] = fmaxf(mx8[e & 7], x);
+          for (int e = 0; e < 64; ++e)
+            if (64 * h + e > lim) u[e] = __float_as_uint(-INFINITY);
         }
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            mx8[c] = max3f(mx8[c], __uint_as_float(u[16 * k + 2 * c]), __uint_as_float(u[16 * k + 2 * c + 1]));
       }
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      const float mx = fmaxf(max3f(mx8[0], mx8[1], mx8[2]), max3f(max3f(mx8[3], mx8[4], mx8[5]), mx8[6], mx8[7]));
       const float m_new = fmaxf(m, mx * scale_log2);
       const bool need = j > 0 && m_new > m + kRescaleThreshold;
       if (__any_sync(0xffffffffu, need)) {
@@ -314,22 +358,47 @@ __global__ void __launch_bounds__(kThreads, 1)
         l *= corr;
       }
       if (j == 0 || need) m = m_new;
-      // P = 2^(s*scale - m): one FFMA + ex2 per element; masked scores are -inf -> 0.
-      // A row that has seen no visible key yet (possible in a later key split) keeps
-      // m = -inf; a finite base keeps its P at exactly 0 instead of NaN.
+      // pass 2: P = 2^(s*scale - m) (scale folded into one packed FFMA), 64 columns at a
+      // time, written back over S as bf16 pairs: P of keys 64h.. goes to columns 32h..,
+      // whose scores were read in the half before.  In a fully visible tile kPolyOf4
+      // pairs in four take the polynomial; masked scores are -inf and go through ex2
+      // (exactly 0).  A row that has seen no visible key yet (possible in a later key
+      // split) keeps m = -inf; the finite base keeps its P at exactly 0 instead of NaN.
       const float neg_m = m == -INFINITY ? 0.f : -m;
-      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+      const float2 sc2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(neg_m, neg_m);
+      float2 rs4[4];
 #pragma unroll
-      for (int e = 0; e < BN; e += 2) {  // packs in place: u[e/2] is already consumed
-        const float p0 = ex2_approx(fmaf(__uint_as_float(u[e]), scale_log2, neg_m));
-        const float p1 = ex2_approx(fmaf(__uint_as_float(u[e + 1]), scale_log2, neg_m));
-        rs4[(e >> 1) & 3] += p0 + p1;
-        u[e >> 1] = pack_bf2(p0, p1);
+      for (int i = 0; i < 4; ++i) rs4[i] = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int h = 0; h < BN / 64; ++h) {
+        uint32_t u[64];
+        tmem_ld64w(sbuf + 64 * h, u);
+        if (full) {
+#pragma unroll
+          for (int pr = 0; pr < 32; ++pr) {
+            const float2 x = __ffma2_rn(make_float2(__uint_as_float(u[2 * pr]), __uint_as_float(u[2 * pr + 1])), sc2, nm2);
+            const float2 pv = (pr & 3) < kPolyOf4 ? exp2_poly2(x) : make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            rs4[pr & 3] = __fadd2_rn(rs4[pr & 3], pv);
+            u[pr] = pack_bf2(pv.x, pv.y);
+          }
+        } else {
+#pragma unroll
+          for (int pr = 0; pr < 32; ++pr) {
+            const float s0 = 64 * h + 2 * pr <= lim ? __uint_as_float(u[2 * pr]) : -INFINITY;
+            const float s1 = 64 * h + 2 * pr + 1 <= lim ? __uint_as_float(u[2 * pr + 1]) : -INFINITY;
+            const float2 x = __ffma2_rn(make_float2(s0, s1), sc2, nm2);
+            const float2 pv = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            rs4[pr & 3] = __fadd2_rn(rs4[pr & 3], pv);
+            u[pr] = pack_bf2(pv.x, pv.y);
+          }
+        }
+        tmem_st32u(sbuf + 32 * h, *reinterpret_cast<const uint32_t(*)[32]>(u));
       }
-      tmem_st64w(sbuf, *reinterpret_cast<uint32_t(*)[64]>(u));
-      l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+      const float2 rsum = __fadd2_rn(__fadd2_rn(rs4[0], rs4[1]), __fadd2_rn(rs4[2], rs4[3]));
+      l += rsum.x + rsum.y;
       tc_fence_before();
       mbar_arrive(&p_full[w]);
+      mbar_arrive(&turn[w ^ 1]);
     }
     if (ok && n_split > 1 && warp_wait(o_full, 0, abort)) {
       // one slice of the keys: unnormalised O with its (max, sum), merged by the combine kernel
@@ -372,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }
