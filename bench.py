@@ -48,6 +48,8 @@ def parse():
                          "by KV head, 64x512 chunks; defaults --shape qwen2.5-32b --chunks 64 --steps 10); "
                          "replay: config 4 (256 requests over a 16x256 chunk pool, split over the GPUs)")
     ap.add_argument("--requests", type=int, default=256, help="replay: total requests over all GPUs")
+    ap.add_argument("--tp-exchange", choices=["peer", "nccl"], default="peer",
+                    help="tp: partial rows over NVLink peer memory (fused kernels) or NCCL all-reduce")
     ap.add_argument("--shape", default=None)
     ap.add_argument("--chunks", type=int, default=None)
     ap.add_argument("--chunk-len", type=int, default=512)
@@ -486,7 +488,7 @@ def run_tp(args):
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-        tp = TensorParallel()
+        tp = TensorParallel(fused=args.tp_exchange == "peer")
     shape = SHAPES[args.shape]
     weights = random_packed(shape, seed=0, device=dev, tp_rank=rank, tp_size=world)
     eng = TorchEngine.from_packed(weights, tp=tp)
@@ -558,6 +560,8 @@ def run_tp(args):
     e2e_total = max_over_ranks(sum(e2e_ms), dev) * 1e-3
     _lib.check_device()
     barrier()
+    if tp is not None and tp._exchange is not None:
+        tp._exchange.close()
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
@@ -573,7 +577,7 @@ def run_tp(args):
             e.update(tflops=round(tf, 1), frac_tensor=round(tf / pk["bf16_tflops_sustained"], 4))
         if d["bytes"]:
             gb = d["bytes"] / (d["ms"] * 1e-3) / 1e9
-            if name == "nccl_all_reduce":
+            if name in ("nccl_all_reduce", "ckv_reduce_add_rmsnorm"):
                 e.update(bus_gbs=round(gb, 1), frac_nvlink=round(gb / 770.0, 4),
                          bus_bytes_per_launch=round(d["bytes"] / d["launches"]))
             else:
@@ -596,6 +600,8 @@ def run_tp(args):
                    "cached_tokens": args.chunks * args.chunk_len, "chunks": f"{args.chunks}x{args.chunk_len}",
                    "max_abs_delta": max_delta, "query_tokens": args.query_len, "recompute_ratio": args.ratio,
                    "n_sink": args.n_sink, "parallelism": f"tp{world} (KV heads {loc.n_kv} per rank)",
+                   "tp_exchange": ("partial rows over NVLink peer memory (ckv_linear_push + "
+                                   "ckv_reduce_add_rmsnorm)" if args.tp_exchange == "peer" else "NCCL all-reduce"),
                    "l2": "inputs larger than L2 every step (weights and cached K/V pages)"},
         "ttft_ms_p50": round(statistics.median(step_ms), 3),
         "selected_tokens": int(len(res.selected)), "recomputed_cached_tokens": res.stats["recomputed_cached_tokens"],

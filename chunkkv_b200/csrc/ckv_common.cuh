@@ -138,6 +138,31 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// ------------------------------------------------ device: cross-GPU counters
+// Counters that other GPUs add to over NVLink: release on the adding side, acquire on
+// the polling side, both at system scope.
+__device__ __forceinline__ void red_release_sys_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Waits (bounded by kWaitLimitNs) until *p has reached `target` (wrap-around safe).
+// Gives up at once when `err_word` already records a wait that ran out, so one lost
+// signal costs one timeout, not one per waiting CTA.
+__device__ __forceinline__ bool wait_counter(const unsigned* p, unsigned target,
+                                             const volatile unsigned* err_word) {
+  if (int(ld_acquire_sys(p) - target) >= 0) return true;
+  const uint64_t t0 = global_ns();
+  while (int(ld_acquire_sys(p) - target) < 0) {
+    if (*err_word & CKV_DEV_ERR_WAIT_TIMEOUT) return false;
+    if (global_ns() - t0 > kWaitLimitNs) return false;
+  }
+  return true;
+}
+
 // ---------------------------------------------------------------- device: TMA
 // 2-D tiled bulk tensor load into this CTA's shared memory (no multicast).
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y,

@@ -146,7 +146,7 @@ class TorchEngine:
             t = t.to(device=self.device, dtype=torch.bfloat16).contiguous()
         return t
 
-    def _block_tail(self, li: int, attn, h, x, act, part, M: int) -> bool:
+    def _block_tail(self, li: int, attn, h, x, act, part, M: int, exch=None, pair: int = 0) -> bool:
         """o_proj + residual, post-attention RMSNorm, SwiGLU MLP + residual of layer `li`
         (torch_engine.py:68-76) over rows [0, M).  Tensor parallel: o_proj and down_proj
         are row-parallel, so their partial rows are summed over the ranks and the
@@ -159,13 +159,24 @@ class TorchEngine:
             ops.linear_swiglu(x, lw.w_gu, act, m=M)
             ops.linear_residual(act, lw.w_down, h, m=M)
             return False
+        nxt = self.w.layers[li + 1].ln1 if li + 1 < s.n_layers else self.w.norm
+        if exch is not None:
+            # partial rows pushed over NVLink to the owning ranks, reduced there with the
+            # residual add and RMSNorm, and gathered back into every rank's h and x
+            for xin, wmat, norm in ((attn, lw.w_o, lw.ln2), (act, lw.w_down, nxt)):
+                buf = exch.recv_toggle
+                exch.recv_toggle ^= 1
+                ops.linear_push(xin[:M], wmat, exch, buf)
+                ops.reduce_add_rmsnorm(exch, buf, pair, M, norm, s.rms_eps)
+                if wmat is lw.w_o:
+                    ops.linear_swiglu(x, lw.w_gu, act, m=M)
+            return True
         ops.linear(attn[:M], lw.w_o, out=part[:M])
         tp.all_reduce_(part[:M])
         ops.add_rmsnorm(h[:M], part[:M], lw.ln2, s.rms_eps, out=x[:M])
         ops.linear_swiglu(x, lw.w_gu, act, m=M)
         ops.linear(act[:M], lw.w_down, out=part[:M])
         tp.all_reduce_(part[:M])
-        nxt = self.w.layers[li + 1].ln1 if li + 1 < s.n_layers else self.w.norm
         ops.add_rmsnorm(h[:M], part[:M], nxt, s.rms_eps, out=x[:M])
         return True
 
@@ -251,13 +262,18 @@ class TorchEngine:
             ops.blend_gather_dense(d["kptr"], d["vptr"], d["dense_meta"], self.inv_freq, K_all, V_all, 0, L,
                                    nbytes=gather_bytes * len(dense_meta) / len(placements))
 
-        h = torch.empty((max(M0, 1), hid), **bf)
-        x = torch.empty_like(h)
+        tp = self.tp
+        exch = tp.exchange(max(M0, 1), hid, dev) if (tp and tp.fused) else None
+        pair = 0  # h / x pair of the exchange in use (the selection moves to the other)
+        if exch is not None:
+            h, x = exch.h[0][:max(M0, 1)], exch.x[0][:max(M0, 1)]
+        else:
+            h = torch.empty((max(M0, 1), hid), **bf)
+            x = torch.empty_like(h)
         q = torch.empty((max(M0, 1), Hq * D), **bf)
         attn = torch.empty_like(q)
         act = torch.empty((max(M0, 1), s.inter), **bf)
-        tp = self.tp
-        part = torch.empty_like(h) if tp else None  # this rank's partial o_proj / down_proj rows
+        part = torch.empty_like(h) if (tp and exch is None) else None  # partial rows for NCCL
         x_ready = False  # x already holds RMSNorm(h) for this layer (fused into the last add)
         if M0:
             ops.embed(self.w.embed, d["tokens"], d["active0"], h[:M0])
@@ -291,7 +307,11 @@ class TorchEngine:
                 else:
                     ops.deviation_select(kc, vc, K_all[1], V_all[1], active, d["pos_flags"], d["sel_meta"],
                                          config.escalate_threshold, ws)
-                h2, x2 = torch.empty_like(h), torch.empty_like(x)
+                if exch is not None:
+                    h2, x2 = exch.h[1 - pair][:h.shape[0]], exch.x[1 - pair][:x.shape[0]]
+                    pair = 1 - pair
+                else:
+                    h2, x2 = torch.empty_like(h), torch.empty_like(x)
                 ops.apply_selection(ws, M, h, h2, x, x2, kc, vc, K_all[1], V_all[1])
                 # the one host sync: selection size, chunk deviations, kept positions
                 n_ch = len(placements)
@@ -327,7 +347,7 @@ class TorchEngine:
                 break
             ops.attention(q, K_all[li], V_all[li], active, attn, m=M, flops=attn_flops,
                           workspace=self._attn_workspace(M, N))
-            x_ready = self._block_tail(li, attn, h, x, act, part, M)
+            x_ready = self._block_tail(li, attn, h, x, act, part, M, exch, pair)
 
         r0 = int(np.searchsorted(active_host, logits_from, side="left"))
         n_log = M - r0
@@ -372,12 +392,16 @@ class TorchEngine:
         out: list[int] = []
         nxt = int(result.logits[-1].float().argmax().item())
         bf = dict(dtype=torch.bfloat16, device=dev)
-        h = torch.empty((1, hid), **bf)
-        x = torch.empty_like(h)
+        exch = self.tp.exchange(1, hid, dev) if (self.tp and self.tp.fused) else None
+        if exch is not None:
+            h, x = exch.h[0][:1], exch.x[0][:1]
+        else:
+            h = torch.empty((1, hid), **bf)
+            x = torch.empty_like(h)
         q = torch.empty((1, Hq * D), **bf)
         attn = torch.empty_like(q)
         act = torch.empty((1, s.inter), **bf)
-        part = torch.empty_like(h) if self.tp else None
+        part = torch.empty_like(h) if (self.tp and exch is None) else None
         tok = torch.empty(1, dtype=torch.int32, device=dev)
         posd = torch.empty(1, dtype=torch.int32, device=dev)
         rope_tab = self.rope_table(cap)
@@ -397,7 +421,7 @@ class TorchEngine:
                 ops.qkv_rope(x, lw.w_qkv, lw.b_qkv, 1, 0, qkv_cols, Hq, H, D, posd, rope_tab, q_out=q,
                              k_cache=K[li], v_cache=V[li])
                 ops.attention(q, K[li], V[li], posd, attn, m=1, workspace=self._attn_workspace(1, cap))
-                x_ready = self._block_tail(li, attn, h, x, act, part, 1)
+                x_ready = self._block_tail(li, attn, h, x, act, part, 1, exch, 0)
             del Kc, Vc
             xf = x if x_ready else ops.rmsnorm(h, self.w.norm, s.rms_eps)
             nxt = int(ops.gemv(xf, self.w.lm_head).float().argmax().item())

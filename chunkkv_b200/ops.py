@@ -258,6 +258,31 @@ def add_rmsnorm(h: torch.Tensor, delta: torch.Tensor, w: torch.Tensor, eps: floa
     return out
 
 
+def linear_push(x: torch.Tensor, w: torch.Tensor, exch, buf: int) -> None:
+    """Row-parallel GEMM whose partial rows go to the owning ranks' receive buffer `buf`."""
+    _cuda(x, w)
+    _bf16(x, w)
+    _contig(x, w)
+    m, k = x.shape
+    n = w.shape[0]
+    tp = exch.tp
+    _run("ckv_linear_push", _ptr(x), _ptr(w), m, n, k, _ptr(exch.recv_tab[buf]), exch.slot,
+         _ptr(exch.flag_tab), _ptr(exch.push_ticket), tp.rank, tp.size, _stream(), flops=2.0 * m * n * k)
+
+
+def reduce_add_rmsnorm(exch, buf: int, pair: int, m: int, w: torch.Tensor, eps: float) -> None:
+    """Sum of the ranks' partial rows in receive buffer `buf` added to h[pair], RMSNorm into
+    x[pair], both gathered to every rank (one exchange: epoch + 1)."""
+    _cuda(w)
+    exch.epoch += 1
+    tp = exch.tp
+    _run("ckv_reduce_add_rmsnorm", _ptr(exch.recv[buf]), exch.slot, tp.rank, tp.size, m, exch.hidden,
+         _ptr(exch.h[pair]), _ptr(exch.x[pair]), _ptr(w), float(eps), _ptr(exch.h_tab[pair]),
+         _ptr(exch.x_tab[pair]), _ptr(exch.recv_cnt), _ptr(exch.gather_cnt), _ptr(exch.gather_tab),
+         _ptr(exch.reduce_ticket), exch.epoch & 0xFFFFFFFF, _stream(),
+         nbytes=2.0 * (tp.size - 1) / tp.size * m * exch.hidden * 2 * 2)
+
+
 def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
            out: torch.Tensor | None = None) -> torch.Tensor:
     _cuda(x, w, bias)

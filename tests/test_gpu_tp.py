@@ -1,5 +1,6 @@
-"""Tensor-parallel blend prefill on 2 GPUs (NCCL), against the reference fixtures and
-against the same engine on one GPU.
+"""Tensor-parallel blend prefill on 2 GPUs, against the reference fixtures and against the
+same engine on one GPU, with both exchanges: partial rows pushed over NVLink peer memory
+(`ckv_linear_push` + `ckv_reduce_add_rmsnorm`, the default) and the NCCL all-reduce.
 
 Each rank holds one of the two KV heads of the `tiny` shape with its query heads
 and half of the MLP.  Checked per scenario, on every rank:
@@ -56,51 +57,54 @@ def _worker(rank, world, port, q):
         from helpers import kl, run_blend, scenario
         from oracle.blend_oracle import select
 
-        tp = TensorParallel()
         out = {}
-        for name in TINY:
-            s = scenario(name)
-            eng = TorchEngine.from_packed(pack(s.shape, s.sd, device=dev, tp_rank=rank, tp_size=world), tp=tp)
-            _, _, pl, res = run_blend(eng, s)
-            torch.cuda.synchronize()
-            N = len(s.tokens)
-            cached = torch.zeros(N, dtype=torch.bool)
-            sink = torch.zeros(N, dtype=torch.bool)
-            for p in pl:
-                cached[p.start:p.start + p.chunk.length] = True
-                if not p.exact:
-                    sink[p.start:min(p.start + p.chunk.length, p.start + s.config.n_sink)] = True
-            ws = eng._ws
-            sel = res.selected.cpu().numpy()
-            ref_sel = select(ws.diff[:N].cpu(), ws.norm[:N].cpu(), cached, sink, pl, s.config)["keep_abs"].numpy()
-            single = TorchEngine.from_packed(pack(s.shape, s.sd, device=dev))
-            _, _, _, res1 = run_blend(single, s)
-            K1, V1 = res1.cache
-            K2, V2 = res.cache
-            hs = slice(rank * K2.shape[1], (rank + 1) * K2.shape[1])
+        for fused in (True, False):
+            tp = TensorParallel(fused=fused)
+            for name in TINY:
+                s = scenario(name)
+                eng = TorchEngine.from_packed(pack(s.shape, s.sd, device=dev, tp_rank=rank, tp_size=world), tp=tp)
+                _, _, pl, res = run_blend(eng, s)
+                torch.cuda.synchronize()
+                N = len(s.tokens)
+                cached = torch.zeros(N, dtype=torch.bool)
+                sink = torch.zeros(N, dtype=torch.bool)
+                for p in pl:
+                    cached[p.start:p.start + p.chunk.length] = True
+                    if not p.exact:
+                        sink[p.start:min(p.start + p.chunk.length, p.start + s.config.n_sink)] = True
+                ws = eng._ws
+                sel = res.selected.cpu().numpy()
+                ref_sel = select(ws.diff[:N].cpu(), ws.norm[:N].cpu(), cached, sink, pl, s.config)["keep_abs"].numpy()
+                single = TorchEngine.from_packed(pack(s.shape, s.sd, device=dev))
+                _, _, _, res1 = run_blend(single, s)
+                K1, V1 = res1.cache
+                K2, V2 = res.cache
+                hs = slice(rank * K2.shape[1], (rank + 1) * K2.shape[1])
 
-            def rel(a, b):
-                a, b = a.float(), b.float()
-                return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+                def rel(a, b):
+                    a, b = a.float(), b.float()
+                    return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
 
-            # positions both runs recomputed or both moved (near-tied selections may differ)
-            same = np.ones(N, bool)
-            diff_sel = np.setxor1d(sel, res1.selected.cpu().numpy())
-            same[diff_sel] = False
-            same_t = torch.from_numpy(same).to(dev)
-            out[name] = {
-                "stats": {k: res.stats[k] for k in ("tokens", "cached_tokens", "recomputed_cached_tokens",
-                                                    "prefill_token_equiv")},
-                "escalated": [c["escalated"] for c in res.stats["chunks"]],
-                "kl_ref": kl(s.arrays["logits"][-1].astype(np.float32), res.logits[-1].float().cpu().numpy()),
-                "kl_single": kl(res1.logits[-1].float().cpu().numpy(), res.logits[-1].float().cpu().numpy()),
-                "sel_exact": bool(np.array_equal(ref_sel, sel)),
-                "selected": sel.tolist(),
-                "logits": res.logits[-1].float().cpu().numpy(),
-                "kv_rel": max(rel(K2[:, :, same_t], K1[:, hs][:, :, same_t]),
-                              rel(V2[:, :, same_t], V1[:, hs][:, :, same_t])),
-            }
-            del eng, single
+                # positions both runs recomputed or both moved (near-tied selections may differ)
+                same = np.ones(N, bool)
+                diff_sel = np.setxor1d(sel, res1.selected.cpu().numpy())
+                same[diff_sel] = False
+                same_t = torch.from_numpy(same).to(dev)
+                out[(name, fused)] = {
+                    "stats": {k: res.stats[k] for k in ("tokens", "cached_tokens", "recomputed_cached_tokens",
+                                                        "prefill_token_equiv")},
+                    "escalated": [c["escalated"] for c in res.stats["chunks"]],
+                    "kl_ref": kl(s.arrays["logits"][-1].astype(np.float32), res.logits[-1].float().cpu().numpy()),
+                    "kl_single": kl(res1.logits[-1].float().cpu().numpy(), res.logits[-1].float().cpu().numpy()),
+                    "sel_exact": bool(np.array_equal(ref_sel, sel)),
+                    "selected": sel.tolist(),
+                    "logits": res.logits[-1].float().cpu().numpy(),
+                    "kv_rel": max(rel(K2[:, :, same_t], K1[:, hs][:, :, same_t]),
+                                  rel(V2[:, :, same_t], V1[:, hs][:, :, same_t])),
+                }
+                del eng, single
+            if tp._exchange is not None:
+                tp._exchange.close()
         _lib.check_device()
         q.put((rank, out))
     except Exception as e:  # noqa: BLE001
@@ -129,15 +133,15 @@ def test_tensor_parallel_2gpu_matches_reference_and_single_gpu(golden):
             p.kill()
     for r in (0, 1):
         assert isinstance(res[r], dict), res[r]
-    for name in TINY:
+    for name, fused in [(n, f) for n in TINY for f in (True, False)]:
         meta, _ = golden(name)
         for r in (0, 1):
-            o = res[r][name]
+            o = res[r][(name, fused)]
             for k, v in o["stats"].items():
                 assert v == meta["stats"][k], (name, r, k)
             assert o["escalated"] == [c["escalated"] for c in meta["stats"]["chunks"]], (name, r)
             assert o["kl_ref"] <= 1e-3 and o["kl_single"] <= 1e-3, (name, r, o["kl_ref"], o["kl_single"])
             assert o["sel_exact"], (name, r)
             assert o["kv_rel"] <= 1e-2, (name, r, o["kv_rel"])
-        assert res[0][name]["selected"] == res[1][name]["selected"], name
-        assert np.array_equal(res[0][name]["logits"], res[1][name]["logits"]), name
+        assert res[0][(name, fused)]["selected"] == res[1][(name, fused)]["selected"], name
+        assert np.array_equal(res[0][(name, fused)]["logits"], res[1][(name, fused)]["logits"]), name
