@@ -577,7 +577,7 @@ def run_tp(args):
             e.update(tflops=round(tf, 1), frac_tensor=round(tf / pk["bf16_tflops_sustained"], 4))
         if d["bytes"]:
             gb = d["bytes"] / (d["ms"] * 1e-3) / 1e9
-            if name in ("nccl_all_reduce", "ckv_reduce_add_rmsnorm"):
+            if name in ("nccl_all_reduce", "ckv_reduce_add_gather"):
                 e.update(bus_gbs=round(gb, 1), frac_nvlink=round(gb / 770.0, 4),
                          bus_bytes_per_launch=round(d["bytes"] / d["launches"]))
             else:
@@ -601,7 +601,7 @@ def run_tp(args):
                    "max_abs_delta": max_delta, "query_tokens": args.query_len, "recompute_ratio": args.ratio,
                    "n_sink": args.n_sink, "parallelism": f"tp{world} (KV heads {loc.n_kv} per rank)",
                    "tp_exchange": ("partial rows over NVLink peer memory (ckv_linear_push + "
-                                   "ckv_reduce_add_rmsnorm)" if args.tp_exchange == "peer" else "NCCL all-reduce"),
+                                   "ckv_reduce_add_gather)" if args.tp_exchange == "peer" else "NCCL all-reduce"),
                    "l2": "inputs larger than L2 every step (weights and cached K/V pages)"},
         "ttft_ms_p50": round(statistics.median(step_ms), 3),
         "selected_tokens": int(len(res.selected)), "recomputed_cached_tokens": res.stats["recomputed_cached_tokens"],

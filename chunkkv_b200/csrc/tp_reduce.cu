@@ -2,10 +2,11 @@
 // the row-parallel GEMM (ckv_linear_push) stores each partial tile straight into the
 // receive buffer of the rank that owns its 128-row block; this kernel, on the owning
 // rank, sums the ranks' partial rows in a fixed rank order, adds them to the residual
-// stream, applies the next RMSNorm, and writes the finished h and x rows to every rank
-// (an all-gather by NVLink stores).  Together they replace the NCCL all-reduce after
-// o_proj and down_proj (torch_engine.py:70-76 residual adds), with the same result on
-// every rank.
+// stream, and writes the finished h rows to every rank (an all-gather by NVLink
+// stores).  Together they replace the NCCL all-reduce after o_proj and down_proj
+// (torch_engine.py:70-76 residual adds), with the same h on every rank; the next
+// RMSNorm then runs locally on every rank (ckv_rmsnorm), which costs less than sending
+// the normed rows too.
 //
 // Ordering: the GEMM's last CTA adds 1 to each rank's receive counter for its own rank
 // (release, system scope) after every CTA has fenced its stores; this kernel's CTAs wait
@@ -24,8 +25,6 @@ CKV_DEFINE_ERR_WORD(tp_reduce)
 namespace ckv {
 namespace {
 
-constexpr int kThreadsRow = 128;
-constexpr int kVec = 5;  // 16-byte vectors per thread: hidden <= 128 * 8 * 5 = 5120
 constexpr int kRowBlock = 128;
 
 struct ReduceArgs {
@@ -33,12 +32,8 @@ struct ReduceArgs {
   int64_t slot;           // elements per source slot
   int rank, ranks;
   int M, hidden;
-  uint16_t* h;            // this rank's residual stream [M][hidden] (updated in place)
-  uint16_t* x;            // this rank's normed rows [M][hidden]
-  const uint16_t* w;      // RMSNorm weight
-  float eps;
-  const uint64_t* h_peer; // [ranks] h of each rank
-  const uint64_t* x_peer; // [ranks] x of each rank
+  const uint16_t* h;      // this rank's residual stream [M][hidden]
+  const uint64_t* h_peer; // [ranks] h of each rank (this rank's own at index rank)
   const unsigned* recv_cnt;    // this rank's receive counters [ranks]
   unsigned* gather_cnt;        // this rank's gather counters [ranks]
   const uint64_t* gather_peer; // [ranks] address of each rank's gather counters
@@ -46,18 +41,11 @@ struct ReduceArgs {
   unsigned epoch;              // counters' value once this exchange is complete
 };
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-
-// One CTA per owned row.  Owned row i: block rank + (i / 128) * ranks, row i % 128 in it.
-__global__ void __launch_bounds__(kThreadsRow) reduce_rmsnorm_kernel(ReduceArgs a) {
-  __shared__ float s_red[kThreadsRow / 32];
+// One warp per owned row, persistent CTAs of kWarps warps.  Owned row i: block
+// rank + (i / 128) * ranks, row i % 128 in it.
+constexpr int kWarps = 8;
+__global__ void __launch_bounds__(kWarps * 32) reduce_gather_kernel(ReduceArgs a, int n_owned) {
   __shared__ int s_ok;
-  const int i = blockIdx.x;
-  const int row = (a.rank + (i / kRowBlock) * a.ranks) * kRowBlock + (i % kRowBlock);
   if (threadIdx.x == 0) {
     bool ok = true;
     for (int q = 0; q < a.ranks && ok; ++q) ok = wait_counter(a.recv_cnt + q, a.epoch, &g_err_word);
@@ -65,84 +53,40 @@ __global__ void __launch_bounds__(kThreadsRow) reduce_rmsnorm_kernel(ReduceArgs 
     s_ok = ok;
   }
   __syncthreads();
-  const int vecs = a.hidden / 8;
-  if (s_ok && row < a.M) {
-    // fixed rank order, fp32: the same bits on every rank
-    float acc[kVec][8];
+  const int lane = threadIdx.x & 31;
+  const int vecs = a.hidden / 8;  // 16-byte vectors per row
+  if (s_ok) {
+    for (int i = blockIdx.x * kWarps + (threadIdx.x >> 5); i < n_owned; i += gridDim.x * kWarps) {
+      const int row = (a.rank + (i / kRowBlock) * a.ranks) * kRowBlock + (i % kRowBlock);
+      if (row >= a.M) continue;
+      // fixed rank order, fp32: the same bits on every rank; then h = bf16(h + bf16(sum))
+      // into every rank's copy of the row, this rank's included
+      const int64_t rbase = int64_t(row) * a.hidden;
+#pragma unroll 4
+      for (int c = lane; c < vecs; c += 32) {
+        float acc[8];
 #pragma unroll
-    for (int v = 0; v < kVec; ++v)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[v][e] = 0.f;
-    for (int q = 0; q < a.ranks; ++q) {
-      const uint4* src = reinterpret_cast<const uint4*>(a.recv + q * a.slot + int64_t(row) * a.hidden);
-#pragma unroll
-      for (int v = 0; v < kVec; ++v) {
-        const int c = threadIdx.x + kThreadsRow * v;
-        if (c < vecs) {
-          const uint4 d = __ldcg(src + c);  // written by other GPUs: not from L1
+        for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+        for (int q = 0; q < a.ranks; ++q) {
+          const uint4 d = __ldcg(reinterpret_cast<const uint4*>(a.recv + q * a.slot + rbase) + c);
           const uint32_t* pw = reinterpret_cast<const uint32_t*>(&d);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            acc[v][2 * e] = __fadd_rn(acc[v][2 * e], lo_bf(pw[e]));
-            acc[v][2 * e + 1] = __fadd_rn(acc[v][2 * e + 1], hi_bf(pw[e]));
+            acc[2 * e] = __fadd_rn(acc[2 * e], lo_bf(pw[e]));
+            acc[2 * e + 1] = __fadd_rn(acc[2 * e + 1], hi_bf(pw[e]));
           }
         }
-      }
-    }
-    // h = bf16(h + bf16(sum)), then y = w * bf16(h * rsqrt(mean(h^2) + eps))
-    uint4* hr = reinterpret_cast<uint4*>(a.h + int64_t(row) * a.hidden);
-    uint4 hv[kVec];
-    float ss = 0.f;
-#pragma unroll
-    for (int v = 0; v < kVec; ++v) {
-      const int c = threadIdx.x + kThreadsRow * v;
-      hv[v] = make_uint4(0u, 0u, 0u, 0u);
-      if (c < vecs) {
-        const uint4 old = hr[c];
+        const uint4 old = reinterpret_cast<const uint4*>(a.h + rbase)[c];
         const uint32_t* po = reinterpret_cast<const uint32_t*>(&old);
-        uint32_t* pn = reinterpret_cast<uint32_t*>(&hv[v]);
+        uint4 hv;
+        uint32_t* pn = reinterpret_cast<uint32_t*>(&hv);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float n0 = __fadd_rn(lo_bf(po[e]), bf16_round(acc[v][2 * e]));
-          const float n1 = __fadd_rn(hi_bf(po[e]), bf16_round(acc[v][2 * e + 1]));
-          pn[e] = pack_bf2(n0, n1);
-          const float f0 = lo_bf(pn[e]), f1 = hi_bf(pn[e]);
-          ss = __fadd_rn(ss, __fmul_rn(f0, f0));
-          ss = __fadd_rn(ss, __fmul_rn(f1, f1));
-        }
+        for (int e = 0; e < 4; ++e)
+          pn[e] = pack_bf2(__fadd_rn(lo_bf(po[e]), bf16_round(acc[2 * e])),
+                           __fadd_rn(hi_bf(po[e]), bf16_round(acc[2 * e + 1])));
+        for (int q = 0; q < a.ranks; ++q) reinterpret_cast<uint4*>(a.h_peer[q] + rbase * 2)[c] = hv;
       }
     }
-    ss = warp_sum(ss);
-    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    const float tot = (s_red[0] + s_red[1]) + (s_red[2] + s_red[3]);
-    const float r = rsqrtf(__fadd_rn(__fmul_rn(tot, 1.0f / float(a.hidden)), a.eps));
-    const uint4* wr = reinterpret_cast<const uint4*>(a.w);
-#pragma unroll
-    for (int v = 0; v < kVec; ++v) {
-      const int c = threadIdx.x + kThreadsRow * v;
-      if (c < vecs) {
-        const uint4 g = __ldg(wr + c);
-        const uint32_t* ph = reinterpret_cast<const uint32_t*>(&hv[v]);
-        const uint32_t* pg = reinterpret_cast<const uint32_t*>(&g);
-        uint4 xo;
-        uint32_t* px = reinterpret_cast<uint32_t*>(&xo);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float n0 = bf16_round(__fmul_rn(lo_bf(ph[e]), r));
-          const float n1 = bf16_round(__fmul_rn(hi_bf(ph[e]), r));
-          px[e] = pack_bf2(__fmul_rn(lo_bf(pg[e]), n0), __fmul_rn(hi_bf(pg[e]), n1));
-        }
-        // every rank's copy of the row, this rank's included
-        const int64_t off = int64_t(row) * a.hidden / 8 + c;
-        for (int q = 0; q < a.ranks; ++q) {
-          reinterpret_cast<uint4*>(a.h_peer[q])[off] = hv[v];
-          reinterpret_cast<uint4*>(a.x_peer[q])[off] = xo;
-        }
-      }
-    }
-  } else {
-    __syncthreads();  // matches the reduction barrier of the rows above
   }
   __threadfence_system();
   __syncthreads();
@@ -225,29 +169,27 @@ int ckv_ipc_free(void* ptr) {
   return CKV_OK;
 }
 
-int ckv_reduce_add_rmsnorm(const uint16_t* recv, int64_t slot_elems, int rank, int ranks, int m,
-                           int hidden, uint16_t* h, uint16_t* x, const uint16_t* w, float eps,
-                           const uint64_t* h_peer, const uint64_t* x_peer, const uint32_t* recv_cnt,
-                           uint32_t* gather_cnt, const uint64_t* gather_peer, uint32_t* ticket,
-                           uint32_t epoch, ckv_stream_t stream) {
-  CKV_REQUIRE(recv && h && x && w && h_peer && x_peer && recv_cnt && gather_cnt && gather_peer && ticket,
-              "ckv_reduce_add_rmsnorm: null pointer");
+int ckv_reduce_add_gather(const uint16_t* recv, int64_t slot_elems, int rank, int ranks, int m,
+                          int hidden, const uint16_t* h, const uint64_t* h_peer,
+                          const uint32_t* recv_cnt, uint32_t* gather_cnt, const uint64_t* gather_peer,
+                          uint32_t* ticket, uint32_t epoch, ckv_stream_t stream) {
+  CKV_REQUIRE(recv && h && h_peer && recv_cnt && gather_cnt && gather_peer && ticket,
+              "ckv_reduce_add_gather: null pointer");
   CKV_REQUIRE(ranks >= 1 && ranks <= CKV_MAX_RANKS && rank >= 0 && rank < ranks,
-              "ckv_reduce_add_rmsnorm: rank %d of %d", rank, ranks);
-  CKV_REQUIRE(hidden > 0 && hidden % 8 == 0 && hidden <= kThreadsRow * 8 * kVec,
-              "ckv_reduce_add_rmsnorm: hidden %d (multiple of 8, at most %d)", hidden,
-              kThreadsRow * 8 * kVec);
-  CKV_REQUIRE(aligned16(recv) && aligned16(h) && aligned16(x) && aligned16(w) && slot_elems % 8 == 0 &&
-                  slot_elems >= int64_t(m) * hidden,
-              "ckv_reduce_add_rmsnorm: alignment or slot size");
+              "ckv_reduce_add_gather: rank %d of %d", rank, ranks);
+  CKV_REQUIRE(hidden > 0 && hidden % 8 == 0, "ckv_reduce_add_gather: hidden %d not a multiple of 8",
+              hidden);
+  CKV_REQUIRE(aligned16(recv) && aligned16(h) && slot_elems % 8 == 0 && slot_elems >= int64_t(m) * hidden,
+              "ckv_reduce_add_gather: alignment or slot size");
   if (m <= 0) return CKV_OK;
-  ReduceArgs a{recv, slot_elems, rank, ranks, m, hidden, h, x, w, eps, h_peer, x_peer,
+  ReduceArgs a{recv, slot_elems, rank, ranks, m, hidden, h, h_peer,
                reinterpret_cast<const unsigned*>(recv_cnt), reinterpret_cast<unsigned*>(gather_cnt),
                gather_peer, reinterpret_cast<unsigned*>(ticket), epoch};
   // every rank launches at least one CTA, so every rank signals its gather counters
-  const int grid = std::max(1, owned_rows(m, rank, ranks));
-  reduce_rmsnorm_kernel<<<grid, kThreadsRow, 0, as_stream(stream)>>>(a);
-  CKV_LAUNCH_CHECK("ckv_reduce_add_rmsnorm");
+  const int n_owned = owned_rows(m, rank, ranks);
+  const int grid = std::max(1, std::min(ceil_div(n_owned, kWarps), 8 * num_sms()));
+  reduce_gather_kernel<<<grid, kWarps * 32, 0, as_stream(stream)>>>(a, n_owned);
+  CKV_LAUNCH_CHECK("ckv_reduce_add_gather");
   return CKV_OK;
 }
 

@@ -26,7 +26,7 @@ class TensorParallel:
 
     def __init__(self, group=None, fused: bool = True):
         """`fused`: o_proj / down_proj exchange their partial rows over NVLink peer memory
-        (`ckv_linear_push` + `ckv_reduce_add_rmsnorm`); False: NCCL all-reduce."""
+        (`ckv_linear_push` + `ckv_reduce_add_gather`); False: NCCL all-reduce."""
         if not (dist.is_available() and dist.is_initialized()):
             raise RuntimeError("TensorParallel needs an initialised torch.distributed process group")
         self.group = group
@@ -81,12 +81,13 @@ class _DeviceArray:
 
 
 class PeerExchange:
-    """Buffers of the NVLink exchange (`ckv_linear_push` + `ckv_reduce_add_rmsnorm`),
+    """Buffers of the NVLink exchange (`ckv_linear_push` + `ckv_reduce_add_gather`),
     allocated by every rank and mapped into every other rank with CUDA IPC:
 
       recv[2]  receive buffers, [ranks][rows][hidden] bf16, alternating between exchanges
-      h[2], x[2]  the residual stream and the normed rows, [rows][hidden] bf16; the pair in
-               use flips when the layer-1 selection shrinks the rows into the other pair
+      h[2], x[2]  the residual stream (gathered from the owning ranks) and the normed rows
+               (computed locally), [rows][hidden] bf16; the pair in use flips when the
+               layer-1 selection shrinks the rows into the other pair
       ctl      uint32 receive counters [ranks], gather counters [ranks], two CTA tickets
 
     Every rank must make the same exchanges in the same order (they do: each rank runs
@@ -138,7 +139,6 @@ class PeerExchange:
         self.flag_tab = table(base["ctl"])                        # receive counters at offset 0
         self.gather_tab = table([b + 4 * self.MAX_RANKS for b in base["ctl"]])
         self.h_tab = [table([b + k * row_bytes for b in base["hx"]]) for k in (0, 2)]
-        self.x_tab = [table([b + k * row_bytes for b in base["hx"]]) for k in (1, 3)]
         bf = torch.bfloat16
 
         def view(ptr, nbytes, shape, dtype):

@@ -270,17 +270,15 @@ def linear_push(x: torch.Tensor, w: torch.Tensor, exch, buf: int) -> None:
          _ptr(exch.flag_tab), _ptr(exch.push_ticket), tp.rank, tp.size, _stream(), flops=2.0 * m * n * k)
 
 
-def reduce_add_rmsnorm(exch, buf: int, pair: int, m: int, w: torch.Tensor, eps: float) -> None:
-    """Sum of the ranks' partial rows in receive buffer `buf` added to h[pair], RMSNorm into
-    x[pair], both gathered to every rank (one exchange: epoch + 1)."""
-    _cuda(w)
+def reduce_add_gather(exch, buf: int, pair: int, m: int) -> None:
+    """Sum of the ranks' partial rows in receive buffer `buf` added to h[pair] and gathered
+    into every rank's h[pair] (one exchange: epoch + 1)."""
     exch.epoch += 1
     tp = exch.tp
-    _run("ckv_reduce_add_rmsnorm", _ptr(exch.recv[buf]), exch.slot, tp.rank, tp.size, m, exch.hidden,
-         _ptr(exch.h[pair]), _ptr(exch.x[pair]), _ptr(w), float(eps), _ptr(exch.h_tab[pair]),
-         _ptr(exch.x_tab[pair]), _ptr(exch.recv_cnt), _ptr(exch.gather_cnt), _ptr(exch.gather_tab),
-         _ptr(exch.reduce_ticket), exch.epoch & 0xFFFFFFFF, _stream(),
-         nbytes=2.0 * (tp.size - 1) / tp.size * m * exch.hidden * 2 * 2)
+    _run("ckv_reduce_add_gather", _ptr(exch.recv[buf]), exch.slot, tp.rank, tp.size, m, exch.hidden,
+         _ptr(exch.h[pair]), _ptr(exch.h_tab[pair]), _ptr(exch.recv_cnt), _ptr(exch.gather_cnt),
+         _ptr(exch.gather_tab), _ptr(exch.reduce_ticket), exch.epoch & 0xFFFFFFFF, _stream(),
+         nbytes=2.0 * (tp.size - 1) / tp.size * m * exch.hidden * 2)
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
