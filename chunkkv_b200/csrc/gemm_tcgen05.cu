@@ -44,7 +44,7 @@ struct GCfg {
   static constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN);
 };
 
-enum Epi { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKV = 3, EPI_PUSH = 4 };
+enum Epi { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKV = 3, EPI_PARTIAL = 4 };
 
 struct EpiParams {
   const uint16_t* bias;  // by absolute column of the full weight (STORE optional, QKV)
@@ -61,11 +61,9 @@ struct EpiParams {
   int n_ctx;
   uint16_t* k_compact;
   uint16_t* v_compact;
-  // EPI_PUSH (tensor parallel): the tile goes to the receive buffer of the rank owning its
-  // 128-row block (block b -> rank b % ranks), in the slot of this rank; the last CTA to
-  // finish then adds 1 to every rank's counter for this rank.
-  const uint64_t* push_dst;   // [ranks] receive buffer of each rank (peer-mapped), bf16
-  int64_t push_slot;          // elements per source-rank slot
+  // EPI_PARTIAL (tensor parallel): the tile is stored like EPI_STORE (this rank's partial
+  // rows, read by the other ranks over NVLink); the last CTA to finish then adds 1 to
+  // every rank's counter for this rank.
   const uint64_t* push_flag;  // [ranks] address of each rank's uint32 counters [ranks]
   unsigned* push_ticket;      // this rank's CTA ticket (left at 0)
   int push_rank, push_ranks;
@@ -100,27 +98,6 @@ __device__ __forceinline__ void epi_store(uint32_t tacc, int row, int M, int n0,
         if (ep.bias) o[e] = __fadd_rn(o[e], bf2f(ep.bias[col + e]));
       }
       store8(ep.out + int64_t(row) * ep.ldo + col, o);
-    }
-  }
-}
-
-// Partial rows of a row-parallel projection, bf16, to the rank that owns the row block
-// (NVLink stores when that is another GPU).
-template <int BN>
-__device__ __forceinline__ void epi_push(uint32_t tacc, int row, int M, int n0, int N,
-                                         const EpiParams& ep) {
-  const int owner = (row / BM) % ep.push_ranks;
-  uint16_t* base = reinterpret_cast<uint16_t*>(ep.push_dst[owner]) + ep.push_rank * ep.push_slot;
-#pragma unroll 1
-  for (int c = 0; c < BN; c += 32) {
-    float v[32];
-    tmem_ld32(tacc + c, v);
-    if (row >= M) continue;
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      const int col = n0 + c + g * 8;
-      if (col >= N) continue;
-      store8(base + int64_t(row) * ep.ldo + col, v + g * 8);
     }
   }
 }
@@ -257,7 +234,7 @@ __device__ __forceinline__ void run_epilogue(uint32_t tacc, int row, int M, int 
   if constexpr (EPI == EPI_STORE) epi_store<BN>(tacc, row, M, n0, N, ep);
   else if constexpr (EPI == EPI_RESID) epi_resid<BN>(tacc, row, M, n0, N, ep);
   else if constexpr (EPI == EPI_SWIGLU) epi_swiglu<BN>(tacc, row, M, n0, N, ep);
-  else if constexpr (EPI == EPI_PUSH) epi_push<BN>(tacc, row, M, n0, N, ep);
+  else if constexpr (EPI == EPI_PARTIAL) epi_store<BN>(tacc, row, M, n0, N, ep);
   else epi_qkv<BN, HD>(tacc, row, M, n0, N, ep);
 }
 
@@ -393,15 +370,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  if constexpr (EPI == EPI_PUSH) __threadfence_system();  // this thread's pushed rows first
+  if constexpr (EPI == EPI_PARTIAL) __threadfence_system();  // this thread's rows first
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
   }
-  if constexpr (EPI == EPI_PUSH) {
-    // the last CTA tells every rank that this rank's partial rows have all landed
+  if constexpr (EPI == EPI_PARTIAL) {
+    // the last CTA tells every rank that this rank's partial rows are all written
     if (threadIdx.x == 0) {
       const unsigned t = atomicAdd(ep.push_ticket, 1u);
       if (t == gridDim.x - 1) {
@@ -490,7 +467,7 @@ int64_t makespan(int M, int N, int bn) {
 template <int EPI, int HD>
 int launch(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, int M, int N, int K,
            const EpiParams& ep, cudaStream_t stream, const char* name) {
-  if constexpr (EPI == EPI_STORE || EPI == EPI_RESID || EPI == EPI_PUSH) {
+  if constexpr (EPI == EPI_STORE || EPI == EPI_RESID || EPI == EPI_PARTIAL) {
     if (M > 0 && makespan(M, N, 224) < makespan(M, N, 256))
       return launch_bn<EPI, HD, 224>(a, lda, b, ldb, M, N, K, ep, stream, name);
   }
@@ -510,24 +487,21 @@ using namespace ckv;
 
 extern "C" {
 
-int ckv_linear_push(const uint16_t* x, const uint16_t* w, int m, int n, int k,
-                    const uint64_t* recv_bufs, int64_t slot_elems, const uint64_t* recv_flags,
-                    uint32_t* ticket, int rank, int ranks, ckv_stream_t stream) {
-  CKV_REQUIRE(recv_bufs && recv_flags && ticket, "ckv_linear_push: null pointer");
+int ckv_linear_partial(const uint16_t* x, const uint16_t* w, uint16_t* out, int m, int n, int k,
+                       const uint64_t* flags, uint32_t* ticket, int rank, int ranks,
+                       ckv_stream_t stream) {
+  CKV_REQUIRE(out && flags && ticket && aligned16(out), "ckv_linear_partial: null or unaligned pointer");
   CKV_REQUIRE(ranks >= 1 && ranks <= CKV_MAX_RANKS && rank >= 0 && rank < ranks,
-              "ckv_linear_push: rank %d of %d", rank, ranks);
-  CKV_REQUIRE(slot_elems >= int64_t(m) * n && slot_elems % 8 == 0,
-              "ckv_linear_push: slot of %lld elements below %d x %d", (long long)slot_elems, m, n);
+              "ckv_linear_partial: rank %d of %d", rank, ranks);
   if (m <= 0) return CKV_OK;
   EpiParams ep = zero_params();
+  ep.out = out;
   ep.ldo = n;
-  ep.push_dst = recv_bufs;
-  ep.push_slot = slot_elems;
-  ep.push_flag = recv_flags;
+  ep.push_flag = flags;
   ep.push_ticket = ticket;
   ep.push_rank = rank;
   ep.push_ranks = ranks;
-  return launch<EPI_PUSH, 128>(x, k, w, k, m, n, k, ep, as_stream(stream), "ckv_linear_push");
+  return launch<EPI_PARTIAL, 128>(x, k, w, k, m, n, k, ep, as_stream(stream), "ckv_linear_partial");
 }
 
 int ckv_linear(const uint16_t* x, const uint16_t* w, const uint16_t* bias, uint16_t* out, int m,

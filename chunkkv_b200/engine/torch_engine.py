@@ -161,12 +161,12 @@ class TorchEngine:
             return False
         nxt = self.w.layers[li + 1].ln1 if li + 1 < s.n_layers else self.w.norm
         if exch is not None:
-            # partial rows pushed over NVLink to the owning ranks, reduced there with the
+            # partial rows read over NVLink by the owning ranks, reduced there with the
             # residual add and gathered back into every rank's h; RMSNorm locally
             for xin, wmat, norm in ((attn, lw.w_o, lw.ln2), (act, lw.w_down, nxt)):
                 buf = exch.recv_toggle
                 exch.recv_toggle ^= 1
-                ops.linear_push(xin[:M], wmat, exch, buf)
+                ops.linear_partial(xin[:M], wmat, exch, buf)
                 ops.reduce_add_gather(exch, buf, pair, M)
                 ops.rmsnorm(h[:M], norm, s.rms_eps, out=x[:M])
                 if wmat is lw.w_o:

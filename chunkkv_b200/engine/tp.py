@@ -26,7 +26,7 @@ class TensorParallel:
 
     def __init__(self, group=None, fused: bool = True):
         """`fused`: o_proj / down_proj exchange their partial rows over NVLink peer memory
-        (`ckv_linear_push` + `ckv_reduce_add_gather`); False: NCCL all-reduce."""
+        (`ckv_linear_partial` + `ckv_reduce_add_gather`); False: NCCL all-reduce."""
         if not (dist.is_available() and dist.is_initialized()):
             raise RuntimeError("TensorParallel needs an initialised torch.distributed process group")
         self.group = group
@@ -81,14 +81,14 @@ class _DeviceArray:
 
 
 class PeerExchange:
-    """Buffers of the NVLink exchange (`ckv_linear_push` + `ckv_reduce_add_gather`),
+    """Buffers of the NVLink exchange (`ckv_linear_partial` + `ckv_reduce_add_gather`),
     allocated by every rank and mapped into every other rank with CUDA IPC:
 
-      recv[2]  receive buffers, [ranks][rows][hidden] bf16, alternating between exchanges
+      part[2]  this rank's partial rows, [rows][hidden] bf16, alternating between exchanges
       h[2], x[2]  the residual stream (gathered from the owning ranks) and the normed rows
                (computed locally), [rows][hidden] bf16; the pair in use flips when the
                layer-1 selection shrinks the rows into the other pair
-      ctl      uint32 receive counters [ranks], gather counters [ranks], two CTA tickets
+      ctl      uint32 partial counters [ranks], gather counters [ranks], two CTA tickets
 
     Every rank must make the same exchanges in the same order (they do: each rank runs
     the same prefill).  `epoch` counts the exchanges made so far."""
@@ -105,7 +105,7 @@ class PeerExchange:
         self.epoch = 0
         self.recv_toggle = 0
         T, row_bytes = tp.size, rows * hidden * 2
-        sizes = {"recv0": T * row_bytes, "recv1": T * row_bytes, "hx": 4 * row_bytes, "ctl": self.CTL_BYTES}
+        sizes = {"part0": row_bytes, "part1": row_bytes, "hx": 4 * row_bytes, "ctl": self.CTL_BYTES}
         self._local: dict[str, int] = {}
         handles: dict[str, bytes] = {}
         lib = _lib.load()
@@ -135,8 +135,8 @@ class PeerExchange:
         def table(vals):
             return torch.tensor(vals, dtype=torch.int64).view(torch.uint64).to(self.device)
 
-        self.recv_tab = [table(base["recv0"]), table(base["recv1"])]
-        self.flag_tab = table(base["ctl"])                        # receive counters at offset 0
+        self.part_tab = [table(base["part0"]), table(base["part1"])]
+        self.flag_tab = table(base["ctl"])                        # partial counters at offset 0
         self.gather_tab = table([b + 4 * self.MAX_RANKS for b in base["ctl"]])
         self.h_tab = [table([b + k * row_bytes for b in base["hx"]]) for k in (0, 2)]
         bf = torch.bfloat16
@@ -147,13 +147,12 @@ class PeerExchange:
         hx = self._local["hx"]
         self.h = [view(hx + k * row_bytes, row_bytes, (rows, hidden), bf) for k in (0, 2)]
         self.x = [view(hx + k * row_bytes, row_bytes, (rows, hidden), bf) for k in (1, 3)]
-        self.recv = [view(self._local[f"recv{i}"], T * row_bytes, (T * rows * hidden,), bf) for i in (0, 1)]
+        self.part = [view(self._local[f"part{i}"], row_bytes, (rows, hidden), bf) for i in (0, 1)]
         ctl = view(self._local["ctl"], self.CTL_BYTES, (self.CTL_BYTES // 4,), torch.int32)
         self.recv_cnt = ctl[:self.MAX_RANKS]
         self.gather_cnt = ctl[self.MAX_RANKS:2 * self.MAX_RANKS]
         self.push_ticket = ctl[2 * self.MAX_RANKS:2 * self.MAX_RANKS + 1]
         self.reduce_ticket = ctl[2 * self.MAX_RANKS + 1:2 * self.MAX_RANKS + 2]
-        self.slot = rows * hidden
         dist.barrier(group=tp.group)
 
     def close(self) -> None:

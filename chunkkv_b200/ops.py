@@ -258,24 +258,24 @@ def add_rmsnorm(h: torch.Tensor, delta: torch.Tensor, w: torch.Tensor, eps: floa
     return out
 
 
-def linear_push(x: torch.Tensor, w: torch.Tensor, exch, buf: int) -> None:
-    """Row-parallel GEMM whose partial rows go to the owning ranks' receive buffer `buf`."""
+def linear_partial(x: torch.Tensor, w: torch.Tensor, exch, buf: int) -> None:
+    """Row-parallel GEMM into this rank's partial buffer `buf`, then a signal to every rank."""
     _cuda(x, w)
     _bf16(x, w)
     _contig(x, w)
     m, k = x.shape
     n = w.shape[0]
     tp = exch.tp
-    _run("ckv_linear_push", _ptr(x), _ptr(w), m, n, k, _ptr(exch.recv_tab[buf]), exch.slot,
-         _ptr(exch.flag_tab), _ptr(exch.push_ticket), tp.rank, tp.size, _stream(), flops=2.0 * m * n * k)
+    _run("ckv_linear_partial", _ptr(x), _ptr(w), _ptr(exch.part[buf]), m, n, k, _ptr(exch.flag_tab),
+         _ptr(exch.push_ticket), tp.rank, tp.size, _stream(), flops=2.0 * m * n * k)
 
 
 def reduce_add_gather(exch, buf: int, pair: int, m: int) -> None:
-    """Sum of the ranks' partial rows in receive buffer `buf` added to h[pair] and gathered
-    into every rank's h[pair] (one exchange: epoch + 1)."""
+    """The ranks' partial rows in buffer `buf` (read over NVLink by the owning ranks) added to
+    h[pair] and gathered into every rank's h[pair] (one exchange: epoch + 1)."""
     exch.epoch += 1
     tp = exch.tp
-    _run("ckv_reduce_add_gather", _ptr(exch.recv[buf]), exch.slot, tp.rank, tp.size, m, exch.hidden,
+    _run("ckv_reduce_add_gather", _ptr(exch.part_tab[buf]), tp.rank, tp.size, m, exch.hidden,
          _ptr(exch.h[pair]), _ptr(exch.h_tab[pair]), _ptr(exch.recv_cnt), _ptr(exch.gather_cnt),
          _ptr(exch.gather_tab), _ptr(exch.reduce_ticket), exch.epoch & 0xFFFFFFFF, _stream(),
          nbytes=2.0 * (tp.size - 1) / tp.size * m * exch.hidden * 2)

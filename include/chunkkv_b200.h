@@ -219,31 +219,29 @@ CKV_API int ckv_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* y, int r
 /* ---- tensor parallel over NVLink peer memory (no collective library) ------------
  * The o_proj / down_proj row-parallel GEMM and the following all-reduce + residual add
  * (torch_engine.py:70-76), split over `ranks` GPUs (one process each):
- *   ckv_linear_push       out = x W^T as bf16 partial rows, each 128-row block stored into
- *                         the receive buffer of rank (block % ranks), slot `rank`
- *                         (recv_bufs[q] + rank * slot_elems + row * n + col); its last CTA
- *                         then adds 1 to recv_flags[q][rank] on every rank q.
- *   ckv_reduce_add_gather on each rank, for the rows it owns: waits until its receive
- *                         counters reach `epoch`, sums the ranks' slots in rank order in
- *                         fp32, h = bf16(h + bf16(sum)), and writes the row into every
- *                         rank's h (h_peer[q]); its last CTA adds 1 to gather_peer[q][rank]
- *                         on every rank and waits until its own gather counters reach
- *                         `epoch`.  The next RMSNorm then runs locally (ckv_rmsnorm).
- * recv_bufs / recv_flags / h_peer / gather_peer are device arrays of `ranks` device
- * addresses (this rank's own at index rank), mapped with ckv_ipc_open.  Counters start at
- * 0 and `epoch` counts the exchanges made so far, this one included.  Two receive buffers
- * must alternate between consecutive exchanges.  Waits are bounded (2 s,
+ *   ckv_linear_partial    out = x W^T, this rank's bf16 partial rows [m][n] in its own
+ *                         buffer; its last CTA then adds 1 to flags[q][rank] on every
+ *                         rank q.
+ *   ckv_reduce_add_gather on each rank, for the 128-row blocks it owns (block b -> rank
+ *                         b % ranks): waits until its partial counters reach `epoch`, reads
+ *                         every rank's partial rows (part_peer[q]) over NVLink, sums them in
+ *                         rank order in fp32, h = bf16(h + bf16(sum)), and writes the row
+ *                         into every rank's h (h_peer[q]); its last CTA adds 1 to
+ *                         gather_peer[q][rank] on every rank and waits until its own gather
+ *                         counters reach `epoch`.  The next RMSNorm then runs locally.
+ * part_peer / flags / h_peer / gather_peer are device arrays of `ranks` device addresses
+ * (this rank's own at index rank), mapped with ckv_ipc_open.  Counters start at 0 and
+ * `epoch` counts the exchanges made so far, this one included.  Two partial buffers must
+ * alternate between consecutive exchanges.  Waits are bounded (2 s,
  * CKV_DEV_ERR_WAIT_TIMEOUT).  No multicast objects are used. */
 #define CKV_MAX_RANKS 8
-CKV_API int ckv_linear_push(const uint16_t* x, const uint16_t* w, int m, int n, int k,
-                            const uint64_t* recv_bufs, int64_t slot_elems,
-                            const uint64_t* recv_flags, uint32_t* ticket, int rank, int ranks,
-                            ckv_stream_t stream);
-CKV_API int ckv_reduce_add_gather(const uint16_t* recv, int64_t slot_elems, int rank, int ranks,
-                                  int m, int hidden, const uint16_t* h, const uint64_t* h_peer,
-                                  const uint32_t* recv_cnt, uint32_t* gather_cnt,
-                                  const uint64_t* gather_peer, uint32_t* ticket, uint32_t epoch,
-                                  ckv_stream_t stream);
+CKV_API int ckv_linear_partial(const uint16_t* x, const uint16_t* w, uint16_t* out, int m, int n,
+                               int k, const uint64_t* flags, uint32_t* ticket, int rank, int ranks,
+                               ckv_stream_t stream);
+CKV_API int ckv_reduce_add_gather(const uint64_t* part_peer, int rank, int ranks, int m, int hidden,
+                                  const uint16_t* h, const uint64_t* h_peer, const uint32_t* part_cnt,
+                                  uint32_t* gather_cnt, const uint64_t* gather_peer, uint32_t* ticket,
+                                  uint32_t epoch, ckv_stream_t stream);
 /* Device memory that other processes can map (CUDA IPC, plain peer mappings): allocate
  * (zeroed) and get its 64-byte handle; open a peer's handle; close / free. */
 CKV_API int ckv_ipc_alloc(int64_t bytes, void** ptr, void* handle64);
