@@ -57,7 +57,7 @@ def parse():
     ap.add_argument("--cpu-layers", type=int, default=3, help="layers the CPU sample executes")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--extra-ratios", default="0.30,0.50", help="also time these ratios (TTFT only)")
-    ap.add_argument("--kernel-case", choices=["swiglu", "oproj", "qkv", "attention", "gather", "deviation"],
+    ap.add_argument("--kernel-case", choices=["swiglu", "oproj", "down", "qkv", "attention", "gather", "deviation"],
                     help="time one kernel at its 7B-bench shape (for ncu captures) instead of the prefill")
     args = ap.parse_args()
     tp = args.workload == "tp"
@@ -600,7 +600,7 @@ def run_tp(args):
                    "cached_tokens": args.chunks * args.chunk_len, "chunks": f"{args.chunks}x{args.chunk_len}",
                    "max_abs_delta": max_delta, "query_tokens": args.query_len, "recompute_ratio": args.ratio,
                    "n_sink": args.n_sink, "parallelism": f"tp{world} (KV heads {loc.n_kv} per rank)",
-                   "tp_exchange": ("partial rows over NVLink peer memory (ckv_linear_push + "
+                   "tp_exchange": ("partial rows over NVLink peer memory (ckv_linear_partial + "
                                    "ckv_reduce_add_gather)" if args.tp_exchange == "peer" else "NCCL all-reduce"),
                    "l2": "inputs larger than L2 every step (weights and cached K/V pages)"},
         "ttft_ms_p50": round(statistics.median(step_ms), 3),
@@ -818,6 +818,9 @@ def run_kernel_case(args):
         fn = lambda: ops.linear_swiglu(x, w, out)  # noqa: E731
     elif args.kernel_case == "oproj":
         a, w, h = rnd(M, Hq * D, scale=1.0), rnd(hid, Hq * D), rnd(M, hid, scale=1.0)
+        fn = lambda: ops.linear_residual(a, w, h)  # noqa: E731
+    elif args.kernel_case == "down":
+        a, w, h = rnd(M, shape.inter, scale=1.0), rnd(hid, shape.inter), rnd(M, hid, scale=1.0)
         fn = lambda: ops.linear_residual(a, w, h)  # noqa: E731
     elif args.kernel_case == "qkv":
         cols = (Hq + 2 * H) * D

@@ -33,11 +33,11 @@ constexpr int kThreads = 192;
 constexpr uint32_t A_BYTES = BM * BK * 2;  // 16 KiB
 constexpr uint32_t TMEM_COLS = 512;        // two accumulators of up to 256 columns
 
-// N-tile width: 256, or 224 when that fills the SMs better (e.g. 3584 columns at
-// M = 938: 128 tiles of 224 instead of 112 of 256 on 148 SMs).
+// N-tile width: 256, or 224 / 208 when that fills the SMs better (e.g. 3584 columns at
+// M = 938: 144 tiles of 208 in one wave instead of 112 of 256 on 148 SMs).
 template <int BN>
 struct GCfg {
-  static_assert(BN % 32 == 0 && BN <= 256, "BN");
+  static_assert(BN % 16 == 0 && BN <= 256, "BN");
   static constexpr uint32_t B_BYTES = BN * BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
@@ -90,7 +90,7 @@ __device__ __forceinline__ void epi_store(uint32_t tacc, int row, int M, int n0,
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       const int col = n0 + c + g * 8;
-      if (col >= N) continue;
+      if (c + g * 8 >= BN || col >= N) continue;  // BN may end mid-chunk (208 = 6.5 x 32)
       float o[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
@@ -113,7 +113,7 @@ __device__ __forceinline__ void epi_resid(uint32_t tacc, int row, int M, int n0,
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       const int col = n0 + c + g * 8;
-      if (col >= N) continue;
+      if (c + g * 8 >= BN || col >= N) continue;
       uint16_t* hp = ep.out + int64_t(row) * ep.ldo + col;
       const uint4 hv = *reinterpret_cast<const uint4*>(hp);
       const uint32_t* hw = reinterpret_cast<const uint32_t*>(&hv);
@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t d_tmem = tmem_base + acc * 256;  // accumulators at columns 0 and 256
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -362,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int mt = tile % m_tiles, nt = tile / m_tiles;
       const int row = mt * BM + sub * 32 + lane;
-      const uint32_t tacc = tmem_base + (uint32_t(sub * 32) << 16) + acc * BN;
+      const uint32_t tacc = tmem_base + (uint32_t(sub * 32) << 16) + acc * 256;
       run_epilogue<EPI, HD, BN>(tacc, row, M, nt * BN, N, ep);
       tc_fence_before();
       __syncwarp();
@@ -468,8 +468,11 @@ template <int EPI, int HD>
 int launch(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, int M, int N, int K,
            const EpiParams& ep, cudaStream_t stream, const char* name) {
   if constexpr (EPI == EPI_STORE || EPI == EPI_RESID || EPI == EPI_PARTIAL) {
-    if (M > 0 && makespan(M, N, 224) < makespan(M, N, 256))
-      return launch_bn<EPI, HD, 224>(a, lda, b, ldb, M, N, K, ep, stream, name);
+    if (M > 0) {
+      const int64_t m256 = makespan(M, N, 256), m224 = makespan(M, N, 224), m208 = makespan(M, N, 208);
+      if (m208 < m224 && m208 < m256) return launch_bn<EPI, HD, 208>(a, lda, b, ldb, M, N, K, ep, stream, name);
+      if (m224 < m256) return launch_bn<EPI, HD, 224>(a, lda, b, ldb, M, N, K, ep, stream, name);
+    }
   }
   return launch_bn<EPI, HD, 256>(a, lda, b, ldb, M, N, K, ep, stream, name);
 }
