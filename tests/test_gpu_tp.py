@@ -1,6 +1,7 @@
 """Tensor-parallel blend prefill on 2 GPUs, against the reference fixtures and against the
-same engine on one GPU, with both exchanges: partial rows pushed over NVLink peer memory
-(`ckv_linear_push` + `ckv_reduce_add_gather`, the default) and the NCCL all-reduce.
+same engine on one GPU, with both exchanges: partial rows read over NVLink peer memory by
+the owning ranks (`ckv_linear_partial` + `ckv_reduce_add_gather`, the default) and the NCCL
+all-reduce.
 
 Each rank holds one of the two KV heads of the `tiny` shape with its query heads
 and half of the MLP.  Checked per scenario, on every rank:
