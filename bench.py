@@ -43,10 +43,11 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ratio", type=float, default=0.15)
     ap.add_argument("--n-sink", type=int, default=4)
-    ap.add_argument("--workload", choices=["dp", "tp", "replay"], default="dp",
+    ap.add_argument("--workload", choices=["dp", "tp", "replay", "micro"], default="dp",
                     help="dp: config 3 (7B, one request per GPU); tp: config 5 (32B split over the GPUs "
                          "by KV head, 64x512 chunks; defaults --shape qwen2.5-32b --chunks 64 --steps 10); "
-                         "replay: config 4 (256 requests over a 16x256 chunk pool, split over the GPUs)")
+                         "replay: config 4 (256 requests over a 16x256 chunk pool, split over the GPUs); "
+                         "micro: config 2 (the K/V bandwidth kernels at the 7B KV shape, one GPU)")
     ap.add_argument("--requests", type=int, default=256, help="replay: total requests over all GPUs")
     ap.add_argument("--tp-exchange", choices=["peer", "nccl"], default="peer",
                     help="tp: partial rows over NVLink peer memory (fused kernels) or NCCL all-reduce")
@@ -765,6 +766,108 @@ def run_replay(args):
     print(json.dumps(out), flush=True)
 
 
+def run_micro(args):
+    """Config 2: the bandwidth-bound kernels at the 7B KV shape (H = 4, D = 128), 28 layers,
+    8 chunks x 256 tokens, Delta uniform in [-4096, 4096].  Each kernel runs on two sets of
+    inputs used alternately, so consecutive launches never find their data in L2; GB/s are
+    the algorithmic bytes (read + write) over the CUDA-event time per launch."""
+    import torch
+
+    from chunkkv_b200 import ops
+    from chunkkv_b200.engine.weights import SHAPES
+    from chunkkv_b200.store.pages import PAGE_TOKENS, PagePool
+
+    dev = torch.device("cuda", 0)
+    shape = SHAPES["qwen2.5-7b"]
+    L, H, D = shape.n_layers, shape.n_kv, shape.head_dim
+    n_ch, cl = 8, 256
+    T = n_ch * cl
+    bf = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(0)
+    inv = shape.rope_theta ** (-torch.arange(0, D, 2, device=dev, dtype=torch.float32) / D)
+    rng = random.Random(1)
+    deltas = [rng.randint(-4096, 4096) for _ in range(n_ch)]
+    pk, pk_kind = peaks()
+
+    def timed(fn, nbytes, reps=None):
+        reps = reps or max(3, args.steps)
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        return {"ms": round(ms, 4), "bytes": int(nbytes), "gbs": round(gbs, 1), "frac_hbm": round(gbs / pk["hbm_gbs"], 4)}
+
+    out = {}
+    # re-RoPE by Delta (TorchEngine.shift_keys), all chunks of all layers in one launch
+    keys = [torch.randn((L * n_ch, H, cl, D), generator=g, device=dev).to(bf) for _ in range(2)]
+    shifted = [torch.empty_like(k) for k in keys]
+    # context, not this library's kernel: a plain device-to-device copy of the same bytes
+    out["reference_copy_same_bytes"] = timed(lambda i: shifted[i % 2].copy_(keys[i % 2]), 2.0 * keys[0].numel() * 2)
+    out["rerope_shift_keys"] = timed(lambda i: ops.shift_keys(keys[i % 2], deltas[0], inv, out=shifted[i % 2]),
+                                     2.0 * keys[0].numel() * 2)
+    # paged gather of K (re-roped) and V for all layers, chunks placed at shifted positions
+    n_pages = T // PAGE_TOKENS
+    pools = [PagePool(L, H, D, n_pages, dev) for _ in range(2)]
+    for pool in pools:
+        pool.pages.normal_(generator=g)
+    table = torch.arange(n_pages, dtype=torch.int32, device=dev)
+    order = list(range(n_ch))
+    rng.shuffle(order)
+    meta = torch.tensor([[c * cl // PAGE_TOKENS, cl, order[c] * cl, deltas[c], 0, L, 0, 0] for c in range(n_ch)],
+                        dtype=torch.int32, device=dev)
+    kall = [torch.empty((L, H, T, D), dtype=bf, device=dev) for _ in range(2)]
+    vall = [torch.empty_like(k) for k in kall]
+    out["gather_paged"] = timed(lambda i: ops.blend_gather_paged(pools[i % 2].pages, table, meta, inv, kall[i % 2],
+                                                                 vall[i % 2], 0, L),
+                                2.0 * 2 * L * H * T * D * 2)
+    # store insert (write-back): one chunk of 256 tokens, all layers, from a result cache
+    ids = torch.arange(cl // PAGE_TOKENS, dtype=torch.int32, device=dev)
+    kp = [torch.tensor([kall[b][li].data_ptr() for li in range(L)], dtype=torch.int64).view(torch.uint64).to(dev)
+          for b in range(2)]
+    vp = [torch.tensor([vall[b][li].data_ptr() for li in range(L)], dtype=torch.int64).view(torch.uint64).to(dev)
+          for b in range(2)]
+    out["scatter_pages_write"] = timed(lambda i: ops.pages_write(pools[i % 2].pages, ids, cl, kp[i % 2], vp[i % 2],
+                                                                 T * D),
+                                       2.0 * 2 * L * H * cl * D * 2)
+    # layer-1 deviation + pooled top-k: fresh = cached + noise on 20 % of tokens
+    # (16 input sets used in turn: 8 MiB per launch would otherwise stay in L2)
+    n_sets = 16
+    Kbs, Vbs, kfs, vfs = [], [], [], []
+    for si in range(n_sets):
+        Kb = torch.randn((H, T, D), generator=g, device=dev).to(bf)
+        Vb = torch.randn((H, T, D), generator=g, device=dev).to(bf)
+        kf = Kb.permute(1, 0, 2).reshape(T, H * D).clone()
+        vf = Vb.permute(1, 0, 2).reshape(T, H * D).clone()
+        noisy = torch.rand(T, generator=g, device=dev) < 0.2
+        kf[noisy] = (kf[noisy].float() + 0.05 * torch.randn(kf[noisy].shape, generator=g, device=dev)).to(bf)
+        Kbs.append(Kb), Vbs.append(Vb), kfs.append(kf), vfs.append(vf)
+    active = torch.arange(T, dtype=torch.int32, device=dev)
+    flags = torch.ones(T, dtype=torch.uint8, device=dev)
+    for c in range(n_ch):
+        flags[c * cl:c * cl + 4] |= 2
+    smeta = torch.tensor([[c * cl, cl, 38, 0] for c in range(n_ch)], dtype=torch.int32, device=dev)
+    ws = ops.SelectWorkspace(T, n_ch, dev)
+    out["deviation_select_fused"] = timed(
+        lambda i: ops.deviation_select(kfs[i % n_sets], vfs[i % n_sets], Kbs[i % n_sets], Vbs[i % n_sets], active,
+                                       flags, smeta, None, ws),
+        4.0 * T * H * D * 2 + 8.0 * T)
+    out["select_from_scores"] = timed(lambda i: ops.select_from_scores(ws.diff[:T], ws.norm[:T], flags, smeta, None, ws),
+                                      8.0 * T)
+    n_sel = int(ws.counts[0])
+    res = {"metric": "config-2 K/V bandwidth kernels (7B KV shape, 28 layers, 8 chunks x 256 tokens)",
+           "unit": "GB/s", "n_gpus": 1, "higher_is_better": True, "peak": pk["hbm_gbs"],
+           "peak_source": f"{pk_kind} hbm_gbs", "selected_tokens": n_sel,
+           "data": "synthetic: N(0,1) bf16 K/V, seeded deltas and noise", "kernels": out}
+    print(json.dumps(res), flush=True)
+
+
 def run_reference(args):
     """CPU reference arm: the oracle port of the reference path on the host cores."""
     if int(os.environ.get("RANK", "0")) != 0:
@@ -882,6 +985,8 @@ def main():
         run_tp(args)
     elif args.workload == "replay":
         run_replay(args)
+    elif args.workload == "micro":
+        run_micro(args)
     else:
         run_ours(args)
 

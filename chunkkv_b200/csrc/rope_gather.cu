@@ -17,6 +17,7 @@ namespace {
 
 constexpr int kPage = CKV_PAGE_TOKENS;
 constexpr int kMaxHalf = 128;  // rot_dims <= 256
+constexpr int kSmemPages = 1024;  // page ids of a chunk kept in shared memory (16k tokens)
 
 struct uint4x2 {
   uint4 a, b;
@@ -48,32 +49,53 @@ __device__ __forceinline__ float2 rope_cs(float pos_or_delta, float inv_freq) {
 }
 
 // Copy `rows` rows of head_dim bf16 from src to dst, rotating by the per-j
-// table cs (smem) when rotate != 0.  Executed by one warp.
+// table cs (smem) when rotate != 0.  Executed by one warp; each lane issues the loads
+// of up to four items before it rotates and stores any of them, so a warp keeps
+// several KiB in flight (the copy is HBM-latency bound otherwise).
 __device__ __forceinline__ void copy_rows_warp(const uint16_t* __restrict__ src, int64_t src_row_stride,
                                                uint16_t* __restrict__ dst, int64_t dst_row_stride,
                                                int rows, int head_dim, int rot, bool rotate,
                                                const float2* cs, int lane) {
+  constexpr int U = 4;
   const int n_pair = rotate ? rot / 16 : 0;      // pair items (two 16 B vectors)
   const int n_copy = (head_dim / 8) - 2 * n_pair;  // plain 16 B vectors
   const int per_row = n_pair + n_copy;
   const int total = rows * per_row;
-  for (int it = lane; it < total; it += 32) {
-    const int r = it / per_row;
-    const int item = it - r * per_row;
-    const uint16_t* s = src + r * src_row_stride;
-    uint16_t* d = dst + r * dst_row_stride;
-    if (item < n_pair) {
-      const int j = item * 8;
-      uint4 v1 = *reinterpret_cast<const uint4*>(s + j);
-      uint4 v2 = *reinterpret_cast<const uint4*>(s + j + rot / 2);
-      rotate8(v1, v2, cs + j);
-      *reinterpret_cast<uint4*>(d + j) = v1;
-      *reinterpret_cast<uint4*>(d + j + rot / 2) = v2;
-    } else {
-      const int c = item - n_pair;
-      // copy vectors: the dims past rot (or every dim when not rotating)
-      const int off = (rotate ? rot : 0) + c * 8;
-      *reinterpret_cast<uint4*>(d + off) = *reinterpret_cast<const uint4*>(s + off);
+  for (int it0 = lane; it0 < total; it0 += 32 * U) {
+    uint4 v1[U], v2[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int it = it0 + 32 * u;
+      if (it >= total) continue;
+      const int r = it / per_row;
+      const int item = it - r * per_row;
+      const uint16_t* s = src + r * src_row_stride;
+      if (item < n_pair) {
+        const int j = item * 8;
+        v1[u] = __ldcs(reinterpret_cast<const uint4*>(s + j));
+        v2[u] = __ldcs(reinterpret_cast<const uint4*>(s + j + rot / 2));
+      } else {
+        const int off = (rotate ? rot : 0) + (item - n_pair) * 8;
+        v1[u] = __ldcs(reinterpret_cast<const uint4*>(s + off));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int it = it0 + 32 * u;
+      if (it >= total) continue;
+      const int r = it / per_row;
+      const int item = it - r * per_row;
+      uint16_t* d = dst + r * dst_row_stride;
+      if (item < n_pair) {
+        const int j = item * 8;
+        rotate8(v1[u], v2[u], cs + j);
+        *reinterpret_cast<uint4*>(d + j) = v1[u];
+        *reinterpret_cast<uint4*>(d + j + rot / 2) = v2[u];
+      } else {
+        // the dims past rot (or every dim when not rotating)
+        const int off = (rotate ? rot : 0) + (item - n_pair) * 8;
+        *reinterpret_cast<uint4*>(d + off) = v1[u];
+      }
     }
   }
 }
@@ -85,6 +107,26 @@ __global__ void rope_table_kernel(const float* __restrict__ inv_freq, int half, 
        i += int64_t(gridDim.x) * blockDim.x) {
     const int p = int(i / half), j = int(i - int64_t(p) * half);
     table[i] = rope_cs(float(p), inv_freq[j]);
+  }
+}
+
+// dst[row] = rotate(src[row], cs(delta)) for every row: the (cos, sin) of the one angle per
+// rotary pair are computed once per CTA into shared memory; warps copy 16-row units
+// (4 KiB at head_dim 128) with copy_rows_warp.
+__global__ void __launch_bounds__(256, 4) shift_rows_kernel(const uint16_t* __restrict__ src,
+                                                         uint16_t* __restrict__ dst, int64_t rows,
+                                                         int head_dim, int rot, int delta,
+                                                         const float* __restrict__ inv_freq) {
+  __shared__ float2 cs[kMaxHalf];
+  for (int j = threadIdx.x; j < rot / 2; j += blockDim.x) cs[j] = rope_cs(float(delta), inv_freq[j]);
+  __syncthreads();
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int64_t n_units = (rows + kPage - 1) / kPage;
+  for (int64_t u = int64_t(blockIdx.x) * 8 + warp; u < n_units; u += int64_t(gridDim.x) * 8) {
+    const int64_t r0 = u * kPage;
+    const int n = int(min(int64_t(kPage), rows - r0));
+    copy_rows_warp(src + r0 * head_dim, head_dim, dst + r0 * head_dim, head_dim, n, head_dim, rot, true, cs,
+                   lane);
   }
 }
 
@@ -125,13 +167,14 @@ __global__ void rope_rows_kernel(const uint16_t* __restrict__ src, uint16_t* __r
 // Unit u -> (block b, layer l, kv, head h), head fastest so consecutive warps
 // stream consecutive 4 KiB pieces of the same page.
 template <bool kPaged>
-__global__ void __launch_bounds__(256) blend_gather_kernel(
+__global__ void __launch_bounds__(256, 4) blend_gather_kernel(
     const uint16_t* __restrict__ pool, int64_t n_pages, const int32_t* __restrict__ page_table,
     const uint64_t* __restrict__ k_ptrs, const uint64_t* __restrict__ v_ptrs,
     const int32_t* __restrict__ chunk_meta, const float* __restrict__ inv_freq, int rot,
     uint16_t* __restrict__ k_out, uint16_t* __restrict__ v_out, int layer_lo, int layer_hi,
     int n_layers, int H, int D, int n_ctx) {
   __shared__ float2 cs[kMaxHalf];
+  __shared__ int s_pages[kSmemPages];  // this chunk's page ids, so no unit waits on a table load
   const int32_t* meta = chunk_meta + blockIdx.y * CKV_META_STRIDE;
   const int table_off = meta[CKV_META_TABLE_OFFSET];
   const int length = meta[CKV_META_LENGTH];
@@ -145,22 +188,24 @@ __global__ void __launch_bounds__(256) blend_gather_kernel(
   const bool rotate = delta != 0;
   if (rotate)
     for (int j = threadIdx.x; j < rot / 2; j += blockDim.x) cs[j] = rope_cs(float(delta), inv_freq[j]);
+  const int n_slots = kPaged ? min(kSmemPages, (src_off + length + kPage - 1) / kPage) : 0;
+  for (int i = threadIdx.x; i < n_slots; i += blockDim.x) s_pages[i] = page_table[table_off + i];
   __syncthreads();
 
   const int nl = le - lb;
   const int n_blocks = (length + kPage - 1) / kPage;
-  const int64_t n_units = int64_t(n_blocks) * nl * 2 * H;
+  const int n_units = n_blocks * nl * 2 * H;  // < 2^31: checked on the host
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int warps = blockDim.x / 32;
   const int64_t layer_elems = int64_t(H) * n_ctx * D;
-  for (int64_t u = int64_t(blockIdx.x) * warps + warp; u < n_units; u += int64_t(gridDim.x) * warps) {
-    int64_t t = u;
-    const int h = int(t % H);
+  for (int u = blockIdx.x * warps + warp; u < n_units; u += gridDim.x * warps) {
+    int t = u;
+    const int h = t % H;
     t /= H;
-    const int kv = int(t % 2);
-    t /= 2;
-    const int l = lb + int(t % nl);
-    const int b = int(t / nl);
+    const int kv = t & 1;
+    t >>= 1;
+    const int l = lb + t % nl;
+    const int b = t / nl;
     const int r0 = b * kPage;
     const int rows = min(kPage, length - r0);
     const int dpos = dst_start + r0;
@@ -178,7 +223,7 @@ __global__ void __launch_bounds__(256) blend_gather_kernel(
         const int tok = src_off + r0 + done;
         const int slot = tok / kPage, in_page = tok % kPage;
         const int take = min(rows - done, kPage - in_page);
-        const int page = page_table[table_off + slot];
+        const int page = slot < kSmemPages ? s_pages[slot] : page_table[table_off + slot];
         if (page < 0 || page >= n_pages) {
           if (lane == 0) atomicOr(&g_err_word, CKV_DEV_ERR_PAGE_RANGE);
         } else {
@@ -277,10 +322,10 @@ int ckv_shift_keys(const uint16_t* src, uint16_t* dst, int64_t rows, int head_di
       }
     return CKV_OK;
   }
-  const int64_t items = rows * (head_dim / 8 - rot_dims / 16);
-  const int grid = static_cast<int>(std::min<int64_t>((items + 255) / 256, 16 * num_sms()));
-  rope_rows_kernel<<<grid, 256, 0, as_stream(stream)>>>(src, dst, rows, head_dim, rot_dims, delta,
-                                                        nullptr, 1, inv_freq);
+  const int64_t units = (rows + kPage - 1) / kPage;
+  const int grid = int(std::min<int64_t>((units + 7) / 8, 4 * num_sms()));
+  shift_rows_kernel<<<grid, 256, 0, as_stream(stream)>>>(src, dst, rows, head_dim, rot_dims, delta,
+                                                         inv_freq);
   CKV_LAUNCH_CHECK("ckv_shift_keys");
   return CKV_OK;
 }
@@ -311,6 +356,8 @@ static int gather_common(const int32_t* chunk_meta, int n_chunks, const float* i
   CKV_REQUIRE(n_chunks >= 0 && n_chunks <= 65535, "blend_gather: n_chunks %d out of range", n_chunks);
   CKV_REQUIRE(layer_lo >= 0 && layer_hi >= layer_lo, "blend_gather: bad layer range");
   CKV_REQUIRE(H > 0 && n_ctx > 0, "blend_gather: bad sizes");
+  CKV_REQUIRE(int64_t((n_ctx + kPage - 1) / kPage) * (layer_hi - layer_lo) * 2 * H < (int64_t(1) << 31),
+              "blend_gather: too many (page, layer, K|V, head) units for one launch");
   return CKV_OK;
 }
 
