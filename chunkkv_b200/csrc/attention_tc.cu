@@ -28,6 +28,10 @@
 // (ex2.approx, 16 results per clock per SM: alone as slow as the tensor core) and a
 // polynomial on the FMA pipe (one pair in four).  Every wait is bounded
 // (ckv_common.cuh).
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
 #include "ckv_common.cuh"
 
 CKV_DEFINE_ERR_WORD(attention_tc)
@@ -506,23 +510,70 @@ struct SplitPlan {
   int tps, max_splits, blocks;
   int64_t bytes;
 };
+// Estimated makespan, in key-tile times, of a split plan with one CTA per SM at a time:
+// the list-scheduling estimate total work / SMs + half the largest CTA (CTAs go out
+// roughly largest first: late row blocks first, splits in order), plus, when split, the
+// partial O writes (about 1.3 tile times per CTA) and the combine (reading every partial
+// at the HBM rate: one tile time per 14.3 MB).  Each CTA costs its key tiles plus a
+// fixed prologue/epilogue; row block b is assumed to reach position (b + 1) / blocks *
+// n_ctx (sorted positions spread over the context, as the engine passes them).
+double plan_cost(int blocks, int Hk, int HD, int n_ctx, int tps, int sms) {
+  const bool split = tps < ceil_div(n_ctx, BN);
+  const double cta_cost = 2.0 + (split ? 1.3 : 0.0);
+  double total = 0.0;
+  int64_t items_all = 0;
+  int max_item = 0;
+  for (int b = 0; b < blocks; ++b) {
+    const int kt = std::max(1, ceil_div((int64_t(b) + 1) * n_ctx / blocks, BN));
+    const int items = ceil_div(kt, tps);
+    total += kt + items * cta_cost;
+    items_all += items;
+    max_item = std::max(max_item, std::min(kt, tps));
+  }
+  total *= Hk;
+  const double combine = split ? double(items_all) * Hk * NQ * BM * (HD * 4 + 8) / 14.3e6 : 0.0;
+  return total / sms + 0.5 * (max_item + cta_cost) + combine;
+}
+
+// Key-split plan: the tiles-per-split with the smallest estimated makespan (no split
+// included).  Plans are cached per shape.
 SplitPlan plan_splits(int M, int Hq, int Hk, int HD, int n_ctx) {
+  struct Key {
+    int M, Hq, Hk, HD, n_ctx, sms;
+  };
+  static std::mutex mu;
+  static std::vector<std::pair<Key, SplitPlan>> cache;
+  const int sms = num_sms();
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto& e : cache)
+      if (e.first.M == M && e.first.Hq == Hq && e.first.Hk == Hk && e.first.HD == HD &&
+          e.first.n_ctx == n_ctx && e.first.sms == sms)
+        return e.second;
+  }
   const int T = BM / (Hq / Hk);
   SplitPlan p;
   p.blocks = ceil_div(M, NQ * T);
   const int max_kt = ceil_div(n_ctx, BN);
-  const int ctas = p.blocks * Hk;
-  const int sms = num_sms();
-  if (ctas >= sms || max_kt <= 4) {
-    p.tps = max_kt;
-    p.max_splits = 1;
-    p.bytes = 0;
-    return p;
+  const double unsplit = plan_cost(p.blocks, Hk, HD, n_ctx, max_kt, sms);
+  int best_tps = max_kt;
+  double best = unsplit;
+  // at most 32 splits: the combine gives each split one lane
+  for (int tps = std::max(2, ceil_div(max_kt, 32)); tps < max_kt; tps = tps < 8 ? tps + 1 : tps + tps / 4) {
+    const double c = plan_cost(p.blocks, Hk, HD, n_ctx, tps, sms);
+    if (c < best) {
+      best = c;
+      best_tps = tps;
+    }
   }
-  const int want = ceil_div(2 * sms, ctas);         // splits per block for about two waves
-  p.tps = std::max(std::max(4, ceil_div(max_kt, want)), ceil_div(max_kt, 32));
-  p.max_splits = ceil_div(max_kt, p.tps);  // <= 32: the combine gives each split one lane
-  p.bytes = int64_t(ctas) * p.max_splits * NQ * BM * (int64_t(HD) * 4 + 8);
+  // the estimate overstates what splitting gains (about twice, measured): split only when
+  // it promises at least 15 %
+  if (best > 0.85 * unsplit) best_tps = max_kt;
+  p.tps = best_tps;
+  p.max_splits = ceil_div(max_kt, p.tps);
+  p.bytes = p.max_splits > 1 ? int64_t(p.blocks) * Hk * p.max_splits * NQ * BM * (int64_t(HD) * 4 + 8) : 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache.size() < 256) cache.push_back({Key{M, Hq, Hk, HD, n_ctx, sms}, p});
   return p;
 }
 
