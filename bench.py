@@ -49,9 +49,8 @@ def parse():
                          "replay: config 4 (256 requests over a 16x256 chunk pool, split over the GPUs); "
                          "micro: config 2 (the K/V bandwidth kernels at the 7B KV shape, one GPU)")
     ap.add_argument("--requests", type=int, default=256, help="replay: total requests over all GPUs")
-    ap.add_argument("--tp-exchange", choices=["auto", "peer", "nccl"], default="auto",
-                    help="tp: partial rows over NVLink peer memory (fused kernels), NCCL all-reduce, "
-                         "or the engine's choice for the group size")
+    ap.add_argument("--tp-exchange", choices=["peer", "nccl"], default="peer",
+                    help="tp: partial rows over NVLink peer memory (fused kernels) or NCCL all-reduce")
     ap.add_argument("--shape", default=None)
     ap.add_argument("--chunks", type=int, default=None)
     ap.add_argument("--chunk-len", type=int, default=512)
@@ -490,7 +489,7 @@ def run_tp(args):
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-        tp = TensorParallel(fused=None if args.tp_exchange == "auto" else args.tp_exchange == "peer")
+        tp = TensorParallel(fused=args.tp_exchange == "peer")
     shape = SHAPES[args.shape]
     weights = random_packed(shape, seed=0, device=dev, tp_rank=rank, tp_size=world)
     eng = TorchEngine.from_packed(weights, tp=tp)
