@@ -63,7 +63,7 @@ _RESTYPES = {"ckv_version": C.c_char_p, "ckv_last_error": C.c_char_p, "ckv_atten
 
 CKV_OK, CKV_ERR_ARG, CKV_ERR_CUDA, CKV_ERR_DEVICE, CKV_ERR_UNSUPPORTED = range(5)
 DEV_ERR_BITS = {
-    0x1: "an mbarrier wait ran past its limit",
+    0x1: "a bounded wait (mbarrier or peer counter) ran past its limit",
     0x2: "a page id outside the pool was skipped",
     0x4: "the selection kept a position that was never computed",
     0x8: "a position or index outside its range was skipped",

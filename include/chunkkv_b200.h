@@ -47,7 +47,7 @@ typedef enum {
 } ckv_status;
 
 /* Device-side error bits reported by ckv_get_device_error(). */
-#define CKV_DEV_ERR_WAIT_TIMEOUT   0x1u  /* an mbarrier wait ran past its limit */
+#define CKV_DEV_ERR_WAIT_TIMEOUT   0x1u  /* a bounded wait (mbarrier or peer counter) ran out */
 #define CKV_DEV_ERR_PAGE_RANGE     0x2u  /* a page id outside [0, n_pages) was skipped */
 #define CKV_DEV_ERR_SELECT_UNCOMPUTED 0x4u /* selection kept a position never computed
                                               (torch_engine.py:151 assert) */

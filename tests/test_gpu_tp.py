@@ -146,3 +146,35 @@ def test_tensor_parallel_2gpu_matches_reference_and_single_gpu(golden):
             assert o["kv_rel"] <= 1e-2, (name, r, o["kv_rel"])
         assert res[0][(name, fused)]["selected"] == res[1][(name, fused)]["selected"], name
         assert np.array_equal(res[0][(name, fused)]["logits"], res[1][(name, fused)]["logits"]), name
+
+
+def test_exchange_wait_runs_out_and_reports_without_a_peer():
+    """Failure detection on one GPU: the reduce kernel of a 2-rank exchange whose peer
+    never signals gives up after its bounded wait (2 s), records CKV_DEV_ERR_WAIT_TIMEOUT
+    and returns; the host reads the error word and the GPU stays usable."""
+    from chunkkv_b200 import _lib, ops
+
+    dev = torch.device("cuda", 0)
+    rows, hidden = 64, 256
+    bf = torch.bfloat16
+    parts = [torch.zeros((rows, hidden), dtype=bf, device=dev) for _ in range(2)]
+    hs = [torch.zeros((rows, hidden), dtype=bf, device=dev) for _ in range(2)]
+    ctl = torch.zeros(64, dtype=torch.int32, device=dev)  # counters: nothing ever signals them
+
+    def table(ts):
+        return torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64).view(torch.uint64).to(dev)
+
+    part_tab, h_tab = table(parts), table(hs)
+    gather_tab = table([ctl[8:], ctl[8:]])
+    _lib.check_device()  # start from a clean error word
+    _lib.call("ckv_reduce_add_gather", part_tab.data_ptr(), 0, 2, rows, hidden, hs[0].data_ptr(),
+              h_tab.data_ptr(), ctl.data_ptr(), ctl[8:].data_ptr(), gather_tab.data_ptr(),
+              ctl[16:].data_ptr(), 1, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert _lib.device_error() & 0x1  # CKV_DEV_ERR_WAIT_TIMEOUT
+    # the context is intact: an ordinary kernel still runs and the error word is clear
+    x = torch.randn((8, hidden), device=dev).to(bf)
+    y = ops.rmsnorm(x, torch.ones(hidden, dtype=bf, device=dev), 1e-6)
+    torch.cuda.synchronize()
+    assert torch.isfinite(y.float()).all()
+    _lib.check_device()
