@@ -43,11 +43,12 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ratio", type=float, default=0.15)
     ap.add_argument("--n-sink", type=int, default=4)
-    ap.add_argument("--workload", choices=["dp", "tp", "replay", "micro"], default="dp",
+    ap.add_argument("--workload", choices=["dp", "tp", "replay", "micro", "decode"], default="dp",
                     help="dp: config 3 (7B, one request per GPU); tp: config 5 (32B split over the GPUs "
                          "by KV head, 64x512 chunks; defaults --shape qwen2.5-32b --chunks 64 --steps 10); "
                          "replay: config 4 (256 requests over a 16x256 chunk pool, split over the GPUs); "
-                         "micro: config 2 (the K/V bandwidth kernels at the 7B KV shape, one GPU)")
+                         "micro: config 2 (the K/V bandwidth kernels at the 7B KV shape, one GPU); "
+                         "decode: greedy decode after the config-3 blend prefill (one GPU)")
     ap.add_argument("--requests", type=int, default=256, help="replay: total requests over all GPUs")
     ap.add_argument("--tp-exchange", choices=["peer", "nccl"], default="peer",
                     help="tp: partial rows over NVLink peer memory (fused kernels) or NCCL all-reduce")
@@ -896,6 +897,54 @@ def run_micro(args):
     print(json.dumps(res), flush=True)
 
 
+def run_decode(args):
+    """Greedy decode after the config-3 blend prefill (TorchEngine.generate,
+    torch_engine.py:180-198): per token, 28 layers of m = 1 projections (fused GEMV
+    kernels) and attention over the blended cache, then the lm_head GEMV.  Reports ms per
+    token and the weight bytes streamed per token against the HBM peak."""
+    import torch
+
+    from chunkkv_b200.engine.base import BlendConfig, Placement
+    from chunkkv_b200.engine.torch_engine import TorchEngine
+    from chunkkv_b200.engine.weights import SHAPES, random_packed
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    shape = SHAPES[args.shape]
+    weights = random_packed(shape, seed=0, device=dev)
+    eng = TorchEngine.from_packed(weights)
+    eng.eos = set()  # random weights: decode the full count
+    chunks, order, query = make_request(shape.vocab, args.chunks, args.chunk_len, args.query_len, request_seed(0))
+    first = eng.prefill(sum(chunks, []))
+    tokens, pl = [], []
+    for c in order:
+        pl.append(Placement(first.chunk(c * args.chunk_len, (c + 1) * args.chunk_len), len(tokens)))
+        tokens += chunks[c]
+    tokens += query
+    res = eng.prefill(tokens, pl, BlendConfig(recompute_ratio=args.ratio, n_sink=args.n_sink))
+    n_new = max(8, args.steps)
+    eng.generate(res, max(4, args.warmup))
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    out = eng.generate(res, n_new)
+    e1.record()
+    torch.cuda.synchronize()
+    ms_tok = e0.elapsed_time(e1) / len(out)
+    pk, pk_kind = peaks()
+    wbytes = weights.nbytes() - weights.embed.numel() * 2 + (weights.lm_head.numel() * 2 if shape.tied else 0)
+    gbs = wbytes / (ms_tok * 1e-3) / 1e9
+    print(json.dumps({
+        "metric": "greedy decode tokens/s after the config-3 blend prefill (one request)",
+        "value": round(1e3 / ms_tok, 2), "unit": "tokens/s", "n_gpus": 1, "steps": len(out),
+        "ms_per_step": round(ms_tok, 4), "higher_is_better": True, "dtype": "bf16",
+        "data": "synthetic: random-init bf16 weights (seed 0)",
+        "config": {"workload": "decode after config 3", "model": f"{args.shape} architecture, random init",
+                   "context_tokens": len(tokens), "new_tokens": len(out)},
+        "weight_bytes_per_token": int(wbytes), "weight_gbs": round(gbs, 1),
+        "frac_hbm": round(gbs / pk["hbm_gbs"], 4), "peak_source": f"{pk_kind} hbm_gbs"}), flush=True)
+
+
 def run_reference(args):
     """CPU reference arm: the oracle port of the reference path on the host cores.
 
@@ -1026,6 +1075,8 @@ def main():
         run_replay(args)
     elif args.workload == "micro":
         run_micro(args)
+    elif args.workload == "decode":
+        run_decode(args)
     else:
         run_ours(args)
 

@@ -61,6 +61,7 @@ uint32_t read_clear_err_gemm();
 uint32_t read_clear_err_attention_tc();
 uint32_t read_clear_err_elementwise();
 uint32_t read_clear_err_tp_reduce();
+uint32_t read_clear_err_gemv_fused();
 
 }  // namespace ckv
 
@@ -82,7 +83,8 @@ int ckv_get_device_error(uint32_t* code) {
   }
   *code = ckv::read_clear_err_rope() | ckv::read_clear_err_select() | ckv::read_clear_err_gemm() |
           ckv::read_clear_err_attention_tc() |
-          ckv::read_clear_err_elementwise() | ckv::read_clear_err_tp_reduce();
+          ckv::read_clear_err_elementwise() | ckv::read_clear_err_tp_reduce() |
+          ckv::read_clear_err_gemv_fused();
   return CKV_OK;
 }
 

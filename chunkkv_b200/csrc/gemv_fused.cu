@@ -1,0 +1,247 @@
+// Decode-time projections (m <= 8 rows): one warp per weight row (or row pair), the
+// weight streamed from HBM once, with the same epilogues and rounding points as the
+// tcgen05 GEMM's (gemm_tcgen05.cu): residual add, SwiGLU, and bias + RoPE + K/V cache
+// scatter (torch_engine.py:61-76, 180-198 greedy decode).  At m <= 8 the GEMM's
+// 128-row tiles would leave all but a handful of SMs idle on the 3584-column
+// projections; here every SM streams weight rows.
+#include "ckv_common.cuh"
+
+CKV_DEFINE_ERR_WORD(gemv_fused)
+
+namespace ckv {
+namespace {
+
+constexpr int kMaxRows = 8;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// acc[m] += dot(w row, x[m]) over this lane's 16-byte vectors of k (R weight rows at once).
+template <int MM, int R>
+__device__ __forceinline__ void dot_rows(const uint16_t* const (&wrow)[R], const uint16_t* __restrict__ x, int k,
+                                         int lane, float (&acc)[R][MM]) {
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int m = 0; m < MM; ++m) acc[r][m] = 0.f;
+  const int vecs = k / 8;
+#pragma unroll 4
+  for (int v = lane; v < vecs; v += 32) {
+    uint4 a[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) a[r] = __ldcs(reinterpret_cast<const uint4*>(wrow[r]) + v);  // streamed once
+#pragma unroll
+    for (int m = 0; m < MM; ++m) {
+      const uint4 b = reinterpret_cast<const uint4*>(x + int64_t(m) * k)[v];
+      const uint32_t* pb = reinterpret_cast<const uint32_t*>(&b);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a[r]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          acc[r][m] = fmaf(lo_bf(pa[e]), lo_bf(pb[e]), acc[r][m]);
+          acc[r][m] = fmaf(hi_bf(pa[e]), hi_bf(pb[e]), acc[r][m]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int m = 0; m < MM; ++m) acc[r][m] = warp_sum(acc[r][m]);
+}
+
+// h[m][n] = bf16(h + bf16(w[n] . x[m]))   (o_proj / down_proj + residual)
+template <int MM>
+__global__ void __launch_bounds__(256) gemv_residual_kernel(const uint16_t* __restrict__ x,
+                                                            const uint16_t* __restrict__ w,
+                                                            uint16_t* __restrict__ h, int n, int k) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (row >= n) return;
+  const uint16_t* wr[1] = {w + int64_t(row) * k};
+  float acc[1][MM];
+  dot_rows<MM, 1>(wr, x, k, lane, acc);
+  if (lane < MM) {
+    float s = acc[0][0];
+#pragma unroll
+    for (int m = 1; m < MM; ++m)
+      if (lane == m) s = acc[0][m];
+    uint16_t* hp = h + int64_t(lane) * n + row;
+    *hp = f2bf(__fadd_rn(bf2f(*hp), bf16_round(s)));
+  }
+}
+
+// out[m][j] = bf16(bf16(silu(bf16(g))) * bf16(u)); gate/up rows interleaved in 128-row blocks
+template <int MM>
+__global__ void __launch_bounds__(256) gemv_swiglu_kernel(const uint16_t* __restrict__ x,
+                                                          const uint16_t* __restrict__ w,
+                                                          uint16_t* __restrict__ out, int inter, int k) {
+  const int j = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (j >= inter) return;
+  const int64_t gate_row = int64_t(j / 128) * 256 + (j % 128);
+  const uint16_t* wr[2] = {w + gate_row * k, w + (gate_row + 128) * k};
+  float acc[2][MM];
+  dot_rows<MM, 2>(wr, x, k, lane, acc);
+  if (lane < MM) {
+    float g = acc[0][0], u = acc[1][0];
+#pragma unroll
+    for (int m = 1; m < MM; ++m)
+      if (lane == m) {
+        g = acc[0][m];
+        u = acc[1][m];
+      }
+    const float gb = bf16_round(g);
+    const float s = bf16_round(__fdiv_rn(gb, __fadd_rn(1.0f, expf(-gb))));
+    out[int64_t(lane) * inter + j] = f2bf(__fmul_rn(s, bf16_round(u)));
+  }
+}
+
+// q / k rows with bias and RoPE at positions[m] (a warp per rotary pair of one head: rows
+// d and d + HD/2), v rows with bias; k and v go to the caches [Hk][n_ctx][HD] at pos.
+template <int MM, int HD>
+__global__ void __launch_bounds__(256) gemv_qkv_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, const uint16_t* __restrict__ bias, int k,
+    int Hq, int Hk, const int32_t* __restrict__ positions, const float2* __restrict__ rope, int rope_max_pos,
+    uint16_t* __restrict__ q_out, uint16_t* __restrict__ k_cache, uint16_t* __restrict__ v_cache, int n_ctx) {
+  constexpr int HALF = HD / 2;
+  const int item = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int n_pair = (Hq + Hk) * HALF;
+  if (item >= n_pair + Hk * HD) return;
+  int pos = 0;
+  bool ok = true;
+  if (lane < MM) {
+    pos = positions[lane];
+    if (pos < 0 || pos >= rope_max_pos || pos >= n_ctx) {
+      atomicOr(&g_err_word, CKV_DEV_ERR_POSITION_RANGE);
+      ok = false;
+    }
+  }
+  if (item < n_pair) {
+    const int head = item / HALF, jj = item - head * HALF;
+    const int r1 = head * HD + jj, r2 = r1 + HALF;
+    const uint16_t* wr[2] = {w + int64_t(r1) * k, w + int64_t(r2) * k};
+    float acc[2][MM];
+    dot_rows<MM, 2>(wr, x, k, lane, acc);
+    if (lane < MM && ok) {
+      float d1 = acc[0][0], d2 = acc[1][0];
+#pragma unroll
+      for (int m = 1; m < MM; ++m)
+        if (lane == m) {
+          d1 = acc[0][m];
+          d2 = acc[1][m];
+        }
+      const float a = bf16_round(__fadd_rn(d1, bf2f(bias[r1])));
+      const float b = bf16_round(__fadd_rn(d2, bf2f(bias[r2])));
+      const float2 cs = rope[int64_t(pos) * HALF + jj];
+      const float o1 = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
+      const float o2 = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
+      uint16_t* dst = head < Hq ? q_out + (int64_t(lane) * Hq + head) * HD
+                                : k_cache + (int64_t(head - Hq) * n_ctx + pos) * HD;
+      dst[jj] = f2bf(o1);
+      dst[jj + HALF] = f2bf(o2);
+    }
+  } else {
+    const int vr = item - n_pair;  // v row: head vr / HD, dim vr % HD
+    const int row = (Hq + Hk) * HD + vr;
+    const uint16_t* wr[1] = {w + int64_t(row) * k};
+    float acc[1][MM];
+    dot_rows<MM, 1>(wr, x, k, lane, acc);
+    if (lane < MM && ok) {
+      float d = acc[0][0];
+#pragma unroll
+      for (int m = 1; m < MM; ++m)
+        if (lane == m) d = acc[0][m];
+      v_cache[(int64_t(vr / HD) * n_ctx + pos) * HD + vr % HD] = f2bf(__fadd_rn(d, bf2f(bias[row])));
+    }
+  }
+}
+
+int check_gemv(const void* x, const void* w, int m, int k, const char* name) {
+  CKV_REQUIRE(x && w, "%s: null pointer", name);
+  CKV_REQUIRE(m >= 1 && m <= kMaxRows, "%s: m=%d outside 1..%d", name, m, kMaxRows);
+  CKV_REQUIRE(k > 0 && k % 8 == 0 && aligned16(x) && aligned16(w), "%s: k %% 8 and 16-byte alignment", name);
+  return CKV_OK;
+}
+
+}  // namespace
+}  // namespace ckv
+
+using namespace ckv;
+
+#define CKV_GEMV_SWITCH(m, LAUNCH) \
+  switch (m) {                     \
+    case 1: LAUNCH(1); break;      \
+    case 2: LAUNCH(2); break;      \
+    case 3: LAUNCH(3); break;      \
+    case 4: LAUNCH(4); break;      \
+    case 5: LAUNCH(5); break;      \
+    case 6: LAUNCH(6); break;      \
+    case 7: LAUNCH(7); break;      \
+    default: LAUNCH(8); break;     \
+  }
+
+extern "C" {
+
+int ckv_gemv_residual(const uint16_t* x, const uint16_t* w, uint16_t* h, int m, int n, int k,
+                      ckv_stream_t stream) {
+  if (int rc = check_gemv(x, w, m, k, "ckv_gemv_residual")) return rc;
+  CKV_REQUIRE(h, "ckv_gemv_residual: null h");
+  if (n <= 0) return CKV_OK;
+  const int grid = ceil_div(n, 8);
+  cudaStream_t s = as_stream(stream);
+#define CKV_L(MM) gemv_residual_kernel<MM><<<grid, 256, 0, s>>>(x, w, h, n, k)
+  CKV_GEMV_SWITCH(m, CKV_L)
+#undef CKV_L
+  CKV_LAUNCH_CHECK("ckv_gemv_residual");
+  return CKV_OK;
+}
+
+int ckv_gemv_swiglu(const uint16_t* x, const uint16_t* w_gate_up, uint16_t* out, int m, int inter, int k,
+                    ckv_stream_t stream) {
+  if (int rc = check_gemv(x, w_gate_up, m, k, "ckv_gemv_swiglu")) return rc;
+  CKV_REQUIRE(out && inter > 0 && inter % 128 == 0, "ckv_gemv_swiglu: inter %d not a multiple of 128", inter);
+  const int grid = ceil_div(inter, 8);
+  cudaStream_t s = as_stream(stream);
+#define CKV_L(MM) gemv_swiglu_kernel<MM><<<grid, 256, 0, s>>>(x, w_gate_up, out, inter, k)
+  CKV_GEMV_SWITCH(m, CKV_L)
+#undef CKV_L
+  CKV_LAUNCH_CHECK("ckv_gemv_swiglu");
+  return CKV_OK;
+}
+
+int ckv_gemv_qkv_rope(const uint16_t* x, const uint16_t* w_qkv, const uint16_t* b_qkv, int m, int k,
+                      int n_q_heads, int n_kv_heads, int head_dim, const int32_t* positions,
+                      const float* rope_table, int rope_max_pos, uint16_t* q_out, uint16_t* k_cache,
+                      uint16_t* v_cache, int n_ctx, ckv_stream_t stream) {
+  if (int rc = check_gemv(x, w_qkv, m, k, "ckv_gemv_qkv_rope")) return rc;
+  CKV_REQUIRE(b_qkv && positions && rope_table && q_out && k_cache && v_cache,
+              "ckv_gemv_qkv_rope: null pointer");
+  CKV_REQUIRE(n_q_heads > 0 && n_kv_heads > 0 && n_ctx > 0 && rope_max_pos > 0, "ckv_gemv_qkv_rope: bad sizes");
+  const int items = (n_q_heads + n_kv_heads) * (head_dim / 2) + n_kv_heads * head_dim;
+  const int grid = ceil_div(items, 8);
+  cudaStream_t s = as_stream(stream);
+  const float2* rope = reinterpret_cast<const float2*>(rope_table);
+  if (head_dim == 128) {
+#define CKV_L(MM)                                                                                     \
+  gemv_qkv_kernel<MM, 128><<<grid, 256, 0, s>>>(x, w_qkv, b_qkv, k, n_q_heads, n_kv_heads, positions, \
+                                                rope, rope_max_pos, q_out, k_cache, v_cache, n_ctx)
+    CKV_GEMV_SWITCH(m, CKV_L)
+#undef CKV_L
+  } else if (head_dim == 64) {
+#define CKV_L(MM)                                                                                    \
+  gemv_qkv_kernel<MM, 64><<<grid, 256, 0, s>>>(x, w_qkv, b_qkv, k, n_q_heads, n_kv_heads, positions, \
+                                               rope, rope_max_pos, q_out, k_cache, v_cache, n_ctx)
+    CKV_GEMV_SWITCH(m, CKV_L)
+#undef CKV_L
+  } else {
+    set_error("ckv_gemv_qkv_rope: head_dim %d (64 or 128)", head_dim);
+    return CKV_ERR_UNSUPPORTED;
+  }
+  CKV_LAUNCH_CHECK("ckv_gemv_qkv_rope");
+  return CKV_OK;
+}
+
+}  // extern "C"

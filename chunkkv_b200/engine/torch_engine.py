@@ -153,6 +153,12 @@ class TorchEngine:
         residual add is fused with the next RMSNorm (the next layer's input norm, or
         the final norm after the last layer); returns True when x then holds it."""
         s, lw, tp = self.shape, self.w.layers[li], self.tp
+        if tp is None and M <= 8:  # decode: one warp per weight row streams the weights
+            ops.gemv_residual(attn[:M], lw.w_o, h)
+            ops.rmsnorm(h[:M], lw.ln2, s.rms_eps, out=x[:M])
+            ops.gemv_swiglu(x[:M], lw.w_gu, act)
+            ops.gemv_residual(act[:M], lw.w_down, h)
+            return False
         if tp is None:
             ops.linear_residual(attn, lw.w_o, h, m=M)
             ops.rmsnorm(h[:M], lw.ln2, s.rms_eps, out=x[:M])
@@ -378,7 +384,10 @@ class TorchEngine:
     @torch.inference_mode()
     def generate(self, result: PrefillResult, max_tokens: int = 32) -> list[int]:
         """Greedy decode continuing a prefill (torch_engine.py:180-198), on the same kernels:
-        the cache grows in place (capacity doubles) instead of a torch.cat per step."""
+        the cache is sized once for the new tokens instead of a torch.cat per step.  The
+        projections are the m = 1 GEMV kernels; the next token and the position stay on
+        the device, and after the first step one decode step is replayed as a CUDA graph
+        (one-GPU engines), so the host only reads back each token id."""
         s = self.shape
         L, H, Hq, D, hid = s.n_layers, s.n_kv, s.n_heads, s.head_dim, s.hidden
         dev = self.device
@@ -402,31 +411,47 @@ class TorchEngine:
         q = torch.empty((1, Hq * D), **bf)
         attn = torch.empty_like(q)
         act = torch.empty((1, s.inter), **bf)
+        xf = torch.empty_like(h)
+        logits = torch.empty((1, s.vocab), **bf)
         part = torch.empty_like(h) if (self.tp and exch is None) else None
-        tok = torch.empty(1, dtype=torch.int32, device=dev)
-        posd = torch.empty(1, dtype=torch.int32, device=dev)
+        tok = torch.full((1,), nxt, dtype=torch.int32, device=dev)
+        posd = torch.full((1,), pos, dtype=torch.int32, device=dev)
         rope_tab = self.rope_table(cap)
-        qkv_cols = (Hq + 2 * H) * D
-        while len(out) < max_tokens and nxt not in self.eos:
-            out.append(nxt)
-            tok.fill_(nxt)
-            posd.fill_(pos)
+        attn_ws = self._attn_workspace(1, cap)
+
+        def step():  # token tok at position posd -> next token in tok, posd + 1
             ops.embed(self.w.embed, tok, None, h)
-            Kc, Vc = K[:, :, :pos + 1], V[:, :, :pos + 1]
             x_ready = False
             for li in range(L):
                 lw = self.w.layers[li]
                 if not x_ready:
                     ops.rmsnorm(h, lw.ln1, s.rms_eps, out=x)
-                # the cache slice of this layer as [H, cap, D] (positions < cap)
-                ops.qkv_rope(x, lw.w_qkv, lw.b_qkv, 1, 0, qkv_cols, Hq, H, D, posd, rope_tab, q_out=q,
-                             k_cache=K[li], v_cache=V[li])
-                ops.attention(q, K[li], V[li], posd, attn, m=1, workspace=self._attn_workspace(1, cap))
+                # q, and k / v into this layer's cache [H, cap, D] at position posd
+                ops.gemv_qkv_rope(x, lw.w_qkv, lw.b_qkv, Hq, H, D, posd, rope_tab, q, K[li], V[li])
+                ops.attention(q, K[li], V[li], posd, attn, m=1, workspace=attn_ws)
                 x_ready = self._block_tail(li, attn, h, x, act, part, 1, exch, 0)
-            del Kc, Vc
-            xf = x if x_ready else ops.rmsnorm(h, self.w.norm, s.rms_eps)
-            nxt = int(ops.gemv(xf, self.w.lm_head).float().argmax().item())
-            pos += 1
+            last = x if x_ready else ops.rmsnorm(h, self.w.norm, s.rms_eps, out=xf)
+            ops.gemv(last, self.w.lm_head, out=logits)
+            tok.copy_(torch.argmax(logits[0]).view(1))
+            posd.add_(1)
+
+        graph = None
+        use_graph = self.tp is None and ops._TIMER is None
+        while len(out) < max_tokens and nxt not in self.eos:
+            out.append(nxt)
+            if graph is not None:
+                graph.replay()
+            else:
+                step()
+                if use_graph and len(out) < max_tokens:
+                    try:
+                        g = torch.cuda.CUDAGraph()
+                        with torch.cuda.graph(g):
+                            step()
+                        graph = g
+                    except RuntimeError:
+                        use_graph = False  # capture refused: keep stepping eagerly
+            nxt = int(tok.item())
         return out
 
     def last_logprobs(self, result: PrefillResult) -> np.ndarray:

@@ -216,6 +216,26 @@ CKV_API int ckv_embed(const uint16_t* table, int vocab, int hidden, const int32_
 CKV_API int ckv_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows, int hidden,
                 float eps, ckv_stream_t stream);
 
+/* ---- decode projections, m <= 8 rows (greedy decode, torch_engine.py:180-198) ------
+ * One warp per weight row (row pair for RoPE), the weight streamed once; same epilogues
+ * and rounding points as ckv_linear_residual / ckv_linear_swiglu / ckv_qkv_rope:
+ *   ckv_gemv_residual   h[m][n] = bf16(h + bf16(x W^T))
+ *   ckv_gemv_swiglu     out[m][j] = bf16(bf16(silu(bf16(g))) * bf16(u)), gate/up rows
+ *                       interleaved in 128-row blocks as for ckv_linear_swiglu
+ *   ckv_gemv_qkv_rope   all q, k, v columns of w_qkv (rows q | k | v) with bias; RoPE at
+ *                       positions[m] from rope_table [rope_max_pos][head_dim/2] (cos, sin);
+ *                       q -> q_out [m][Hq*D], k / v -> caches [Hk][n_ctx][D] at the row's
+ *                       position (an out-of-range position is skipped and recorded). */
+CKV_API int ckv_gemv_residual(const uint16_t* x, const uint16_t* w, uint16_t* h, int m, int n, int k,
+                              ckv_stream_t stream);
+CKV_API int ckv_gemv_swiglu(const uint16_t* x, const uint16_t* w_gate_up, uint16_t* out, int m,
+                            int inter, int k, ckv_stream_t stream);
+CKV_API int ckv_gemv_qkv_rope(const uint16_t* x, const uint16_t* w_qkv, const uint16_t* b_qkv, int m,
+                              int k, int n_q_heads, int n_kv_heads, int head_dim,
+                              const int32_t* positions, const float* rope_table, int rope_max_pos,
+                              uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache, int n_ctx,
+                              ckv_stream_t stream);
+
 /* ---- tensor parallel over NVLink peer memory (no collective library) ------------
  * The o_proj / down_proj row-parallel GEMM and the following all-reduce + residual add
  * (torch_engine.py:70-76), split over `ranks` GPUs (one process each):

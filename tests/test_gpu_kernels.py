@@ -406,6 +406,47 @@ def test_linear_residual_and_swiglu():
     assert rel_err(out, ref2) <= 1e-2
 
 
+@pytest.mark.parametrize("m", [1, 3, 8])
+def test_decode_gemv_epilogues_match_the_gemm_path(m):
+    """ckv_gemv_residual / _swiglu / _qkv_rope (m <= 8) against the tcgen05 GEMM entry points
+    with the same epilogues, and against fp32 references."""
+    from chunkkv_b200.engine.weights import interleave_gate_up
+
+    hid, inter, Hq, H, D, N = 896, 1024, 7, 1, 128, 300
+    g = torch.Generator(device=DEV).manual_seed(m)
+    x = torch.randn((m, hid), generator=g, device=DEV).to(BF)
+    a = torch.randn((m, inter), generator=g, device=DEV).to(BF)
+    w = (torch.randn((hid, inter), generator=g, device=DEV) * 0.02).to(BF)
+    h = torch.randn((m, hid), generator=g, device=DEV).to(BF)
+    h1, h2 = h.clone(), h.clone()
+    ops.gemv_residual(a, w, h1)
+    ops.linear_residual(a, w, h2)
+    ref = h.float() + (a.float() @ w.float().T).to(BF).float()
+    assert rel_err(h1, ref) <= 1e-2 and rel_err(h1, h2) <= 1e-2
+    wg = (torch.randn((inter, hid), generator=g, device=DEV) * 0.02).to(BF)
+    wu = (torch.randn((inter, hid), generator=g, device=DEV) * 0.02).to(BF)
+    wgu = interleave_gate_up(wg, wu)
+    o1 = torch.empty((m, inter), dtype=BF, device=DEV)
+    o2 = torch.empty_like(o1)
+    ops.gemv_swiglu(x, wgu, o1)
+    ops.linear_swiglu(x, wgu, o2)
+    ref2 = (F.silu((x.float() @ wg.float().T).to(BF)) * (x.float() @ wu.float().T).to(BF)).float()
+    assert rel_err(o1, ref2) <= 1e-2 and rel_err(o1, o2) <= 1e-2
+    cols = (Hq + 2 * H) * D
+    wq = (torch.randn((cols, hid), generator=g, device=DEV) * 0.05).to(BF)
+    bq = (torch.randn(cols, generator=g, device=DEV) * 0.05).to(BF)
+    pos = torch.randperm(N, generator=g, device=DEV)[:m].sort().values.to(torch.int32)
+    tab = ops.rope_table(inv_freq(D), 512)
+    q1, q2 = torch.empty((m, Hq * D), dtype=BF, device=DEV), torch.empty((m, Hq * D), dtype=BF, device=DEV)
+    K1, V1 = torch.zeros((H, N, D), dtype=BF, device=DEV), torch.zeros((H, N, D), dtype=BF, device=DEV)
+    K2, V2 = K1.clone(), V1.clone()
+    ops.gemv_qkv_rope(x, wq, bq, Hq, H, D, pos, tab, q1, K1, V1)
+    ops.qkv_rope(x, wq, bq, m, 0, cols, Hq, H, D, pos, tab, q_out=q2, k_cache=K2, v_cache=V2)
+    assert rel_err(q1, q2) <= 1e-2
+    assert rel_err(K1[:, pos.long()], K2[:, pos.long()]) <= 1e-2
+    assert rel_err(V1[:, pos.long()], V2[:, pos.long()]) <= 1e-2
+
+
 @pytest.mark.parametrize("Hq,H,D,hid", [(28, 4, 128, 512), (14, 2, 64, 896), (4, 2, 64, 256),
                                         (5, 1, 128, 5120)])
 def test_qkv_rope_scatter_and_compact(Hq, H, D, hid):
