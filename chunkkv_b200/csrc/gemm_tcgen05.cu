@@ -28,19 +28,20 @@ namespace ckv {
 namespace {
 
 constexpr int BM = 128, BK = 64, UMMA_K = 16;
-constexpr int STAGES = 4;
 constexpr int kThreads = 192;
 constexpr uint32_t A_BYTES = BM * BK * 2;  // 16 KiB
 constexpr uint32_t TMEM_COLS = 512;        // two accumulators of up to 256 columns
 
 // N-tile width: 256, or 224 / 208 when that fills the SMs better (e.g. 3584 columns at
 // M = 938: 144 tiles of 208 in one wave instead of 112 of 256 on 148 SMs).
-template <int BN>
+template <int BN, int ST = 4>
 struct GCfg {
   static_assert(BN % 16 == 0 && BN <= 256, "BN");
   static constexpr uint32_t B_BYTES = BN * BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = ST;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+  static_assert(SMEM_BYTES <= 227 * 1024, "stages do not fit in shared memory");
   static constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN);
 };
 
@@ -245,12 +246,13 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
     if (global_ns() - t0 > kWaitLimitNs) break;
 }
 
-template <int EPI, int HD, int BN>
+template <int EPI, int HD, int BN, int ST>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 int M, int N, int K, EpiParams ep) {
-  using C = GCfg<BN>;
+  using C = GCfg<BN, ST>;
   constexpr uint32_t B_BYTES = C::B_BYTES, STAGE_BYTES = C::STAGE_BYTES, IDESC = C::IDESC;
+  constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -434,7 +436,7 @@ int make_map(CUtensorMap* map, const void* ptr, int rows, int k, int64_t ld, int
   return CKV_OK;
 }
 
-template <int EPI, int HD, int BN>
+template <int EPI, int HD, int BN, int ST = 4>
 int launch_bn(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, int M, int N, int K,
               const EpiParams& ep, cudaStream_t stream, const char* name) {
   CKV_REQUIRE(a && b, "%s: null operand", name);
@@ -447,11 +449,11 @@ int launch_bn(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, in
   CUtensorMap ma, mb;
   if (int rc = make_map(&ma, a, M, K, lda, BM)) return rc;
   if (int rc = make_map(&mb, b, N, K, ldb, BN)) return rc;
-  auto kern = gemm_kernel<EPI, HD, BN>;
-  if (int rc = set_smem_limit(reinterpret_cast<const void*>(kern), GCfg<BN>::SMEM_BYTES)) return rc;
+  auto kern = gemm_kernel<EPI, HD, BN, ST>;
+  if (int rc = set_smem_limit(reinterpret_cast<const void*>(kern), GCfg<BN, ST>::SMEM_BYTES)) return rc;
   const int tiles = ceil_div(M, BM) * ceil_div(N, BN);
   const int grid = std::min(tiles, num_sms());
-  kern<<<grid, kThreads, GCfg<BN>::SMEM_BYTES, stream>>>(ma, mb, M, N, K, ep);
+  kern<<<grid, kThreads, GCfg<BN, ST>::SMEM_BYTES, stream>>>(ma, mb, M, N, K, ep);
   CKV_LAUNCH_CHECK(name);
   return CKV_OK;
 }
@@ -470,8 +472,15 @@ int launch(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, int M
   if constexpr (EPI == EPI_STORE || EPI == EPI_RESID || EPI == EPI_PARTIAL) {
     if (M > 0) {
       const int64_t m256 = makespan(M, N, 256), m224 = makespan(M, N, 224), m208 = makespan(M, N, 208);
-      if (m208 < m224 && m208 < m256) return launch_bn<EPI, HD, 208>(a, lda, b, ldb, M, N, K, ep, stream, name);
-      if (m224 < m256) return launch_bn<EPI, HD, 224>(a, lda, b, ldb, M, N, K, ep, stream, name);
+      // a long K loop (one tile per SM for a long time) gains from a fifth stage in flight;
+      // a short one loses (less L1 left for the epilogue): measured at K = 18944 / 3584
+      const bool deep = K >= 8192;
+      if (m208 < m224 && m208 < m256)
+        return deep ? launch_bn<EPI, HD, 208, 5>(a, lda, b, ldb, M, N, K, ep, stream, name)
+                    : launch_bn<EPI, HD, 208, 4>(a, lda, b, ldb, M, N, K, ep, stream, name);
+      if (m224 < m256)
+        return deep ? launch_bn<EPI, HD, 224, 5>(a, lda, b, ldb, M, N, K, ep, stream, name)
+                    : launch_bn<EPI, HD, 224, 4>(a, lda, b, ldb, M, N, K, ep, stream, name);
     }
   }
   return launch_bn<EPI, HD, 256>(a, lda, b, ldb, M, N, K, ep, stream, name);
