@@ -28,6 +28,12 @@
 // (ex2.approx, 16 results per clock per SM: alone as slow as the tensor core) and a
 // polynomial on the FMA pipe (one pair in four).  Every wait is bounded
 // (ckv_common.cuh).
+// The kernel is persistent: one CTA per SM runs work items (row block, KV head, key
+// split) one after another on the same TMEM allocation and barriers.  The producer warp
+// claims items from a counter in the workspace and publishes them through a small ring
+// in shared memory; a softmax warpgroup loads the next item's Q as soon as its last S
+// MMA of the current item is done, so the next item's first S MMA overlaps this item's
+// last P V and its epilogue.
 #include <algorithm>
 #include <mutex>
 #include <vector>
@@ -58,7 +64,7 @@ struct Cfg {
   static constexpr uint32_t Q_BYTES = BM * HD * 2;
   static constexpr uint32_t KV_TILE = BN * HD * 2;
   // at least 120 KiB so two CTAs never share an SM: each allocates all 512 TMEM columns
-  static constexpr uint32_t SMEM_NEED = 1024 + NQ * Q_BYTES + (KS + VS) * KV_TILE + 256;
+  static constexpr uint32_t SMEM_NEED = 1024 + NQ * Q_BYTES + (KS + VS) * KV_TILE + 512;
   static constexpr uint32_t SMEM = SMEM_NEED > 120 * 1024 ? SMEM_NEED : 120 * 1024;
   static constexpr uint32_t IDESC_S = umma_idesc_bf16(BM, BN);
   static constexpr uint32_t IDESC_PV = umma_idesc_bf16(BM, HD) | (1u << 16);  // B MN-major
@@ -106,14 +112,28 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   return d;
 }
 
+// Work items: (row block rb, KV head hk, key split z).  Slot k of the item list is
+// z-major, then head, then row block from the last (longest) one down, so items go
+// out roughly longest first.  A slot whose split lies past its block's last key tile
+// is empty and skipped.
+struct Item {
+  int rb, hk, split, n_split, kt0, n_kt, pad0, pad1;  // rb < 0: no more work
+};
+constexpr int kItemSlots = 4;  // ring of items published by the producer warp
+
 // 10 warps: two of the four SM sub-partitions hold three warps, so the register
 // file allows at most 16384 / (3 * 32) = 170 registers per thread.
+// Persistent: one CTA per SM keeps its TMEM, barriers and pipeline across items.  With
+// `sched` (two zeroed words: next slot, CTAs done) CTAs take slots from an atomic
+// counter, and the last CTA to run out of work sets both words back to 0; without it
+// CTA c takes slots c, c + gridDim.x, ...
 template <int HD>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                         const uint16_t* __restrict__ q, const int32_t* __restrict__ positions,
                         uint16_t* __restrict__ out, int M, int Hq, int Hk, int n_ctx, float scale_log2,
-                        int tps, int max_splits, float* __restrict__ part_o, float2* __restrict__ part_ml) {
+                        int tps, int max_splits, int blocks, unsigned* __restrict__ sched,
+                        float* __restrict__ part_o, float2* __restrict__ part_ml) {
   using C = Cfg<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -121,28 +141,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sQ = smem;                      // [NQ][Q_BYTES]
   uint8_t* sK = sQ + NQ * C::Q_BYTES;      // [KS][KV_TILE]
   uint8_t* sV = sK + KS * C::KV_TILE;      // [VS][KV_TILE]
-  uint64_t* k_full = reinterpret_cast<uint64_t*>(sV + VS * C::KV_TILE);
+  Item* items = reinterpret_cast<Item*>(sV + VS * C::KV_TILE);  // [kItemSlots]
+  uint64_t* k_full = reinterpret_cast<uint64_t*>(items + kItemSlots);
   uint64_t* k_empty = k_full + KS;
   uint64_t* v_full = k_empty + KS;
   uint64_t* v_empty = v_full + VS;
   uint64_t* s_full = v_empty + VS;  // [NQ]
   uint64_t* p_full = s_full + NQ;   // [NQ]
   uint64_t* o_done = p_full + NQ;   // [NQ]
-  uint64_t* q_ready = o_done + NQ;
-  uint64_t* o_full = q_ready + 1;
+  uint64_t* q_ready = o_done + NQ;  // [NQ]
+  uint64_t* turn = q_ready + NQ;    // [NQ]: softmax warpgroup w may run its next tile
+  uint64_t* item_full = turn + NQ;  // [kItemSlots]
+  uint64_t* item_empty = item_full + kItemSlots;  // [kItemSlots]
+  uint64_t* o_full = item_empty + kItemSlots;
   uint64_t* drain = o_full + 1;
-  uint64_t* turn = drain + 1;  // [NQ]: softmax warpgroup w may run its next tile
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(turn + NQ);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* s_maxpos = reinterpret_cast<int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = Hq / Hk;
   const int T = BM / G;  // tokens per Q tile
-  const int hk = blockIdx.y;
-  const int rb = gridDim.x - 1 - blockIdx.x;  // late (long) blocks first
-  const int t0 = rb * NQ * T;
-  const int n_tok = min(NQ * T, M - t0);
+  const int n_slots = blocks * Hk * max_splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < KS; ++s) {
@@ -157,34 +176,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s_full[w], 1);
       mbar_init(&p_full[w], 128);
       mbar_init(&o_done[w], 1);
+      mbar_init(&q_ready[w], 128);
       mbar_init(&turn[w], 128);
     }
-    mbar_init(q_ready, NQ * 128);
+    for (int s = 0; s < kItemSlots; ++s) {
+      mbar_init(&item_full[s], 1);
+      mbar_init(&item_empty[s], 1 + NQ * 4);  // the MMA thread and each softmax warp
+    }
     mbar_init(o_full, 1);
     mbar_init(drain, 1);
     *abort = 0;
-    *s_maxpos = 0;
     fence_barrier_init();
     fence_async_smem();
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < n_tok; i += kThreads) {
-    int p = positions[t0 + i];
-    if (p < 0 || p >= n_ctx) {
-      atomicOr(&g_err_word, CKV_DEV_ERR_POSITION_RANGE);
-      p = p < 0 ? 0 : n_ctx - 1;
-    }
-    atomicMax(s_maxpos, p);
-  }
-  __syncthreads();
-  // key tiles 0..max position, cut into splits of `tps` tiles (blockIdx.z = split)
-  const int n_kt_all = (*s_maxpos + BN) / BN;
-  const int n_split = (n_kt_all + tps - 1) / tps;
-  const int split = blockIdx.z;
-  if (split >= n_split) return;  // whole CTA leaves before touching TMEM
-  const int kt0 = split * tps;
-  const int n_kt = min(tps, n_kt_all - kt0);  // tiles of this CTA: kt0 .. kt0 + n_kt - 1
-  if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
   }
@@ -195,36 +198,105 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == kWarpTma) {
-    // ---------------------------------------------------------------- TMA producer
-    if (lane == 0) {
-      int nk = 0, nv = 0;  // tiles whose K / V load was issued
-      for (int j = 0; j < n_kt; ++j) {
-        const int sk = j % KS, sv = j % VS;
-        if (!mbar_wait(&k_empty[sk], ((j / KS) & 1) ^ 1, abort, &g_err_word)) break;
-        mbar_expect_tx(&k_full[sk], C::KV_TILE);
+    // ------------------------------------------- item scheduler + TMA producer (one warp)
+    int it = 0;          // items published
+    int nk = 0, nv = 0;  // K / V tile loads issued (all items)
+    int cursor = blockIdx.x;
+    bool ok = true;
+    while (ok) {
+      // next non-empty slot: the warp reads the block's positions for its last key tile
+      Item rec{-1, 0, 0, 0, 0, 0, 0, 0};
+      while (true) {
+        int slot = cursor;
+        if (sched != nullptr) {
+          if (lane == 0) slot = int(atomicAdd(&sched[0], 1u));
+          slot = __shfl_sync(0xffffffffu, slot, 0);
+        } else {
+          cursor += gridDim.x;
+        }
+        if (slot >= n_slots) break;
+        const int z = slot / (Hk * blocks);
+        const int rem = slot - z * (Hk * blocks);
+        const int hk = rem / blocks;
+        const int rb = blocks - 1 - (rem - hk * blocks);
+        const int t0 = rb * NQ * T;
+        const int n_tok = min(NQ * T, M - t0);
+        int mx = 0;
+        for (int i = lane; i < n_tok; i += 32) {
+          int p = positions[t0 + i];
+          if (p < 0 || p >= n_ctx) {
+            if (z == 0 && hk == 0) atomicOr(&g_err_word, CKV_DEV_ERR_POSITION_RANGE);
+            p = p < 0 ? 0 : n_ctx - 1;
+          }
+          mx = max(mx, p);
+        }
 #pragma unroll
-        for (int a = 0; a < C::ATOMS; ++a)
-          tma_load_3d(sK + sk * C::KV_TILE + a * ATOM_BYTES, &tmK, a * 64, (kt0 + j) * BN, hk, &k_full[sk]);
-        ++nk;
-        if (!mbar_wait(&v_empty[sv], ((j / VS) & 1) ^ 1, abort, &g_err_word)) break;
-        mbar_expect_tx(&v_full[sv], C::KV_TILE);
-#pragma unroll
-        for (int a = 0; a < C::ATOMS; ++a)
-          tma_load_3d(sV + sv * C::KV_TILE + a * ATOM_BYTES, &tmV, a * 64, (kt0 + j) * BN, hk, &v_full[sv]);
-        ++nv;
+        for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const int kt_all = mx / BN + 1;  // key tiles 0 .. last visible key
+        const int n_split = (kt_all + tps - 1) / tps;
+        if (z < n_split) {
+          rec = Item{rb, hk, z, n_split, z * tps, min(tps, kt_all - z * tps), 0, 0};
+          break;
+        }
       }
-      if (nv < n_kt) {  // aborted: let the copies already issued land
+      // publish (a record with rb < 0 tells the consumers to stop), then load its tiles
+      if (lane == 0) {
+        const int s = it % kItemSlots;
+        if (mbar_wait(&item_empty[s], ((it / kItemSlots) & 1) ^ 1, abort, &g_err_word)) {
+          items[s] = rec;
+          mbar_arrive(&item_full[s]);
+        } else {
+          ok = false;
+        }
+        for (int j = 0; j < rec.n_kt && ok && rec.rb >= 0; ++j) {
+          const int gk = nk;
+          if (!mbar_wait(&k_empty[gk % KS], ((gk / KS) & 1) ^ 1, abort, &g_err_word)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&k_full[gk % KS], C::KV_TILE);
+#pragma unroll
+          for (int a = 0; a < C::ATOMS; ++a)
+            tma_load_3d(sK + (gk % KS) * C::KV_TILE + a * ATOM_BYTES, &tmK, a * 64, (rec.kt0 + j) * BN, rec.hk,
+                        &k_full[gk % KS]);
+          ++nk;
+          const int gv = nv;
+          if (!mbar_wait(&v_empty[gv % VS], ((gv / VS) & 1) ^ 1, abort, &g_err_word)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&v_full[gv % VS], C::KV_TILE);
+#pragma unroll
+          for (int a = 0; a < C::ATOMS; ++a)
+            tma_load_3d(sV + (gv % VS) * C::KV_TILE + a * ATOM_BYTES, &tmV, a * 64, (rec.kt0 + j) * BN, rec.hk,
+                        &v_full[gv % VS]);
+          ++nv;
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (rec.rb < 0) break;
+      ++it;
+    }
+    if (lane == 0) {
+      if (!ok) {  // aborted: let the copies already issued land
         for (int i = (nk > KS ? nk - KS : 0); i < nk; ++i) drain_wait(&k_full[i % KS], (i / KS) & 1);
         for (int i = (nv > VS ? nv - VS : 0); i < nv; ++i) drain_wait(&v_full[i % VS], (i / VS) & 1);
+      }
+      if (sched != nullptr) {
+        // every CTA arrives here once, after its last claim on the slot counter; the
+        // last one leaves both words at 0 for the next launch
+        if (atomicAdd(&sched[1], 1u) == gridDim.x - 1) {
+          atomicExch(&sched[0], 0u);
+          atomicExch(&sched[1], 0u);
+        }
       }
     }
   } else if (warp == kWarpMma) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      bool ok = mbar_wait(q_ready, 0, abort, &g_err_word);
-      auto issue_s = [&](int w, int j) {
+      auto issue_s = [&](int w, int gt) {
         const uint32_t q0 = smem_u32(sQ + w * C::Q_BYTES);
-        const uint32_t k0 = smem_u32(sK + (j % KS) * C::KV_TILE);
+        const uint32_t k0 = smem_u32(sK + (gt % KS) * C::KV_TILE);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
@@ -233,213 +305,287 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_commit(&s_full[w]);
       };
-      auto issue_pv = [&](int w, int j) {
-        const uint32_t v0 = smem_u32(sV + (j % VS) * C::KV_TILE);
+      auto issue_pv = [&](int w, int gt, bool first) {
+        const uint32_t v0 = smem_u32(sV + (gt % VS) * C::KV_TILE);
         const uint32_t pbuf = tmem + w * BN;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
           tc_mma_f16_ts(tmem + O_COL + w * 128, pbuf + kk * 8, umma_desc_sw128_mn(v0 + kk * 16 * 128, ATOM_BYTES),
-                        C::IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+                        C::IDESC_PV, (!first || kk > 0) ? 1u : 0u);
         tc_commit(&o_done[w]);
       };
-      if (ok && mbar_wait(&k_full[0], 0, abort, &g_err_word)) {
-        tc_fence_after();
-        for (int w = 0; w < NQ; ++w) issue_s(w, 0);
-        tc_commit(&k_empty[0]);
-      } else {
-        ok = false;
-      }
-      for (int j = 0; j < n_kt && ok; ++j) {
-        const int nxt = j + 1;
+      bool ok = true;
+      int g = 0;  // key tiles consumed (all items)
+      for (int it = 0; ok; ++it) {
+        const int s = it % kItemSlots;
+        if (!mbar_wait(&item_full[s], (it / kItemSlots) & 1, abort, &g_err_word)) {
+          ok = false;
+          break;
+        }
+        const int n_kt = items[s].rb < 0 ? -1 : items[s].n_kt;
+        mbar_arrive(&item_empty[s]);
+        if (n_kt < 0) break;
+        // S of the first tile, per Q tile as soon as that tile's Q is in smem
+        if (!mbar_wait(&k_full[g % KS], (g / KS) & 1, abort, &g_err_word)) {
+          ok = false;
+          break;
+        }
         for (int w = 0; w < NQ && ok; ++w) {
-          if (!mbar_wait(&p_full[w], j & 1, abort, &g_err_word) ||
-              (w == 0 && !mbar_wait(&v_full[j % VS], (j / VS) & 1, abort, &g_err_word))) {
+          if (!mbar_wait(&q_ready[w], it & 1, abort, &g_err_word)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_pv(w, j);
-          if (w == NQ - 1) tc_commit(&v_empty[j % VS]);
-          if (nxt < n_kt) {
-            if (w == 0 && !mbar_wait(&k_full[nxt % KS], (nxt / KS) & 1, abort, &g_err_word)) {
+          issue_s(w, g);
+        }
+        if (!ok) break;
+        tc_commit(&k_empty[g % KS]);
+        for (int j = 0; j < n_kt && ok; ++j) {
+          const int gt = g + j, nxt = gt + 1;
+          for (int w = 0; w < NQ && ok; ++w) {
+            if (!mbar_wait(&p_full[w], gt & 1, abort, &g_err_word) ||
+                (w == 0 && !mbar_wait(&v_full[gt % VS], (gt / VS) & 1, abort, &g_err_word))) {
               ok = false;
               break;
             }
             tc_fence_after();
-            issue_s(w, nxt);
-            if (w == NQ - 1) tc_commit(&k_empty[nxt % KS]);
+            issue_pv(w, gt, j == 0);
+            if (w == NQ - 1) tc_commit(&v_empty[gt % VS]);
+            if (j + 1 < n_kt) {
+              if (w == 0 && !mbar_wait(&k_full[nxt % KS], (nxt / KS) & 1, abort, &g_err_word)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_s(w, nxt);
+              if (w == NQ - 1) tc_commit(&k_empty[nxt % KS]);
+            }
           }
         }
+        if (ok) tc_commit(o_full);
+        g += n_kt;
       }
-      if (ok) {
-        tc_commit(o_full);
-      } else {
+      if (!ok) {
         tc_commit(drain);
         drain_wait(drain, 0);
       }
     }
-  } else if (warp < kWarpTma) {
+  } else {
     // ------------------------------------------------- softmax / correction / epilogue
     const int w = warp >> 2;         // Q tile of this warpgroup
     const int sub = warp & 3;        // TMEM sub-partition (lanes 32*sub .. +31)
     const int r = sub * 32 + lane;   // row in the Q tile == TMEM lane
-    const int tr = r / G, g = r - (r / G) * G;
-    const int tt = w * T + tr;       // token index in the CTA
-    const bool valid = r < T * G && tt < n_tok;
-    const int tok = t0 + (valid ? tt : 0);
-    // padding rows see every key: they never force the masked path on their warp
-    int pos = n_ctx - 1;
-    if (valid) pos = min(max(positions[tok], 0), n_ctx - 1);
-    const uint16_t* qrow = q + (int64_t(tok) * Hq + hk * G + g) * HD;
-    uint8_t* myQ = sQ + w * C::Q_BYTES;
-#pragma unroll
-    for (int c = 0; c < HD / 8; ++c) {
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (valid) v = *reinterpret_cast<const uint4*>(qrow + c * 8);
-      *reinterpret_cast<uint4*>(myQ + (c >> 3) * ATOM_BYTES + sw128(r, c & 7)) = v;
-    }
-    fence_async_smem();
-    mbar_arrive(q_ready);
-
+    const int tr = r / G, g_head = r - (r / G) * G;
     const uint32_t lane_base = tmem + (uint32_t(sub * 32) << 16);
     const uint32_t sbuf = lane_base + w * BN;
     const uint32_t obuf = lane_base + O_COL + w * 128;
-    float m = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_kt; ++j) {
-      if (!warp_wait(&s_full[w], j & 1, abort)) {
-        ok = false;
-        break;
+    uint8_t* myQ = sQ + w * C::Q_BYTES;
+
+    // item `it` from the ring; every lane reads it, one lane per warp releases the slot
+    auto take = [&](int it, Item& rec) -> bool {
+      const int s = it % kItemSlots;
+      if (!warp_wait(&item_full[s], (it / kItemSlots) & 1, abort)) return false;
+      rec = items[s];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[s]);
+      return true;
+    };
+    // this thread's row of an item: token, its position, whether the row is real
+    struct Row {
+      int tok, pos;
+      bool valid;
+    };
+    auto row_of = [&](const Item& rec) -> Row {
+      const int t0 = rec.rb * NQ * T;
+      const int n_tok = min(NQ * T, M - t0);
+      const int tt = w * T + tr;  // token index in the item
+      Row x;
+      x.valid = r < T * G && tt < n_tok;
+      x.tok = t0 + (x.valid ? tt : 0);
+      // padding rows see every key: they never force the masked path on their warp
+      x.pos = n_ctx - 1;
+      if (x.valid) x.pos = min(max(positions[x.tok], 0), n_ctx - 1);
+      return x;
+    };
+    // Q rows of an item into this warpgroup's smem tile (its previous S MMAs are done)
+    auto load_q = [&](const Item& rec, const Row& x) {
+      const uint16_t* qrow = q + (int64_t(x.tok) * Hq + rec.hk * G + g_head) * HD;
+#pragma unroll
+      for (int c = 0; c < HD / 8; ++c) {
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (x.valid) v = *reinterpret_cast<const uint4*>(qrow + c * 8);
+        *reinterpret_cast<uint4*>(myQ + (c >> 3) * ATOM_BYTES + sw128(r, c & 7)) = v;
       }
-      // the two warpgroups take turns (0, 1, 0, 1, ...): each runs its softmax alone on
-      // the SM sub-partitions while the tensor core works on the other Q tile
-      if ((w == 1 || j > 0) && !warp_wait(&turn[w], (w == 0 ? j - 1 : j) & 1, abort)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const int lim = pos - (kt0 + j) * BN;  // keys at index > lim are masked
-      const bool full = __all_sync(0xffffffffu, lim >= BN - 1);  // whole tile visible to the warp
-      // pass 1: row max of the raw scores (scale > 0 commutes with max), 64 columns at a
-      // time, 8 chains of 3-input max
-      float mx8[8];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) mx8[c] = -INFINITY;
-#pragma unroll
-      for (int h = 0; h < BN / 64; ++h) {
-        uint32_t u[64];
-        tmem_ld64w(sbuf + 64 * h, u);
-        if (!full) {
-#pragma unroll
-          for (int e = 0; e < 64; ++e)
-            if (64 * h + e > lim) u[e] = __float_as_uint(-INFINITY);
+      fence_async_smem();
+      mbar_arrive(&q_ready[w]);
+    };
+
+    Item cur;
+    bool ok = take(0, cur);
+    Row row{0, 0, false};
+    if (ok && cur.rb >= 0) {
+      row = row_of(cur);
+      load_q(cur, row);
+    }
+    int g = 0;  // key tiles consumed (all items)
+    for (int it = 0; ok && cur.rb >= 0; ++it) {
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < cur.n_kt; ++j) {
+        const int gt = g + j;
+        if (!warp_wait(&s_full[w], gt & 1, abort)) {
+          ok = false;
+          break;
         }
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-#pragma unroll
-          for (int c = 0; c < 8; ++c)
-            mx8[c] = max3f(mx8[c], __uint_as_float(u[16 * k + 2 * c]), __uint_as_float(u[16 * k + 2 * c + 1]));
-      }
-      const float mx = fmaxf(max3f(mx8[0], mx8[1], mx8[2]), max3f(max3f(mx8[3], mx8[4], mx8[5]), mx8[6], mx8[7]));
-      const float m_new = fmaxf(m, mx * scale_log2);
-      const bool need = j > 0 && m_new > m + kRescaleThreshold;
-      if (__any_sync(0xffffffffu, need)) {
-        // O may be touched only after P(j-1) V(j-1) has landed
-        if (!warp_wait(&o_done[w], (j - 1) & 1, abort)) {
+        // the two warpgroups take turns (0, 1, 0, 1, ...): each runs its softmax alone on
+        // the SM sub-partitions while the tensor core works on the other Q tile
+        if ((w == 1 || gt > 0) && !warp_wait(&turn[w], (w == 0 ? gt - 1 : gt) & 1, abort)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const float corr = need ? ex2_approx(m - m_new) : 1.0f;
+        const int lim = row.pos - (cur.kt0 + j) * BN;  // keys at index > lim are masked
+        const bool full = __all_sync(0xffffffffu, lim >= BN - 1);  // whole tile visible to the warp
+        // pass 1: row max of the raw scores (scale > 0 commutes with max), 64 columns at a
+        // time, 8 chains of 3-input max
+        float mx8[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) mx8[c] = -INFINITY;
+#pragma unroll
+        for (int h = 0; h < BN / 64; ++h) {
+          uint32_t u[64];
+          tmem_ld64w(sbuf + 64 * h, u);
+          if (!full) {
+#pragma unroll
+            for (int e = 0; e < 64; ++e)
+              if (64 * h + e > lim) u[e] = __float_as_uint(-INFINITY);
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              mx8[c] = max3f(mx8[c], __uint_as_float(u[16 * k + 2 * c]), __uint_as_float(u[16 * k + 2 * c + 1]));
+        }
+        const float mx = fmaxf(max3f(mx8[0], mx8[1], mx8[2]), max3f(max3f(mx8[3], mx8[4], mx8[5]), mx8[6], mx8[7]));
+        const float m_new = fmaxf(m, mx * scale_log2);
+        const bool need = j > 0 && m_new > m + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need)) {
+          // O may be touched only after P(j-1) V(j-1) has landed
+          if (!warp_wait(&o_done[w], (gt - 1) & 1, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const float corr = need ? ex2_approx(m - m_new) : 1.0f;
+#pragma unroll 1
+          for (int c = 0; c < HD; c += 32) {
+            float o[32];
+            tmem_ld32(obuf + c, o);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] *= corr;
+            tmem_st32(obuf + c, o);
+          }
+          l *= corr;
+        }
+        if (j == 0 || need) m = m_new;
+        // pass 2: P = 2^(s*scale - m) (scale folded into one packed FFMA), 64 columns at a
+        // time, written back over S as bf16 pairs: P of keys 64h.. goes to columns 32h..,
+        // whose scores were read in the half before.  In a fully visible tile kPolyOf4
+        // pairs in four take the polynomial; masked scores are -inf and go through ex2
+        // (exactly 0).  A row that has seen no visible key yet (possible in a later key
+        // split) keeps m = -inf; the finite base keeps its P at exactly 0 instead of NaN.
+        const float neg_m = m == -INFINITY ? 0.f : -m;
+        const float2 sc2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(neg_m, neg_m);
+        float2 rs4[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) rs4[i] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int h = 0; h < BN / 64; ++h) {
+          uint32_t u[64];
+          tmem_ld64w(sbuf + 64 * h, u);
+          if (full) {
+#pragma unroll
+            for (int pr = 0; pr < 32; ++pr) {
+              const float2 x = __ffma2_rn(make_float2(__uint_as_float(u[2 * pr]), __uint_as_float(u[2 * pr + 1])), sc2, nm2);
+              const float2 pv = (pr & 3) < kPolyOf4 ? exp2_poly2(x) : make_float2(ex2_approx(x.x), ex2_approx(x.y));
+              rs4[pr & 3] = __fadd2_rn(rs4[pr & 3], pv);
+              u[pr] = pack_bf2(pv.x, pv.y);
+            }
+          } else {
+#pragma unroll
+            for (int pr = 0; pr < 32; ++pr) {
+              const float s0 = 64 * h + 2 * pr <= lim ? __uint_as_float(u[2 * pr]) : -INFINITY;
+              const float s1 = 64 * h + 2 * pr + 1 <= lim ? __uint_as_float(u[2 * pr + 1]) : -INFINITY;
+              const float2 x = __ffma2_rn(make_float2(s0, s1), sc2, nm2);
+              const float2 pv = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+              rs4[pr & 3] = __fadd2_rn(rs4[pr & 3], pv);
+              u[pr] = pack_bf2(pv.x, pv.y);
+            }
+          }
+          tmem_st32u(sbuf + 32 * h, *reinterpret_cast<const uint32_t(*)[32]>(u));
+        }
+        const float2 rsum = __fadd2_rn(__fadd2_rn(rs4[0], rs4[1]), __fadd2_rn(rs4[2], rs4[3]));
+        l += rsum.x + rsum.y;
+        tc_fence_before();
+        mbar_arrive(&p_full[w]);
+        mbar_arrive(&turn[w ^ 1]);
+      }
+      if (!ok) break;
+      g += cur.n_kt;
+      // the next item's Q goes in now (this tile's S MMAs are done), overlapping the
+      // last P V of this item and the epilogue below
+      Item nxt;
+      ok = take(it + 1, nxt);
+      Row nrow = row;
+      if (ok && nxt.rb >= 0) {
+        nrow = row_of(nxt);
+        load_q(nxt, nrow);
+      }
+      if (!ok || !warp_wait(o_full, it & 1, abort)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (cur.n_split > 1) {
+        // one slice of the keys: unnormalised O with its (max, sum), merged by the combine kernel
+        const int64_t prow =
+            (int64_t((cur.rb * Hk + cur.hk) * max_splits + cur.split)) * (NQ * BM) + w * BM + r;
+        float* po = part_o + prow * HD;
 #pragma unroll 1
         for (int c = 0; c < HD; c += 32) {
           float o[32];
           tmem_ld32(obuf + c, o);
+          if (row.valid) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] *= corr;
-          tmem_st32(obuf + c, o);
-        }
-        l *= corr;
-      }
-      if (j == 0 || need) m = m_new;
-      // pass 2: P = 2^(s*scale - m) (scale folded into one packed FFMA), 64 columns at a
-      // time, written back over S as bf16 pairs: P of keys 64h.. goes to columns 32h..,
-      // whose scores were read in the half before.  In a fully visible tile kPolyOf4
-      // pairs in four take the polynomial; masked scores are -inf and go through ex2
-      // (exactly 0).  A row that has seen no visible key yet (possible in a later key
-      // split) keeps m = -inf; the finite base keeps its P at exactly 0 instead of NaN.
-      const float neg_m = m == -INFINITY ? 0.f : -m;
-      const float2 sc2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(neg_m, neg_m);
-      float2 rs4[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) rs4[i] = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int h = 0; h < BN / 64; ++h) {
-        uint32_t u[64];
-        tmem_ld64w(sbuf + 64 * h, u);
-        if (full) {
-#pragma unroll
-          for (int pr = 0; pr < 32; ++pr) {
-            const float2 x = __ffma2_rn(make_float2(__uint_as_float(u[2 * pr]), __uint_as_float(u[2 * pr + 1])), sc2, nm2);
-            const float2 pv = (pr & 3) < kPolyOf4 ? exp2_poly2(x) : make_float2(ex2_approx(x.x), ex2_approx(x.y));
-            rs4[pr & 3] = __fadd2_rn(rs4[pr & 3], pv);
-            u[pr] = pack_bf2(pv.x, pv.y);
-          }
-        } else {
-#pragma unroll
-          for (int pr = 0; pr < 32; ++pr) {
-            const float s0 = 64 * h + 2 * pr <= lim ? __uint_as_float(u[2 * pr]) : -INFINITY;
-            const float s1 = 64 * h + 2 * pr + 1 <= lim ? __uint_as_float(u[2 * pr + 1]) : -INFINITY;
-            const float2 x = __ffma2_rn(make_float2(s0, s1), sc2, nm2);
-            const float2 pv = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-            rs4[pr & 3] = __fadd2_rn(rs4[pr & 3], pv);
-            u[pr] = pack_bf2(pv.x, pv.y);
+            for (int qd = 0; qd < 8; ++qd)
+              *reinterpret_cast<float4*>(po + c + 4 * qd) = make_float4(o[4 * qd], o[4 * qd + 1], o[4 * qd + 2], o[4 * qd + 3]);
           }
         }
-        tmem_st32u(sbuf + 32 * h, *reinterpret_cast<const uint32_t(*)[32]>(u));
+        if (row.valid) part_ml[prow] = make_float2(m, l);
+      } else {
+        const float inv = l > 0.f ? 1.0f / l : 0.f;
+        uint16_t* orow = out + (int64_t(row.tok) * Hq + cur.hk * G + g_head) * HD;
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 32) {
+          float o[32];
+          tmem_ld32(obuf + c, o);
+          if (row.valid) {
+#pragma unroll
+            for (int qd = 0; qd < 4; ++qd) {
+              uint4 v;
+              v.x = pack_bf2(o[8 * qd + 0] * inv, o[8 * qd + 1] * inv);
+              v.y = pack_bf2(o[8 * qd + 2] * inv, o[8 * qd + 3] * inv);
+              v.z = pack_bf2(o[8 * qd + 4] * inv, o[8 * qd + 5] * inv);
+              v.w = pack_bf2(o[8 * qd + 6] * inv, o[8 * qd + 7] * inv);
+              *reinterpret_cast<uint4*>(orow + c + 8 * qd) = v;
+            }
+          }
+        }
       }
-      const float2 rsum = __fadd2_rn(__fadd2_rn(rs4[0], rs4[1]), __fadd2_rn(rs4[2], rs4[3]));
-      l += rsum.x + rsum.y;
+      // O has been read: the next item's first P V (which overwrites it) is issued only
+      // after this warpgroup's next p_full
       tc_fence_before();
-      mbar_arrive(&p_full[w]);
-      mbar_arrive(&turn[w ^ 1]);
-    }
-    if (ok && n_split > 1 && warp_wait(o_full, 0, abort)) {
-      // one slice of the keys: unnormalised O with its (max, sum), merged by the combine kernel
-      tc_fence_after();
-      const int64_t prow = (int64_t((rb * Hk + hk) * max_splits + split)) * (NQ * BM) + w * BM + r;
-      float* po = part_o + prow * HD;
-#pragma unroll 1
-      for (int c = 0; c < HD; c += 32) {
-        float o[32];
-        tmem_ld32(obuf + c, o);
-        if (valid) {
-#pragma unroll
-          for (int qd = 0; qd < 8; ++qd)
-            *reinterpret_cast<float4*>(po + c + 4 * qd) = make_float4(o[4 * qd], o[4 * qd + 1], o[4 * qd + 2], o[4 * qd + 3]);
-        }
-      }
-      if (valid) part_ml[prow] = make_float2(m, l);
-    } else if (ok && warp_wait(o_full, 0, abort)) {
-      tc_fence_after();
-      const float inv = l > 0.f ? 1.0f / l : 0.f;
-      uint16_t* orow = out + (int64_t(tok) * Hq + hk * G + g) * HD;
-#pragma unroll 1
-      for (int c = 0; c < HD; c += 32) {
-        float o[32];
-        tmem_ld32(obuf + c, o);
-        if (valid) {
-#pragma unroll
-          for (int qd = 0; qd < 4; ++qd) {
-            uint4 v;
-            v.x = pack_bf2(o[8 * qd + 0] * inv, o[8 * qd + 1] * inv);
-            v.y = pack_bf2(o[8 * qd + 2] * inv, o[8 * qd + 3] * inv);
-            v.z = pack_bf2(o[8 * qd + 4] * inv, o[8 * qd + 5] * inv);
-            v.w = pack_bf2(o[8 * qd + 6] * inv, o[8 * qd + 7] * inv);
-            *reinterpret_cast<uint4*>(orow + c + 8 * qd) = v;
-          }
-        }
-      }
+      cur = nxt;
+      row = nrow;
     }
   }
 
@@ -508,18 +654,24 @@ __global__ void __launch_bounds__(kCombineWarps * 32) attention_combine_kernel(
 // Key-split plan: split only when the unsplit grid leaves SMs idle.
 struct SplitPlan {
   int tps, max_splits, blocks;
-  int64_t bytes;
+  int64_t bytes;  // partial O and (max, sum) of every split item
 };
-// Estimated makespan, in key-tile times, of a split plan with one CTA per SM at a time:
-// the list-scheduling estimate total work / SMs + half the largest CTA (CTAs go out
-// roughly largest first: late row blocks first, splits in order), plus, when split, the
-// partial O writes (about 1.3 tile times per CTA) and the combine (reading every partial
-// at the HBM rate: one tile time per 14.3 MB).  Each CTA costs its key tiles plus a
-// fixed prologue/epilogue; row block b is assumed to reach position (b + 1) / blocks *
-// n_ctx (sorted positions spread over the context, as the engine passes them).
+// The workspace starts with the scheduler's two words (next slot, CTAs done), padded to
+// 256 bytes; the split partials follow.
+constexpr int64_t kSchedBytes = 256;
+// Fixed cost of one item, in key-tile times, for the persistent kernel: its first S
+// MMA and the epilogue are only partly hidden behind the neighbouring items; a split
+// item also writes its fp32 partial O.
+constexpr double kItemCost = 0.7;
+constexpr double kSplitItemCost = 1.0;
+// Estimated makespan, in key-tile times, of a split plan: the list-scheduling estimate
+// total work / SMs + half the largest item (items go out roughly largest first), plus,
+// when split, the combine (reading every partial at the HBM rate: one tile time per
+// 14.3 MB).  Row block b is assumed to reach position (b + 1) / blocks * n_ctx (sorted
+// positions spread over the context, as the engine passes them).
 double plan_cost(int blocks, int Hk, int HD, int n_ctx, int tps, int sms) {
   const bool split = tps < ceil_div(n_ctx, BN);
-  const double cta_cost = 2.0 + (split ? 1.3 : 0.0);
+  const double cta_cost = kItemCost + (split ? kSplitItemCost : 0.0);
   double total = 0.0;
   int64_t items_all = 0;
   int max_item = 0;
@@ -566,9 +718,8 @@ SplitPlan plan_splits(int M, int Hq, int Hk, int HD, int n_ctx) {
       best_tps = tps;
     }
   }
-  // the estimate overstates what splitting gains (about twice, measured): split only when
-  // it promises at least 15 %
-  if (best > 0.85 * unsplit) best_tps = max_kt;
+  // split only when the estimate promises at least 10 %
+  if (best > 0.90 * unsplit) best_tps = max_kt;
   p.tps = best_tps;
   p.max_splits = ceil_div(max_kt, p.tps);
   p.bytes = p.max_splits > 1 ? int64_t(p.blocks) * Hk * p.max_splits * NQ * BM * (int64_t(HD) * 4 + 8) : 0;
@@ -627,17 +778,24 @@ int launch(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int3
   auto kern = attention_tc_kernel<HD>;
   if (int rc = set_smem_limit(reinterpret_cast<const void*>(kern), Cfg<HD>::SMEM)) return rc;
   SplitPlan p = plan_splits(M, Hq, Hk, HD, n_ctx);
-  if (p.max_splits > 1 && (workspace == nullptr || ws_bytes < p.bytes)) {  // no room: one split
+  // scheduler words when the workspace has room for them; split partials when it has
+  // room for those too
+  unsigned* sched = ws_bytes >= kSchedBytes ? static_cast<unsigned*>(workspace) : nullptr;
+  if (p.max_splits > 1 && ws_bytes < kSchedBytes + p.bytes) {  // no room: one split
     p.tps = ceil_div(n_ctx, BN);
     p.max_splits = 1;
   }
-  float* part_o = static_cast<float*>(workspace);
+  float* part_o = p.max_splits > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kSchedBytes)
+                                   : nullptr;
   float2* part_ml = p.max_splits > 1
                         ? reinterpret_cast<float2*>(part_o + int64_t(p.blocks) * Hk * p.max_splits * NQ * BM * HD)
                         : nullptr;
   const float sl2 = scale * 1.4426950408889634f;
-  kern<<<dim3(p.blocks, Hk, p.max_splits), kThreads, Cfg<HD>::SMEM, stream>>>(
-      mk, mv, q, positions, out, M, Hq, Hk, n_ctx, sl2, p.tps, p.max_splits, part_o, part_ml);
+  const int64_t n_slots = int64_t(p.blocks) * Hk * p.max_splits;
+  CKV_REQUIRE(n_slots < (int64_t(1) << 31) - 4 * 1024 * 1024, "ckv_attention: too many work items");
+  const int grid = int(std::min<int64_t>(n_slots, num_sms()));
+  kern<<<grid, kThreads, Cfg<HD>::SMEM, stream>>>(mk, mv, q, positions, out, M, Hq, Hk, n_ctx, sl2, p.tps,
+                                                   p.max_splits, p.blocks, sched, part_o, part_ml);
   CKV_LAUNCH_CHECK("ckv_attention");
   if (p.max_splits > 1) {
     attention_combine_kernel<HD><<<dim3(p.blocks * (NQ * BM / kCombineWarps), Hk), kCombineWarps * 32, 0, stream>>>(
@@ -657,7 +815,7 @@ extern "C" int64_t ckv_attention_workspace_size(int m, int n_q_heads, int n_kv_h
   if (m <= 0 || n_kv_heads <= 0 || n_q_heads % n_kv_heads != 0 || n_ctx <= 0 ||
       (head_dim != 64 && head_dim != 128) || n_q_heads / n_kv_heads > BM)
     return 0;
-  return plan_splits(m, n_q_heads, n_kv_heads, head_dim, n_ctx).bytes;
+  return kSchedBytes + plan_splits(m, n_q_heads, n_kv_heads, head_dim, n_ctx).bytes;
 }
 
 extern "C" int ckv_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,

@@ -118,14 +118,13 @@ class TorchEngine:
             ws = self._ws = ops.SelectWorkspace(max(n, 1024), max(n_chunks, 64), self.device)
         return ws
 
-    def _attn_workspace(self, m: int, n_ctx: int) -> torch.Tensor | None:
-        """Key-split scratch of the attention kernel, grown on demand and reused."""
+    def _attn_workspace(self, m: int, n_ctx: int) -> torch.Tensor:
+        """Scheduler words and key-split scratch of the attention kernel, zeroed once,
+        grown on demand and reused."""
         s = self.shape
         need = ops.attention_workspace_bytes(m, s.n_heads, s.n_kv, s.head_dim, n_ctx)
-        if need == 0:
-            return None
         if self._attn_ws is None or self._attn_ws.numel() < need:
-            self._attn_ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+            self._attn_ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
         return self._attn_ws
 
     def shift_keys(self, keys: torch.Tensor, delta: int) -> torch.Tensor:

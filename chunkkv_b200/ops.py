@@ -319,16 +319,31 @@ def qkv_rope(x, w_qkv, b_qkv, m, col_begin, col_end, n_q_heads, n_kv_heads, head
 
 
 def attention_workspace_bytes(m: int, n_q_heads: int, n_kv_heads: int, head_dim: int, n_ctx: int) -> int:
-    """Bytes of workspace that let ckv_attention split long rows along the keys (0: never)."""
+    """Bytes of attention workspace for a shape: 256 bytes of scheduler words, plus the
+    key-split partials when the shape benefits from splitting the keys."""
     return int(_lib.load().ckv_attention_workspace_size(m, n_q_heads, n_kv_heads, head_dim, n_ctx))
+
+
+ATTN_SCHED_BYTES = 256
+_attn_scratch: dict[torch.device, torch.Tensor] = {}
+
+
+def attention_workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    """A zeroed attention workspace of at least `nbytes`, kept per device and grown on
+    demand.  Every launch leaves its scheduler words at zero again, so the buffer is
+    reused as it is by later launches in stream order."""
+    ws = _attn_scratch.get(device)
+    if ws is None or ws.numel() < nbytes:
+        ws = _attn_scratch[device] = torch.zeros(max(nbytes, ATTN_SCHED_BYTES), dtype=torch.uint8, device=device)
+    return ws
 
 
 def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, positions: torch.Tensor,
               out: torch.Tensor, m: int | None = None, scale: float | None = None,
               flops: float = 0.0, workspace: torch.Tensor | None = None) -> torch.Tensor:
     """q/out [m, Hq, D]; caches [H, n_ctx, D]; key j visible to row i iff j <= positions[i].
-    Without `workspace` a scratch buffer is taken from torch's allocator when the
-    shape benefits from splitting the keys."""
+    `workspace` must have been zeroed once when allocated (``attention_workspace``);
+    without it the per-device scratch buffer is used."""
     _cuda(q, k_cache, v_cache, positions, out)
     H, n_ctx, D = k_cache.shape
     m = q.shape[0] if m is None else m
@@ -336,9 +351,11 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos
     scale = 1.0 / math.sqrt(D) if scale is None else scale
     need = attention_workspace_bytes(m, Hq, H, D, n_ctx)
     if workspace is None:
-        workspace = torch.empty(need, dtype=torch.uint8, device=q.device) if need else None
-    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
-    split = 0 < need <= ws_bytes  # split-KV: the attention kernel plus its combine kernel
+        workspace = attention_workspace(need, q.device)
+    ws_bytes = workspace.numel() * workspace.element_size()
+    if ws_bytes == 0:  # an empty workspace: static scheduling, no key split
+        workspace = None
+    split = ATTN_SCHED_BYTES < need <= ws_bytes  # split-KV: the attention kernel plus its combine kernel
     _run("ckv_attention", _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(positions), _ptr(out), m, Hq,
          H, D, n_ctx, float(scale), _ptr(workspace), ws_bytes, _stream(), flops=flops,
          kernels=2 if split else 1)

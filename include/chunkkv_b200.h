@@ -309,9 +309,15 @@ CKV_API int ckv_qkv_rope(const uint16_t* x, const uint16_t* w_qkv, const uint16_
  * position mask key j visible iff j <= positions[i] (torch_engine.py:68-70,157),
  * GQA n_q_heads / n_kv_heads (at most 128 query heads per KV head).
  * q/out [m][Hq][D]; caches [H][n_ctx][D]; head_dim 64 or 128.  tcgen05/TMEM kernel.
- * `workspace` (16-byte aligned, may be NULL) lets long rows be split along the keys
- * when the unsplit grid would leave SMs idle; ckv_attention_workspace_size() gives
- * the bytes that enables it (0: never split for this shape). */
+ * The kernel is persistent (one CTA per SM) and takes its work items from two
+ * scheduler words at the start of `workspace` (16-byte aligned): zero them once when
+ * the buffer is allocated; every call leaves them at zero again, so calls may reuse the
+ * buffer in stream order but must not overlap on the GPU.  Past those 256 bytes the
+ * workspace holds the partials that let long rows be split along the keys when whole
+ * rows would leave SMs idle.  ckv_attention_workspace_size() gives the bytes for both
+ * (at least 256).  With a smaller workspace the keys are not split; with NULL the
+ * items are assigned statically (CTA c takes items c, c + grid, ...).  Every schedule
+ * gives the same result up to the key split's rounding. */
 CKV_API int64_t ckv_attention_workspace_size(int m, int n_q_heads, int n_kv_heads, int head_dim,
                                              int n_ctx);
 CKV_API int ckv_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,

@@ -501,6 +501,54 @@ def test_attention_matches_masked_sdpa(Hq, H, D, N, m):
     assert rel_err(out, ref) <= 1e-2
 
 
+def _attention_case(Hq, H, D, N, m, seed, sort=True):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    q = torch.randn((m, Hq, D), generator=g, device=DEV).to(BF)
+    K = torch.randn((H, N, D), generator=g, device=DEV).to(BF)
+    V = torch.randn((H, N, D), generator=g, device=DEV).to(BF)
+    pos = torch.randperm(N, generator=g, device=DEV)[:m]
+    pos = (pos.sort().values if sort else pos).to(torch.int32)
+    return q, K, V, pos
+
+
+@pytest.mark.parametrize("Hq,H,D,N,m", [(28, 4, 128, 5248, 938), (28, 4, 128, 3000, 3000), (5, 1, 128, 9000, 2000)])
+def test_attention_schedules_agree(Hq, H, D, N, m):
+    """The persistent kernel's three schedules: slots from the workspace counter with key
+    splits, the counter without splits, and static slots (no workspace).  The two
+    unsplit ones compute every row the same way, bit for bit; the split one within
+    bf16 rounding.  Every launch leaves the scheduler words at zero."""
+    q, K, V, pos = _attention_case(Hq, H, D, N, m, seed=m)
+    if m == N:
+        pos = torch.arange(N, device=DEV, dtype=torch.int32)
+    need = ops.attention_workspace_bytes(m, Hq, H, D, N)
+    ws = torch.zeros(need, dtype=torch.uint8, device=DEV)
+    split_out, dyn_out, static_out = (torch.empty_like(q) for _ in range(3))
+    for _ in range(3):  # repeated launches reuse the same scheduler words
+        ops.attention(q, K, V, pos, split_out, workspace=ws)
+    ops.attention(q, K, V, pos, dyn_out, workspace=ws[:ops.ATTN_SCHED_BYTES])
+    ops.attention(q, K, V, pos, static_out, workspace=ws[:0])
+    torch.cuda.synchronize()
+    assert int(ws[:8].count_nonzero()) == 0
+    assert torch.equal(dyn_out, static_out)
+    mask = pos.long()[:, None] >= torch.arange(N, device=DEV)[None, :]
+    ref = F.scaled_dot_product_attention(q.float().transpose(0, 1)[None], K.float()[None], V.float()[None],
+                                         attn_mask=mask, enable_gqa=True)[0].transpose(0, 1)
+    assert rel_err(split_out, ref) <= 1e-2
+    assert rel_err(dyn_out, ref) <= 1e-2
+
+
+def test_attention_unsorted_positions():
+    """Row blocks whose positions are not sorted: each row still sees exactly its keys."""
+    Hq, H, D, N, m = 28, 4, 128, 2600, 500
+    q, K, V, pos = _attention_case(Hq, H, D, N, m, seed=7, sort=False)
+    out = torch.empty_like(q)
+    ops.attention(q, K, V, pos, out)
+    mask = pos.long()[:, None] >= torch.arange(N, device=DEV)[None, :]
+    ref = F.scaled_dot_product_attention(q.float().transpose(0, 1)[None], K.float()[None], V.float()[None],
+                                         attn_mask=mask, enable_gqa=True)[0].transpose(0, 1)
+    assert rel_err(out, ref) <= 1e-2
+
+
 # ------------------------------------------------------------- elementwise
 @pytest.mark.parametrize("hid", [64, 896, 3584, 5120])
 def test_rmsnorm_matches_reference_formula(hid):
