@@ -16,18 +16,21 @@
 //   P_w (bf16)        stored back over S_w in TMEM (two values per column)
 //   O_w += P_w V_j    tcgen05.mma with A read from TMEM, B = V tile read MN-major (the
 //                     cache stores V as [key][d], d contiguous), fp32 in TMEM
-// The two Q tiles ping-pong: while warpgroup 0 runs the softmax of tile j the tensor
-// core runs P_1 V_{j-1} and S_1(j), and the other way round.  tcgen05.mma ops of
-// one thread execute in issue order, so S_w(j+1) may be issued right after
-// P_w(j) V_j, which reads the same TMEM columns.  K and V stages are released
+// The two Q tiles interleave on the tensor core: while warpgroup 0 runs the softmax of
+// tile j the tensor core runs P_1 V_{j-1} and S_1(j), and the other way round.  The
+// warpgroups are not made to take turns: once the MMA issue is its own warp, two
+// softmax warpgroups running side by side hide each other's latencies (measured
+// 5-8 % faster than strict alternation).  tcgen05.mma ops of one thread execute in
+// issue order, so S_w(j+1) may be issued right after P_w(j) V_j, which reads the same
+// TMEM columns.  K and V stages are released
 // separately (K after both S, V after both P.V).
 // Warps: 0..3 and 4..7 = softmax / correction / epilogue of Q tiles 0 and 1,
 // 8 = TMA producer, 9 = MMA issuer + TMEM owner.  A softmax thread reads its S row
 // from TMEM twice, 64 columns at a time (row max, then exponentials), so it never
-// holds more than half a row.  The exponentials are split between the MUFU unit
-// (ex2.approx, 16 results per clock per SM: alone as slow as the tensor core) and a
-// polynomial on the FMA pipe (one pair in four).  Every wait is bounded
-// (ckv_common.cuh).
+// holds more than half a row.  The exponentials run on the MUFU unit (ex2.approx, 16
+// results per clock per SM); moving a share of them to a polynomial on the FMA pipe
+// was slower once the two warpgroups overlap (issue-bound, not MUFU-bound).  Every
+// wait is bounded (ckv_common.cuh).
 // The kernel is persistent: one CTA per SM runs work items (row block, KV head, key
 // split) one after another on the same TMEM allocation and barriers.  The producer warp
 // claims items from a counter in the workspace and publishes them through a small ring
@@ -56,7 +59,6 @@ constexpr uint32_t TMEM_COLS = 512;  // S/P of tile w at [128w, 128w+128), O of 
 constexpr uint32_t O_COL = 256;
 constexpr uint32_t ATOM_BYTES = 128 * 128;  // one [128 rows][64 bf16] swizzle-128 atom
 constexpr float kRescaleThreshold = 8.0f;   // log2 units
-constexpr int kPolyOf4 = 1;                 // exponential pairs in four on the FMA pipe
 
 template <int HD>
 struct Cfg {
@@ -85,25 +87,6 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = global_ns();
   while (!mbar_try_wait(bar, parity))
     if (global_ns() - t0 > kWaitLimitNs) break;
-}
-
-// 2^x for a pair, on the FMA pipe: x = n + f with n = round(x), f in [-0.5, 0.5];
-// 2^f by a degree-3 polynomial fitted here to 2^f on [-0.5, 0.5] (relative error
-// 7.5e-5, under 4 % of a bf16 rounding step); 2^n added to the exponent bits.  The
-// rounding uses the float add of 1.5 * 2^23.  x <= 8 on this path; x is clamped at
-// -126 so 2^n stays in range (the result is then below 2^-125, as good as 0).
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-  x.x = fmaxf(x.x, -126.f);
-  x.y = fmaxf(x.y, -126.f);
-  const float2 magic = make_float2(12582912.f, 12582912.f);
-  const float2 t = __fadd2_rn(x, magic);
-  const float2 n = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
-  const float2 f = __fadd2_rn(x, make_float2(-n.x, -n.y));
-  float2 p = __ffma2_rn(make_float2(0.05517132f, 0.05517132f), f, make_float2(0.24261054f, 0.24261054f));
-  p = __ffma2_rn(p, f, make_float2(0.69326097f, 0.69326097f));
-  p = __ffma2_rn(p, f, make_float2(0.99992812f, 0.99992812f));
-  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
-                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
 }
 
 __device__ __forceinline__ float max3f(float a, float b, float c) {
@@ -150,8 +133,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_full = s_full + NQ;   // [NQ]
   uint64_t* o_done = p_full + NQ;   // [NQ]
   uint64_t* q_ready = o_done + NQ;  // [NQ]
-  uint64_t* turn = q_ready + NQ;    // [NQ]: softmax warpgroup w may run its next tile
-  uint64_t* item_full = turn + NQ;  // [kItemSlots]
+  uint64_t* item_full = q_ready + NQ;  // [kItemSlots]
   uint64_t* item_empty = item_full + kItemSlots;  // [kItemSlots]
   uint64_t* o_full = item_empty + kItemSlots;
   uint64_t* drain = o_full + 1;
@@ -177,7 +159,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&p_full[w], 128);
       mbar_init(&o_done[w], 1);
       mbar_init(&q_ready[w], 128);
-      mbar_init(&turn[w], 128);
     }
     for (int s = 0; s < kItemSlots; ++s) {
       mbar_init(&item_full[s], 1);
@@ -436,12 +417,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        // the two warpgroups take turns (0, 1, 0, 1, ...): each runs its softmax alone on
-        // the SM sub-partitions while the tensor core works on the other Q tile
-        if ((w == 1 || gt > 0) && !warp_wait(&turn[w], (w == 0 ? gt - 1 : gt) & 1, abort)) {
-          ok = false;
-          break;
-        }
         tc_fence_after();
         const int lim = row.pos - (cur.kt0 + j) * BN;  // keys at index > lim are masked
         const bool full = __all_sync(0xffffffffu, lim >= BN - 1);  // whole tile visible to the warp
@@ -489,9 +464,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j == 0 || need) m = m_new;
         // pass 2: P = 2^(s*scale - m) (scale folded into one packed FFMA), 64 columns at a
         // time, written back over S as bf16 pairs: P of keys 64h.. goes to columns 32h..,
-        // whose scores were read in the half before.  In a fully visible tile kPolyOf4
-        // pairs in four take the polynomial; masked scores are -inf and go through ex2
-        // (exactly 0).  A row that has seen no visible key yet (possible in a later key
+        // whose scores were read in the half before.  Masked scores are -inf and give
+        // exactly 0.  A row that has seen no visible key yet (possible in a later key
         // split) keeps m = -inf; the finite base keeps its P at exactly 0 instead of NaN.
         const float neg_m = m == -INFINITY ? 0.f : -m;
         const float2 sc2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(neg_m, neg_m);
@@ -506,7 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int pr = 0; pr < 32; ++pr) {
               const float2 x = __ffma2_rn(make_float2(__uint_as_float(u[2 * pr]), __uint_as_float(u[2 * pr + 1])), sc2, nm2);
-              const float2 pv = (pr & 3) < kPolyOf4 ? exp2_poly2(x) : make_float2(ex2_approx(x.x), ex2_approx(x.y));
+              const float2 pv = make_float2(ex2_approx(x.x), ex2_approx(x.y));
               rs4[pr & 3] = __fadd2_rn(rs4[pr & 3], pv);
               u[pr] = pack_bf2(pv.x, pv.y);
             }
@@ -527,7 +501,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         l += rsum.x + rsum.y;
         tc_fence_before();
         mbar_arrive(&p_full[w]);
-        mbar_arrive(&turn[w ^ 1]);
       }
       if (!ok) break;
       g += cur.n_kt;
