@@ -43,13 +43,17 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ratio", type=float, default=0.15)
     ap.add_argument("--n-sink", type=int, default=4)
-    ap.add_argument("--workload", choices=["dp", "tp", "replay", "micro", "decode"], default="dp",
+    ap.add_argument("--workload", choices=["dp", "tp", "replay", "micro", "decode", "policies"], default="dp",
                     help="dp: config 3 (7B, one request per GPU); tp: config 5 (32B split over the GPUs "
                          "by KV head, 64x512 chunks; defaults --shape qwen2.5-32b --chunks 64 --steps 10); "
                          "replay: config 4 (256 requests over a 16x256 chunk pool, split over the GPUs); "
                          "micro: config 2 (the K/V bandwidth kernels at the 7B KV shape, one GPU); "
-                         "decode: greedy decode after the config-3 blend prefill (one GPU)")
-    ap.add_argument("--requests", type=int, default=256, help="replay: total requests over all GPUs")
+                         "decode: greedy decode after the config-3 blend prefill (one GPU); "
+                         "policies: a synthetic multi-tenant stream under P0-P4 with TTFT, compute, KL and "
+                         "greedy agreement against P0 (one GPU)")
+    ap.add_argument("--requests", type=int, default=256,
+                    help="replay: total requests over all GPUs; policies: requests per policy (default 48)")
+    ap.add_argument("--max-new", type=int, default=8, help="policies: greedy tokens per request")
     ap.add_argument("--tp-exchange", choices=["peer", "nccl"], default="peer",
                     help="tp: partial rows over NVLink peer memory (fused kernels) or NCCL all-reduce")
     ap.add_argument("--shape", default=None)
@@ -70,6 +74,8 @@ def parse():
         args.chunks = 64 if tp else 10
     if tp and "--steps" not in sys.argv:
         args.steps = 10
+    if args.workload == "policies" and "--requests" not in sys.argv:
+        args.requests = 48
     if args.workload == "replay":
         if "--ratio" not in sys.argv:
             args.ratio = 0.30
@@ -688,12 +694,13 @@ def run_replay(args):
     import torch.distributed as dist
 
     from chunkkv_b200 import _lib
-    from chunkkv_b200.engine.base import BlendConfig, Placement
     from chunkkv_b200.engine.torch_engine import TorchEngine
     from chunkkv_b200.engine.weights import SHAPES, random_packed
+    from chunkkv_b200.gate import GateConfig, ReuseGate
+    from chunkkv_b200.runtime import ChunkReuseRuntime
     from chunkkv_b200.store.keys import LookupKey, token_hash
     from chunkkv_b200.store.kvstore import Entry, KVStore
-    from chunkkv_b200.types import TrustLevel
+    from chunkkv_b200.types import ChunkedRequest, Segment, TrustLevel
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -709,29 +716,30 @@ def run_replay(args):
     pool, reqs = replay_requests(args.requests, shape.vocab)
     store = KVStore(budget_bytes=40 << 30, pool_bytes=40 << 30, device=dev)
     warm = eng.prefill(sum(pool, []))
-    keys = [LookupKey.build(c, shape.name, None) for c in pool]
-    for i, k in enumerate(keys):
-        store.put(k, Entry(warm.chunk(i * 256, (i + 1) * 256), "pool", token_hash([]), TrustLevel.SYSTEM))
+    for i, c in enumerate(pool):
+        store.put(LookupKey.build(c, shape.name, None),
+                  Entry(warm.chunk(i * 256, (i + 1) * 256), "pool", token_hash([]), TrustLevel.SYSTEM))
     del warm
     sizes = [200 + 256 * len(p) + 16 for _, p, _ in reqs]
     mine = lpt_assign(sizes, world)[rank]
-    cfg = BlendConfig(recompute_ratio=args.ratio, n_sink=args.n_sink)
+    # policy P3 of the reference's bench/policies.py: every stored chunk is blended at
+    # the fixed ratio, lookup keys without the tenant
+    gate = ReuseGate(GateConfig(mode="always_blend", ratio_same_context=args.ratio))
+    runtime = ChunkReuseRuntime(eng, shape.name, store, gate, provenance=False)
+
+    def request(i) -> ChunkedRequest:
+        prefix, picks, query = reqs[i]
+        segs = [Segment(0, "system", TrustLevel.SYSTEM, 0, list(prefix), reusable=False)]
+        tokens = list(prefix)
+        for c in picks:
+            segs.append(Segment(len(segs), "tool", TrustLevel.TOOL, len(tokens), pool[c]))
+            tokens += pool[c]
+        segs.append(Segment(len(segs), "user", TrustLevel.USER, len(tokens), list(query), reusable=False))
+        return ChunkedRequest(tokens + list(query), segs, f"tenant{i % 4}", "replay")
 
     def serve(i):
-        prefix, picks, query = reqs[i]
-        tokens, pl, segs = list(prefix), [], []
-        for c in picks:
-            entry = store.get(keys[c])[0]
-            pl.append(Placement(entry.kv, len(tokens)))
-            segs.append((c, len(tokens)))
-            tokens += pool[c]
-        tokens += query
-        res = eng.prefill(tokens, pl, cfg)
-        lp = eng.last_logprobs(res)
-        for c, st in segs:
-            store.put(keys[c], Entry(res.chunk(st, st + 256), f"req{i}", token_hash(tokens[:st]),
-                                     TrustLevel.SYSTEM))
-        return len(tokens), lp
+        out = runtime.prefill(request(i))
+        return out.stats["tokens"], eng.last_logprobs(out.result)
 
     for i in mine[:max(1, args.warmup)]:
         serve(i)
@@ -778,8 +786,9 @@ def run_replay(args):
         "steps": args.requests, "warmup": max(1, args.warmup), "ms_per_step": round(total_ms / max(1, len(mine)), 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: random-init bf16 weights (seed 0), seeded random prefixes, pool chunks and queries",
-        "config": {"workload": "BASELINE config 4: DP replay; per request store lookups, blend prefill, "
-                               "log-probs and write-back of the chunk segments (direct placements, no gate)",
+        "config": {"workload": "BASELINE config 4: DP replay through ChunkReuseRuntime with policy P3 "
+                               "(always_blend gate, provenance off): per request store lookups, gate, blend "
+                               "prefill, log-probs and write-back of the chunk segments",
                    "model": f"{args.shape} architecture, random init", "requests": args.requests,
                    "pool": "16x256", "prefix_tokens": 200, "query_tokens": 16, "recompute_ratio": args.ratio,
                    "n_sink": args.n_sink, "store_bytes_per_gpu": 40 << 30,
@@ -794,6 +803,86 @@ def run_replay(args):
         "clocks": clk.summary(),
     }
     print(json.dumps(out), flush=True)
+
+
+def policy_requests(n_req: int, vocab: int, seed: int = 11):
+    """A multi-tenant agent stream at model scale: two agents' system prompts (300
+    tokens, SYSTEM), a pool of 12 tool documents (256-512 tokens, TOOL, reusable),
+    3-6 documents per request in random order, sometimes after a user turn (which
+    lowers the trust floor of what follows), and a 32-64 token user query; four
+    tenants.  The shape of the reference's multi-agent traces, with seeded ids."""
+    from chunkkv_b200.types import ChunkedRequest, Segment, TrustLevel
+
+    rng = random.Random(seed)
+
+    def toks(k):
+        return [rng.randrange(vocab) for _ in range(k)]
+
+    systems = {"agentA": toks(300), "agentB": toks(300)}
+    docs = [toks(rng.randrange(256, 513)) for _ in range(12)]
+    out = []
+    for i in range(n_req):
+        ctx = "agentA" if rng.random() < 0.6 else "agentB"
+        segs, tokens = [], []
+
+        def add(role, trust, t, reusable=True):
+            segs.append(Segment(len(segs), role, trust, len(tokens), list(t), reusable))
+            tokens.extend(t)
+
+        add("system", TrustLevel.SYSTEM, systems[ctx])
+        if rng.random() < 0.2:
+            add("user", TrustLevel.USER, toks(24), reusable=False)
+        for d in rng.sample(range(len(docs)), rng.randint(3, 6)):
+            add("tool", TrustLevel.TOOL, docs[d])
+        add("user", TrustLevel.USER, toks(rng.randint(32, 64)), reusable=False)
+        out.append((f"r{i}", ChunkedRequest(tokens, segs, f"tenant{i % 4}", ctx)))
+    return out
+
+
+def run_policies(args):
+    """Policies P0-P4 over one engine (the reference's bench/replay.py + report.py,
+    policies of bench/policies.py): every request of the stream under each policy,
+    P0 first as the reference for KL and greedy agreement; TTFT is wall clock around
+    prefill + first-token log-probs, as the reference measures it."""
+    import torch
+
+    from chunkkv_b200.engine.torch_engine import TorchEngine
+    from chunkkv_b200.engine.weights import SHAPES, random_packed
+    from chunkkv_b200.harness import replay_policy, summarize
+    from chunkkv_b200.policies import DESCRIPTIONS, POLICIES, build
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    shape = SHAPES[args.shape]
+    eng = TorchEngine.from_packed(random_packed(shape, seed=0, device=dev))
+    eng.eos = set()  # random weights: always generate max_new tokens
+    reqs = policy_requests(args.requests, shape.vocab)
+    eng.last_logprobs(eng.prefill(reqs[0][1].tokens))  # warm-up (plans, workspaces)
+    ref: dict = {}
+    summary = {}
+    for pol in POLICIES:
+        rt = build(pol, eng, shape.name, budget_bytes=3 << 30, ratio=args.ratio)
+        rows = replay_policy(pol, rt, eng, reqs, ref, max_new=args.max_new, sync=torch.cuda.synchronize)
+        s = summarize(rows)
+        s["tokens"] = int(sum(r["tokens"] for r in rows))
+        s["description"] = DESCRIPTIONS[pol]
+        summary[pol] = s
+        del rt
+        torch.cuda.empty_cache()
+    p1 = summary["P1"]["ttft_p50"]
+    for s in summary.values():
+        s["speedup_vs_p1"] = round(p1 / s["ttft_p50"], 3)
+        s["ttft_p50_ms"], s["ttft_p95_ms"] = round(s.pop("ttft_p50") * 1e3, 3), round(s.pop("ttft_p95") * 1e3, 3)
+    print(json.dumps({
+        "metric": "policy replay TTFT p50 under P4 (gate + provenance keys)",
+        "value": summary["P4"]["ttft_p50_ms"], "unit": "ms", "n_gpus": 1, "steps": len(reqs),
+        "higher_is_better": False, "dtype": "bf16",
+        "data": "synthetic: random-init bf16 weights (seed 0), seeded multi-tenant agent stream",
+        "config": {"workload": "P0-P4 policy replay (bench/replay.py + report.py of the reference)",
+                   "model": f"{args.shape} architecture, random init", "requests": len(reqs),
+                   "ratio": args.ratio, "max_new": args.max_new, "store_budget_bytes": 3 << 30},
+        "policies": summary,
+    }), flush=True)
 
 
 def run_micro(args):
@@ -1080,6 +1169,8 @@ def main():
         run_replay(args)
     elif args.workload == "micro":
         run_micro(args)
+    elif args.workload == "policies":
+        run_policies(args)
     elif args.workload == "decode":
         run_decode(args)
     else:

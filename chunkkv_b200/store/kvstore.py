@@ -19,7 +19,7 @@ from dataclasses import dataclass, field
 
 from chunkkv_b200.engine.base import CacheChunkKV
 from chunkkv_b200.store.keys import LookupKey
-from chunkkv_b200.store.pages import PAGE_TOKENS, PagedChunkKV, PagePool
+from chunkkv_b200.store.pages import PAGE_TOKENS, PagedChunkKV, PagePool, chunk_shape, write_chunk
 from chunkkv_b200.types import TrustLevel
 
 _ids = itertools.count()
@@ -85,13 +85,10 @@ class KVStore:
 
     # -- paging ------------------------------------------------------------------
     def _ensure_pool(self, kv) -> PagePool:
-        if isinstance(kv, CacheChunkKV) and kv.viewable:
-            L, k0 = kv.n_layers, kv.view(0, 0)
-        else:
-            L, k0 = len(kv.keys), kv.keys[0]
-        H, D = k0.shape[-3], k0.shape[-1]
+        L, H, D = chunk_shape(kv)
         if self.pool is None:
             nbytes = self._pool_bytes or (self.budget + self.budget // 8)
+            k0 = kv.view(0, 0) if isinstance(kv, CacheChunkKV) and kv.viewable else kv.keys[0]
             dev = self._device or (k0.device if getattr(k0, "is_cuda", False) else "cuda")
             self.pool = PagePool.for_bytes(L, H, D, nbytes, device=dev)
         elif not self.pool.matches(L, H, D):
@@ -103,22 +100,15 @@ class KVStore:
         if isinstance(kv, PagedChunkKV):
             return
         pool = self._ensure_pool(kv)
-        length = kv.length
-        need = (length + PAGE_TOKENS - 1) // PAGE_TOKENS
+        need = (kv.length + PAGE_TOKENS - 1) // PAGE_TOKENS
         if need > pool.n_pages:
-            raise ValueError(f"chunk of {length} tokens does not fit the page pool")
+            raise ValueError(f"chunk of {kv.length} tokens does not fit the page pool")
         ids = pool.alloc(need)
         while ids is None:
             if not self._evict_one(protect):
                 raise MemoryError("page pool exhausted")
             ids = pool.alloc(need)
-        if isinstance(kv, CacheChunkKV) and kv.viewable:
-            # straight from the engine result's cache: no per-layer copies
-            L = pool.n_layers
-            pool.write(ids, length, [kv.view(li, 0) for li in range(L)], [kv.view(li, 1) for li in range(L)])
-        else:
-            pool.write(ids, length, list(kv.keys), list(kv.values))
-        entry.kv = PagedChunkKV(pool, ids, length, kv.start)
+        entry.kv = write_chunk(pool, kv, ids)
 
     def _drop(self, e: Entry) -> None:
         self.bytes -= entry_bytes(e)

@@ -138,6 +138,13 @@ class PagedChunkKV:
         p = self.pool
         return p.n_layers * 2 * p.n_kv_heads * self._length * p.head_dim * 2
 
+    def prefix(self, n: int) -> "PagedChunkKV":
+        """The chunk's first `n` tokens: the same pages, no copy."""
+        if not 0 <= n <= self._length:
+            raise ValueError(f"prefix of {n} tokens from a chunk of {self._length}")
+        pages = (self.src_offset + n + PAGE_TOKENS - 1) // PAGE_TOKENS
+        return PagedChunkKV(self.pool, self.page_ids[:pages], n, self.start, self.src_offset)
+
     def materialize(self, layer_lo: int = 0, layer_hi: int | None = None):
         """Dense copies [layers, H, len, D] of K and V (as stored, no shift)."""
         p = self.pool
@@ -152,3 +159,29 @@ class PagedChunkKV:
         inv = torch.zeros(p.head_dim // 2, dtype=torch.float32, device=dev)  # unused at delta 0
         ops.blend_gather_paged(p.pages, table, meta, inv, k, v, layer_lo, layer_hi)
         return k, v
+
+
+def chunk_shape(kv) -> tuple[int, int, int]:
+    """(layers, KV heads, head_dim) of a chunk given as per-layer tensors or a cache view."""
+    from chunkkv_b200.engine.base import CacheChunkKV
+
+    if isinstance(kv, CacheChunkKV) and kv.viewable:
+        L, k0 = kv.n_layers, kv.view(0, 0)
+    else:
+        L, k0 = len(kv.keys), kv.keys[0]
+    return L, k0.shape[-3], k0.shape[-1]
+
+
+def write_chunk(pool: PagePool, kv, page_ids: np.ndarray) -> PagedChunkKV:
+    """Copy a chunk's K/V into `page_ids` of the pool (one launch) and return the paged
+    view.  A cache view of an engine result (CacheChunkKV) is read in place, without
+    the per-layer copies."""
+    from chunkkv_b200.engine.base import CacheChunkKV
+
+    length = kv.length
+    if isinstance(kv, CacheChunkKV) and kv.viewable:
+        L = pool.n_layers
+        pool.write(page_ids, length, [kv.view(li, 0) for li in range(L)], [kv.view(li, 1) for li in range(L)])
+    else:
+        pool.write(page_ids, length, list(kv.keys), list(kv.values))
+    return PagedChunkKV(pool, page_ids, length, kv.start)
