@@ -33,10 +33,12 @@
 // wait is bounded (ckv_common.cuh).
 // The kernel is persistent: one CTA per SM runs work items (row block, KV head, key
 // split) one after another on the same TMEM allocation and barriers.  The producer warp
-// claims items from a counter in the workspace and publishes them through a small ring
-// in shared memory; a softmax warpgroup loads the next item's Q as soon as its last S
-// MMA of the current item is done, so the next item's first S MMA overlaps this item's
-// last P V and its epilogue.
+// claims items from a counter in the workspace and publishes them, with their tokens'
+// positions, through a small ring in shared memory.  It loads each Q tile by TMA (a 3-D
+// box of G heads x T tokens lands as the packed rows) as soon as the current item's
+// last S MMA on that tile is done, so the next item's first S MMA overlaps this item's
+// last P V and its epilogue.  Each Q tile has its own "O complete" barrier, so one
+// warpgroup's epilogue never waits for the other's last tile.
 #include <algorithm>
 #include <mutex>
 #include <vector>
@@ -64,18 +66,17 @@ template <int HD>
 struct Cfg {
   static constexpr int ATOMS = HD / 64;
   static constexpr uint32_t Q_BYTES = BM * HD * 2;
+  // bytes one Q tile's TMA boxes deliver: G heads x T tokens x HD (rows past G * T stay)
+  __host__ __device__ static constexpr uint32_t Q_TX(int g, int t) { return uint32_t(HD) * g * t * 2; }
   static constexpr uint32_t KV_TILE = BN * HD * 2;
   // at least 120 KiB so two CTAs never share an SM: each allocates all 512 TMEM columns
-  static constexpr uint32_t SMEM_NEED = 1024 + NQ * Q_BYTES + (KS + VS) * KV_TILE + 512;
+  // + item ring (4 x 32 B) with its token positions (4 x NQ x BM ints), the softmax
+  // warps' store staging tiles (8 x 32 rows x 80 B), barriers and flags
+  static constexpr uint32_t SMEM_NEED = 1024 + NQ * Q_BYTES + (KS + VS) * KV_TILE + 4096 + 20480 + 512;
   static constexpr uint32_t SMEM = SMEM_NEED > 120 * 1024 ? SMEM_NEED : 120 * 1024;
   static constexpr uint32_t IDESC_S = umma_idesc_bf16(BM, BN);
   static constexpr uint32_t IDESC_PV = umma_idesc_bf16(BM, HD) | (1u << 16);  // B MN-major
 };
-
-// byte offset of 16-byte chunk `ch` (of a 64-element atom row) of row r, swizzle-128
-__device__ __forceinline__ uint32_t sw128(int r, int ch) {
-  return uint32_t(r) * 128u + uint32_t((ch ^ (r & 7)) << 4);
-}
 
 // all lanes wait; the warp agrees on the outcome so collective TMEM ops stay converged
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
@@ -103,6 +104,13 @@ struct Item {
   int rb, hk, split, n_split, kt0, n_kt, pad0, pad1;  // rb < 0: no more work
 };
 constexpr int kItemSlots = 4;  // ring of items published by the producer warp
+// Epilogue staging: per softmax warp 32 rows x 16 words, rows padded to 20 words (80 B)
+// so that the 16-byte writes of eight consecutive lanes fall in distinct banks
+constexpr int kStageStride = 20;
+constexpr uint32_t kStageBytes = NQ * 4 * 32 * kStageStride * 4;
+static_assert(kItemSlots * (sizeof(Item) + NQ * BM * sizeof(int)) + kStageBytes + 40 * sizeof(uint64_t) + 8 <=
+                  4096 + 20480 + 512,
+              "item ring, positions, staging and barriers must fit the shared-memory reserve");
 
 // 10 warps: two of the four SM sub-partitions hold three warps, so the register
 // file allows at most 16384 / (3 * 32) = 170 registers per thread.
@@ -113,7 +121,7 @@ constexpr int kItemSlots = 4;  // ring of items published by the producer warp
 template <int HD>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                        const uint16_t* __restrict__ q, const int32_t* __restrict__ positions,
+                        const __grid_constant__ CUtensorMap tmQ, const int32_t* __restrict__ positions,
                         uint16_t* __restrict__ out, int M, int Hq, int Hk, int n_ctx, float scale_log2,
                         int tps, int max_splits, int blocks, unsigned* __restrict__ sched,
                         float* __restrict__ part_o, float2* __restrict__ part_ml) {
@@ -125,18 +133,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sK = sQ + NQ * C::Q_BYTES;      // [KS][KV_TILE]
   uint8_t* sV = sK + KS * C::KV_TILE;      // [VS][KV_TILE]
   Item* items = reinterpret_cast<Item*>(sV + VS * C::KV_TILE);  // [kItemSlots]
-  uint64_t* k_full = reinterpret_cast<uint64_t*>(items + kItemSlots);
+  int* s_pos = reinterpret_cast<int*>(items + kItemSlots);      // [kItemSlots][NQ * BM] token positions
+  uint32_t* s_stage = reinterpret_cast<uint32_t*>(s_pos + kItemSlots * NQ * BM);  // [8 warps][32][20]
+  uint64_t* k_full = reinterpret_cast<uint64_t*>(s_stage + kStageBytes / 4);
   uint64_t* k_empty = k_full + KS;
   uint64_t* v_full = k_empty + KS;
   uint64_t* v_empty = v_full + VS;
   uint64_t* s_full = v_empty + VS;  // [NQ]
   uint64_t* p_full = s_full + NQ;   // [NQ]
   uint64_t* o_done = p_full + NQ;   // [NQ]
-  uint64_t* q_ready = o_done + NQ;  // [NQ]
-  uint64_t* item_full = q_ready + NQ;  // [kItemSlots]
+  uint64_t* q_ready = o_done + NQ;  // [NQ]: Q tile w of the next item landed (TMA)
+  uint64_t* q_free = q_ready + NQ;  // [NQ]: the current item's last S MMA of tile w is done
+  uint64_t* o_full = q_free + NQ;   // [NQ]: the current item's last P V of tile w is done
+  uint64_t* item_full = o_full + NQ;  // [kItemSlots]
   uint64_t* item_empty = item_full + kItemSlots;  // [kItemSlots]
-  uint64_t* o_full = item_empty + kItemSlots;
-  uint64_t* drain = o_full + 1;
+  uint64_t* drain = item_empty + kItemSlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -158,20 +169,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s_full[w], 1);
       mbar_init(&p_full[w], 128);
       mbar_init(&o_done[w], 1);
-      mbar_init(&q_ready[w], 128);
+      mbar_init(&q_ready[w], 1);
+      mbar_init(&q_free[w], 1);
+      mbar_init(&o_full[w], 1);
     }
     for (int s = 0; s < kItemSlots; ++s) {
       mbar_init(&item_full[s], 1);
       mbar_init(&item_empty[s], 1 + NQ * 4);  // the MMA thread and each softmax warp
     }
-    mbar_init(o_full, 1);
     mbar_init(drain, 1);
     *abort = 0;
     fence_barrier_init();
     fence_async_smem();
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmQ);
   }
+  // Q rows past G * T (padding of a tile) are never loaded: zero them once
+  for (int i = threadIdx.x; i < NQ * C::ATOMS * (BM - G * T) * 8; i += kThreads) {
+    const int per_atom = (BM - G * T) * 8;  // 16-byte chunks
+    const int wa = i / per_atom, c = i - wa * per_atom;
+    *reinterpret_cast<uint4*>(sQ + wa * ATOM_BYTES + (G * T) * 128 + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+  }
+  fence_async_smem();
   if (warp == kWarpMma) tmem_alloc(tmem_slot, TMEM_COLS);
   tc_fence_before();
   __syncthreads();
@@ -182,11 +202,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------- item scheduler + TMA producer (one warp)
     int it = 0;          // items published
     int nk = 0, nv = 0;  // K / V tile loads issued (all items)
+    int nq[NQ] = {};     // Q tile loads issued per tile
     int cursor = blockIdx.x;
     bool ok = true;
     while (ok) {
       // next non-empty slot: the warp reads the block's positions for its last key tile
       Item rec{-1, 0, 0, 0, 0, 0, 0, 0};
+      int pv[NQ * BM / 32];  // the item's token positions, lane + 32 j (clamped)
       while (true) {
         int slot = cursor;
         if (sched != nullptr) {
@@ -203,12 +225,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int t0 = rb * NQ * T;
         const int n_tok = min(NQ * T, M - t0);
         int mx = 0;
-        for (int i = lane; i < n_tok; i += 32) {
-          int p = positions[t0 + i];
-          if (p < 0 || p >= n_ctx) {
-            if (z == 0 && hk == 0) atomicOr(&g_err_word, CKV_DEV_ERR_POSITION_RANGE);
-            p = p < 0 ? 0 : n_ctx - 1;
+#pragma unroll
+        for (int j = 0; j < NQ * BM / 32; ++j) {
+          const int i = lane + 32 * j;
+          int p = 0;
+          if (i < n_tok) {
+            p = positions[t0 + i];
+            if (p < 0 || p >= n_ctx) {
+              if (z == 0 && hk == 0) atomicOr(&g_err_word, CKV_DEV_ERR_POSITION_RANGE);
+              p = p < 0 ? 0 : n_ctx - 1;
+            }
           }
+          pv[j] = p;
           mx = max(mx, p);
         }
 #pragma unroll
@@ -220,14 +248,34 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
       }
-      // publish (a record with rb < 0 tells the consumers to stop), then load its tiles
+      // publish the record and its positions (a record with rb < 0 tells the consumers
+      // to stop), then load its Q tiles and its K/V tiles
+      const int s = it % kItemSlots;
+      bool free_slot = true;
+      if (lane == 0) free_slot = mbar_wait(&item_empty[s], ((it / kItemSlots) & 1) ^ 1, abort, &g_err_word);
+      if (!__shfl_sync(0xffffffffu, free_slot ? 1 : 0, 0)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int j = 0; j < NQ * BM / 32; ++j) s_pos[s * NQ * BM + lane + 32 * j] = pv[j];
+      __threadfence_block();
+      __syncwarp();
       if (lane == 0) {
-        const int s = it % kItemSlots;
-        if (mbar_wait(&item_empty[s], ((it / kItemSlots) & 1) ^ 1, abort, &g_err_word)) {
-          items[s] = rec;
-          mbar_arrive(&item_full[s]);
-        } else {
-          ok = false;
+        items[s] = rec;
+        mbar_arrive(&item_full[s]);
+        // Q tile w of this item, once the previous item's last S MMA on tile w is done
+        for (int w = 0; w < NQ && ok && rec.rb >= 0; ++w) {
+          if (it > 0 && !mbar_wait(&q_free[w], (it - 1) & 1, abort, &g_err_word)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&q_ready[w], C::Q_TX(G, T));
+          ++nq[w];
+#pragma unroll
+          for (int a = 0; a < C::ATOMS; ++a)
+            tma_load_3d(sQ + w * C::Q_BYTES + a * ATOM_BYTES, &tmQ, a * 64, rec.hk * G,
+                        rec.rb * NQ * T + w * T, &q_ready[w]);
         }
         for (int j = 0; j < rec.n_kt && ok && rec.rb >= 0; ++j) {
           const int gk = nk;
@@ -262,6 +310,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) {  // aborted: let the copies already issued land
         for (int i = (nk > KS ? nk - KS : 0); i < nk; ++i) drain_wait(&k_full[i % KS], (i / KS) & 1);
         for (int i = (nv > VS ? nv - VS : 0); i < nv; ++i) drain_wait(&v_full[i % VS], (i / VS) & 1);
+        for (int w = 0; w < NQ; ++w)
+          if (nq[w] > 0) drain_wait(&q_ready[w], (nq[w] - 1) & 1);
       }
       if (sched != nullptr) {
         // every CTA arrives here once, after its last claim on the slot counter; the
@@ -275,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kWarpMma) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      auto issue_s = [&](int w, int gt) {
+      auto issue_s = [&](int w, int gt, bool last) {
         const uint32_t q0 = smem_u32(sQ + w * C::Q_BYTES);
         const uint32_t k0 = smem_u32(sK + (gt % KS) * C::KV_TILE);
 #pragma unroll
@@ -285,6 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                      kk > 0 ? 1u : 0u);
         }
         tc_commit(&s_full[w]);
+        if (last) tc_commit(&q_free[w]);  // Q tile w may be overwritten for the next item
       };
       auto issue_pv = [&](int w, int gt, bool first) {
         const uint32_t v0 = smem_u32(sV + (gt % VS) * C::KV_TILE);
@@ -317,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          issue_s(w, g);
+          issue_s(w, g, n_kt == 1);
         }
         if (!ok) break;
         tc_commit(&k_empty[g % KS]);
@@ -331,6 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             issue_pv(w, gt, j == 0);
+            if (j + 1 == n_kt) tc_commit(&o_full[w]);  // O of tile w is final
             if (w == NQ - 1) tc_commit(&v_empty[gt % VS]);
             if (j + 1 < n_kt) {
               if (w == 0 && !mbar_wait(&k_full[nxt % KS], (nxt / KS) & 1, abort, &g_err_word)) {
@@ -338,12 +390,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
               }
               tc_fence_after();
-              issue_s(w, nxt);
+              issue_s(w, nxt, j + 2 == n_kt);
               if (w == NQ - 1) tc_commit(&k_empty[nxt % KS]);
             }
           }
         }
-        if (ok) tc_commit(o_full);
         g += n_kt;
       }
       if (!ok) {
@@ -356,58 +407,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int w = warp >> 2;         // Q tile of this warpgroup
     const int sub = warp & 3;        // TMEM sub-partition (lanes 32*sub .. +31)
     const int r = sub * 32 + lane;   // row in the Q tile == TMEM lane
-    const int tr = r / G, g_head = r - (r / G) * G;
+    const int tr = r / G;           // token of the row in the Q tile
     const uint32_t lane_base = tmem + (uint32_t(sub * 32) << 16);
     const uint32_t sbuf = lane_base + w * BN;
     const uint32_t obuf = lane_base + O_COL + w * 128;
-    uint8_t* myQ = sQ + w * C::Q_BYTES;
 
-    // item `it` from the ring; every lane reads it, one lane per warp releases the slot
-    auto take = [&](int it, Item& rec) -> bool {
-      const int s = it % kItemSlots;
-      if (!warp_wait(&item_full[s], (it / kItemSlots) & 1, abort)) return false;
-      rec = items[s];
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&item_empty[s]);
-      return true;
-    };
     // this thread's row of an item: token, its position, whether the row is real
     struct Row {
       int tok, pos;
       bool valid;
     };
-    auto row_of = [&](const Item& rec) -> Row {
-      const int t0 = rec.rb * NQ * T;
-      const int n_tok = min(NQ * T, M - t0);
+    // item `it` from the ring with this thread's row of it (the position comes from the
+    // ring's copy, read before the slot is released); one lane per warp releases it
+    auto take = [&](int it, Item& rec, Row& x) -> bool {
+      const int s = it % kItemSlots;
+      if (!warp_wait(&item_full[s], (it / kItemSlots) & 1, abort)) return false;
+      rec = items[s];
+      const int n_tok = min(NQ * T, M - rec.rb * NQ * T);
       const int tt = w * T + tr;  // token index in the item
-      Row x;
-      x.valid = r < T * G && tt < n_tok;
-      x.tok = t0 + (x.valid ? tt : 0);
+      x.valid = rec.rb >= 0 && r < T * G && tt < n_tok;
+      x.tok = rec.rb * NQ * T + (x.valid ? tt : 0);
       // padding rows see every key: they never force the masked path on their warp
-      x.pos = n_ctx - 1;
-      if (x.valid) x.pos = min(max(positions[x.tok], 0), n_ctx - 1);
-      return x;
-    };
-    // Q rows of an item into this warpgroup's smem tile (its previous S MMAs are done)
-    auto load_q = [&](const Item& rec, const Row& x) {
-      const uint16_t* qrow = q + (int64_t(x.tok) * Hq + rec.hk * G + g_head) * HD;
-#pragma unroll
-      for (int c = 0; c < HD / 8; ++c) {
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (x.valid) v = *reinterpret_cast<const uint4*>(qrow + c * 8);
-        *reinterpret_cast<uint4*>(myQ + (c >> 3) * ATOM_BYTES + sw128(r, c & 7)) = v;
-      }
-      fence_async_smem();
-      mbar_arrive(&q_ready[w]);
+      x.pos = x.valid ? s_pos[s * NQ * BM + tt] : n_ctx - 1;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[s]);
+      return true;
     };
 
     Item cur;
-    bool ok = take(0, cur);
     Row row{0, 0, false};
-    if (ok && cur.rb >= 0) {
-      row = row_of(cur);
-      load_q(cur, row);
-    }
+    bool ok = take(0, cur, row);
     int g = 0;  // key tiles consumed (all items)
     for (int it = 0; ok && cur.rb >= 0; ++it) {
       float m = -INFINITY, l = 0.f;
@@ -504,54 +533,78 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       g += cur.n_kt;
-      // the next item's Q goes in now (this tile's S MMAs are done), overlapping the
-      // last P V of this item and the epilogue below
+      // the next item's record (its Q tiles are already on their way by TMA), then
+      // this item's epilogue once its last P V on this tile is done
       Item nxt;
-      ok = take(it + 1, nxt);
-      Row nrow = row;
-      if (ok && nxt.rb >= 0) {
-        nrow = row_of(nxt);
-        load_q(nxt, nrow);
-      }
-      if (!ok || !warp_wait(o_full, it & 1, abort)) {
+      Row nrow{0, 0, false};
+      ok = take(it + 1, nxt, nrow);
+      if (!ok || !warp_wait(&o_full[w], it & 1, abort)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      // Stores go through this warp's staging tile: a lane holds one row (TMEM lane) of
+      // O, and a store whose 32 lanes hit 32 rows is replayed once per row.  So 16 words
+      // of each row (64 bytes: 32 bf16 outputs or 16 fp32 partials) are staged, then
+      // written four lanes per row, eight rows per instruction.  dst[k]: element offset
+      // (in out, or part_o when split) of the first column of this warp's row
+      // 8k + lane / 4, -1 for padding rows and rows past M.
+      int64_t dst[4];
+      {
+        const int t0 = cur.rb * NQ * T;
+        const int n_tok = min(NQ * T, M - t0);
+        const int64_t split_base = int64_t((cur.rb * Hk + cur.hk) * max_splits + cur.split) * (NQ * BM) + w * BM;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int rq = sub * 32 + 8 * k + (lane >> 2);
+          const int tq = rq / G, gq = rq - tq * G, ttq = w * T + tq;
+          const bool vq = rq < T * G && ttq < n_tok;
+          dst[k] = !vq ? -1
+                       : (cur.n_split > 1 ? (split_base + rq) * HD
+                                          : (int64_t(t0 + ttq) * Hq + cur.hk * G + gq) * HD);
+        }
+      }
+      uint32_t* stg = s_stage + warp * (32 * kStageStride);
+      auto flush = [&](const uint32_t(&v)[16], uint8_t* base, int elem, int col_bytes) {
+        uint4* mine = reinterpret_cast<uint4*>(stg + lane * kStageStride);
+#pragma unroll
+        for (int qd = 0; qd < 4; ++qd) mine[qd] = make_uint4(v[4 * qd], v[4 * qd + 1], v[4 * qd + 2], v[4 * qd + 3]);
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint4 x = reinterpret_cast<const uint4*>(stg + (8 * k + (lane >> 2)) * kStageStride)[lane & 3];
+          if (dst[k] >= 0) *reinterpret_cast<uint4*>(base + dst[k] * elem + col_bytes + (lane & 3) * 16) = x;
+        }
+        __syncwarp();
+      };
       if (cur.n_split > 1) {
         // one slice of the keys: unnormalised O with its (max, sum), merged by the combine kernel
-        const int64_t prow =
-            (int64_t((cur.rb * Hk + cur.hk) * max_splits + cur.split)) * (NQ * BM) + w * BM + r;
-        float* po = part_o + prow * HD;
 #pragma unroll 1
         for (int c = 0; c < HD; c += 32) {
           float o[32];
           tmem_ld32(obuf + c, o);
-          if (row.valid) {
 #pragma unroll
-            for (int qd = 0; qd < 8; ++qd)
-              *reinterpret_cast<float4*>(po + c + 4 * qd) = make_float4(o[4 * qd], o[4 * qd + 1], o[4 * qd + 2], o[4 * qd + 3]);
+          for (int h = 0; h < 2; ++h) {
+            uint32_t v[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(o[16 * h + e]);
+            flush(v, reinterpret_cast<uint8_t*>(part_o), 4, (c + 16 * h) * 4);
           }
         }
-        if (row.valid) part_ml[prow] = make_float2(m, l);
+        if (row.valid) {
+          const int64_t prow = int64_t((cur.rb * Hk + cur.hk) * max_splits + cur.split) * (NQ * BM) + w * BM + r;
+          part_ml[prow] = make_float2(m, l);
+        }
       } else {
         const float inv = l > 0.f ? 1.0f / l : 0.f;
-        uint16_t* orow = out + (int64_t(row.tok) * Hq + cur.hk * G + g_head) * HD;
 #pragma unroll 1
         for (int c = 0; c < HD; c += 32) {
           float o[32];
           tmem_ld32(obuf + c, o);
-          if (row.valid) {
+          uint32_t v[16];
 #pragma unroll
-            for (int qd = 0; qd < 4; ++qd) {
-              uint4 v;
-              v.x = pack_bf2(o[8 * qd + 0] * inv, o[8 * qd + 1] * inv);
-              v.y = pack_bf2(o[8 * qd + 2] * inv, o[8 * qd + 3] * inv);
-              v.z = pack_bf2(o[8 * qd + 4] * inv, o[8 * qd + 5] * inv);
-              v.w = pack_bf2(o[8 * qd + 6] * inv, o[8 * qd + 7] * inv);
-              *reinterpret_cast<uint4*>(orow + c + 8 * qd) = v;
-            }
-          }
+          for (int e = 0; e < 16; ++e) v[e] = pack_bf2(o[2 * e] * inv, o[2 * e + 1] * inv);
+          flush(v, reinterpret_cast<uint8_t*>(out), 2, c * 2);
         }
       }
       // O has been read: the next item's first P V (which overwrites it) is issued only
@@ -741,13 +794,36 @@ int make_cache_map(CUtensorMap* map, const void* ptr, int H, int n_ctx, int HD) 
   return CKV_OK;
 }
 
+// q [M][Hq][HD] as a 3-D map (HD, Hq, M), box = 64 x G heads x T tokens: one box is the
+// 64-column half of a packed Q tile, rows (token, head) token-major; tokens past M read 0
+int make_q_map(CUtensorMap* map, const void* ptr, int M, int Hq, int G, int T, int HD) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) {
+    set_error("cuTensorMapEncodeTiled unavailable");
+    return CKV_ERR_CUDA;
+  }
+  cuuint64_t dims[3] = {cuuint64_t(HD), cuuint64_t(Hq), cuuint64_t(M)};
+  cuuint64_t strides[2] = {cuuint64_t(HD) * 2, cuuint64_t(Hq) * HD * 2};
+  cuuint32_t box[3] = {64, cuuint32_t(G), cuuint32_t(T)};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled (q) failed (%d)", int(r));
+    return CKV_ERR_CUDA;
+  }
+  return CKV_OK;
+}
+
 template <int HD>
 int launch(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* positions, uint16_t* out,
            int M, int Hq, int Hk, int n_ctx, float scale, void* workspace, int64_t ws_bytes,
            cudaStream_t stream) {
-  CUtensorMap mk, mv;
+  CUtensorMap mk, mv, mq;
   if (int rc = make_cache_map(&mk, kc, Hk, n_ctx, HD)) return rc;
   if (int rc = make_cache_map(&mv, vc, Hk, n_ctx, HD)) return rc;
+  if (int rc = make_q_map(&mq, q, M, Hq, Hq / Hk, BM / (Hq / Hk), HD)) return rc;
   auto kern = attention_tc_kernel<HD>;
   if (int rc = set_smem_limit(reinterpret_cast<const void*>(kern), Cfg<HD>::SMEM)) return rc;
   SplitPlan p = plan_splits(M, Hq, Hk, HD, n_ctx);
@@ -767,7 +843,7 @@ int launch(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int3
   const int64_t n_slots = int64_t(p.blocks) * Hk * p.max_splits;
   CKV_REQUIRE(n_slots < (int64_t(1) << 31) - 4 * 1024 * 1024, "ckv_attention: too many work items");
   const int grid = int(std::min<int64_t>(n_slots, num_sms()));
-  kern<<<grid, kThreads, Cfg<HD>::SMEM, stream>>>(mk, mv, q, positions, out, M, Hq, Hk, n_ctx, sl2, p.tps,
+  kern<<<grid, kThreads, Cfg<HD>::SMEM, stream>>>(mk, mv, mq, positions, out, M, Hq, Hk, n_ctx, sl2, p.tps,
                                                    p.max_splits, p.blocks, sched, part_o, part_ml);
   CKV_LAUNCH_CHECK("ckv_attention");
   if (p.max_splits > 1) {
