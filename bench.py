@@ -1015,22 +1015,33 @@ def run_decode(args):
     n_new = max(8, args.steps)
     eng.generate(res, max(4, args.warmup))
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    out = eng.generate(res, n_new)
-    e1.record()
-    torch.cuda.synchronize()
-    ms_tok = e0.elapsed_time(e1) / len(out)
+
+    def timed(n):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        toks = eng.generate(res, n)
+        e1.record()
+        torch.cuda.synchronize()
+        return toks, e0.elapsed_time(e1)
+
+    # Each generate call runs its first step eagerly and captures one CUDA graph for the
+    # rest; the steady-state time per token is the difference of two call lengths.
+    short, ms_short = timed(8)
+    out, ms_long = timed(n_new + 8)
+    ms_tok = (ms_long - ms_short) / (len(out) - len(short))
     pk, pk_kind = peaks()
     wbytes = weights.nbytes() - weights.embed.numel() * 2 + (weights.lm_head.numel() * 2 if shape.tied else 0)
     gbs = wbytes / (ms_tok * 1e-3) / 1e9
     print(json.dumps({
         "metric": "greedy decode tokens/s after the config-3 blend prefill (one request)",
-        "value": round(1e3 / ms_tok, 2), "unit": "tokens/s", "n_gpus": 1, "steps": len(out),
+        "value": round(1e3 / ms_tok, 2), "unit": "tokens/s", "n_gpus": 1, "steps": len(out) - len(short),
         "ms_per_step": round(ms_tok, 4), "higher_is_better": True, "dtype": "bf16",
         "data": "synthetic: random-init bf16 weights (seed 0)",
         "config": {"workload": "decode after config 3", "model": f"{args.shape} architecture, random init",
                    "context_tokens": len(tokens), "new_tokens": len(out)},
+        "ms_per_token_with_capture": round(ms_long / len(out), 4),
+        "note": "ms_per_step = (time of a generate call of n + 8 tokens - one of 8) / n: the per-call "
+                "eager first step and graph capture cancel",
         "weight_bytes_per_token": int(wbytes), "weight_gbs": round(gbs, 1),
         "frac_hbm": round(gbs / pk["hbm_gbs"], 4), "peak_source": f"{pk_kind} hbm_gbs"}), flush=True)
 

@@ -816,10 +816,247 @@ int make_q_map(CUtensorMap* map, const void* ptr, int M, int Hq, int G, int T, i
   return CKV_OK;
 }
 
+// ---------------------------------------------------------------------------------
+// One query token (decode): split-KV on CUDA cores.  The tensor-core kernel would fill
+// a 128-row Q tile with G rows; here a CTA takes one KV head and one 64-key chunk for
+// the G query heads of that head.  The chunk's K and V rows come into shared memory by
+// coalesced loads, all in flight at once; each thread scores one key for up to half of
+// the heads, a warp per head turns the scores into exponentials relative to the
+// chunk's max, and each thread then accumulates one output column over the keys.  Chunks past the
+// query's position write nothing; the combine merges the chunks up to it, so one grid
+// (sized for n_ctx) serves every position, as a replayed CUDA graph needs.
+constexpr int kDecKeys = 64;
+
+inline int dec_chunks(int n_ctx) { return ceil_div(n_ctx, kDecKeys); }
+inline int64_t dec_bytes(int Hq, int HD, int n_ctx) {
+  return int64_t(dec_chunks(n_ctx)) * Hq * (int64_t(HD) * 4 + 8);
+}
+
+// scores of key `kk` of the chunk for heads [G0, G1) into s_p (log2 domain)
+template <int HD, int G0, int G1, int KROW, int G>
+__device__ __forceinline__ void decode_scores(const uint16_t (*s_k)[KROW], const float (*s_q)[HD],
+                                              float (*s_p)[kDecKeys], int kk, bool visible, float scale_log2) {
+  float acc[G1 - G0 > 0 ? G1 - G0 : 1];
+#pragma unroll
+  for (int g = 0; g < G1 - G0; ++g) acc[g] = 0.f;
+#pragma unroll 4
+  for (int ch = 0; ch < HD / 8; ++ch) {
+    const uint4 kv = *reinterpret_cast<const uint4*>(&s_k[kk][ch * 8]);
+    const uint32_t* kw = reinterpret_cast<const uint32_t*>(&kv);
+    float kf[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      kf[2 * e] = lo_bf(kw[e]);
+      kf[2 * e + 1] = hi_bf(kw[e]);
+    }
+#pragma unroll
+    for (int g = 0; g < G1 - G0; ++g) {
+      const float4 qa = *reinterpret_cast<const float4*>(&s_q[G0 + g][ch * 8]);
+      const float4 qb = *reinterpret_cast<const float4*>(&s_q[G0 + g][ch * 8 + 4]);
+      acc[g] = fmaf(qa.x, kf[0], fmaf(qa.y, kf[1], fmaf(qa.z, kf[2], fmaf(qa.w, kf[3], acc[g]))));
+      acc[g] = fmaf(qb.x, kf[4], fmaf(qb.y, kf[5], fmaf(qb.z, kf[6], fmaf(qb.w, kf[7], acc[g]))));
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G1 - G0; ++g) s_p[G0 + g][kk] = visible ? acc[g] * scale_log2 : -INFINITY;
+}
+
+template <int HD, int G>
+__global__ void __launch_bounds__(HD) decode_attention_kernel(
+    const uint16_t* __restrict__ q, const uint16_t* __restrict__ kc, const uint16_t* __restrict__ vc,
+    const int32_t* __restrict__ positions, int Hk, int n_ctx, float scale_log2, float* __restrict__ part_o,
+    float2* __restrict__ part_ml) {
+  // K rows padded by 16 bytes so that eight lanes reading eight rows hit distinct banks
+  constexpr int kKRow = HD + 8;
+  __shared__ __align__(16) uint16_t s_k[kDecKeys][kKRow];
+  __shared__ __align__(16) uint16_t s_v[kDecKeys][HD];
+  __shared__ __align__(16) float s_q[G][HD];
+  __shared__ __align__(16) float s_p[G][kDecKeys];
+  __shared__ float s_ml[G][2];
+  const int c = blockIdx.x, hk = blockIdx.y;
+  const int Hq = G * Hk;
+  int pos = positions[0];
+  pos = pos < 0 ? 0 : (pos >= n_ctx ? n_ctx - 1 : pos);
+  const int key0 = c * kDecKeys;
+  if (key0 > pos) return;  // nothing visible in this chunk: the combine skips it
+  const int t = threadIdx.x;
+  const int n_keys = min(kDecKeys, pos + 1 - key0);
+  // the chunk's K and V rows (zeros past the last visible key), all loads in flight at once
+  {
+    constexpr int kPer = kDecKeys / 8;  // 16-byte vectors per thread, of K and of V
+    const uint4* kg = reinterpret_cast<const uint4*>(kc + (int64_t(hk) * n_ctx + key0) * HD);
+    const uint4* vg = reinterpret_cast<const uint4*>(vc + (int64_t(hk) * n_ctx + key0) * HD);
+    uint4 kv[kPer], vv[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int idx = t + HD * i, row = idx / (HD / 8);
+      kv[i] = row < n_keys ? __ldg(kg + idx) : make_uint4(0u, 0u, 0u, 0u);
+      vv[i] = row < n_keys ? __ldg(vg + idx) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) s_q[g][t] = bf2f(q[int64_t(hk * G + g) * HD + t]);
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int idx = t + HD * i, row = idx / (HD / 8), ch = idx % (HD / 8);
+      *reinterpret_cast<uint4*>(&s_k[row][ch * 8]) = kv[i];
+      *reinterpret_cast<uint4*>(&s_v[row][ch * 8]) = vv[i];
+    }
+  }
+  __syncthreads();
+  // scores: with HD = 128 two threads per key, the first half of the heads and the rest
+  // (a warp-uniform split: warps 0-1 and 2-3); with HD = 64 one thread per key
+  {
+    const int kk = t % kDecKeys;
+    const bool vis = kk < n_keys;
+    if constexpr (HD / kDecKeys == 2) {
+      if (t < kDecKeys)
+        decode_scores<HD, 0, G / 2, kKRow, G>(s_k, s_q, s_p, kk, vis, scale_log2);
+      else
+        decode_scores<HD, G / 2, G, kKRow, G>(s_k, s_q, s_p, kk, vis, scale_log2);
+    } else {
+      decode_scores<HD, 0, G, kKRow, G>(s_k, s_q, s_p, kk, vis, scale_log2);
+    }
+  }
+  __syncthreads();
+  // per head: chunk max, exponentials, sum (one warp per head)
+  const int warp = t >> 5, lane = t & 31;
+  for (int g = warp; g < G; g += HD / 32) {
+    const float a = s_p[g][lane], b = s_p[g][lane + 32];
+    float mx = fmaxf(a, b);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float pa = exp2f(a - mx), pb = exp2f(b - mx);  // key0 <= pos: mx is finite
+    s_p[g][lane] = pa;
+    s_p[g][lane + 32] = pb;
+    float sum = pa + pb;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) {
+      s_ml[g][0] = mx;
+      s_ml[g][1] = sum;
+    }
+  }
+  __syncthreads();
+  // P V: thread t owns output column t for every head (rows past the visible keys are 0);
+  // P is read four keys at a time
+  float o[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) o[g] = 0.f;
+#pragma unroll 2
+  for (int j = 0; j < kDecKeys; j += 4) {
+    const float v0 = bf2f(s_v[j][t]), v1 = bf2f(s_v[j + 1][t]), v2 = bf2f(s_v[j + 2][t]),
+                v3 = bf2f(s_v[j + 3][t]);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float4 p4 = *reinterpret_cast<const float4*>(&s_p[g][j]);
+      o[g] = fmaf(p4.x, v0, fmaf(p4.y, v1, fmaf(p4.z, v2, fmaf(p4.w, v3, o[g]))));
+    }
+  }
+  const int64_t row0 = int64_t(c) * Hq + hk * G;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    part_o[(row0 + g) * HD + t] = o[g];
+    if (t == 0) part_ml[row0 + g] = make_float2(s_ml[g][0], s_ml[g][1]);
+  }
+}
+
+// Merge the chunks of the decode kernel: out = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c.
+// A CTA takes one query head and 32 output columns; its 32 warps take chunks w, w + 32,
+// ... (one column per lane, loads coalesced), and meet in shared memory.
+constexpr int kDecCombineWarps = 32;
+template <int HD>
+__global__ void __launch_bounds__(kDecCombineWarps * 32) decode_combine_kernel(
+    const int32_t* __restrict__ positions, uint16_t* __restrict__ out, int Hq, int n_ctx,
+    const float* __restrict__ part_o, const float2* __restrict__ part_ml) {
+  __shared__ float s_red[kDecCombineWarps];
+  __shared__ float s_acc[kDecCombineWarps][33];
+  __shared__ float s_l[kDecCombineWarps];
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int hq = blockIdx.x, col = blockIdx.y * 32 + lane;
+  int pos = positions[0];
+  pos = pos < 0 ? 0 : (pos >= n_ctx ? n_ctx - 1 : pos);
+  const int n = pos / kDecKeys + 1;  // chunks that hold visible keys
+  float mx = -INFINITY;
+  for (int c = threadIdx.x; c < n; c += kDecCombineWarps * 32) mx = fmaxf(mx, part_ml[int64_t(c) * Hq + hq].x);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) s_red[wp] = mx;
+  __syncthreads();
+  mx = s_red[0];
+#pragma unroll
+  for (int i = 1; i < kDecCombineWarps; ++i) mx = fmaxf(mx, s_red[i]);
+  float L = 0.f, acc = 0.f;
+#pragma unroll 4
+  for (int c = wp; c < n; c += kDecCombineWarps) {
+    const float2 ml = part_ml[int64_t(c) * Hq + hq];
+    const float wgt = exp2f(ml.x - mx);
+    L = fmaf(wgt, ml.y, L);
+    acc = fmaf(wgt, part_o[(int64_t(c) * Hq + hq) * HD + col], acc);
+  }
+  s_acc[wp][lane] = acc;
+  if (lane == 0) s_l[wp] = L;
+  __syncthreads();
+  if (wp == 0) {
+    float a = 0.f, l = 0.f;
+#pragma unroll 8
+    for (int k = 0; k < kDecCombineWarps; ++k) {
+      a += s_acc[k][lane];
+      l += s_l[k];
+    }
+    out[int64_t(hq) * HD + col] = f2bf(l > 0.f ? a / l : 0.f);
+  }
+}
+
+template <int HD, int G>
+void launch_decode_g(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* positions,
+                     int Hk, int n_ctx, float sl2, float* part_o, float2* part_ml, cudaStream_t stream) {
+  decode_attention_kernel<HD, G><<<dim3(dec_chunks(n_ctx), Hk), HD, 0, stream>>>(q, kc, vc, positions, Hk, n_ctx,
+                                                                                sl2, part_o, part_ml);
+}
+
+// G values with a compiled decode kernel (Qwen2 shapes: 1 MHA, 2 / 4 / 5 / 6 / 7 / 8 GQA, 16)
+inline bool decode_g_ok(int G) {
+  return G == 1 || G == 2 || G == 4 || G == 5 || G == 6 || G == 7 || G == 8 || G == 16;
+}
+
+template <int HD>
+int launch_decode(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* positions,
+                  uint16_t* out, int Hq, int Hk, int n_ctx, float scale, void* workspace, cudaStream_t stream) {
+  float* part_o = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kSchedBytes);
+  float2* part_ml = reinterpret_cast<float2*>(part_o + int64_t(dec_chunks(n_ctx)) * Hq * HD);
+  const float sl2 = scale * 1.4426950408889634f;
+  switch (Hq / Hk) {
+    case 1: launch_decode_g<HD, 1>(q, kc, vc, positions, Hk, n_ctx, sl2, part_o, part_ml, stream); break;
+    case 2: launch_decode_g<HD, 2>(q, kc, vc, positions, Hk, n_ctx, sl2, part_o, part_ml, stream); break;
+    case 4: launch_decode_g<HD, 4>(q, kc, vc, positions, Hk, n_ctx, sl2, part_o, part_ml, stream); break;
+    case 5: launch_decode_g<HD, 5>(q, kc, vc, positions, Hk, n_ctx, sl2, part_o, part_ml, stream); break;
+    case 6: launch_decode_g<HD, 6>(q, kc, vc, positions, Hk, n_ctx, sl2, part_o, part_ml, stream); break;
+    case 7: launch_decode_g<HD, 7>(q, kc, vc, positions, Hk, n_ctx, sl2, part_o, part_ml, stream); break;
+    case 8: launch_decode_g<HD, 8>(q, kc, vc, positions, Hk, n_ctx, sl2, part_o, part_ml, stream); break;
+    case 16: launch_decode_g<HD, 16>(q, kc, vc, positions, Hk, n_ctx, sl2, part_o, part_ml, stream); break;
+    default:
+      set_error("ckv_attention(decode): %d query heads per KV head", Hq / Hk);
+      return CKV_ERR_UNSUPPORTED;
+  }
+  CKV_LAUNCH_CHECK("ckv_attention(decode)");
+  decode_combine_kernel<HD><<<dim3(Hq, HD / 32), kDecCombineWarps * 32, 0, stream>>>(positions, out, Hq, n_ctx,
+                                                                                      part_o, part_ml);
+  CKV_LAUNCH_CHECK("ckv_attention(decode combine)");
+  return CKV_OK;
+}
+
+// decode path: one query token, a G with a compiled decode kernel, and room for
+// the chunk partials after the scheduler words
+inline bool use_decode(int M, int Hq, int Hk, int HD, int n_ctx, int64_t ws_bytes) {
+  return M == 1 && decode_g_ok(Hq / Hk) && ws_bytes >= kSchedBytes + dec_bytes(Hq, HD, n_ctx);
+}
+
 template <int HD>
 int launch(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* positions, uint16_t* out,
            int M, int Hq, int Hk, int n_ctx, float scale, void* workspace, int64_t ws_bytes,
            cudaStream_t stream) {
+  if (use_decode(M, Hq, Hk, HD, n_ctx, ws_bytes))
+    return launch_decode<HD>(q, kc, vc, positions, out, Hq, Hk, n_ctx, scale, workspace, stream);
   CUtensorMap mk, mv, mq;
   if (int rc = make_cache_map(&mk, kc, Hk, n_ctx, HD)) return rc;
   if (int rc = make_cache_map(&mv, vc, Hk, n_ctx, HD)) return rc;
@@ -864,6 +1101,7 @@ extern "C" int64_t ckv_attention_workspace_size(int m, int n_q_heads, int n_kv_h
   if (m <= 0 || n_kv_heads <= 0 || n_q_heads % n_kv_heads != 0 || n_ctx <= 0 ||
       (head_dim != 64 && head_dim != 128) || n_q_heads / n_kv_heads > BM)
     return 0;
+  if (m == 1 && decode_g_ok(n_q_heads / n_kv_heads)) return kSchedBytes + dec_bytes(n_q_heads, head_dim, n_ctx);
   return kSchedBytes + plan_splits(m, n_q_heads, n_kv_heads, head_dim, n_ctx).bytes;
 }
 

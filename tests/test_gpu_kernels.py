@@ -483,7 +483,8 @@ def test_qkv_rope_scatter_and_compact(Hq, H, D, hid):
 
 # --------------------------------------------------------------- attention
 @pytest.mark.parametrize("Hq,H,D,N,m", [(28, 4, 128, 1500, 300), (14, 2, 64, 700, 700), (4, 2, 64, 100, 37),
-                                        (7, 1, 128, 4100, 1)])
+                                        (7, 1, 128, 4100, 1), (14, 2, 64, 700, 1), (16, 1, 128, 3000, 1),
+                                        (20, 1, 64, 500, 1)])
 def test_attention_matches_masked_sdpa(Hq, H, D, N, m):
     g = torch.Generator(device=DEV).manual_seed(N)
     q = torch.randn((m, Hq, D), generator=g, device=DEV).to(BF)
@@ -535,6 +536,28 @@ def test_attention_schedules_agree(Hq, H, D, N, m):
                                          attn_mask=mask, enable_gqa=True)[0].transpose(0, 1)
     assert rel_err(split_out, ref) <= 1e-2
     assert rel_err(dyn_out, ref) <= 1e-2
+
+
+@pytest.mark.parametrize("pos", [0, 63, 64, 2000, 4099])
+def test_decode_attention_matches_tensor_core_path(pos):
+    """One query token: the split-KV decode kernel (workspace from attention_workspace_bytes)
+    against the tensor-core kernel (no workspace) and masked SDPA, at positions on and
+    next to the 64-key chunk edges."""
+    Hq, H, D, N = 28, 4, 128, 4100
+    g = torch.Generator(device=DEV).manual_seed(pos)
+    q = torch.randn((1, Hq, D), generator=g, device=DEV).to(BF)
+    K = torch.randn((H, N, D), generator=g, device=DEV).to(BF)
+    V = torch.randn((H, N, D), generator=g, device=DEV).to(BF)
+    p = torch.tensor([pos], dtype=torch.int32, device=DEV)
+    ws = torch.zeros(ops.attention_workspace_bytes(1, Hq, H, D, N), dtype=torch.uint8, device=DEV)
+    dec, tc = torch.empty_like(q), torch.empty_like(q)
+    ops.attention(q, K, V, p, dec, workspace=ws)
+    ops.attention(q, K, V, p, tc, workspace=ws[:0])
+    mask = p.long()[:, None] >= torch.arange(N, device=DEV)[None, :]
+    ref = F.scaled_dot_product_attention(q.float().transpose(0, 1)[None], K.float()[None], V.float()[None],
+                                         attn_mask=mask, enable_gqa=True)[0].transpose(0, 1)
+    assert rel_err(dec, ref) <= 1e-2 and rel_err(tc, ref) <= 1e-2
+    assert rel_err(dec, tc) <= 1e-2
 
 
 def test_attention_unsorted_positions():
