@@ -317,7 +317,10 @@ CKV_API int ckv_qkv_rope(const uint16_t* x, const uint16_t* w_qkv, const uint16_
  * rows would leave SMs idle.  ckv_attention_workspace_size() gives the bytes for both
  * (at least 256).  With a smaller workspace the keys are not split; with NULL the
  * items are assigned statically (CTA c takes items c, c + grid, ...).  Every schedule
- * gives the same result up to the key split's rounding. */
+ * gives the same result up to the key split's rounding.  One query token (m == 1) with
+ * 1, 2, 4, 5, 6, 7, 8 or 16 query heads per KV head and a workspace of the size given
+ * for m == 1 takes a split-KV path on CUDA cores instead (decode); it reads the
+ * position on the device, so a captured launch serves every later position. */
 CKV_API int64_t ckv_attention_workspace_size(int m, int n_q_heads, int n_kv_heads, int head_dim,
                                              int n_ctx);
 CKV_API int ckv_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
