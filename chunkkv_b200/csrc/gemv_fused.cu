@@ -20,30 +20,42 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 // acc[m] += dot(w row, x[m]) over this lane's 16-byte vectors of k (R weight rows at once).
+// Each lane requests U vectors of every row before it multiplies any of them: at m <= 2
+// eight (the weights are the whole cost, and HBM needs many bytes in flight per SM), else
+// four (x's rows take the registers).
 template <int MM, int R>
 __device__ __forceinline__ void dot_rows(const uint16_t* const (&wrow)[R], const uint16_t* __restrict__ x, int k,
                                          int lane, float (&acc)[R][MM]) {
+  constexpr int U = MM <= 2 ? 8 : 4;
 #pragma unroll
   for (int r = 0; r < R; ++r)
 #pragma unroll
     for (int m = 0; m < MM; ++m) acc[r][m] = 0.f;
   const int vecs = k / 8;
-#pragma unroll 4
-  for (int v = lane; v < vecs; v += 32) {
-    uint4 a[R];
+  for (int v0 = lane; v0 < vecs; v0 += 32 * U) {
+    uint4 a[U][R];
 #pragma unroll
-    for (int r = 0; r < R; ++r) a[r] = __ldcs(reinterpret_cast<const uint4*>(wrow[r]) + v);  // streamed once
+    for (int u = 0; u < U; ++u)
 #pragma unroll
-    for (int m = 0; m < MM; ++m) {
-      const uint4 b = reinterpret_cast<const uint4*>(x + int64_t(m) * k)[v];
-      const uint32_t* pb = reinterpret_cast<const uint32_t*>(&b);
+      for (int r = 0; r < R; ++r)
+        a[u][r] = v0 + 32 * u < vecs ? __ldcs(reinterpret_cast<const uint4*>(wrow[r]) + v0 + 32 * u)  // streamed once
+                                     : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a[r]);
+    for (int u = 0; u < U; ++u) {
+      const int v = v0 + 32 * u;
+      if (v >= vecs) break;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          acc[r][m] = fmaf(lo_bf(pa[e]), lo_bf(pb[e]), acc[r][m]);
-          acc[r][m] = fmaf(hi_bf(pa[e]), hi_bf(pb[e]), acc[r][m]);
+      for (int m = 0; m < MM; ++m) {
+        const uint4 b = reinterpret_cast<const uint4*>(x + int64_t(m) * k)[v];
+        const uint32_t* pb = reinterpret_cast<const uint32_t*>(&b);
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a[u][r]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            acc[r][m] = fmaf(lo_bf(pa[e]), lo_bf(pb[e]), acc[r][m]);
+            acc[r][m] = fmaf(hi_bf(pa[e]), hi_bf(pb[e]), acc[r][m]);
+          }
         }
       }
     }
