@@ -58,6 +58,7 @@ SIGNATURES: dict[str, list] = {
     "ckv_qkv_rope": [_p, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _p, _p, _i32, _p, _p, _p,
                      _i32, _p, _p, _p],
     "ckv_attention_workspace_size": [_i32, _i32, _i32, _i32, _i32],
+    "ckv_attention_launches": [_i32, _i32, _i32, _i32, _i32, _i64],
     "ckv_attention": [_p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _i32, _f32, _p, _i64, _p],
     "ckv_gemv": [_p, _p, _p, _i32, _i32, _i32, _p],
     "ckv_log_softmax": [_p, _i32, _p, _p],

@@ -876,6 +876,8 @@ __global__ void __launch_bounds__(HD) decode_attention_kernel(
   const int c = blockIdx.x, hk = blockIdx.y;
   const int Hq = G * Hk;
   int pos = positions[0];
+  if ((pos < 0 || pos >= n_ctx) && c == 0 && hk == 0 && threadIdx.x == 0)
+    atomicOr(&g_err_word, CKV_DEV_ERR_POSITION_RANGE);
   pos = pos < 0 ? 0 : (pos >= n_ctx ? n_ctx - 1 : pos);
   const int key0 = c * kDecKeys;
   if (key0 > pos) return;  // nothing visible in this chunk: the combine skips it
@@ -1103,6 +1105,16 @@ extern "C" int64_t ckv_attention_workspace_size(int m, int n_q_heads, int n_kv_h
     return 0;
   if (m == 1 && decode_g_ok(n_q_heads / n_kv_heads)) return kSchedBytes + dec_bytes(n_q_heads, head_dim, n_ctx);
   return kSchedBytes + plan_splits(m, n_q_heads, n_kv_heads, head_dim, n_ctx).bytes;
+}
+
+extern "C" int ckv_attention_launches(int m, int n_q_heads, int n_kv_heads, int head_dim, int n_ctx,
+                                      int64_t workspace_bytes) {
+  if (m <= 0 || n_kv_heads <= 0 || n_q_heads % n_kv_heads != 0 || n_ctx <= 0 ||
+      (head_dim != 64 && head_dim != 128) || n_q_heads / n_kv_heads > BM)
+    return 0;
+  if (use_decode(m, n_q_heads, n_kv_heads, head_dim, n_ctx, workspace_bytes)) return 2;  // + its combine
+  const SplitPlan p = plan_splits(m, n_q_heads, n_kv_heads, head_dim, n_ctx);
+  return p.max_splits > 1 && workspace_bytes >= kSchedBytes + p.bytes ? 2 : 1;  // + the combine kernel
 }
 
 extern "C" int ckv_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,

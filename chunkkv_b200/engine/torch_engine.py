@@ -22,6 +22,7 @@ There is no CPU path: a missing library raises (chunkkv_b200._lib).
 
 from __future__ import annotations
 
+import array
 import math
 
 import numpy as np
@@ -201,7 +202,13 @@ class TorchEngine:
         if N == 0:
             raise ValueError("empty request")
 
-        tok_np = np.asarray(tokens, dtype=np.int64)
+        if isinstance(tokens, list):  # the reference's list[int]: a C-level conversion
+            try:
+                tok_np = np.frombuffer(array.array("q", tokens), dtype=np.int64)
+            except (OverflowError, TypeError):
+                tok_np = np.asarray(tokens, dtype=np.int64)
+        else:
+            tok_np = np.asarray(tokens, dtype=np.int64)
         if tok_np.min() < 0 or tok_np.max() >= s.vocab:
             raise ValueError("token id outside the vocabulary")
         plan = plan_arrays(N, placements, config.n_sink)

@@ -355,10 +355,10 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos
     ws_bytes = workspace.numel() * workspace.element_size()
     if ws_bytes == 0:  # an empty workspace: static scheduling, no key split
         workspace = None
-    split = ATTN_SCHED_BYTES < need <= ws_bytes  # split-KV: the attention kernel plus its combine kernel
+    kernels = int(_lib.load().ckv_attention_launches(m, Hq, H, D, n_ctx, ws_bytes))
     _run("ckv_attention", _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(positions), _ptr(out), m, Hq,
          H, D, n_ctx, float(scale), _ptr(workspace), ws_bytes, _stream(), flops=flops,
-         kernels=2 if split else 1)
+         kernels=max(kernels, 1))
     return out
 
 

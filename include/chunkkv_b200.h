@@ -323,6 +323,11 @@ CKV_API int ckv_qkv_rope(const uint16_t* x, const uint16_t* w_qkv, const uint16_
  * position on the device, so a captured launch serves every later position. */
 CKV_API int64_t ckv_attention_workspace_size(int m, int n_q_heads, int n_kv_heads, int head_dim,
                                              int n_ctx);
+/* Kernels one ckv_attention call launches at this shape and workspace size: 1, or 2 when
+ * a merge kernel follows (key splits, or the decode path); 0 for a shape ckv_attention
+ * refuses. */
+CKV_API int ckv_attention_launches(int m, int n_q_heads, int n_kv_heads, int head_dim, int n_ctx,
+                                   int64_t workspace_bytes);
 CKV_API int ckv_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
                           const int32_t* positions, uint16_t* out, int m, int n_q_heads,
                           int n_kv_heads, int head_dim, int n_ctx, float scale, void* workspace,

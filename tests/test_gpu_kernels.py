@@ -560,6 +560,24 @@ def test_decode_attention_matches_tensor_core_path(pos):
     assert rel_err(dec, tc) <= 1e-2
 
 
+def test_attention_position_out_of_range_is_reported_not_faulted():
+    """A position past the cache is clamped by the kernels and reported in the device
+    error word (bit 0x8), on the split-KV decode path and on the tensor-core path."""
+    Hq, H, D, N = 28, 4, 128, 300
+    g = torch.Generator(device=DEV).manual_seed(5)
+    q = torch.randn((1, Hq, D), generator=g, device=DEV).to(BF)
+    K = torch.randn((H, N, D), generator=g, device=DEV).to(BF)
+    V = torch.randn((H, N, D), generator=g, device=DEV).to(BF)
+    p = torch.tensor([N + 5], dtype=torch.int32, device=DEV)
+    ws = torch.zeros(ops.attention_workspace_bytes(1, Hq, H, D, N), dtype=torch.uint8, device=DEV)
+    out = torch.empty_like(q)
+    ops.attention(q, K, V, p, out, workspace=ws)
+    assert _lib.device_error() & 0x8
+    ops.attention(q, K, V, p, out, workspace=ws[:0])
+    assert _lib.device_error() & 0x8
+    assert torch.isfinite(out.float()).all()
+
+
 def test_attention_unsorted_positions():
     """Row blocks whose positions are not sorted: each row still sees exactly its keys."""
     Hq, H, D, N, m = 28, 4, 128, 2600, 500
