@@ -57,11 +57,13 @@ __global__ void __launch_bounds__(kRmsThreads) rmsnorm_kernel(uint16_t* __restri
   const uint4* wr = reinterpret_cast<const uint4*>(w);
   uint4* yr = reinterpret_cast<uint4*>(y + int64_t(row) * hidden);
   const int vecs = hidden / 8;
-  uint4 v[kRmsVec];
+  // the row and the weight are requested together: one memory latency, not two
+  uint4 v[kRmsVec], wv[kRmsVec];
 #pragma unroll
   for (int i = 0; i < kRmsVec; ++i) {
     const int c = threadIdx.x + kRmsThreads * i;
     v[i] = c < vecs ? __ldcs(xr + c) : make_uint4(0u, 0u, 0u, 0u);
+    wv[i] = c < vecs ? __ldg(wr + c) : make_uint4(0u, 0u, 0u, 0u);
   }
   if constexpr (kAdd) {
     const uint4* dr = reinterpret_cast<const uint4*>(delta + int64_t(row) * hidden);
@@ -99,9 +101,8 @@ __global__ void __launch_bounds__(kRmsThreads) rmsnorm_kernel(uint16_t* __restri
   for (int i = 0; i < kRmsVec; ++i) {
     const int c = threadIdx.x + kRmsThreads * i;
     if (c < vecs) {
-      const uint4 g = __ldg(wr + c);
       const uint32_t* p = reinterpret_cast<const uint32_t*>(&v[i]);
-      const uint32_t* q = reinterpret_cast<const uint32_t*>(&g);
+      const uint32_t* q = reinterpret_cast<const uint32_t*>(&wv[i]);
       uint4 o;
       uint32_t* po = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll

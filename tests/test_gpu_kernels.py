@@ -484,7 +484,8 @@ def test_qkv_rope_scatter_and_compact(Hq, H, D, hid):
 # --------------------------------------------------------------- attention
 @pytest.mark.parametrize("Hq,H,D,N,m", [(28, 4, 128, 1500, 300), (14, 2, 64, 700, 700), (4, 2, 64, 100, 37),
                                         (7, 1, 128, 4100, 1), (14, 2, 64, 700, 1), (16, 1, 128, 3000, 1),
-                                        (20, 1, 64, 500, 1)])
+                                        (20, 1, 64, 500, 1), (10, 2, 128, 900, 1), (16, 2, 64, 600, 1),
+                                        (6, 6, 64, 300, 1)])
 def test_attention_matches_masked_sdpa(Hq, H, D, N, m):
     g = torch.Generator(device=DEV).manual_seed(N)
     q = torch.randn((m, Hq, D), generator=g, device=DEV).to(BF)
