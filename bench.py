@@ -1025,9 +1025,12 @@ def run_decode(args):
         return toks, e0.elapsed_time(e1)
 
     # Each generate call runs its first step eagerly and captures one CUDA graph for the
-    # rest; the steady-state time per token is the difference of two call lengths.
-    short, ms_short = timed(8)
-    out, ms_long = timed(n_new + 8)
+    # rest; the steady-state time per token is the difference of two call lengths (the
+    # median of three calls each, since the capture time varies from call to call).
+    shorts = [timed(8) for _ in range(3)]
+    longs = [timed(n_new + 8) for _ in range(3)]
+    short, ms_short = shorts[0][0], statistics.median(t for _, t in shorts)
+    out, ms_long = longs[0][0], statistics.median(t for _, t in longs)
     ms_tok = (ms_long - ms_short) / (len(out) - len(short))
     pk, pk_kind = peaks()
     wbytes = weights.nbytes() - weights.embed.numel() * 2 + (weights.lm_head.numel() * 2 if shape.tied else 0)

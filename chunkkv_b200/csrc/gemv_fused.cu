@@ -19,14 +19,15 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-// acc[m] += dot(w row, x[m]) over this lane's 16-byte vectors of k (R weight rows at once).
-// Each lane requests U vectors of every row before it multiplies any of them: at m <= 2
-// eight (the weights are the whole cost, and HBM needs many bytes in flight per SM), else
-// four (x's rows take the registers).
+// acc[m] += dot(w row, x[m]) over this lane's 16-byte vectors of k (R weight rows at once;
+// x's rows are ldx apart, k by default).  Each lane requests U vectors of every row
+// before it multiplies any of them: 8 / R at m <= 2 (the weights are the whole cost, and
+// HBM needs many bytes in flight per SM), else 4 / R (x's rows take the registers).
 template <int MM, int R>
 __device__ __forceinline__ void dot_rows(const uint16_t* const (&wrow)[R], const uint16_t* __restrict__ x, int k,
-                                         int lane, float (&acc)[R][MM]) {
-  constexpr int U = MM <= 2 ? 8 : 4;
+                                         int lane, float (&acc)[R][MM], int64_t ldx = -1) {
+  constexpr int U = (MM <= 2 ? 8 : 4) / R > 0 ? (MM <= 2 ? 8 : 4) / R : 1;
+  if (ldx < 0) ldx = k;
 #pragma unroll
   for (int r = 0; r < R; ++r)
 #pragma unroll
@@ -46,7 +47,7 @@ __device__ __forceinline__ void dot_rows(const uint16_t* const (&wrow)[R], const
       if (v >= vecs) break;
 #pragma unroll
       for (int m = 0; m < MM; ++m) {
-        const uint4 b = reinterpret_cast<const uint4*>(x + int64_t(m) * k)[v];
+        const uint4 b = reinterpret_cast<const uint4*>(x + int64_t(m) * ldx)[v];
         const uint32_t* pb = reinterpret_cast<const uint32_t*>(&b);
 #pragma unroll
         for (int r = 0; r < R; ++r) {
@@ -66,16 +67,38 @@ __device__ __forceinline__ void dot_rows(const uint16_t* const (&wrow)[R], const
     for (int m = 0; m < MM; ++m) acc[r][m] = warp_sum(acc[r][m]);
 }
 
-// h[m][n] = bf16(h + bf16(w[n] . x[m]))   (o_proj / down_proj + residual)
-template <int MM>
+// h[m][n] = bf16(h + bf16(w[n] . x[m]))   (o_proj / down_proj + residual).  S warps share
+// a row, each taking k / S of it (long rows: the down projection's 18944), and their
+// partial sums meet in shared memory; a CTA of 8 warps covers 8 / S rows.
+template <int MM, int S>
 __global__ void __launch_bounds__(256) gemv_residual_kernel(const uint16_t* __restrict__ x,
                                                             const uint16_t* __restrict__ w,
                                                             uint16_t* __restrict__ h, int n, int k) {
-  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (row >= n) return;
-  const uint16_t* wr[1] = {w + int64_t(row) * k};
+  __shared__ float s_part[8][MM];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (8 / S) + warp / S, slice = warp % S;
+  const int ks = k / S;  // a multiple of 8: checked on the host
   float acc[1][MM];
-  dot_rows<MM, 1>(wr, x, k, lane, acc);
+  if (row < n) {
+    const uint16_t* wr[1] = {w + int64_t(row) * k + int64_t(slice) * ks};
+    dot_rows<MM, 1>(wr, x + int64_t(slice) * ks, ks, lane, acc, k);
+  }
+  if (S > 1) {
+    if (lane == 0 && row < n)
+#pragma unroll
+      for (int m = 0; m < MM; ++m) s_part[warp][m] = acc[0][m];
+    __syncthreads();
+    if (row >= n || slice != 0) return;
+#pragma unroll
+    for (int m = 0; m < MM; ++m) {
+      float t = s_part[warp][m];
+#pragma unroll
+      for (int q = 1; q < S; ++q) t += s_part[warp + q][m];
+      acc[0][m] = t;
+    }
+  } else if (row >= n) {
+    return;
+  }
   if (lane < MM) {
     float s = acc[0][0];
 #pragma unroll
@@ -202,11 +225,18 @@ int ckv_gemv_residual(const uint16_t* x, const uint16_t* w, uint16_t* h, int m, 
   if (int rc = check_gemv(x, w, m, k, "ckv_gemv_residual")) return rc;
   CKV_REQUIRE(h, "ckv_gemv_residual: null h");
   if (n <= 0) return CKV_OK;
-  const int grid = ceil_div(n, 8);
   cudaStream_t s = as_stream(stream);
-#define CKV_L(MM) gemv_residual_kernel<MM><<<grid, 256, 0, s>>>(x, w, h, n, k)
-  CKV_GEMV_SWITCH(m, CKV_L)
+  if (k >= 8192 && k % 32 == 0) {  // long rows: four warps per row
+    const int grid = ceil_div(n, 2);
+#define CKV_L(MM) gemv_residual_kernel<MM, 4><<<grid, 256, 0, s>>>(x, w, h, n, k)
+    CKV_GEMV_SWITCH(m, CKV_L)
 #undef CKV_L
+  } else {
+    const int grid = ceil_div(n, 8);
+#define CKV_L(MM) gemv_residual_kernel<MM, 1><<<grid, 256, 0, s>>>(x, w, h, n, k)
+    CKV_GEMV_SWITCH(m, CKV_L)
+#undef CKV_L
+  }
   CKV_LAUNCH_CHECK("ckv_gemv_residual");
   return CKV_OK;
 }

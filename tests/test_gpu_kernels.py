@@ -406,6 +406,25 @@ def test_linear_residual_and_swiglu():
     assert rel_err(out, ref2) <= 1e-2
 
 
+@pytest.mark.parametrize("m,k", [(1, 9472), (3, 18944)])
+def test_decode_gemv_residual_long_rows(m, k):
+    """Long rows (k >= 8192: four warps per row, partial sums through shared memory) against
+    the tcgen05 residual GEMM and an fp32 reference."""
+    g = torch.Generator(device=DEV).manual_seed(k + m)
+    a = torch.randn((m, k), generator=g, device=DEV).to(BF)
+    for n in (528, 517):  # 517: the last CTA's second row is past n
+        w = (torch.randn((n, k), generator=g, device=DEV) * 0.02).to(BF)
+        h = torch.randn((m, n), generator=g, device=DEV).to(BF)
+        h1 = h.clone()
+        ops.gemv_residual(a, w, h1)
+        ref = h.float() + (a.float() @ w.float().T).to(BF).float()
+        assert rel_err(h1, ref) <= 1e-2
+        if n % 16 == 0:  # the GEMM path takes multiples of 16
+            h2 = h.clone()
+            ops.linear_residual(a, w, h2)
+            assert rel_err(h1, h2) <= 1e-2
+
+
 @pytest.mark.parametrize("m", [1, 3, 8])
 def test_decode_gemv_epilogues_match_the_gemm_path(m):
     """ckv_gemv_residual / _swiglu / _qkv_rope (m <= 8) against the tcgen05 GEMM entry points
