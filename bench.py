@@ -64,7 +64,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--extra-ratios", default="0.30,0.50", help="also time these ratios (TTFT only)")
     ap.add_argument("--kernel-case", choices=["swiglu", "oproj", "down", "qkv", "attention", "gather", "deviation",
-                                              "decode_swiglu"],
+                                              "decode_swiglu", "decode_down"],
                     help="time one kernel at its 7B-bench shape (for ncu captures) instead of the prefill")
     args = ap.parse_args()
     tp = args.workload == "tp"
@@ -1118,6 +1118,9 @@ def run_kernel_case(args):
         w, out = rnd(2 * shape.inter, hid), torch.empty((1, shape.inter), dtype=bf, device=dev)
         x1 = x[:1].contiguous()
         fn = lambda: ops.gemv_swiglu(x1, w, out)  # noqa: E731
+    elif args.kernel_case == "decode_down":  # one decode row through the residual GEMV (k = inter)
+        a1, w, h1 = rnd(1, shape.inter, scale=1.0), rnd(hid, shape.inter), rnd(1, hid, scale=1.0)
+        fn = lambda: ops.gemv_residual(a1, w, h1)  # noqa: E731
     elif args.kernel_case == "down":
         a, w, h = rnd(M, shape.inter, scale=1.0), rnd(hid, shape.inter), rnd(M, hid, scale=1.0)
         fn = lambda: ops.linear_residual(a, w, h)  # noqa: E731
