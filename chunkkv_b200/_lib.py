@@ -47,6 +47,9 @@ SIGNATURES: dict[str, list] = {
     "ckv_gemv_residual": [_p, _p, _p, _i32, _i32, _i32, _p],
     "ckv_gemv_swiglu": [_p, _p, _p, _i32, _i32, _i32, _p],
     "ckv_gemv_qkv_rope": [_p, _p, _p, _i32, _i32, _i32, _i32, _i32, _p, _p, _i32, _p, _p, _p, _i32, _p],
+    "ckv_gemv_swiglu_rmsnorm": [_p, _p, _f32, _p, _p, _i32, _i32, _i32, _p],
+    "ckv_gemv_qkv_rope_rmsnorm": [_p, _p, _f32, _p, _p, _i32, _i32, _i32, _i32, _i32, _p, _p, _i32, _p, _p, _p,
+                                  _i32, _p],
     "ckv_reduce_add_gather": [_p, _i32, _i32, _i32, _i32, _p, _p, _p, _p, _p, _p, C.c_uint32, _p],
     "ckv_ipc_alloc": [_i64, _p, _p],
     "ckv_ipc_open": [_p, _p],

@@ -67,6 +67,65 @@ __device__ __forceinline__ void dot_rows(const uint16_t* const (&wrow)[R], const
     for (int m = 0; m < MM; ++m) acc[r][m] = warp_sum(acc[r][m]);
 }
 
+// Request the first `bytes` of a weight row towards L2 (one 128-byte line per lane and
+// step): a fused-norm CTA issues this before it normalises, so its first weight batch is
+// on the way while the norm's loads and reductions run.
+__device__ __forceinline__ void prefetch_row_l2(const uint16_t* row, int bytes, int lane) {
+  const char* p = reinterpret_cast<const char*>(row);
+  for (int off = lane * 128; off < bytes; off += 32 * 128)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p + off));
+}
+
+// RMSNorm of the MM rows of h into shared memory (rows kNormMaxK apart), with the rounding
+// of rmsnorm_kernel: y = bf16(w * bf16(h * rsqrt(mean(h^2) + eps))), fp32 inside.  Every
+// thread of the CTA takes part; each CTA of a fused projection builds its own copy (7 KB
+// from L2 per row at the 7B width), which costs less than a separate launch.
+constexpr int kNormMaxK = 5120;
+constexpr int kNormMaxRows = 4;
+template <int MM>
+__device__ __forceinline__ void norm_rows(const uint16_t* __restrict__ h, const uint16_t* __restrict__ norm_w,
+                                          float eps, int k, uint16_t* s_x, float* s_red) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int vecs = k / 8;
+  const uint4* wr = reinterpret_cast<const uint4*>(norm_w);
+#pragma unroll 1
+  for (int m = 0; m < MM; ++m) {
+    const uint4* hr = reinterpret_cast<const uint4*>(h + int64_t(m) * k);
+    float ss = 0.f;
+    for (int c = threadIdx.x; c < vecs; c += blockDim.x) {
+      const uint4 v = hr[c];
+      const uint32_t* p = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float f0 = lo_bf(p[e]), f1 = hi_bf(p[e]);
+        ss = __fadd_rn(ss, __fmul_rn(f0, f0));
+        ss = __fadd_rn(ss, __fmul_rn(f1, f1));
+      }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) s_red[warp] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int i = 0; i < nw; ++i) tot += s_red[i];
+    const float r = rsqrtf(__fadd_rn(__fmul_rn(tot, 1.0f / float(k)), eps));
+    for (int c = threadIdx.x; c < vecs; c += blockDim.x) {
+      const uint4 v = hr[c], g = __ldg(wr + c);
+      const uint32_t* p = reinterpret_cast<const uint32_t*>(&v);
+      const uint32_t* q = reinterpret_cast<const uint32_t*>(&g);
+      uint4 o;
+      uint32_t* po = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float n0 = bf16_round(__fmul_rn(lo_bf(p[e]), r));
+        const float n1 = bf16_round(__fmul_rn(hi_bf(p[e]), r));
+        po[e] = pack_bf2(__fmul_rn(lo_bf(q[e]), n0), __fmul_rn(hi_bf(q[e]), n1));
+      }
+      *reinterpret_cast<uint4*>(s_x + int64_t(m) * kNormMaxK + c * 8) = o;
+    }
+    __syncthreads();  // s_red is reused by the next row; s_x complete for the dot products
+  }
+}
+
 // h[m][n] = bf16(h + bf16(w[n] . x[m]))   (o_proj / down_proj + residual).  S warps share
 // a row, each taking k / S of it (long rows: the down projection's 18944), and their
 // partial sums meet in shared memory; a CTA of 8 warps covers 8 / S rows.
@@ -110,16 +169,31 @@ __global__ void __launch_bounds__(256) gemv_residual_kernel(const uint16_t* __re
 }
 
 // out[m][j] = bf16(bf16(silu(bf16(g))) * bf16(u)); gate/up rows interleaved in 128-row blocks
-template <int MM>
+// With kNorm, x is RMSNorm(h) with norm_w, built by the CTA (norm_rows).
+template <int MM, bool kNorm>
 __global__ void __launch_bounds__(256) gemv_swiglu_kernel(const uint16_t* __restrict__ x,
                                                           const uint16_t* __restrict__ w,
-                                                          uint16_t* __restrict__ out, int inter, int k) {
+                                                          uint16_t* __restrict__ out, int inter, int k,
+                                                          const uint16_t* __restrict__ norm_w, float eps) {
+  __shared__ __align__(16) uint16_t s_x[kNorm ? MM * kNormMaxK : 8];
+  __shared__ float s_red[8];
+  const uint16_t* xin = x;
+  int64_t ldx = k;
   const int j = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (j >= inter) return;
   const int64_t gate_row = int64_t(j / 128) * 256 + (j % 128);
   const uint16_t* wr[2] = {w + gate_row * k, w + (gate_row + 128) * k};
+  if constexpr (kNorm) {
+    if (j < inter) {
+      prefetch_row_l2(wr[0], min(k * 2, 4096), lane);
+      prefetch_row_l2(wr[1], min(k * 2, 4096), lane);
+    }
+    norm_rows<MM>(x, norm_w, eps, k, s_x, s_red);
+    xin = s_x;
+    ldx = kNormMaxK;
+  }
+  if (j >= inter) return;
   float acc[2][MM];
-  dot_rows<MM, 2>(wr, x, k, lane, acc);
+  dot_rows<MM, 2>(wr, xin, k, lane, acc, ldx);
   if (lane < MM) {
     float g = acc[0][0], u = acc[1][0];
 #pragma unroll
@@ -136,14 +210,31 @@ __global__ void __launch_bounds__(256) gemv_swiglu_kernel(const uint16_t* __rest
 
 // q / k rows with bias and RoPE at positions[m] (a warp per rotary pair of one head: rows
 // d and d + HD/2), v rows with bias; k and v go to the caches [Hk][n_ctx][HD] at pos.
-template <int MM, int HD>
+template <int MM, int HD, bool kNorm>
 __global__ void __launch_bounds__(256) gemv_qkv_kernel(
     const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, const uint16_t* __restrict__ bias, int k,
     int Hq, int Hk, const int32_t* __restrict__ positions, const float2* __restrict__ rope, int rope_max_pos,
-    uint16_t* __restrict__ q_out, uint16_t* __restrict__ k_cache, uint16_t* __restrict__ v_cache, int n_ctx) {
+    uint16_t* __restrict__ q_out, uint16_t* __restrict__ k_cache, uint16_t* __restrict__ v_cache, int n_ctx,
+    const uint16_t* __restrict__ norm_w, float eps) {
   constexpr int HALF = HD / 2;
+  __shared__ __align__(16) uint16_t s_x[kNorm ? MM * kNormMaxK : 8];
+  __shared__ float s_red[8];
+  const uint16_t* xin = x;
+  int64_t ldx = k;
   const int item = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   const int n_pair = (Hq + Hk) * HALF;
+  if constexpr (kNorm) {
+    if (item < n_pair) {
+      const int head = item / HALF, jj = item - head * HALF;
+      prefetch_row_l2(w + int64_t(head * HD + jj) * k, min(k * 2, 4096), lane);
+      prefetch_row_l2(w + int64_t(head * HD + jj + HALF) * k, min(k * 2, 4096), lane);
+    } else if (item < n_pair + Hk * HD) {
+      prefetch_row_l2(w + int64_t((Hq + Hk) * HD + item - n_pair) * k, min(k * 2, 8192), lane);
+    }
+    norm_rows<MM>(x, norm_w, eps, k, s_x, s_red);
+    xin = s_x;
+    ldx = kNormMaxK;
+  }
   if (item >= n_pair + Hk * HD) return;
   int pos = 0;
   bool ok = true;
@@ -159,7 +250,7 @@ __global__ void __launch_bounds__(256) gemv_qkv_kernel(
     const int r1 = head * HD + jj, r2 = r1 + HALF;
     const uint16_t* wr[2] = {w + int64_t(r1) * k, w + int64_t(r2) * k};
     float acc[2][MM];
-    dot_rows<MM, 2>(wr, x, k, lane, acc);
+    dot_rows<MM, 2>(wr, xin, k, lane, acc, ldx);
     if (lane < MM && ok) {
       float d1 = acc[0][0], d2 = acc[1][0];
 #pragma unroll
@@ -183,7 +274,7 @@ __global__ void __launch_bounds__(256) gemv_qkv_kernel(
     const int row = (Hq + Hk) * HD + vr;
     const uint16_t* wr[1] = {w + int64_t(row) * k};
     float acc[1][MM];
-    dot_rows<MM, 1>(wr, x, k, lane, acc);
+    dot_rows<MM, 1>(wr, xin, k, lane, acc, ldx);
     if (lane < MM && ok) {
       float d = acc[0][0];
 #pragma unroll
@@ -205,6 +296,95 @@ int check_gemv(const void* x, const void* w, int m, int k, const char* name) {
 }  // namespace ckv
 
 using namespace ckv;
+
+// x rows, or (norm_w != nullptr) the rows of h to RMSNorm first: at most kNormMaxRows rows
+// of at most kNormMaxK columns, the CTA's copy in shared memory
+static int check_norm(const uint16_t* norm_w, int m, int k, const char* name) {
+  if (norm_w == nullptr) return CKV_OK;
+  CKV_REQUIRE(aligned16(norm_w), "%s: norm weight must be 16-byte aligned", name);
+  CKV_REQUIRE(m <= kNormMaxRows && k <= kNormMaxK, "%s: m=%d, k=%d beyond the fused norm's %d x %d", name, m, k,
+              kNormMaxRows, kNormMaxK);
+  return CKV_OK;
+}
+
+#define CKV_NORM_SWITCH(m, LAUNCH, NORM) \
+  switch (m) {                           \
+    case 1: LAUNCH(1, NORM); break;      \
+    case 2: LAUNCH(2, NORM); break;      \
+    case 3: LAUNCH(3, NORM); break;      \
+    case 4: LAUNCH(4, NORM); break;      \
+    case 5: LAUNCH(5, NORM); break;      \
+    case 6: LAUNCH(6, NORM); break;      \
+    case 7: LAUNCH(7, NORM); break;      \
+    default: LAUNCH(8, NORM); break;     \
+  }
+#define CKV_NORM_SWITCH4(m, LAUNCH) \
+  switch (m) {                      \
+    case 1: LAUNCH(1, true); break; \
+    case 2: LAUNCH(2, true); break; \
+    case 3: LAUNCH(3, true); break; \
+    default: LAUNCH(4, true); break; \
+  }
+
+static int gemv_swiglu_launch(const uint16_t* x, const uint16_t* norm_w, float eps, const uint16_t* w_gate_up,
+                              uint16_t* out, int m, int inter, int k, ckv_stream_t stream, const char* name) {
+  if (int rc = check_gemv(x, w_gate_up, m, k, name)) return rc;
+  if (int rc = check_norm(norm_w, m, k, name)) return rc;
+  CKV_REQUIRE(out && inter > 0 && inter % 128 == 0, "%s: inter %d not a multiple of 128", name, inter);
+  const int grid = ceil_div(inter, 8);
+  cudaStream_t s = as_stream(stream);
+#define CKV_L(MM, NORM) gemv_swiglu_kernel<MM, NORM><<<grid, 256, 0, s>>>(x, w_gate_up, out, inter, k, norm_w, eps)
+  if (norm_w) {
+    CKV_NORM_SWITCH4(m, CKV_L)
+  } else {
+    CKV_NORM_SWITCH(m, CKV_L, false)
+  }
+#undef CKV_L
+  CKV_LAUNCH_CHECK(name);
+  return CKV_OK;
+}
+
+static int gemv_qkv_launch(const uint16_t* x, const uint16_t* norm_w, float eps, const uint16_t* w_qkv,
+                           const uint16_t* b_qkv, int m, int k, int n_q_heads, int n_kv_heads, int head_dim,
+                           const int32_t* positions, const float* rope_table, int rope_max_pos, uint16_t* q_out,
+                           uint16_t* k_cache, uint16_t* v_cache, int n_ctx, ckv_stream_t stream, const char* name) {
+  if (int rc = check_gemv(x, w_qkv, m, k, name)) return rc;
+  if (int rc = check_norm(norm_w, m, k, name)) return rc;
+  CKV_REQUIRE(b_qkv && positions && rope_table && q_out && k_cache && v_cache, "%s: null pointer", name);
+  CKV_REQUIRE(n_q_heads > 0 && n_kv_heads > 0 && n_ctx > 0 && rope_max_pos > 0, "%s: bad sizes", name);
+  const int items = (n_q_heads + n_kv_heads) * (head_dim / 2) + n_kv_heads * head_dim;
+  const int grid = ceil_div(items, 8);
+  cudaStream_t s = as_stream(stream);
+  const float2* rope = reinterpret_cast<const float2*>(rope_table);
+  if (head_dim == 128) {
+#define CKV_L(MM, NORM)                                                                                        \
+  gemv_qkv_kernel<MM, 128, NORM><<<grid, 256, 0, s>>>(x, w_qkv, b_qkv, k, n_q_heads, n_kv_heads, positions,    \
+                                                      rope, rope_max_pos, q_out, k_cache, v_cache, n_ctx, norm_w, \
+                                                      eps)
+    if (norm_w) {
+      CKV_NORM_SWITCH4(m, CKV_L)
+    } else {
+      CKV_NORM_SWITCH(m, CKV_L, false)
+    }
+#undef CKV_L
+  } else if (head_dim == 64) {
+#define CKV_L(MM, NORM)                                                                                       \
+  gemv_qkv_kernel<MM, 64, NORM><<<grid, 256, 0, s>>>(x, w_qkv, b_qkv, k, n_q_heads, n_kv_heads, positions,    \
+                                                     rope, rope_max_pos, q_out, k_cache, v_cache, n_ctx, norm_w, \
+                                                     eps)
+    if (norm_w) {
+      CKV_NORM_SWITCH4(m, CKV_L)
+    } else {
+      CKV_NORM_SWITCH(m, CKV_L, false)
+    }
+#undef CKV_L
+  } else {
+    set_error("%s: head_dim %d (64 or 128)", name, head_dim);
+    return CKV_ERR_UNSUPPORTED;
+  }
+  CKV_LAUNCH_CHECK(name);
+  return CKV_OK;
+}
 
 #define CKV_GEMV_SWITCH(m, LAUNCH) \
   switch (m) {                     \
@@ -243,47 +423,32 @@ int ckv_gemv_residual(const uint16_t* x, const uint16_t* w, uint16_t* h, int m, 
 
 int ckv_gemv_swiglu(const uint16_t* x, const uint16_t* w_gate_up, uint16_t* out, int m, int inter, int k,
                     ckv_stream_t stream) {
-  if (int rc = check_gemv(x, w_gate_up, m, k, "ckv_gemv_swiglu")) return rc;
-  CKV_REQUIRE(out && inter > 0 && inter % 128 == 0, "ckv_gemv_swiglu: inter %d not a multiple of 128", inter);
-  const int grid = ceil_div(inter, 8);
-  cudaStream_t s = as_stream(stream);
-#define CKV_L(MM) gemv_swiglu_kernel<MM><<<grid, 256, 0, s>>>(x, w_gate_up, out, inter, k)
-  CKV_GEMV_SWITCH(m, CKV_L)
-#undef CKV_L
-  CKV_LAUNCH_CHECK("ckv_gemv_swiglu");
-  return CKV_OK;
+  return gemv_swiglu_launch(x, nullptr, 0.f, w_gate_up, out, m, inter, k, stream, "ckv_gemv_swiglu");
+}
+
+int ckv_gemv_swiglu_rmsnorm(const uint16_t* h, const uint16_t* norm_w, float eps, const uint16_t* w_gate_up,
+                            uint16_t* out, int m, int inter, int k, ckv_stream_t stream) {
+  CKV_REQUIRE(norm_w, "ckv_gemv_swiglu_rmsnorm: null norm weight");
+  return gemv_swiglu_launch(h, norm_w, eps, w_gate_up, out, m, inter, k, stream, "ckv_gemv_swiglu_rmsnorm");
 }
 
 int ckv_gemv_qkv_rope(const uint16_t* x, const uint16_t* w_qkv, const uint16_t* b_qkv, int m, int k,
                       int n_q_heads, int n_kv_heads, int head_dim, const int32_t* positions,
                       const float* rope_table, int rope_max_pos, uint16_t* q_out, uint16_t* k_cache,
                       uint16_t* v_cache, int n_ctx, ckv_stream_t stream) {
-  if (int rc = check_gemv(x, w_qkv, m, k, "ckv_gemv_qkv_rope")) return rc;
-  CKV_REQUIRE(b_qkv && positions && rope_table && q_out && k_cache && v_cache,
-              "ckv_gemv_qkv_rope: null pointer");
-  CKV_REQUIRE(n_q_heads > 0 && n_kv_heads > 0 && n_ctx > 0 && rope_max_pos > 0, "ckv_gemv_qkv_rope: bad sizes");
-  const int items = (n_q_heads + n_kv_heads) * (head_dim / 2) + n_kv_heads * head_dim;
-  const int grid = ceil_div(items, 8);
-  cudaStream_t s = as_stream(stream);
-  const float2* rope = reinterpret_cast<const float2*>(rope_table);
-  if (head_dim == 128) {
-#define CKV_L(MM)                                                                                     \
-  gemv_qkv_kernel<MM, 128><<<grid, 256, 0, s>>>(x, w_qkv, b_qkv, k, n_q_heads, n_kv_heads, positions, \
-                                                rope, rope_max_pos, q_out, k_cache, v_cache, n_ctx)
-    CKV_GEMV_SWITCH(m, CKV_L)
-#undef CKV_L
-  } else if (head_dim == 64) {
-#define CKV_L(MM)                                                                                    \
-  gemv_qkv_kernel<MM, 64><<<grid, 256, 0, s>>>(x, w_qkv, b_qkv, k, n_q_heads, n_kv_heads, positions, \
-                                               rope, rope_max_pos, q_out, k_cache, v_cache, n_ctx)
-    CKV_GEMV_SWITCH(m, CKV_L)
-#undef CKV_L
-  } else {
-    set_error("ckv_gemv_qkv_rope: head_dim %d (64 or 128)", head_dim);
-    return CKV_ERR_UNSUPPORTED;
-  }
-  CKV_LAUNCH_CHECK("ckv_gemv_qkv_rope");
-  return CKV_OK;
+  return gemv_qkv_launch(x, nullptr, 0.f, w_qkv, b_qkv, m, k, n_q_heads, n_kv_heads, head_dim, positions,
+                         rope_table, rope_max_pos, q_out, k_cache, v_cache, n_ctx, stream, "ckv_gemv_qkv_rope");
+}
+
+int ckv_gemv_qkv_rope_rmsnorm(const uint16_t* h, const uint16_t* norm_w, float eps, const uint16_t* w_qkv,
+                              const uint16_t* b_qkv, int m, int k, int n_q_heads, int n_kv_heads, int head_dim,
+                              const int32_t* positions, const float* rope_table, int rope_max_pos,
+                              uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache, int n_ctx,
+                              ckv_stream_t stream) {
+  CKV_REQUIRE(norm_w, "ckv_gemv_qkv_rope_rmsnorm: null norm weight");
+  return gemv_qkv_launch(h, norm_w, eps, w_qkv, b_qkv, m, k, n_q_heads, n_kv_heads, head_dim, positions,
+                         rope_table, rope_max_pos, q_out, k_cache, v_cache, n_ctx, stream,
+                         "ckv_gemv_qkv_rope_rmsnorm");
 }
 
 }  // extern "C"

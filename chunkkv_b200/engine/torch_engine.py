@@ -128,6 +128,10 @@ class TorchEngine:
             self._attn_ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
         return self._attn_ws
 
+    def _fused_norm(self, m: int) -> bool:
+        """Whether a decode projection of m rows can take RMSNorm(h) itself."""
+        return m <= ops.GEMV_NORM_MAX_ROWS and self.shape.hidden <= ops.GEMV_NORM_MAX_K
+
     def shift_keys(self, keys: torch.Tensor, delta: int) -> torch.Tensor:
         """Re-RoPE post-RoPE keys (1, H, L, D) by `delta` (torch_engine.py:56-59)."""
         if delta == 0:
@@ -155,8 +159,11 @@ class TorchEngine:
         s, lw, tp = self.shape, self.w.layers[li], self.tp
         if tp is None and M <= 8:  # decode: one warp per weight row streams the weights
             ops.gemv_residual(attn[:M], lw.w_o, h)
-            ops.rmsnorm(h[:M], lw.ln2, s.rms_eps, out=x[:M])
-            ops.gemv_swiglu(x[:M], lw.w_gu, act)
+            if self._fused_norm(M):  # the post-attention RMSNorm inside the gate/up GEMV
+                ops.gemv_swiglu(h[:M], lw.w_gu, act, norm_w=lw.ln2, eps=s.rms_eps)
+            else:
+                ops.rmsnorm(h[:M], lw.ln2, s.rms_eps, out=x[:M])
+                ops.gemv_swiglu(x[:M], lw.w_gu, act)
             ops.gemv_residual(act[:M], lw.w_down, h)
             return False
         if tp is None:
@@ -430,10 +437,14 @@ class TorchEngine:
             x_ready = False
             for li in range(L):
                 lw = self.w.layers[li]
-                if not x_ready:
-                    ops.rmsnorm(h, lw.ln1, s.rms_eps, out=x)
                 # q, and k / v into this layer's cache [H, cap, D] at position posd
-                ops.gemv_qkv_rope(x, lw.w_qkv, lw.b_qkv, Hq, H, D, posd, rope_tab, q, K[li], V[li])
+                if not x_ready and self._fused_norm(1):  # the input RMSNorm inside the QKV GEMV
+                    ops.gemv_qkv_rope(h, lw.w_qkv, lw.b_qkv, Hq, H, D, posd, rope_tab, q, K[li], V[li],
+                                      norm_w=lw.ln1, eps=s.rms_eps)
+                else:
+                    if not x_ready:
+                        ops.rmsnorm(h, lw.ln1, s.rms_eps, out=x)
+                    ops.gemv_qkv_rope(x, lw.w_qkv, lw.b_qkv, Hq, H, D, posd, rope_tab, q, K[li], V[li])
                 ops.attention(q, K[li], V[li], posd, attn, m=1, workspace=attn_ws)
                 x_ready = self._block_tail(li, attn, h, x, act, part, 1, exch, 0)
             last = x if x_ready else ops.rmsnorm(h, self.w.norm, s.rms_eps, out=xf)

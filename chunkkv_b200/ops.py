@@ -381,26 +381,43 @@ def gemv_residual(x: torch.Tensor, w: torch.Tensor, h: torch.Tensor) -> torch.Te
     return h
 
 
-def gemv_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
-    """SwiGLU of the interleaved gate/up projection for m = x rows <= 8 (decode)."""
+GEMV_NORM_MAX_ROWS, GEMV_NORM_MAX_K = 4, 5120  # the fused-RMSNorm GEMVs' limits
+
+
+def gemv_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor,
+                norm_w: torch.Tensor | None = None, eps: float = 1e-6) -> torch.Tensor:
+    """SwiGLU of the interleaved gate/up projection for m = x rows <= 8 (decode).  With
+    `norm_w`, x is the hidden state h and the projection takes RMSNorm(h) (m <= 4)."""
     _cuda(x, w_gate_up, out)
     m, k = x.shape
     inter = w_gate_up.shape[0] // 2
-    _run("ckv_gemv_swiglu", _ptr(x), _ptr(w_gate_up), _ptr(out), m, inter, k, _stream(),
-         flops=2.0 * m * 2 * inter * k, nbytes=2.0 * 2 * inter * k)
+    if norm_w is None:
+        _run("ckv_gemv_swiglu", _ptr(x), _ptr(w_gate_up), _ptr(out), m, inter, k, _stream(),
+             flops=2.0 * m * 2 * inter * k, nbytes=2.0 * 2 * inter * k)
+    else:
+        _cuda(norm_w)
+        _run("ckv_gemv_swiglu_rmsnorm", _ptr(x), _ptr(norm_w), float(eps), _ptr(w_gate_up), _ptr(out), m, inter,
+             k, _stream(), flops=2.0 * m * 2 * inter * k, nbytes=2.0 * 2 * inter * k)
     return out
 
 
 def gemv_qkv_rope(x: torch.Tensor, w_qkv: torch.Tensor, b_qkv: torch.Tensor, Hq: int, Hk: int, D: int,
                   positions: torch.Tensor, rope_tab: torch.Tensor, q_out: torch.Tensor,
-                  k_cache: torch.Tensor, v_cache: torch.Tensor) -> None:
-    """q/k/v of m = x rows <= 8 with bias and RoPE; k, v written into the caches (decode)."""
+                  k_cache: torch.Tensor, v_cache: torch.Tensor, norm_w: torch.Tensor | None = None,
+                  eps: float = 1e-6) -> None:
+    """q/k/v of m = x rows <= 8 with bias and RoPE; k, v written into the caches (decode).
+    With `norm_w`, x is the hidden state h and the projection takes RMSNorm(h) (m <= 4)."""
     _cuda(x, w_qkv, b_qkv, positions, rope_tab, q_out, k_cache, v_cache)
     m, k = x.shape
     n_ctx = k_cache.shape[1]
-    _run("ckv_gemv_qkv_rope", _ptr(x), _ptr(w_qkv), _ptr(b_qkv), m, k, Hq, Hk, D, _ptr(positions),
-         _ptr(rope_tab), rope_tab.shape[0], _ptr(q_out), _ptr(k_cache), _ptr(v_cache), n_ctx, _stream(),
-         flops=2.0 * m * w_qkv.shape[0] * k, nbytes=2.0 * w_qkv.shape[0] * k)
+    args = (_ptr(w_qkv), _ptr(b_qkv), m, k, Hq, Hk, D, _ptr(positions), _ptr(rope_tab), rope_tab.shape[0],
+            _ptr(q_out), _ptr(k_cache), _ptr(v_cache), n_ctx, _stream())
+    work = dict(flops=2.0 * m * w_qkv.shape[0] * k, nbytes=2.0 * w_qkv.shape[0] * k)
+    if norm_w is None:
+        _run("ckv_gemv_qkv_rope", _ptr(x), *args, **work)
+    else:
+        _cuda(norm_w)
+        _run("ckv_gemv_qkv_rope_rmsnorm", _ptr(x), _ptr(norm_w), float(eps), *args, **work)
 
 
 def log_softmax(row: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:

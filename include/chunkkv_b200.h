@@ -235,6 +235,18 @@ CKV_API int ckv_gemv_qkv_rope(const uint16_t* x, const uint16_t* w_qkv, const ui
                               const int32_t* positions, const float* rope_table, int rope_max_pos,
                               uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache, int n_ctx,
                               ckv_stream_t stream);
+/* The same two projections of x = RMSNorm(h) with norm_w (the rounding of ckv_rmsnorm,
+ * Qwen2RMSNorm before the attention and before the MLP): each CTA normalises the rows
+ * itself, saving the separate RMSNorm launch of a decode step.  m <= 4, k <= 5120. */
+CKV_API int ckv_gemv_swiglu_rmsnorm(const uint16_t* h, const uint16_t* norm_w, float eps,
+                                    const uint16_t* w_gate_up, uint16_t* out, int m, int inter, int k,
+                                    ckv_stream_t stream);
+CKV_API int ckv_gemv_qkv_rope_rmsnorm(const uint16_t* h, const uint16_t* norm_w, float eps,
+                                      const uint16_t* w_qkv, const uint16_t* b_qkv, int m, int k,
+                                      int n_q_heads, int n_kv_heads, int head_dim,
+                                      const int32_t* positions, const float* rope_table,
+                                      int rope_max_pos, uint16_t* q_out, uint16_t* k_cache,
+                                      uint16_t* v_cache, int n_ctx, ckv_stream_t stream);
 
 /* ---- tensor parallel over NVLink peer memory (no collective library) ------------
  * The o_proj / down_proj row-parallel GEMM and the following all-reduce + residual add

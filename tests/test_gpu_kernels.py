@@ -406,6 +406,38 @@ def test_linear_residual_and_swiglu():
     assert rel_err(out, ref2) <= 1e-2
 
 
+@pytest.mark.parametrize("m,hid", [(1, 3584), (2, 896), (4, 5120)])
+def test_decode_gemv_fused_rmsnorm_matches_rmsnorm_then_gemv(m, hid):
+    """ckv_gemv_swiglu_rmsnorm / ckv_gemv_qkv_rope_rmsnorm (each CTA normalises h itself)
+    against ckv_rmsnorm followed by the plain GEMVs: the same rounding points, so they may
+    differ only where the sum of squares, added in another order, moves the scale."""
+    from chunkkv_b200.engine.weights import interleave_gate_up
+
+    inter, Hq, H, D, N = 1024, 8, 2, 128, 300
+    g = torch.Generator(device=DEV).manual_seed(hid + m)
+    h = torch.randn((m, hid), generator=g, device=DEV).to(BF)
+    lnw = (1 + 0.1 * torch.randn(hid, generator=g, device=DEV)).to(BF)
+    x = ops.rmsnorm(h, lnw, 1e-6)
+    wgu = interleave_gate_up((torch.randn((inter, hid), generator=g, device=DEV) * 0.02).to(BF),
+                             (torch.randn((inter, hid), generator=g, device=DEV) * 0.02).to(BF))
+    o1, o2 = (torch.empty((m, inter), dtype=BF, device=DEV) for _ in range(2))
+    ops.gemv_swiglu(h, wgu, o1, norm_w=lnw, eps=1e-6)
+    ops.gemv_swiglu(x, wgu, o2)
+    assert rel_err(o1, o2) <= 1e-2
+    assert (o1 != o2).float().mean() < 0.02
+    cols = (Hq + 2 * H) * D
+    wq = (torch.randn((cols, hid), generator=g, device=DEV) * 0.05).to(BF)
+    bq = (torch.randn(cols, generator=g, device=DEV) * 0.05).to(BF)
+    pos = torch.randperm(N, generator=g, device=DEV)[:m].sort().values.to(torch.int32)
+    tab = ops.rope_table(inv_freq(D), 512)
+    q1, q2 = (torch.empty((m, Hq * D), dtype=BF, device=DEV) for _ in range(2))
+    K1, V1, K2, V2 = (torch.zeros((H, N, D), dtype=BF, device=DEV) for _ in range(4))
+    ops.gemv_qkv_rope(h, wq, bq, Hq, H, D, pos, tab, q1, K1, V1, norm_w=lnw, eps=1e-6)
+    ops.gemv_qkv_rope(x, wq, bq, Hq, H, D, pos, tab, q2, K2, V2)
+    assert rel_err(q1, q2) <= 1e-2 and (q1 != q2).float().mean() < 0.02
+    assert rel_err(K1, K2) <= 1e-2 and rel_err(V1, V2) <= 1e-2
+
+
 @pytest.mark.parametrize("m,k", [(1, 9472), (3, 18944)])
 def test_decode_gemv_residual_long_rows(m, k):
     """Long rows (k >= 8192: four warps per row, partial sums through shared memory) against
