@@ -94,6 +94,102 @@ def _contig(*ts: torch.Tensor | None) -> None:
             raise ValueError("expected a contiguous tensor")
 
 
+def _buf(name: str, t: torch.Tensor, numel: int, dtype: torch.dtype = BF16, cols: int | None = None) -> None:
+    """`t` is a contiguous `dtype` tensor of at least `numel` elements (with a last
+    dimension of `cols`, when given): the kernels index it as a dense row-major array."""
+    if t.dtype != dtype:
+        raise ValueError(f"{name}: expected {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name}: expected a contiguous tensor")
+    if cols is not None and (t.dim() == 0 or t.shape[-1] != cols):
+        raise ValueError(f"{name}: expected rows of {cols} elements, got shape {tuple(t.shape)}")
+    if t.numel() < numel:
+        raise ValueError(f"{name}: has {t.numel()} elements, needs at least {numel}")
+
+
+def _weight(name: str, w: torch.Tensor, n: int | None, k: int) -> int:
+    """`w` is a contiguous bf16 [n][k] matrix (any n when `n` is None); returns n."""
+    if w.dim() != 2 or w.shape[1] != k or (n is not None and w.shape[0] != n):
+        raise ValueError(f"{name}: expected shape ({'n' if n is None else n}, {k}), got {tuple(w.shape)}")
+    _buf(name, w, 0)
+    return w.shape[0]
+
+
+def _cache(name: str, c: torch.Tensor, heads: int, head_dim: int) -> None:
+    """One layer's K or V cache: contiguous bf16 [heads, n_ctx, head_dim]."""
+    if c.dim() != 3 or c.shape[0] != heads or c.shape[2] != head_dim:
+        raise ValueError(f"{name}: expected shape ({heads}, n_ctx, {head_dim}), got {tuple(c.shape)}")
+    _buf(name, c, 0)
+
+
+def _rope_tab(tab: torch.Tensor, head_dim: int) -> None:
+    """A table from ``rope_table``: contiguous float32 [max_pos, head_dim / 2, 2]."""
+    if tab.dim() != 3 or tab.shape[1] * 2 != head_dim or tab.shape[2] != 2:
+        raise ValueError(f"rope_tab: expected shape (max_pos, {head_dim // 2}, 2), got {tuple(tab.shape)}")
+    _buf("rope_tab", tab, 0, dtype=torch.float32)
+
+
+def _rows_k(x: torch.Tensor) -> tuple[int, int]:
+    """The (rows, k) of a contiguous bf16 [m, k] GEMV input."""
+    if x.dim() != 2:
+        raise ValueError(f"x: expected an [m, k] matrix, got shape {tuple(x.shape)}")
+    _buf("x", x, 0)
+    return x.shape[0], x.shape[1]
+
+
+def _pool(pool: torch.Tensor) -> tuple[int, int, int, int]:
+    """A page pool [n_pages][n_layers][2][H][PAGE_TOKENS][D]: returns (n_pages, n_layers, H, D)."""
+    if pool.dim() != 6 or pool.shape[2] != 2 or pool.shape[4] != PAGE_TOKENS:
+        raise ValueError(f"pool: expected shape (pages, layers, 2, H, {PAGE_TOKENS}, D), got {tuple(pool.shape)}")
+    _buf("pool", pool, 0)
+    return pool.shape[0], pool.shape[1], pool.shape[3], pool.shape[5]
+
+
+def _table(name: str, t: torch.Tensor, stride: int) -> int:
+    """An int32 [rows][stride] metadata table: returns rows."""
+    if t.dim() != 2 or t.shape[1] != stride:
+        raise ValueError(f"{name}: expected shape (rows, {stride}), got {tuple(t.shape)}")
+    _buf(name, t, 0, dtype=torch.int32)
+    return t.shape[0]
+
+
+def _addresses(name: str, t: torch.Tensor, n: int) -> None:
+    """A device array of at least `n` 64-bit device addresses."""
+    if t.element_size() != 8 or t.is_floating_point():
+        raise ValueError(f"{name}: expected 64-bit integer addresses, got {t.dtype}")
+    _buf(name, t, n, dtype=t.dtype)
+
+
+def _gather_out(k_out: torch.Tensor, v_out: torch.Tensor, H: int, D: int, layer_lo: int, layer_hi: int) -> None:
+    """Blended caches [>= layer_hi - layer_lo][H][n_ctx][D], both of one shape."""
+    for name, t in (("k_out", k_out), ("v_out", v_out)):
+        if t.dim() != 4 or t.shape[1] != H or t.shape[3] != D or t.shape[0] < layer_hi - layer_lo:
+            raise ValueError(f"{name}: expected shape (>= {layer_hi - layer_lo}, {H}, n_ctx, {D}), "
+                             f"got {tuple(t.shape)}")
+        _buf(name, t, 0)
+    if k_out.shape != v_out.shape:
+        raise ValueError("k_out and v_out differ in shape")
+    if not 0 <= layer_lo <= layer_hi:
+        raise ValueError(f"layer range [{layer_lo}, {layer_hi}) is empty or negative")
+
+
+def _fresh_rows(k_fresh: torch.Tensor, v_fresh: torch.Tensor, rows: int, H: int, D: int) -> None:
+    """Fresh k/v rows [>= rows][>= H*D] with unit column stride and one common row stride."""
+    for name, t in (("k_fresh", k_fresh), ("v_fresh", v_fresh)):
+        if t.dtype != BF16:
+            raise ValueError(f"{name}: expected {BF16}, got {t.dtype}")
+        if t.dim() != 2 or t.stride(1) != 1 or t.shape[1] < H * D or t.shape[0] < rows:
+            raise ValueError(f"{name}: expected rows of {H * D} contiguous elements (at least {rows} rows), "
+                             f"got shape {tuple(t.shape)} with strides {t.stride()}")
+    if k_fresh.stride(0) != v_fresh.stride(0):
+        raise ValueError("k_fresh and v_fresh differ in row stride")
+
+
+def _select_ws(ws: "SelectWorkspace", n_ctx: int, n_chunks: int) -> None:
+    if ws.keep_abs.numel() < n_ctx or ws.diff.numel() < n_ctx or ws.flags.numel() < n_ctx or ws.rel.numel() < n_chunks:
+        raise ValueError(f"selection workspace too small for {n_ctx} positions and {n_chunks} chunks")
+
+
 # ------------------------------------------------------------------ re-RoPE
 def rope_table(inv_freq: torch.Tensor, max_pos: int) -> torch.Tensor:
     """(cos, sin) of fp32(p * inv_freq[j]) for p < max_pos: float32 [max_pos, half, 2]."""
@@ -141,8 +237,14 @@ def blend_gather_paged(pool: torch.Tensor, page_table: torch.Tensor, chunk_meta:
                        layer_lo: int, layer_hi: int, rot_dims: int | None = None,
                        nbytes: float = 0.0) -> None:
     """Moved cached chunks (paged) -> blended cache k_out/v_out [layers, H, N, D]."""
+    n_pages, n_layers, H, D = _pool(pool)
+    _buf("page_table", page_table, 0, dtype=torch.int32)
+    _table("chunk_meta", chunk_meta, META_STRIDE)
+    _buf("inv_freq", inv_freq, (D if rot_dims is None else rot_dims) // 2, dtype=torch.float32)
+    _gather_out(k_out, v_out, H, D, layer_lo, layer_hi)
+    if layer_hi > n_layers:
+        raise ValueError(f"layer range [{layer_lo}, {layer_hi}) past the pool's {n_layers} layers")
     _cuda(pool, page_table, chunk_meta, inv_freq, k_out, v_out)
-    n_pages, n_layers, _, H, _, D = pool.shape
     _run("ckv_blend_gather_paged", _ptr(pool), n_pages, _ptr(page_table), _ptr(chunk_meta),
               chunk_meta.shape[0], _ptr(inv_freq), D if rot_dims is None else rot_dims, _ptr(k_out),
               _ptr(v_out), layer_lo, layer_hi, n_layers, H, D, k_out.shape[2], _stream(), nbytes=nbytes)
@@ -153,8 +255,15 @@ def blend_gather_dense(k_ptrs: torch.Tensor, v_ptrs: torch.Tensor, chunk_meta: t
                        layer_lo: int, layer_hi: int, rot_dims: int | None = None,
                        nbytes: float = 0.0) -> None:
     """Moved cached chunks (per-layer tensors, by address) -> blended cache."""
-    _cuda(k_ptrs, v_ptrs, chunk_meta, inv_freq, k_out, v_out)
+    if k_out.dim() != 4:
+        raise ValueError(f"k_out: expected shape (layers, H, n_ctx, D), got {tuple(k_out.shape)}")
     H, D = k_out.shape[1], k_out.shape[3]
+    _gather_out(k_out, v_out, H, D, layer_lo, layer_hi)
+    _table("chunk_meta", chunk_meta, META_STRIDE)
+    _addresses("k_ptrs", k_ptrs, 0)
+    _addresses("v_ptrs", v_ptrs, k_ptrs.numel())
+    _buf("inv_freq", inv_freq, (D if rot_dims is None else rot_dims) // 2, dtype=torch.float32)
+    _cuda(k_ptrs, v_ptrs, chunk_meta, inv_freq, k_out, v_out)
     _run("ckv_blend_gather_dense", _ptr(k_ptrs), _ptr(v_ptrs), _ptr(chunk_meta),
               chunk_meta.shape[0], _ptr(inv_freq), D if rot_dims is None else rot_dims, _ptr(k_out),
               _ptr(v_out), layer_lo, layer_hi, H, D, k_out.shape[2], _stream(), nbytes=nbytes)
@@ -162,8 +271,13 @@ def blend_gather_dense(k_ptrs: torch.Tensor, v_ptrs: torch.Tensor, chunk_meta: t
 
 def pages_write(pool: torch.Tensor, page_ids: torch.Tensor, length: int, k_ptrs: torch.Tensor,
                 v_ptrs: torch.Tensor, head_stride: int) -> None:
+    """`length` tokens of every layer's (H, >= length, D) sources, by address, into the
+    pages page_ids[0 .. ceil(length / 16))."""
+    n_pages, n_layers, H, D = _pool(pool)
+    _buf("page_ids", page_ids, -(-length // PAGE_TOKENS), dtype=torch.int32)
+    _addresses("k_ptrs", k_ptrs, n_layers)
+    _addresses("v_ptrs", v_ptrs, n_layers)
     _cuda(pool, page_ids, k_ptrs, v_ptrs)
-    n_pages, n_layers, _, H, _, D = pool.shape
     _run("ckv_pages_write", _ptr(pool), n_pages, _ptr(page_ids), length, _ptr(k_ptrs),
               _ptr(v_ptrs), head_stride, n_layers, H, D, _stream())
 
@@ -173,8 +287,16 @@ def deviation_select(k_fresh: torch.Tensor, v_fresh: torch.Tensor, k_base: torch
                      v_base: torch.Tensor, active: torch.Tensor, pos_flags: torch.Tensor,
                      sel_meta: torch.Tensor, threshold: float | None, ws: "SelectWorkspace") -> None:
     """Layer-1 deviation + pooled top-k into the workspace (no host sync)."""
-    _cuda(k_fresh, v_fresh, k_base, v_base, active, pos_flags, sel_meta)
+    if k_base.dim() != 3:
+        raise ValueError(f"k_base: expected shape (H, n_ctx, D), got {tuple(k_base.shape)}")
     H, n_ctx, D = k_base.shape
+    _cache("k_base", k_base, H, D)
+    _cache("v_base", v_base, H, D)
+    _buf("active", active, 0, dtype=torch.int32)
+    _fresh_rows(k_fresh, v_fresh, active.numel(), H, D)
+    _buf("pos_flags", pos_flags, n_ctx, dtype=torch.uint8)
+    _select_ws(ws, n_ctx, _table("sel_meta", sel_meta, SEL_META_STRIDE))
+    _cuda(k_fresh, v_fresh, k_base, v_base, active, pos_flags, sel_meta)
     _run("ckv_deviation_select", _ptr(k_fresh), _ptr(v_fresh), k_fresh.stride(0), _ptr(k_base),
               _ptr(v_base), _ptr(active), active.numel(), _ptr(pos_flags), n_ctx, _ptr(sel_meta),
               sel_meta.shape[0], int(threshold is not None), float(threshold or 0.0), H, D,
@@ -186,8 +308,16 @@ def deviation_scores(k_fresh: torch.Tensor, v_fresh: torch.Tensor, k_base: torch
                      v_base: torch.Tensor, active: torch.Tensor, pos_flags: torch.Tensor,
                      ws: "SelectWorkspace") -> None:
     """Layer-1 diff/norm of the given KV heads into ws.diff / ws.norm (no selection)."""
-    _cuda(k_fresh, v_fresh, k_base, v_base, active, pos_flags)
+    if k_base.dim() != 3:
+        raise ValueError(f"k_base: expected shape (H, n_ctx, D), got {tuple(k_base.shape)}")
     H, n_ctx, D = k_base.shape
+    _cache("k_base", k_base, H, D)
+    _cache("v_base", v_base, H, D)
+    _buf("active", active, 0, dtype=torch.int32)
+    _fresh_rows(k_fresh, v_fresh, active.numel(), H, D)
+    _buf("pos_flags", pos_flags, n_ctx, dtype=torch.uint8)
+    _select_ws(ws, n_ctx, 0)
+    _cuda(k_fresh, v_fresh, k_base, v_base, active, pos_flags)
     _run("ckv_deviation_scores", _ptr(k_fresh), _ptr(v_fresh), k_fresh.stride(0), _ptr(k_base),
          _ptr(v_base), _ptr(active), active.numel(), _ptr(pos_flags), n_ctx, H, D, _ptr(ws.diff),
          _ptr(ws.norm), _stream())
@@ -196,6 +326,13 @@ def deviation_scores(k_fresh: torch.Tensor, v_fresh: torch.Tensor, k_base: torch
 def select_from_scores(diff: torch.Tensor, norm: torch.Tensor, pos_flags: torch.Tensor,
                        sel_meta: torch.Tensor, threshold: float | None,
                        ws: "SelectWorkspace") -> None:
+    """The pooled selection from summed fp32 scores diff/norm [n_ctx] (every non-exact
+    position active), into the workspace."""
+    n_ctx = pos_flags.numel()
+    _buf("pos_flags", pos_flags, n_ctx, dtype=torch.uint8)
+    _buf("diff", diff, n_ctx, dtype=torch.float32)
+    _buf("norm", norm, n_ctx, dtype=torch.float32)
+    _select_ws(ws, n_ctx, _table("sel_meta", sel_meta, SEL_META_STRIDE))
     _cuda(diff, norm, pos_flags, sel_meta)
     _run("ckv_select_from_scores", _ptr(diff), _ptr(norm), _ptr(pos_flags), pos_flags.numel(),
               _ptr(sel_meta), sel_meta.shape[0], int(threshold is not None), float(threshold or 0.0),
@@ -222,7 +359,19 @@ class SelectWorkspace:
 
 def apply_selection(ws: SelectWorkspace, max_rows: int, h_in, h_out, x_in, x_out, k_fresh, v_fresh,
                     k_cache, v_cache) -> None:
+    """Rows sel[:counts[0]] of h_in/x_in -> h_out/x_out, and their fresh k/v into the
+    caches at keep_abs (at most `max_rows` rows)."""
+    if k_cache.dim() != 3:
+        raise ValueError(f"k_cache: expected shape (H, n_ctx, D), got {tuple(k_cache.shape)}")
     H, n_ctx, D = k_cache.shape
+    _cache("k_cache", k_cache, H, D)
+    _cache("v_cache", v_cache, H, D)
+    hidden = h_in.shape[-1]
+    for name, t in (("h_in", h_in), ("h_out", h_out), ("x_in", x_in), ("x_out", x_out)):
+        _buf(name, t, max_rows * hidden, cols=hidden)
+    _fresh_rows(k_fresh, v_fresh, max_rows, H, D)
+    _select_ws(ws, n_ctx, 0)
+    _cuda(h_in, h_out, x_in, x_out, k_fresh, v_fresh, k_cache, v_cache)
     _run("ckv_apply_selection", _ptr(ws.sel), _ptr(ws.keep_abs), _ptr(ws.counts), max_rows,
               _ptr(h_in), _ptr(h_out), _ptr(x_in), _ptr(x_out), h_in.shape[-1], _ptr(k_fresh),
               _ptr(v_fresh), k_fresh.stride(0), _ptr(k_cache), _ptr(v_cache), H, D, n_ctx, _stream())
@@ -231,18 +380,29 @@ def apply_selection(ws: SelectWorkspace, max_rows: int, h_in, h_out, x_in, x_out
 # ------------------------------------------------------------ decoder pieces
 def embed(table: torch.Tensor, tokens: torch.Tensor, rows: torch.Tensor | None,
           out: torch.Tensor) -> torch.Tensor:
-    _cuda(table, tokens, rows, out)
     n = out.shape[0]
+    if table.dim() != 2:
+        raise ValueError(f"table: expected a [vocab, hidden] matrix, got shape {tuple(table.shape)}")
+    _buf("table", table, 0)
+    _buf("out", out, n * table.shape[1], cols=table.shape[1])
+    _buf("tokens", tokens, 0 if rows is not None else n, dtype=torch.int32)
+    if rows is not None:
+        _buf("rows", rows, n, dtype=torch.int32)
+    _cuda(table, tokens, rows, out)
     _run("ckv_embed", _ptr(table), table.shape[0], table.shape[1], _ptr(tokens), _ptr(rows), n,
               _ptr(out), _stream())
     return out
 
 
 def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
-    _cuda(x, w)
-    _bf16(x, w)
+    hidden = x.shape[-1]
+    rows = x.numel() // hidden if hidden else 0
+    _buf("x", x, 0)
+    _buf("w", w, hidden)
+    if out is not None:
+        _buf("out", out, rows * hidden, cols=hidden)
+    _cuda(x, w, out)
     out = torch.empty_like(x) if out is None else out
-    rows = x.numel() // x.shape[-1]
     _run("ckv_rmsnorm", _ptr(x), _ptr(w), _ptr(out), rows, x.shape[-1], float(eps), _stream())
     return out
 
@@ -250,9 +410,12 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | No
 def add_rmsnorm(h: torch.Tensor, delta: torch.Tensor, w: torch.Tensor, eps: float,
                 out: torch.Tensor) -> torch.Tensor:
     """h = bf16(h + delta) in place, then out = RMSNorm(h)."""
+    rows = h.numel() // h.shape[-1] if h.shape[-1] else 0
+    _buf("h", h, 0)
+    _buf("delta", delta, rows * h.shape[-1], cols=h.shape[-1])
+    _buf("w", w, h.shape[-1])
+    _buf("out", out, rows * h.shape[-1], cols=h.shape[-1])
     _cuda(h, delta, w, out)
-    _bf16(h, delta, w, out)
-    rows = h.numel() // h.shape[-1]
     _run("ckv_add_rmsnorm", _ptr(h), _ptr(delta), _ptr(w), _ptr(out), rows, h.shape[-1], float(eps),
          _stream())
     return out
@@ -283,35 +446,70 @@ def reduce_add_gather(exch, buf: int, pair: int, m: int) -> None:
 
 def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
            out: torch.Tensor | None = None) -> torch.Tensor:
-    _cuda(x, w, bias)
-    _bf16(x, w, bias)
-    _contig(x, w)
-    m, k = x.numel() // x.shape[-1], x.shape[-1]
-    n = w.shape[0]
+    k = x.shape[-1]
+    m = x.numel() // k if k else 0
+    _buf("x", x, 0)
+    n = _weight("w", w, None, k)
+    if bias is not None:
+        _buf("bias", bias, n)
+    if out is not None:
+        _buf("out", out, m * n, cols=n)
+    _cuda(x, w, bias, out)
     out = torch.empty((*x.shape[:-1], n), dtype=BF16, device=x.device) if out is None else out
     _run("ckv_linear", _ptr(x), _ptr(w), _ptr(bias), _ptr(out), m, n, k, _stream(), flops=2.0 * m * n * k)
     return out
 
 
 def linear_residual(x: torch.Tensor, w: torch.Tensor, h: torch.Tensor, m: int | None = None) -> torch.Tensor:
+    """h[:m] = bf16(h + bf16(x[:m] W^T)) (m defaults to all rows of x)."""
+    k = x.shape[-1]
+    m = (x.numel() // k if k else 0) if m is None else m
+    _buf("x", x, m * k)
+    n = _weight("w", w, None, k)
+    _buf("h", h, m * n, cols=n)
     _cuda(x, w, h)
-    m = x.numel() // x.shape[-1] if m is None else m
-    _run("ckv_linear_residual", _ptr(x), _ptr(w), _ptr(h), m, w.shape[0], x.shape[-1], _stream(),
-         flops=2.0 * m * w.shape[0] * x.shape[-1])
+    _run("ckv_linear_residual", _ptr(x), _ptr(w), _ptr(h), m, n, k, _stream(), flops=2.0 * m * n * k)
     return h
 
 
 def linear_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor, m: int | None = None) -> torch.Tensor:
+    """out[:m] = SwiGLU of x[:m] through the interleaved gate/up weight [2*inter][k]."""
+    k = x.shape[-1]
+    m = (x.numel() // k if k else 0) if m is None else m
+    _buf("x", x, m * k)
+    n2 = _weight("w_gate_up", w_gate_up, None, k)
+    _buf("out", out, m * (n2 // 2), cols=n2 // 2)
     _cuda(x, w_gate_up, out)
-    m = x.numel() // x.shape[-1] if m is None else m
-    _run("ckv_linear_swiglu", _ptr(x), _ptr(w_gate_up), _ptr(out), m, w_gate_up.shape[0] // 2,
-         x.shape[-1], _stream(), flops=2.0 * m * w_gate_up.shape[0] * x.shape[-1])
+    _run("ckv_linear_swiglu", _ptr(x), _ptr(w_gate_up), _ptr(out), m, n2 // 2, k, _stream(),
+         flops=2.0 * m * n2 * k)
     return out
 
 
 def qkv_rope(x, w_qkv, b_qkv, m, col_begin, col_end, n_q_heads, n_kv_heads, head_dim, positions,
              rope_tab, q_out=None, k_cache=None, v_cache=None, k_compact=None, v_compact=None) -> None:
+    """Columns [col_begin, col_end) of the QKV projection of x[:m] with bias and RoPE at
+    positions[:m]: q -> q_out, k/v -> the caches [H, n_ctx, D] and/or compact [m, H*D] rows."""
+    k = x.shape[-1]
+    _buf("x", x, m * k)
+    n = _weight("w_qkv", w_qkv, (n_q_heads + 2 * n_kv_heads) * head_dim, k)
+    if not 0 <= col_begin <= col_end <= n:
+        raise ValueError(f"columns [{col_begin}, {col_end}) outside the {n} rows of w_qkv")
+    if b_qkv is not None:
+        _buf("b_qkv", b_qkv, n)
+    _buf("positions", positions, m, dtype=torch.int32)
+    _rope_tab(rope_tab, head_dim)
+    if q_out is not None:
+        _buf("q_out", q_out, m * n_q_heads * head_dim)
     n_ctx = k_cache.shape[1] if k_cache is not None else 0
+    for name, c in (("k_cache", k_cache), ("v_cache", v_cache)):
+        if c is not None:
+            _cache(name, c, n_kv_heads, head_dim)
+            if c.shape[1] != n_ctx:
+                raise ValueError("k_cache and v_cache differ in length")
+    for name, c in (("k_compact", k_compact), ("v_compact", v_compact)):
+        if c is not None:
+            _buf(name, c, m * n_kv_heads * head_dim)
+    _cuda(x, w_qkv, b_qkv, positions, rope_tab, q_out, k_cache, v_cache, k_compact, v_compact)
     _run("ckv_qkv_rope", _ptr(x), _ptr(w_qkv), _ptr(b_qkv), m, x.shape[-1], col_begin, col_end,
               n_q_heads, n_kv_heads, head_dim, _ptr(positions), _ptr(rope_tab), rope_tab.shape[0],
               _ptr(q_out), _ptr(k_cache), _ptr(v_cache), n_ctx, _ptr(k_compact), _ptr(v_compact),
@@ -344,10 +542,19 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos
     """q/out [m, Hq, D]; caches [H, n_ctx, D]; key j visible to row i iff j <= positions[i].
     `workspace` must have been zeroed once when allocated (``attention_workspace``);
     without it the per-device scratch buffer is used."""
-    _cuda(q, k_cache, v_cache, positions, out)
+    if k_cache.dim() != 3:
+        raise ValueError(f"k_cache: expected shape (H, n_ctx, D), got {tuple(k_cache.shape)}")
     H, n_ctx, D = k_cache.shape
     m = q.shape[0] if m is None else m
     Hq = q.shape[-2] if q.dim() == 3 else q.shape[-1] // D
+    _cache("k_cache", k_cache, H, D)
+    _cache("v_cache", v_cache, H, D)
+    if v_cache.shape[1] != n_ctx:
+        raise ValueError("k_cache and v_cache differ in length")
+    _buf("q", q, m * Hq * D)
+    _buf("out", out, m * Hq * D)
+    _buf("positions", positions, m, dtype=torch.int32)
+    _cuda(q, k_cache, v_cache, positions, out, workspace)
     scale = 1.0 / math.sqrt(D) if scale is None else scale
     need = attention_workspace_bytes(m, Hq, H, D, n_ctx)
     if workspace is None:
@@ -363,8 +570,12 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos
 
 
 def gemv(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    _cuda(x, w)
-    m, k = x.shape
+    """out [m, n] = bf16(x W^T) for m = x rows <= 8 (lm_head on the logit rows)."""
+    m, k = _rows_k(x)
+    n = _weight("w", w, None, k)
+    if out is not None:
+        _buf("out", out, m * n, cols=n)
+    _cuda(x, w, out)
     out = torch.empty((m, w.shape[0]), dtype=BF16, device=x.device) if out is None else out
     _run("ckv_gemv", _ptr(x), _ptr(w), _ptr(out), m, w.shape[0], k, _stream(),
          flops=2.0 * m * w.shape[0] * k, nbytes=2.0 * w.shape[0] * k)
@@ -373,9 +584,10 @@ def gemv(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> t
 
 def gemv_residual(x: torch.Tensor, w: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
     """h[:m] = bf16(h + bf16(x W^T)) for m = x rows <= 8 (decode)."""
+    m, k = _rows_k(x)
+    n = _weight("w", w, None, k)
+    _buf("h", h, m * n, cols=n)
     _cuda(x, w, h)
-    m, k = x.shape
-    n = w.shape[0]
     _run("ckv_gemv_residual", _ptr(x), _ptr(w), _ptr(h), m, n, k, _stream(),
          flops=2.0 * m * n * k, nbytes=2.0 * n * k)
     return h
@@ -388,14 +600,16 @@ def gemv_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor,
                 norm_w: torch.Tensor | None = None, eps: float = 1e-6) -> torch.Tensor:
     """SwiGLU of the interleaved gate/up projection for m = x rows <= 8 (decode).  With
     `norm_w`, x is the hidden state h and the projection takes RMSNorm(h) (m <= 4)."""
-    _cuda(x, w_gate_up, out)
-    m, k = x.shape
-    inter = w_gate_up.shape[0] // 2
+    m, k = _rows_k(x)
+    inter = _weight("w_gate_up", w_gate_up, None, k) // 2
+    _buf("out", out, m * inter, cols=inter)
+    if norm_w is not None:
+        _buf("norm_w", norm_w, k)
+    _cuda(x, w_gate_up, out, norm_w)
     if norm_w is None:
         _run("ckv_gemv_swiglu", _ptr(x), _ptr(w_gate_up), _ptr(out), m, inter, k, _stream(),
              flops=2.0 * m * 2 * inter * k, nbytes=2.0 * 2 * inter * k)
     else:
-        _cuda(norm_w)
         _run("ckv_gemv_swiglu_rmsnorm", _ptr(x), _ptr(norm_w), float(eps), _ptr(w_gate_up), _ptr(out), m, inter,
              k, _stream(), flops=2.0 * m * 2 * inter * k, nbytes=2.0 * 2 * inter * k)
     return out
@@ -407,8 +621,19 @@ def gemv_qkv_rope(x: torch.Tensor, w_qkv: torch.Tensor, b_qkv: torch.Tensor, Hq:
                   eps: float = 1e-6) -> None:
     """q/k/v of m = x rows <= 8 with bias and RoPE; k, v written into the caches (decode).
     With `norm_w`, x is the hidden state h and the projection takes RMSNorm(h) (m <= 4)."""
-    _cuda(x, w_qkv, b_qkv, positions, rope_tab, q_out, k_cache, v_cache)
-    m, k = x.shape
+    m, k = _rows_k(x)
+    _weight("w_qkv", w_qkv, (Hq + 2 * Hk) * D, k)
+    _buf("b_qkv", b_qkv, (Hq + 2 * Hk) * D)
+    _buf("positions", positions, m, dtype=torch.int32)
+    _rope_tab(rope_tab, D)
+    _buf("q_out", q_out, m * Hq * D)
+    _cache("k_cache", k_cache, Hk, D)
+    _cache("v_cache", v_cache, Hk, D)
+    if v_cache.shape[1] != k_cache.shape[1]:
+        raise ValueError("k_cache and v_cache differ in length")
+    if norm_w is not None:
+        _buf("norm_w", norm_w, k)
+    _cuda(x, w_qkv, b_qkv, positions, rope_tab, q_out, k_cache, v_cache, norm_w)
     n_ctx = k_cache.shape[1]
     args = (_ptr(w_qkv), _ptr(b_qkv), m, k, Hq, Hk, D, _ptr(positions), _ptr(rope_tab), rope_tab.shape[0],
             _ptr(q_out), _ptr(k_cache), _ptr(v_cache), n_ctx, _stream())
@@ -416,12 +641,14 @@ def gemv_qkv_rope(x: torch.Tensor, w_qkv: torch.Tensor, b_qkv: torch.Tensor, Hq:
     if norm_w is None:
         _run("ckv_gemv_qkv_rope", _ptr(x), *args, **work)
     else:
-        _cuda(norm_w)
         _run("ckv_gemv_qkv_rope_rmsnorm", _ptr(x), _ptr(norm_w), float(eps), *args, **work)
 
 
 def log_softmax(row: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    _cuda(row)
+    _buf("row", row, 0)
+    if out is not None:
+        _buf("out", out, row.numel(), dtype=torch.float32)
+    _cuda(row, out)
     out = torch.empty(row.numel(), dtype=torch.float32, device=row.device) if out is None else out
     _run("ckv_log_softmax", _ptr(row), row.numel(), _ptr(out), _stream())
     return out

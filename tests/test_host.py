@@ -51,6 +51,111 @@ def test_ops_refuse_cpu_tensors():
         ops.rmsnorm(x, x[0], 1e-6)
 
 
+def test_ops_check_shapes_before_launching():
+    """The wrappers reject tensors the kernels would index out of bounds (wrong dtype,
+    strides, shapes or too few elements) on the host, before any device check."""
+    bf, i32, f32 = torch.bfloat16, torch.int32, torch.float32
+    x, w = torch.zeros((4, 64), dtype=bf), torch.zeros((32, 64), dtype=bf)
+    bad = [
+        (lambda: ops.linear(x, torch.zeros((32, 48), dtype=bf)), "shape"),
+        (lambda: ops.linear(x.float(), w), "bfloat16"),
+        (lambda: ops.linear(x, w, out=torch.zeros((4, 16), dtype=bf)), "rows of 32"),
+        (lambda: ops.linear_residual(x, w, torch.zeros((2, 32), dtype=bf)), "at least 128"),
+        (lambda: ops.linear_residual(x.t(), w.t(), torch.zeros((64, 4), dtype=bf)), "contiguous"),
+        (lambda: ops.linear_swiglu(x, w, torch.zeros((4, 32), dtype=bf)), "rows of 16"),
+        (lambda: ops.gemv(x[0], w), r"\[m, k\]"),
+        (lambda: ops.gemv_residual(x, w, torch.zeros((4, 31), dtype=bf)), "rows of 32"),
+        (lambda: ops.gemv_swiglu(x, w, torch.zeros((4, 16), dtype=bf), norm_w=torch.zeros(63, dtype=bf)),
+         "norm_w"),
+        (lambda: ops.rmsnorm(x, torch.zeros(32, dtype=bf), 1e-6), "at least 64"),
+        (lambda: ops.add_rmsnorm(x, x[:2], x[0], 1e-6, x.clone()), "delta"),
+        (lambda: ops.embed(w, torch.zeros(4, dtype=torch.int64), None, x), "int32"),
+        (lambda: ops.embed(w, torch.zeros(3, dtype=i32), None, x), "tokens"),
+        (lambda: ops.log_softmax(x[0], out=torch.zeros(64, dtype=bf)), "float32"),
+    ]
+    # attention: q [m, Hq, D], caches [H, n_ctx, D], positions int32 [m]
+    q, K = torch.zeros((3, 4, 16), dtype=bf), torch.zeros((2, 40, 16), dtype=bf)
+    pos = torch.zeros(3, dtype=i32)
+    bad += [
+        (lambda: ops.attention(q, K, K[:, :30].contiguous(), pos, q.clone()), "length"),
+        (lambda: ops.attention(q, K, K.transpose(1, 2).contiguous(), pos, q.clone()), "v_cache"),
+        (lambda: ops.attention(q, K, K, pos.long(), q.clone()), "int32"),
+        (lambda: ops.attention(q, K, K, pos[:2], q.clone()), "positions"),
+        (lambda: ops.attention(q, K, K, pos, q[:2].clone()), "out"),
+    ]
+    # QKV + RoPE: w_qkv [(Hq + 2H) * D, k], rope table float32 [max_pos, D / 2, 2]
+    Hq, H, D, k = 4, 2, 16, 64
+    wq, bq = torch.zeros(((Hq + 2 * H) * D, k), dtype=bf), torch.zeros((Hq + 2 * H) * D, dtype=bf)
+    tab, qo = torch.zeros((64, D // 2, 2), dtype=f32), torch.zeros((4, Hq * D), dtype=bf)
+    Kc = torch.zeros((H, 40, D), dtype=bf)
+    p4 = torch.zeros(4, dtype=i32)
+    bad += [
+        (lambda: ops.qkv_rope(x, wq[:100], bq, 4, 0, 100, Hq, H, D, p4, tab, q_out=qo), "w_qkv"),
+        (lambda: ops.qkv_rope(x, wq, bq, 4, 0, 200, Hq, H, D, p4, tab, q_out=qo), "columns"),
+        (lambda: ops.qkv_rope(x, wq, bq, 4, 0, 128, Hq, H, D, p4, tab.double(), q_out=qo), "float32"),
+        (lambda: ops.qkv_rope(x, wq, bq, 4, 0, 128, Hq, H, D, p4, tab[:, :4], q_out=qo), "rope_tab"),
+        (lambda: ops.qkv_rope(x, wq, bq, 4, 0, 128, Hq, H, D, p4, tab, q_out=qo, k_cache=Kc,
+                              v_cache=Kc[:, :20].contiguous()), "length"),
+        (lambda: ops.qkv_rope(x, wq, bq, 4, 64, 128, Hq, H, D, p4, tab,
+                              k_compact=torch.zeros((4, 16), dtype=bf)), "k_compact"),
+        (lambda: ops.gemv_qkv_rope(x, wq, bq, Hq, H, D, p4[:3], tab, qo, Kc, Kc), "positions"),
+        (lambda: ops.gemv_qkv_rope(x, wq, bq, Hq, H, D, p4, tab, qo, Kc[:1], Kc), "k_cache"),
+    ]
+    # gather / store write / selection: pool [pages, layers, 2, H, 16, D], meta int32 [n, 8]
+    pool = torch.zeros((4, 3, 2, H, ops.PAGE_TOKENS, D), dtype=bf)
+    table, meta = torch.zeros(4, dtype=i32), torch.zeros((2, ops.META_STRIDE), dtype=i32)
+    inv = torch.zeros(D // 2, dtype=f32)
+    ko = torch.zeros((3, H, 40, D), dtype=bf)
+    ptrs = torch.zeros(3, dtype=torch.int64)
+    ws = ops.SelectWorkspace(40, 2, "cpu")
+    kf, act, fl = torch.zeros((40, H * D), dtype=bf), torch.zeros(40, dtype=i32), torch.zeros(40, dtype=torch.uint8)
+    smeta = torch.zeros((2, ops.SEL_META_STRIDE), dtype=i32)
+    bad += [
+        (lambda: ops.blend_gather_paged(pool[:, :, :1], table, meta, inv, ko, ko.clone(), 0, 3), "pool"),
+        (lambda: ops.blend_gather_paged(pool, table, meta[:, :4], inv, ko, ko.clone(), 0, 3), "chunk_meta"),
+        (lambda: ops.blend_gather_paged(pool, table, meta, inv, ko[:2], ko[:2].clone(), 0, 3), "k_out"),
+        (lambda: ops.blend_gather_paged(pool, table, meta, inv, ko, ko[:, :, :20].clone(), 0, 3), "v_out|shape"),
+        (lambda: ops.blend_gather_paged(pool, table, meta, inv, ko, ko.clone(), 1, 4), "past the pool"),
+        (lambda: ops.blend_gather_paged(pool, table, meta, inv[:3], ko, ko.clone(), 0, 3), "inv_freq"),
+        (lambda: ops.blend_gather_dense(ptrs.float(), ptrs, meta, inv, ko, ko.clone(), 0, 3), "addresses"),
+        (lambda: ops.pages_write(pool, table[:1], 40, ptrs, ptrs, 40 * D), "page_ids"),
+        (lambda: ops.pages_write(pool, table, 40, ptrs[:2], ptrs, 40 * D), "k_ptrs"),
+        (lambda: ops.deviation_select(kf[:, :D], kf, Kc, Kc, act, fl, smeta, None, ws), "k_fresh"),
+        (lambda: ops.deviation_select(kf, kf, Kc, Kc, act, fl[:30], smeta, None, ws), "pos_flags"),
+        (lambda: ops.deviation_select(kf, kf, Kc, Kc, act, fl, smeta[:, :2], None, ws), "sel_meta"),
+        (lambda: ops.deviation_select(kf, kf, Kc, Kc, act, fl, smeta, None, ops.SelectWorkspace(20, 2, "cpu")),
+         "workspace"),
+        (lambda: ops.select_from_scores(ws.diff.double(), ws.norm, fl, smeta, None, ws), "float32"),
+        (lambda: ops.apply_selection(ws, 40, kf, kf[:20].clone(), kf, kf, kf, kf, Kc, Kc), "h_out"),
+    ]
+    for fn, msg in bad:
+        with pytest.raises(ValueError, match=msg):
+            fn()
+    # the same calls with consistent arguments get as far as the device check
+    good = [
+        lambda: ops.blend_gather_paged(pool, table, meta, inv, ko, ko.clone(), 0, 3),
+        lambda: ops.blend_gather_dense(ptrs, ptrs, meta, inv, ko, ko.clone(), 0, 3),
+        lambda: ops.pages_write(pool, table, 40, ptrs, ptrs, 40 * D),
+        lambda: ops.deviation_select(kf, kf, Kc, Kc, act, fl, smeta, None, ws),
+        lambda: ops.deviation_scores(kf, kf, Kc, Kc, act, fl, ws),
+        lambda: ops.select_from_scores(ws.diff, ws.norm, fl, smeta, None, ws),
+        lambda: ops.apply_selection(ws, 40, kf, kf.clone(), kf, kf.clone(), kf, kf, Kc, Kc),
+    ]
+    good += [
+        lambda: ops.linear(x, w, out=torch.zeros((4, 32), dtype=bf)),
+        lambda: ops.linear_residual(x, w, torch.zeros((4, 32), dtype=bf)),
+        lambda: ops.linear_swiglu(x, w, torch.zeros((4, 16), dtype=bf)),
+        lambda: ops.gemv_swiglu(x, w, torch.zeros((4, 16), dtype=bf), norm_w=torch.zeros(64, dtype=bf)),
+        lambda: ops.embed(w, torch.zeros(4, dtype=i32), None, x),
+        lambda: ops.attention(q, K, K, pos, q.clone()),
+        lambda: ops.qkv_rope(x, wq, bq, 4, 0, 128, Hq, H, D, p4, tab, q_out=qo, k_cache=Kc, v_cache=Kc),
+        lambda: ops.gemv_qkv_rope(x, wq, bq, Hq, H, D, p4, tab, qo, Kc, Kc),
+    ]
+    for fn in good:
+        with pytest.raises(ValueError, match="CUDA"):
+            fn()
+
+
 class _C:
     def __init__(self, n):
         self.length = n
