@@ -50,13 +50,13 @@ __device__ __forceinline__ float2 rope_cs(float pos_or_delta, float inv_freq) {
 
 // Copy `rows` rows of head_dim bf16 from src to dst, rotating by the per-j
 // table cs (smem) when rotate != 0.  Executed by one warp; each lane issues the loads
-// of up to four items before it rotates and stores any of them, so a warp keeps
+// of up to U items before it rotates and stores any of them, so a warp keeps
 // several KiB in flight (the copy is HBM-latency bound otherwise).
+template <int U = 4>
 __device__ __forceinline__ void copy_rows_warp(const uint16_t* __restrict__ src, int64_t src_row_stride,
                                                uint16_t* __restrict__ dst, int64_t dst_row_stride,
                                                int rows, int head_dim, int rot, bool rotate,
                                                const float2* cs, int lane) {
-  constexpr int U = 4;
   const int n_pair = rotate ? rot / 16 : 0;      // pair items (two 16 B vectors)
   const int n_copy = (head_dim / 8) - 2 * n_pair;  // plain 16 B vectors
   const int per_row = n_pair + n_copy;
@@ -279,7 +279,8 @@ __global__ void __launch_bounds__(256) pages_write_kernel(
     }
     const uint16_t* src = reinterpret_cast<const uint16_t*>(base) + h * head_stride + int64_t(r0) * D;
     uint16_t* dst = pool + (((int64_t(page) * n_layers + l) * 2 + kv) * H + h) * kPage * D;
-    copy_rows_warp(src, D, dst, D, rows, D, 0, false, nullptr, lane);
+    // a whole 16-token page plane (4 KiB at D = 128) in flight per warp: one round trip
+    copy_rows_warp<8>(src, D, dst, D, rows, D, 0, false, nullptr, lane);
   }
 }
 
