@@ -18,6 +18,8 @@ namespace {
 constexpr int kPage = CKV_PAGE_TOKENS;
 constexpr int kMaxHalf = 128;  // rot_dims <= 256
 constexpr int kSmemPages = 1024;  // page ids of a chunk kept in shared memory (16k tokens)
+constexpr int kCopyWarps = 8;     // warps of a 256-thread copy CTA
+constexpr int kStageVec = 256;    // 16-byte vectors in a warp's staging slot (4 KiB)
 
 struct uint4x2 {
   uint4 a, b;
@@ -46,6 +48,23 @@ __device__ __forceinline__ void rotate8(uint4& v1, uint4& v2, const float2* cs) 
 __device__ __forceinline__ float2 rope_cs(float pos_or_delta, float inv_freq) {
   const float a = __fmul_rn(pos_or_delta, inv_freq);
   return make_float2(cosf(a), sinf(a));
+}
+
+// n_vec contiguous 16-byte vectors from src to dst by one warp, through the warp's 4 KiB
+// shared staging slot: cp.async puts a whole slot of loads in flight (a 16-token page plane
+// at head_dim 128 in one round trip) without holding them in registers.  Each lane stores
+// only the vectors it copied itself, so its own wait_group is the only ordering needed.
+__device__ __forceinline__ void copy_flat_warp(const uint4* __restrict__ src, uint4* __restrict__ dst,
+                                               int n_vec, uint4* stage, int lane) {
+  const unsigned stage_s = static_cast<unsigned>(__cvta_generic_to_shared(stage));
+  for (int i0 = 0; i0 < n_vec; i0 += kStageVec) {
+    const int n = min(kStageVec, n_vec - i0);
+    for (int i = lane; i < n; i += 32)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(stage_s + 16u * i), "l"(src + i0 + i)
+                   : "memory");
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+    for (int i = lane; i < n; i += 32) __stcs(dst + i0 + i, stage[i]);
+  }
 }
 
 // Copy `rows` rows of head_dim bf16 from src to dst, rotating by the per-j
@@ -177,6 +196,7 @@ __global__ void __launch_bounds__(256, 4) blend_gather_kernel(
     int n_layers, int H, int D, int n_ctx) {
   __shared__ float2 cs[kMaxHalf];
   __shared__ int s_pages[kSmemPages];  // this chunk's page ids, so no unit waits on a table load
+  __shared__ __align__(16) uint4 s_stage[kCopyWarps][kStageVec];  // plain (V, Δ = 0) units
   const int32_t* meta = chunk_meta + blockIdx.y * CKV_META_STRIDE;
   const int table_off = meta[CKV_META_TABLE_OFFSET];
   const int length = meta[CKV_META_LENGTH];
@@ -231,7 +251,11 @@ __global__ void __launch_bounds__(256, 4) blend_gather_kernel(
           if (lane == 0) atomicOr(&g_err_word, CKV_DEV_ERR_PAGE_RANGE);
         } else {
           const uint16_t* src = pool + ((((int64_t(page) * n_layers + l) * 2 + kv) * H + h) * kPage + in_page) * D;
-          copy_rows_warp(src, D, dst + int64_t(done) * D, D, take, D, rot, rot_this, cs, lane);
+          if (rot_this)
+            copy_rows_warp(src, D, dst + int64_t(done) * D, D, take, D, rot, true, cs, lane);
+          else
+            copy_flat_warp(reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst + int64_t(done) * D),
+                           take * (D / 8), s_stage[warp], lane);
         }
         done += take;
       }
@@ -243,7 +267,11 @@ __global__ void __launch_bounds__(256, 4) blend_gather_kernel(
       }
       const uint16_t* src = reinterpret_cast<const uint16_t*>(base) + h * head_stride +
                             int64_t(src_off + r0) * D;
-      copy_rows_warp(src, D, dst, D, rows, D, rot, rot_this, cs, lane);
+      if (rot_this)
+        copy_rows_warp(src, D, dst, D, rows, D, rot, true, cs, lane);
+      else
+        copy_flat_warp(reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst), rows * (D / 8),
+                       s_stage[warp], lane);
     }
   }
 }
@@ -253,6 +281,7 @@ __global__ void __launch_bounds__(256) pages_write_kernel(
     uint16_t* __restrict__ pool, int64_t n_pages, const int32_t* __restrict__ page_ids, int length,
     const uint64_t* __restrict__ k_ptrs, const uint64_t* __restrict__ v_ptrs, int64_t head_stride,
     int n_layers, int H, int D) {
+  __shared__ __align__(16) uint4 s_stage[kCopyWarps][kStageVec];
   const int n_blocks = (length + kPage - 1) / kPage;
   const int64_t n_units = int64_t(n_blocks) * n_layers * 2 * H;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -279,8 +308,8 @@ __global__ void __launch_bounds__(256) pages_write_kernel(
     }
     const uint16_t* src = reinterpret_cast<const uint16_t*>(base) + h * head_stride + int64_t(r0) * D;
     uint16_t* dst = pool + (((int64_t(page) * n_layers + l) * 2 + kv) * H + h) * kPage * D;
-    // a whole 16-token page plane (4 KiB at D = 128) in flight per warp: one round trip
-    copy_rows_warp<8>(src, D, dst, D, rows, D, 0, false, nullptr, lane);
+    copy_flat_warp(reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst), rows * (D / 8),
+                   s_stage[warp], lane);
   }
 }
 
