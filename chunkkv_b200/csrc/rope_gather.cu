@@ -59,6 +59,7 @@ __device__ __forceinline__ void copy_flat_warp(const uint4* __restrict__ src, ui
   const unsigned stage_s = static_cast<unsigned>(__cvta_generic_to_shared(stage));
   for (int i0 = 0; i0 < n_vec; i0 += kStageVec) {
     const int n = min(kStageVec, n_vec - i0);
+    __syncwarp();  // the slot's previous contents have been read by every lane
     for (int i = lane; i < n; i += 32)
       asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(stage_s + 16u * i), "l"(src + i0 + i)
                    : "memory");
@@ -67,53 +68,39 @@ __device__ __forceinline__ void copy_flat_warp(const uint4* __restrict__ src, ui
   }
 }
 
-// Copy `rows` rows of head_dim bf16 from src to dst, rotating by the per-j
-// table cs (smem) when rotate != 0.  Executed by one warp; each lane issues the loads
-// of up to U items before it rotates and stores any of them, so a warp keeps
-// several KiB in flight (the copy is HBM-latency bound otherwise).
-template <int U = 4>
-__device__ __forceinline__ void copy_rows_warp(const uint16_t* __restrict__ src, int64_t src_row_stride,
-                                               uint16_t* __restrict__ dst, int64_t dst_row_stride,
-                                               int rows, int head_dim, int rot, bool rotate,
-                                               const float2* cs, int lane) {
-  const int n_pair = rotate ? rot / 16 : 0;      // pair items (two 16 B vectors)
-  const int n_copy = (head_dim / 8) - 2 * n_pair;  // plain 16 B vectors
-  const int per_row = n_pair + n_copy;
-  const int total = rows * per_row;
-  for (int it0 = lane; it0 < total; it0 += 32 * U) {
-    uint4 v1[U], v2[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int it = it0 + 32 * u;
-      if (it >= total) continue;
-      const int r = it / per_row;
-      const int item = it - r * per_row;
-      const uint16_t* s = src + r * src_row_stride;
+// `rows` rows of head_dim bf16, contiguous on both sides, rotated by the per-j table cs
+// (smem).  The rows come into the warp's staging slot by cp.async (a 16-row slice at
+// head_dim 128 in one fill, every load in flight, none held in registers); then each lane
+// takes rotary pairs (vectors p and p + rot/16 of a row) and the unrotated vectors past
+// rot out of shared memory and stores them.
+__device__ __forceinline__ void rotate_rows_staged_warp(const uint16_t* __restrict__ src,
+                                                        uint16_t* __restrict__ dst, int rows, int head_dim,
+                                                        int rot, const float2* cs, uint4* stage, int lane) {
+  const int vec_row = head_dim / 8;               // 16-byte vectors per row
+  const int rows_per_fill = kStageVec / vec_row;  // >= 8: head_dim <= 256
+  const int n_pair = rot / 16;                    // partner vector of p is p + n_pair
+  const int per_row = vec_row - n_pair;           // pair items + unrotated vectors
+  const unsigned stage_s = static_cast<unsigned>(__cvta_generic_to_shared(stage));
+  for (int r0 = 0; r0 < rows; r0 += rows_per_fill) {
+    const int nr = min(rows_per_fill, rows - r0);
+    const uint4* s4 = reinterpret_cast<const uint4*>(src + int64_t(r0) * head_dim);
+    uint4* d4 = reinterpret_cast<uint4*>(dst + int64_t(r0) * head_dim);
+    __syncwarp();  // every lane has read the slot's previous contents
+    for (int i = lane; i < nr * vec_row; i += 32)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(stage_s + 16u * i), "l"(s4 + i) : "memory");
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+    __syncwarp();  // every lane's copies have landed: lanes read each other's vectors below
+    for (int it = lane; it < nr * per_row; it += 32) {
+      const int r = it / per_row, item = it - r * per_row;
+      const int base = r * vec_row;
       if (item < n_pair) {
-        const int j = item * 8;
-        v1[u] = __ldcs(reinterpret_cast<const uint4*>(s + j));
-        v2[u] = __ldcs(reinterpret_cast<const uint4*>(s + j + rot / 2));
+        uint4 v1 = stage[base + item], v2 = stage[base + item + n_pair];
+        rotate8(v1, v2, cs + item * 8);
+        __stcs(d4 + base + item, v1);
+        __stcs(d4 + base + item + n_pair, v2);
       } else {
-        const int off = (rotate ? rot : 0) + (item - n_pair) * 8;
-        v1[u] = __ldcs(reinterpret_cast<const uint4*>(s + off));
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int it = it0 + 32 * u;
-      if (it >= total) continue;
-      const int r = it / per_row;
-      const int item = it - r * per_row;
-      uint16_t* d = dst + r * dst_row_stride;
-      if (item < n_pair) {
-        const int j = item * 8;
-        rotate8(v1[u], v2[u], cs + j);
-        __stcs(reinterpret_cast<uint4*>(d + j), v1[u]);
-        __stcs(reinterpret_cast<uint4*>(d + j + rot / 2), v2[u]);
-      } else {
-        // the dims past rot (or every dim when not rotating)
-        const int off = (rotate ? rot : 0) + (item - n_pair) * 8;
-        __stcs(reinterpret_cast<uint4*>(d + off), v1[u]);
+        const int v = item + n_pair;  // vectors 2 * n_pair .. vec_row - 1
+        __stcs(d4 + base + v, stage[base + v]);
       }
     }
   }
@@ -131,12 +118,13 @@ __global__ void rope_table_kernel(const float* __restrict__ inv_freq, int half, 
 
 // dst[row] = rotate(src[row], cs(delta)) for every row: the (cos, sin) of the one angle per
 // rotary pair are computed once per CTA into shared memory; warps copy 16-row units
-// (4 KiB at head_dim 128) with copy_rows_warp.
+// (4 KiB at head_dim 128) through each warp's shared staging slot.
 __global__ void __launch_bounds__(256, 4) shift_rows_kernel(const uint16_t* __restrict__ src,
                                                          uint16_t* __restrict__ dst, int64_t rows,
                                                          int head_dim, int rot, int delta,
                                                          const float* __restrict__ inv_freq) {
   __shared__ float2 cs[kMaxHalf];
+  __shared__ __align__(16) uint4 s_stage[kCopyWarps][kStageVec];
   for (int j = threadIdx.x; j < rot / 2; j += blockDim.x) cs[j] = rope_cs(float(delta), inv_freq[j]);
   __syncthreads();
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -144,8 +132,7 @@ __global__ void __launch_bounds__(256, 4) shift_rows_kernel(const uint16_t* __re
   for (int64_t u = int64_t(blockIdx.x) * 8 + warp; u < n_units; u += int64_t(gridDim.x) * 8) {
     const int64_t r0 = u * kPage;
     const int n = int(min(int64_t(kPage), rows - r0));
-    copy_rows_warp(src + r0 * head_dim, head_dim, dst + r0 * head_dim, head_dim, n, head_dim, rot, true, cs,
-                   lane);
+    rotate_rows_staged_warp(src + r0 * head_dim, dst + r0 * head_dim, n, head_dim, rot, cs, s_stage[warp], lane);
   }
 }
 
@@ -252,7 +239,7 @@ __global__ void __launch_bounds__(256, 4) blend_gather_kernel(
         } else {
           const uint16_t* src = pool + ((((int64_t(page) * n_layers + l) * 2 + kv) * H + h) * kPage + in_page) * D;
           if (rot_this)
-            copy_rows_warp(src, D, dst + int64_t(done) * D, D, take, D, rot, true, cs, lane);
+            rotate_rows_staged_warp(src, dst + int64_t(done) * D, take, D, rot, cs, s_stage[warp], lane);
           else
             copy_flat_warp(reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst + int64_t(done) * D),
                            take * (D / 8), s_stage[warp], lane);
@@ -268,7 +255,7 @@ __global__ void __launch_bounds__(256, 4) blend_gather_kernel(
       const uint16_t* src = reinterpret_cast<const uint16_t*>(base) + h * head_stride +
                             int64_t(src_off + r0) * D;
       if (rot_this)
-        copy_rows_warp(src, D, dst, D, rows, D, rot, true, cs, lane);
+        rotate_rows_staged_warp(src, dst, rows, D, rot, cs, s_stage[warp], lane);
       else
         copy_flat_warp(reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst), rows * (D / 8),
                        s_stage[warp], lane);
