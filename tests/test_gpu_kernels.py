@@ -57,8 +57,10 @@ def test_rope_table_matches_torch(D):
     assert (tab[..., 1] - ang.sin()).abs().max() < 1e-6
 
 
-@pytest.mark.parametrize("D,delta", [(64, 37), (128, -4096), (128, 4095), (64, 16384)])
+@pytest.mark.parametrize("D,delta", [(64, 37), (128, -4096), (128, 4095), (64, 16384), (256, 1234)])
 def test_shift_keys_matches_reference_rotation(D, delta):
+    """Head dims 64 / 128 take one fill of a warp's 4 KiB staging slot per 16-row unit, 256 takes
+    two (8 rows each)."""
     g = torch.Generator(device=DEV).manual_seed(1)
     k = torch.randn((1, 4, 300, D), generator=g, device=DEV).to(BF)
     inv = inv_freq(D)
@@ -121,7 +123,7 @@ def _chunk_dense(pool, ids, length, src_off=0):
     return t[:, 0, :, src_off:src_off + length], t[:, 1, :, src_off:src_off + length]
 
 
-@pytest.mark.parametrize("L,H,D", [(3, 4, 128), (4, 2, 64)])
+@pytest.mark.parametrize("L,H,D", [(3, 4, 128), (4, 2, 64), (2, 2, 256)])
 def test_blend_gather_paged(L, H, D):
     pool = _make_pool(L, H, D, 64)
     rng = np.random.default_rng(0)
@@ -154,8 +156,9 @@ def test_blend_gather_paged(L, H, D):
     assert (k_out.float() != k_ref.float()).float().mean() < 1e-3
 
 
-def test_blend_gather_dense_and_pages_roundtrip():
-    L, H, D, length = 3, 4, 128, 77
+@pytest.mark.parametrize("D", [64, 128, 256])
+def test_blend_gather_dense_and_pages_roundtrip(D):
+    L, H, length = 3, 4, 77
     from chunkkv_b200.store.pages import PagedChunkKV, PagePool
 
     pool = PagePool(L, H, D, 16, DEV)
