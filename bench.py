@@ -90,7 +90,7 @@ def peaks() -> tuple[dict, str]:
         try:
             d = json.loads(p.read_text())
             return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured"
-        except Exception:
+        except (OSError, ValueError, KeyError, TypeError):  # unreadable or partial: use the fallback
             pass
     return dict(FALLBACK_PEAKS), "fallback"
 
@@ -140,7 +140,7 @@ class ClockSampler:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
                                           "-i", str(self.index), "-lms", "200"], stdout=self.file,
                                          stderr=subprocess.DEVNULL)
-        except Exception:
+        except OSError:  # no nvidia-smi: the line then reports no clock samples
             self.proc = None
         return self
 
@@ -149,7 +149,7 @@ class ClockSampler:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
-            except Exception:
+            except subprocess.TimeoutExpired:
                 self.proc.kill()
         return False
 
