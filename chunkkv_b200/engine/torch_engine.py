@@ -230,6 +230,7 @@ class TorchEngine:
             lb = 1 if (config.full_first_layer and not p.exact) else 0
             delta = p.start - c.start
             if isinstance(c, PagedChunkKV):
+                c.check_alive()
                 paged_meta.append([len(page_table), c.length, p.start, delta, lb, L, c.src_offset, 0])
                 page_table.extend(c.page_ids.tolist())
             else:

@@ -195,6 +195,7 @@ class PrefixCacheRuntime:
         _, (_, kv) = self._seqs.popitem(last=False)
         self.bytes -= kv.nbytes
         self.pool.release(kv.page_ids)
+        kv.revoke()
 
     def _keep(self, toks: np.ndarray, result: PrefillResult) -> None:
         whole = result.chunk(0, toks.size)

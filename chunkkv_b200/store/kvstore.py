@@ -6,7 +6,9 @@ entries per key (oldest dropped), and an entry whose (prefix_hash,
 context_trust) is already stored is not stored again.  The K/V itself lives
 in one PagePool on the device: `put` copies an entry's per-layer tensors into
 pages with one kernel launch and swaps `entry.kv` for a PagedChunkKV view that
-the engine gathers from directly.  The pool is created at the first put
+the engine gathers from directly.  An evicted entry's pages go back to the pool
+and its PagedChunkKV is revoked (reading it raises ValueError), where the
+reference's evicted tensors would stay readable.  The pool is created at the first put
 (shapes taken from that entry) unless one is passed in; when it runs out of
 pages, least-recently-used keys are evicted as for the byte budget.
 """
@@ -71,7 +73,12 @@ class KVStore:
         if any(e.prefix_hash == entry.prefix_hash and e.context_trust == entry.context_trust for e in entries):
             self._data.move_to_end(key)
             return
-        self._store_pages(entry, protect=key)
+        try:
+            self._store_pages(entry, protect=key)
+        except BaseException:
+            if not self._data.get(key):  # no key left behind without entries
+                self._data.pop(key, None)
+            raise
         entries = self._data.setdefault(key, entries)
         entries.append(entry)
         self.bytes += entry_bytes(entry)
@@ -114,6 +121,7 @@ class KVStore:
         self.bytes -= entry_bytes(e)
         if isinstance(e.kv, PagedChunkKV) and e.kv.pool is self.pool:
             self.pool.release(e.kv.page_ids)
+            e.kv.revoke()  # the pages may be rewritten: reading this entry's K/V now raises
 
     def _evict_one(self, protect: LookupKey | None = None) -> bool:
         for key in self._data:

@@ -113,12 +113,44 @@ class _LayerList:
         return (self[i] for i in range(len(self)))
 
 
-class PagedChunkKV:
-    """ChunkKV-compatible view of a chunk stored in a PagePool."""
+class _Lease:
+    """Shared by a stored chunk and every view made from it (``prefix``); cleared when the
+    owner (a KVStore or the prefix cache) gives the pages back to the pool."""
 
-    def __init__(self, pool: PagePool, page_ids: np.ndarray, length: int, start: int, src_offset: int = 0):
+    __slots__ = ("alive",)
+
+    def __init__(self):
+        self.alive = True
+
+
+class PagedChunkKV:
+    """ChunkKV-compatible view of a chunk stored in a PagePool.
+
+    Unlike the reference's per-layer tensors, which stay valid after their store entry is
+    evicted, a paged chunk's pages go back to the pool on eviction and may then be
+    rewritten with another chunk.  Eviction therefore revokes the chunk: reading its K/V
+    afterwards (``keys``/``values``, ``materialize``, ``prefix``, or a prefill placement)
+    raises ValueError instead of returning another chunk's data.  ``length``, ``start``
+    and ``nbytes`` stay readable."""
+
+    def __init__(self, pool: PagePool, page_ids: np.ndarray, length: int, start: int, src_offset: int = 0,
+                 lease: _Lease | None = None):
         self.pool, self.page_ids, self.start = pool, np.asarray(page_ids, np.int32), int(start)
         self._length, self.src_offset = int(length), int(src_offset)
+        self._lease = _Lease() if lease is None else lease
+
+    @property
+    def alive(self) -> bool:
+        """False once the owner has evicted the chunk and released its pages."""
+        return self._lease.alive
+
+    def revoke(self) -> None:
+        """Mark the chunk (and every view sharing its pages) as evicted."""
+        self._lease.alive = False
+
+    def check_alive(self) -> None:
+        if not self._lease.alive:
+            raise ValueError("this chunk was evicted from its store; its pages may now hold another chunk")
 
     @property
     def length(self) -> int:
@@ -140,13 +172,15 @@ class PagedChunkKV:
 
     def prefix(self, n: int) -> "PagedChunkKV":
         """The chunk's first `n` tokens: the same pages, no copy."""
+        self.check_alive()
         if not 0 <= n <= self._length:
             raise ValueError(f"prefix of {n} tokens from a chunk of {self._length}")
         pages = (self.src_offset + n + PAGE_TOKENS - 1) // PAGE_TOKENS
-        return PagedChunkKV(self.pool, self.page_ids[:pages], n, self.start, self.src_offset)
+        return PagedChunkKV(self.pool, self.page_ids[:pages], n, self.start, self.src_offset, self._lease)
 
     def materialize(self, layer_lo: int = 0, layer_hi: int | None = None):
         """Dense copies [layers, H, len, D] of K and V (as stored, no shift)."""
+        self.check_alive()
         p = self.pool
         layer_hi = p.n_layers if layer_hi is None else layer_hi
         dev = p.pages.device

@@ -250,6 +250,54 @@ def test_kvstore_lru_budget_variants_and_dedup():
     assert pool.released  # evicted pages went back to the pool
 
 
+def test_evicted_paged_chunks_are_revoked_with_their_views():
+    """An evicted entry's pages go back to the pool and may be rewritten, so its
+    PagedChunkKV and every prefix view of it refuse to be read (on the host, before any
+    kernel), while the kept entries stay readable."""
+    from chunkkv_b200.store.kvstore import KVStore
+
+    pool = FakePool()
+    per_tok = 2 * 2 * 1 * 8 * 2
+    st = KVStore(budget_bytes=2 * 100 * per_tok, pool=pool)
+    k = [LookupKey.build([i], "m", None) for i in range(3)]
+    for key in k:
+        st.put(key, _entry(pool, 100))
+    evicted = _entry(pool, 100)  # stands for an entry the caller kept from an earlier get()
+    st2 = KVStore(budget_bytes=100 * per_tok, pool=pool)
+    st2.put(k[0], evicted)
+    view = evicted.kv.prefix(40)
+    st2.put(k[1], _entry(pool, 100))  # over budget: k[0] goes, and with it `evicted`
+    assert st2.get(k[0]) == [] and not evicted.kv.alive and not view.alive
+    for read in (lambda: evicted.kv.materialize(), lambda: evicted.kv.keys[0], lambda: view.values[0],
+                 lambda: evicted.kv.prefix(10)):
+        with pytest.raises(ValueError, match="evicted"):
+            read()
+    assert evicted.kv.length == 100 and evicted.kv.nbytes == 100 * per_tok  # bookkeeping still works
+    assert st.get(k[0]) == [] and all(e.kv.alive for key in k[1:] for e in st.get(key))
+
+
+def test_kvstore_put_that_fails_leaves_no_empty_key():
+    from chunkkv_b200.store.kvstore import Entry, KVStore
+    from chunkkv_b200.store.pages import PAGE_TOKENS
+    from chunkkv_b200.types import TrustLevel
+
+    class TinyPool(FakePool):
+        n_pages = 4
+
+        def matches(self, L, H, D):
+            return True
+
+        def alloc(self, n):
+            return None  # never room: the new key is the only one, so nothing can be evicted
+
+    st = KVStore(pool=TinyPool())
+    key = LookupKey.build([7], "m", None)
+    ks = [torch.zeros((1, 1, 2 * PAGE_TOKENS, 8), dtype=torch.bfloat16) for _ in range(2)]
+    with pytest.raises(MemoryError):
+        st.put(key, Entry(ChunkKV(ks, ks, 0), "c", "p", TrustLevel.SYSTEM))
+    assert key not in st._data and len(st) == 0 and st.bytes == 0
+
+
 def test_kvstore_entry_bytes_match_reference_count():
     from chunkkv_b200.store.kvstore import Entry
     from chunkkv_b200.types import TrustLevel
