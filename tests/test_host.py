@@ -43,6 +43,23 @@ def test_status_codes_map_to_reference_exceptions():
         _lib.call("ckv_attention", 16, 16, 16, 16, 16, 1, 1, 1, 96, 8, 1.0, None, 0, None)
 
 
+def test_fused_norm_gemv_limits_are_refused_before_launch():
+    """The RMSNorm-fused decode GEMVs keep the normalised rows in shared memory: more than 4
+    rows, more than 5120 columns or a missing norm weight is refused on the host."""
+    swiglu = "ckv_gemv_swiglu_rmsnorm"  # (h, norm_w, eps, w, out, m, inter, k, stream)
+    for args, msg in [((16, 16, 1e-6, 16, 16, 5, 128, 64, None), "fused norm"),
+                      ((16, 16, 1e-6, 16, 16, 1, 128, 5128, None), "fused norm"),
+                      ((16, None, 1e-6, 16, 16, 1, 128, 64, None), "null norm")]:
+        with pytest.raises(ValueError):
+            _lib.call(swiglu, *args)
+        assert msg in _lib.last_error()
+    # (h, norm_w, eps, w, b, m, k, Hq, Hk, D, positions, rope, max_pos, q, K, V, n_ctx, stream)
+    with pytest.raises(ValueError):
+        _lib.call("ckv_gemv_qkv_rope_rmsnorm", 16, 16, 1e-6, 16, 16, 6, 64, 4, 2, 64, 16, 16, 64, 16, 16, 16,
+                  40, None)
+    assert "fused norm" in _lib.last_error()
+
+
 def test_ops_refuse_cpu_tensors():
     x = torch.zeros((4, 64), dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="CUDA"):
