@@ -210,6 +210,33 @@ def test_result_chunks_are_views_until_read_then_copies():
     assert ks[0].abs().sum() > 0  # the copy is detached from the cache
 
 
+def test_evicted_store_chunk_is_refused_by_prefill():
+    """An entry evicted from the store gives its pages back; a caller still holding its
+    PagedChunkKV cannot place it in a prefill (ValueError before any launch), while the
+    entry that replaced it serves as usual."""
+    from chunkkv_b200.store.keys import LookupKey
+    from chunkkv_b200.store.kvstore import Entry, KVStore
+    from chunkkv_b200.types import TrustLevel
+
+    s = scenario("tiny_bf16")
+    eng = engine_for(s)
+    doc = s.first_tokens[0][:64]
+    res = eng.prefill(doc)
+    per_entry = s.shape.n_layers * 2 * s.shape.n_kv * 64 * s.shape.head_dim * 2
+    store = KVStore(budget_bytes=per_entry)  # room for exactly one entry
+    k1, k2 = LookupKey.build([1], "m", None), LookupKey.build([2], "m", None)
+    store.put(k1, Entry(res.chunk(0, 64), "c", "p1", TrustLevel.SYSTEM))
+    old = store.get(k1)[0].kv
+    store.put(k2, Entry(res.chunk(0, 64), "c", "p2", TrustLevel.SYSTEM))
+    assert store.get(k1) == [] and not old.alive
+    query = doc + [1, 2, 3]
+    with pytest.raises(ValueError, match="evicted"):
+        eng.prefill(query, [Placement(old, 0)], BlendConfig())
+    new = store.get(k2)[0].kv
+    out = eng.prefill(query, [Placement(new, 0)], BlendConfig())
+    assert torch.isfinite(out.logits.float()).all()
+
+
 def test_logits_for_unrecomputed_positions_raise():
     s = scenario("tiny_fp32")
     eng = engine_for(s)
