@@ -1,6 +1,6 @@
 """Generate the golden fixtures by running the REFERENCE TorchEngine on CPU.
 
-    python tests/golden/make_golden.py [--ref /path/to/chunkkv/src] [names...]
+    python tests/golden/make_golden.py --ref /path/to/chunkkv/src [names...]
 
 Needs the reference source tree (sarvanithin/chunkkv, src/ importable) and the
 transformers Qwen2 model; it runs only where those exist, never in the tests.
@@ -146,7 +146,7 @@ def run(name: str, ref_src: str) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference/src", help="reference src/ directory")
+    ap.add_argument("--ref", required=True, help="the reference project's src/ directory")
     ap.add_argument("names", nargs="*", default=list(SCENARIOS))
     a = ap.parse_args()
     torch.set_num_threads(max(1, torch.get_num_threads()))

@@ -1,6 +1,6 @@
 """Generate report_summary.json with the REFERENCE's bench/report.py.
 
-    python tests/golden/make_report_golden.py [--ref /path/to/chunkkv]
+    python tests/golden/make_report_golden.py --ref /path/to/chunkkv
 
 Seeded synthetic replay rows (the fields bench/replay.py writes) go through the
 reference's summarize() and boot_ci(); rows and results are saved so the tests can
@@ -41,7 +41,7 @@ def rows(policy: str, seed: int, n: int = 23) -> list[dict]:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="the reference project checkout (sarvanithin/chunkkv)")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.ref) / "src"))
     sys.path.insert(0, args.ref)

@@ -1,6 +1,6 @@
 """Generate runtime_policies.json by running the REFERENCE runtimes (P0-P4).
 
-    python tests/golden/make_runtime_golden.py [--ref /path/to/chunkkv]
+    python tests/golden/make_runtime_golden.py --ref /path/to/chunkkv
 
 Needs the reference source tree (sarvanithin/chunkkv: src/ and bench/); it runs
 only where that exists, never in the tests.  The request stream of
@@ -36,7 +36,7 @@ def describe(placements, blend) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="the reference project checkout (sarvanithin/chunkkv)")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.ref) / "src"))
     sys.path.insert(0, args.ref)
