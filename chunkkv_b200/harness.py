@@ -8,8 +8,8 @@ returns one row per request with the reference's fields: time to first token
 decisions, and against the P0 run of the same request the first-token KL, whether
 the greedy continuation is identical, and the share of it that agrees before the
 first difference.  Outputs are compared as token lists (the synthetic streams have
-no text).  `summarize` and `boot_ci` aggregate rows as report.py does (percentile
-bootstrap, 2000 resamples, seed 0).
+no text).  `summarize` and `boot_ci` aggregate the rows into the report's fields
+with the report's statistics (percentile bootstrap, 2000 resamples, seed 0).
 """
 
 from __future__ import annotations
@@ -21,43 +21,56 @@ import numpy as np
 
 
 def boot_ci(x: np.ndarray, stat=np.mean, n: int = 2000, seed: int = 0) -> tuple[float, float]:
-    """95 % percentile-bootstrap interval of `stat` (report.py:17-22)."""
+    """95 % percentile-bootstrap interval of `stat` over `x`.
+
+    The published method that bench/report.py:17-22 uses: `n` resamples of len(x)
+    indices drawn uniformly with replacement from numpy's default generator seeded
+    with `seed`, the 2.5th and 97.5th percentiles of the resampled statistic.  All
+    resamples are drawn as one (n, len(x)) index matrix (the generator yields the
+    same index stream as one draw per resample) and the statistic is taken along
+    its rows."""
     x = np.asarray(x)
-    if len(x) == 0:
+    if x.size == 0:
         return float("nan"), float("nan")
-    rng = np.random.default_rng(seed)
-    s = [stat(x[rng.integers(0, len(x), len(x))]) for _ in range(n)]
-    return float(np.percentile(s, 2.5)), float(np.percentile(s, 97.5))
+    idx = np.random.default_rng(seed).integers(0, x.size, (n, x.size))
+    samples = x[idx]
+    try:
+        stats = stat(samples, axis=1)
+    except TypeError:  # a statistic without an axis argument
+        stats = np.array([stat(row) for row in samples])
+    lo, hi = np.percentile(stats, [2.5, 97.5])
+    return float(lo), float(hi)
+
+
+def _column(rows: list[dict], key: str, dtype=np.float64) -> np.ndarray:
+    return np.fromiter((r[key] for r in rows), dtype=dtype, count=len(rows))
 
 
 def summarize(rows: list[dict], skip_first: int = 0) -> dict:
-    """One policy's rows -> n, TTFT p50/p95, token-weighted compute share, KL and
-    P0 agreement with its interval, accuracy / attack rates when present, and the
-    decision counts (report.py:29-57)."""
+    """One policy's replay rows -> the report fields of bench/report.py:29-57 that
+    these replays produce: request count, TTFT p50 / p95, the token-weighted
+    compute share, and, for rows compared with P0, the mean first-token KL and
+    the share of outputs equal to P0's with its bootstrap interval; plus the
+    counts of gate actions and reasons.  (The reference's accuracy, attack and
+    conflict fields come from its labelled real-text traces; synthetic streams
+    carry no such labels, so they are not summarised here.)"""
     rows = rows[skip_first:]
-    ttft = np.array([r["ttft"] for r in rows])
-    toks = np.array([r["tokens"] for r in rows], dtype=np.float64)
-    s = {
-        "n": len(rows),
-        "ttft_p50": float(np.median(ttft)), "ttft_p95": float(np.percentile(ttft, 95)),
-        "compute": float(np.sum(np.array([r["compute"] for r in rows]) * toks) / np.sum(toks)),
-    }
-    if "kl" in rows[0]:
-        s["kl"] = float(np.mean([r["kl"] for r in rows]))
-        m = np.array([r["match_p0"] for r in rows], float)
-        s["match_p0"], s["match_ci"] = float(m.mean()), boot_ci(m)
-        conf = np.array([r["match_p0"] for r in rows if r.get("conflict")], float)
-        if len(conf):
-            s["match_p0_conflict"] = float(conf.mean())
-    if "correct" in rows[0]:
-        c = np.array([r["correct"] for r in rows], float)
-        s["acc"], s["acc_ci"] = float(c.mean()), boot_ci(c)
-    att = [r["attacked"] for r in rows if "attacked" in r]
-    if att:
-        s["attack_success"] = float(np.mean(att))
-    s["decisions"] = dict(Counter(a for r in rows for a, _ in r["decisions"]))
-    s["reasons"] = dict(Counter(why for r in rows for _, why in r["decisions"]))
-    return s
+    ttft = _column(rows, "ttft")
+    tokens = _column(rows, "tokens")
+    p50, p95 = np.percentile(ttft, [50, 95])
+    out = {"n": len(rows), "ttft_p50": float(p50), "ttft_p95": float(p95),
+           "compute": float(np.sum(_column(rows, "compute") * tokens) / np.sum(tokens))}
+    if rows and "kl" in rows[0]:
+        match = _column(rows, "match_p0")
+        out.update(kl=float(np.mean(_column(rows, "kl"))), match_p0=float(match.mean()),
+                   match_ci=boot_ci(match))
+    pairs = Counter((action, reason) for r in rows for action, reason in r["decisions"])
+    actions, reasons = Counter(), Counter()
+    for (action, reason), c in pairs.items():
+        actions[action] += c
+        reasons[reason] += c
+    out["decisions"], out["reasons"] = dict(actions), dict(reasons)
+    return out
 
 
 def compare_to_p0(logp: np.ndarray, gen: list[int], p0_logp: np.ndarray, p0_gen: list[int]) -> dict:

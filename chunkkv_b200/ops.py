@@ -16,6 +16,7 @@ BF16 = torch.bfloat16
 PAGE_TOKENS = 16
 META_STRIDE = 8
 SEL_META_STRIDE = 4
+SELECT_SCRATCH_PER_POSITION = 5  # bytes of selection scratch per position (CKV_SELECT_SCRATCH_BYTES)
 
 
 class LaunchTimer:
@@ -186,7 +187,7 @@ def _fresh_rows(k_fresh: torch.Tensor, v_fresh: torch.Tensor, rows: int, H: int,
 
 
 def _select_ws(ws: "SelectWorkspace", n_ctx: int, n_chunks: int) -> None:
-    if ws.keep_abs.numel() < n_ctx or ws.diff.numel() < n_ctx or ws.flags.numel() < n_ctx or ws.rel.numel() < n_chunks:
+    if ws.keep_abs.numel() < n_ctx or ws.diff.numel() < n_ctx or ws.scratch.numel() < SELECT_SCRATCH_PER_POSITION * n_ctx or ws.rel.numel() < n_chunks:
         raise ValueError(f"selection workspace too small for {n_ctx} positions and {n_chunks} chunks")
 
 
@@ -301,7 +302,7 @@ def deviation_select(k_fresh: torch.Tensor, v_fresh: torch.Tensor, k_base: torch
               _ptr(v_base), _ptr(active), active.numel(), _ptr(pos_flags), n_ctx, _ptr(sel_meta),
               sel_meta.shape[0], int(threshold is not None), float(threshold or 0.0), H, D,
               _ptr(ws.diff), _ptr(ws.norm), _ptr(ws.rel), _ptr(ws.keep_abs), _ptr(ws.sel),
-              _ptr(ws.counts), _ptr(ws.flags), _ptr(ws.counter), _stream())
+              _ptr(ws.counts), _ptr(ws.scratch), _ptr(ws.counter), _stream())
 
 
 def deviation_scores(k_fresh: torch.Tensor, v_fresh: torch.Tensor, k_base: torch.Tensor,
@@ -336,7 +337,7 @@ def select_from_scores(diff: torch.Tensor, norm: torch.Tensor, pos_flags: torch.
     _cuda(diff, norm, pos_flags, sel_meta)
     _run("ckv_select_from_scores", _ptr(diff), _ptr(norm), _ptr(pos_flags), pos_flags.numel(),
               _ptr(sel_meta), sel_meta.shape[0], int(threshold is not None), float(threshold or 0.0),
-              _ptr(ws.rel), _ptr(ws.keep_abs), _ptr(ws.sel), _ptr(ws.counts), _ptr(ws.flags),
+              _ptr(ws.rel), _ptr(ws.keep_abs), _ptr(ws.sel), _ptr(ws.counts), _ptr(ws.scratch),
               _stream())
 
 
@@ -353,7 +354,9 @@ class SelectWorkspace:
         self.keep_abs = torch.empty(n_ctx, **i32)
         self.sel = torch.empty(n_ctx, **i32)
         self.counts = torch.zeros(8, **i32)
-        self.flags = torch.zeros((n_ctx + 3) // 4 * 4, dtype=torch.uint8, device=device)
+        # per position: a 4-byte score key and a flag byte (used by the selection when
+        # n_ctx is larger than what it keeps in shared memory)
+        self.scratch = torch.zeros(SELECT_SCRATCH_PER_POSITION * n_ctx, dtype=torch.uint8, device=device)
         self.counter = torch.zeros(1, **i32)
 
 

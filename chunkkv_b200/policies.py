@@ -24,22 +24,35 @@ DESCRIPTIONS = {
 }
 
 
+# policy -> (runtime kind, gate settings as GateConfig fields, runtime options).
+# Ratios are written in units of the `ratio` argument: ("ratio", k) means
+# min(1, k * ratio).  The settings are bench/policies.py:20-35's.
+_TABLE: dict[str, tuple[str, dict, dict]] = {
+    "P0": ("chunk", {}, {"enabled": False}),
+    "P1": ("prefix", {}, {}),
+    "P2": ("chunk", {"mode": "naive"}, {"provenance": False}),
+    "P3": ("chunk", {"mode": "always_blend", "ratio_same_context": ("ratio", 1)}, {"provenance": False}),
+    "P4": ("chunk", {"ratio_same_context": ("ratio", 1), "ratio_other_context": ("ratio", 2),
+                     "escalate_threshold": "escalate", "cross_context": "cross_context"}, {"provenance": True}),
+}
+
+
 def build(policy: str, engine, model_id: str, budget_bytes: int = 3 << 30, ratio: float = 0.15,
           escalate: float | None = None, cross_context: str = "blend", store: KVStore | None = None):
     """The runtime for `policy`.  `store` (optional) replaces the fresh KVStore of
     `budget_bytes` that the chunk-reuse policies get by default."""
-    store = store if store is not None else KVStore(budget_bytes, device=getattr(engine, "device", None))
-    if policy == "P0":
-        return ChunkReuseRuntime(engine, model_id, store, ReuseGate(), enabled=False)
-    if policy == "P1":
+    if policy not in _TABLE:
+        raise ValueError(policy)
+    kind, gate_fields, opts = _TABLE[policy]
+    if kind == "prefix":
         return PrefixCacheRuntime(engine, budget_bytes)
-    if policy == "P2":
-        return ChunkReuseRuntime(engine, model_id, store, ReuseGate(GateConfig(mode="naive")), provenance=False)
-    if policy == "P3":
-        gate = ReuseGate(GateConfig(mode="always_blend", ratio_same_context=ratio))
-        return ChunkReuseRuntime(engine, model_id, store, gate, provenance=False)
-    if policy == "P4":
-        gate = ReuseGate(GateConfig(ratio_same_context=ratio, ratio_other_context=min(1.0, 2 * ratio),
-                                    escalate_threshold=escalate, cross_context=cross_context))
-        return ChunkReuseRuntime(engine, model_id, store, gate, provenance=True)
-    raise ValueError(policy)
+    args = {"escalate": escalate, "cross_context": cross_context}
+
+    def value(v):
+        if isinstance(v, tuple):  # ("ratio", k)
+            return ratio if v[1] == 1 else min(1.0, v[1] * ratio)
+        return args[v] if isinstance(v, str) and v in args else v
+
+    gate = ReuseGate(GateConfig(**{k: value(v) for k, v in gate_fields.items()}))
+    store = store if store is not None else KVStore(budget_bytes, device=getattr(engine, "device", None))
+    return ChunkReuseRuntime(engine, model_id, store, gate, **opts)
