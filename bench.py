@@ -64,7 +64,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--extra-ratios", default="0.30,0.50", help="also time these ratios (TTFT only)")
     ap.add_argument("--kernel-case", choices=["swiglu", "oproj", "down", "qkv", "attention", "gather", "deviation",
-                                              "decode_swiglu", "decode_down"],
+                                              "deviation_scores", "select", "decode_swiglu", "decode_down"],
                     help="time one kernel at its 7B-bench shape (for ncu captures) instead of the prefill")
     args = ap.parse_args()
     tp = args.workload == "tp"
@@ -1151,7 +1151,7 @@ def run_kernel_case(args):
         kc, vc = rnd(H, N, D, scale=1.0), rnd(H, N, D, scale=1.0)
         out = torch.empty_like(q)
         fn = lambda: ops.attention(q, kc, vc, pos, out)  # noqa: E731
-    elif args.kernel_case == "deviation":
+    elif args.kernel_case in ("deviation", "deviation_scores", "select"):
         # every position active (layer 1 of a blend), cached chunks with 4 sinks each and
         # a fresh query tail; enough input sets, used in turn, that none is still in L2
         # when its turn comes again (algorithmic bytes: 4 x H x D x 2 B per position)
@@ -1180,8 +1180,15 @@ def run_kernel_case(args):
         def fn():
             kf, vf, Kb, Vb = sets[turn[0] % n_sets]
             turn[0] += 1
-            ops.deviation_select(kf, vf, Kb, Vb, act, flags, meta, None, ws)
-        kernel_bytes = nbytes
+            if args.kernel_case == "deviation":
+                ops.deviation_select(kf, vf, Kb, Vb, act, flags, meta, None, ws)
+            elif args.kernel_case == "deviation_scores":  # phase 1 alone
+                ops.deviation_scores(kf, vf, Kb, Vb, act, flags, ws)
+            else:  # "select": phase 2 alone, from the scores already in the workspace
+                ops.select_from_scores(ws.diff[:N], ws.norm[:N], flags, meta, None, ws)
+        if args.kernel_case == "select":
+            ops.deviation_scores(*sets[0], act, flags, ws)
+        kernel_bytes = nbytes if args.kernel_case != "select" else 8 * N
     else:  # gather: 10 chunks x 512 tokens x 27 layers from the page pool
         from chunkkv_b200.store.pages import PagePool
 

@@ -164,6 +164,16 @@ __device__ __forceinline__ bool wait_counter(const unsigned* p, unsigned target,
 }
 
 // ---------------------------------------------------------------- device: TMA
+// Untiled bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned)
+// from global memory into this CTA's shared memory, completing on `bar` (no multicast).
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 2-D tiled bulk tensor load into this CTA's shared memory (no multicast).
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y,
                                             uint64_t* bar) {

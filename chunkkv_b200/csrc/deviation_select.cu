@@ -4,18 +4,23 @@
 // warp per row with all of the row's loads in flight):
 //   diff = sum_{h,d} fp32(bf16(k - K))^2 + sum fp32(bf16(v - V))^2   (torch_engine.py:118-119)
 //   norm = sum fp32(k)^2 + sum fp32(v)^2                             (torch_engine.py:120)
+// and, for rows that are eligible unless their chunk escalates (cached, not a
+// sink, inside a pooled chunk), a shared-memory histogram of the top 11 bits of
+// the score, added into a global histogram in the control block.
 // Phase 2 (the last CTA to finish, found with an atomic ticket — no waiting):
 //   per-chunk rel = sum diff / sum norm over the chunk span           (torch_engine.py:132)
 //   keep = ~cached | sink | escalated spans; pool = pooled spans     (torch_engine.py:125-140)
 //   budget = min(sum of per-chunk budgets, |pool & ~keep|)          (torch_engine.py:139,142)
 //   top-`budget` eligible positions by diff: a three-level radix select
-//   (11, 11 and 9 bits) on the fp32 bit pattern of diff >= 0, with
-//   warp-aggregated shared-memory histograms; equal scores: lower position
-//   first — the reference's argsort leaves that order undefined,
-//   torch_engine.py:144
+//   (11, 11 and 9 bits) on the fp32 bit pattern of diff >= 0 — the first
+//   level's histogram is phase 1's unless a chunk escalated, an exact position
+//   lies in the pool, or there was no phase 1 (selection from given scores);
+//   equal scores: lower position first — the reference's argsort leaves that
+//   order undefined, torch_engine.py:144
 //   keep_abs = ascending kept positions, sel = index in the active list (146-150).
 // Phase 2 keeps one 4-byte score key and one flag byte per position in shared
-// memory when n_ctx <= kSmemPositions, otherwise in the caller's scratch.
+// memory when n_ctx <= kSmemPositions, otherwise in the caller's scratch, and
+// walks them four positions per lane at a time.
 #include "ckv_common.cuh"
 
 CKV_DEFINE_ERR_WORD(select)
@@ -25,14 +30,27 @@ namespace {
 
 constexpr int kThreads = 1024;
 constexpr int kWarps = kThreads / 32;
-// positions whose keys and flags phase 2 holds in shared memory (5 bytes each)
-constexpr int kSmemPositions = 20480;
-constexpr uint32_t kNotEligible = 0xffffffffu;  // key of a position outside the pool
+// positions whose keys and flags phase 2 holds in shared memory (5 bytes each: 210 KiB
+// at the limit, beside about 9 KiB of static shared memory)
+constexpr int kSmemPositions = 43008;
+constexpr int kStaticSmem = 10 * 1024;  // bound on the kernels' static shared memory
+// chunk tables up to this size are copied to shared memory for phase 1's histogram
+constexpr int kPhase1Chunks = 1024;
+constexpr int kBins = 2048;  // first radix level: score bits [30:20]
 
 // pos_flags input bits
 constexpr uint8_t kInCached = 1, kInSink = 2, kInExact = 4;
 // working flag bits
-constexpr uint8_t kKeep = 1, kExact = 2, kCached = 4, kKept = 0x80;
+constexpr uint8_t kKeep = 1, kExact = 2, kCached = 4, kPool = 8, kKept = 0x80;
+
+// Control block (global, CKV_SELECT_CONTROL_BYTES): ticket counter, then the phase-1
+// histogram.  Zero before the first launch; every launch leaves it zero.
+struct Control {
+  unsigned ticket;
+  unsigned pad[63];
+  unsigned hist[kBins];
+};
+static_assert(sizeof(Control) == CKV_SELECT_CONTROL_BYTES, "control block layout");
 
 struct SelectArgs {
   const float* diff;
@@ -47,12 +65,18 @@ struct SelectArgs {
   int32_t* keep_abs;
   int32_t* sel;
   int32_t* counts;
-  uint32_t* keys_scratch;   // [n_ctx] used when n_ctx > kSmemPositions
-  uint8_t* flags_scratch;   // [n_ctx]
+  uint32_t* keys_scratch;   // [round16(n_ctx)] used when n_ctx > kSmemPositions
+  uint8_t* flags_scratch;   // [round16(n_ctx)]
 };
 
-__host__ __device__ constexpr int dyn_smem_bytes(int n_ctx) {
-  return n_ctx <= kSmemPositions ? int((5 * size_t(n_ctx) + 15) / 16 * 16) : 0;
+__host__ __device__ constexpr int round16(int n) { return (n + 15) / 16 * 16; }
+// dynamic shared memory of the fused kernel: phase 1's copy of the chunk table, later
+// phase 2's keys and flags (when they fit) in the same bytes
+__host__ __device__ constexpr int dyn_smem_bytes(int n_ctx, int n_chunks) {
+  return (n_ctx <= kSmemPositions ? 5 * round16(n_ctx) : 0) >
+                 16 * (n_chunks < kPhase1Chunks ? n_chunks : kPhase1Chunks)
+             ? (n_ctx <= kSmemPositions ? 5 * round16(n_ctx) : 0)
+             : 16 * (n_chunks < kPhase1Chunks ? n_chunks : kPhase1Chunks);
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -60,46 +84,39 @@ __device__ __forceinline__ float warp_sum(float v) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
-
-__device__ __forceinline__ int4 add4(int4 a, int4 b) {
-  return make_int4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
 }
-__device__ __forceinline__ int4 sub4(int4 a, int4 b) {
-  return make_int4(a.x - b.x, a.y - b.y, a.z - b.z, a.w - b.w);
-}
-__device__ __forceinline__ int4 shfl_up4(int4 v, int o) {
-  return make_int4(__shfl_up_sync(0xffffffffu, v.x, o), __shfl_up_sync(0xffffffffu, v.y, o),
-                   __shfl_up_sync(0xffffffffu, v.z, o), __shfl_up_sync(0xffffffffu, v.w, o));
-}
-
-// Block-wide exclusive scan of four ints in thread order (all kThreads threads call it);
-// *total receives the block sums.
-__device__ int4 block_scan4(int4 v, int4* total, int4* s_warp) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int4 inc = v;
+// inclusive scan over the lanes
+__device__ __forceinline__ int warp_incl(int v) {
+  const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const int4 t = shfl_up4(inc, o);
-    if (lane >= o) inc = add4(inc, t);
+    const int t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
   }
-  if (lane == 31) s_warp[warp] = inc;
+  return v;
+}
+
+// Exclusive scan over the kWarps warps of one int per warp (lane 0's value counts);
+// returns the warp's base, *total the block sum.  All kThreads threads call it.
+__device__ int warp_bases(int v, int* total, int* s_w) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) s_w[warp] = v;
   __syncthreads();
   if (warp == 0) {
-    const int4 w = s_warp[lane];  // kWarps == 32
-    int4 wi = w;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int4 t = shfl_up4(wi, o);
-      if (lane >= o) wi = add4(wi, t);
-    }
-    s_warp[lane] = sub4(wi, w);
-    if (lane == 31) s_warp[kWarps] = wi;
+    const int x = s_w[lane];  // kWarps == 32
+    const int inc = warp_incl(x);
+    s_w[lane] = inc - x;
+    if (lane == 31) s_w[kWarps] = inc;
   }
   __syncthreads();
-  const int4 r = add4(s_warp[warp], sub4(inc, v));
-  *total = s_warp[kWarps];
-  __syncthreads();  // s_warp reusable after return
-  return r;
+  const int base = s_w[warp];
+  *total = s_w[kWarps];
+  __syncthreads();
+  return base;
 }
 
 // Ordering key of a score: the bit pattern of a non-negative fp32 value is monotonic in
@@ -110,27 +127,33 @@ __device__ __forceinline__ uint32_t score_key(float d) {
   return ((u & 0x80000000u) || u > 0x7f800000u) ? 0u : u;
 }
 
-// Histogram add with one shared-memory atomic per distinct bin in the warp (many
-// positions share a bin, e.g. every token whose fresh K/V equal the cached ones).
+// Histogram add.  When every active lane of the warp has the same bin (keys that
+// cluster, e.g. every token whose fresh K/V equal the cached ones), one lane adds them
+// all; otherwise each lane adds its own (keys mostly in distinct bins).
 // Warp-uniform call: every lane of the warp must reach it.
 __device__ __forceinline__ void hist_add(uint32_t* hist, uint32_t bin, bool on) {
   const unsigned act = __ballot_sync(0xffffffffu, on);
-  if (on) {
-    const unsigned peers = __match_any_sync(act, bin);
-    if (int(threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hist[bin], unsigned(__popc(peers)));
+  if (act == 0u) return;
+  const int leader = __ffs(act) - 1;
+  const uint32_t b0 = __shfl_sync(0xffffffffu, bin, leader);
+  if (__ballot_sync(0xffffffffu, on && bin == b0) == act) {
+    if (int(threadIdx.x & 31) == leader) atomicAdd(&hist[b0], unsigned(__popc(act)));
+  } else if (on) {
+    atomicAdd(&hist[bin], 1u);
   }
 }
 
 // Bins of `hist` (nbins = 2048 or 512) ranked from the top.  Returns the number of
 // keys counted; for k' = min(k, that number) > 0, *s_bin and *s_k receive the bin that
 // holds the k'-th largest key and the key's rank inside that bin.
-__device__ int rank_bins(const uint32_t* hist, int nbins, int k, int4* s_warp, int* s_bin,
-                         int* s_k) {
+__device__ int rank_bins(const uint32_t* hist, int nbins, int k, int* s_w, int* s_bin, int* s_k) {
   const int b0 = nbins - 1 - 2 * int(threadIdx.x), b1 = b0 - 1;
   const int c0 = b0 >= 0 ? int(hist[b0]) : 0, c1 = b1 >= 0 ? int(hist[b1]) : 0;
-  int4 tot;
-  const int excl = block_scan4(make_int4(c0 + c1, 0, 0, 0), &tot, s_warp).x;
-  const int kk = min(k, tot.x);
+  const int inc = warp_incl(c0 + c1);
+  int tot;
+  const int wb = warp_bases(__shfl_sync(0xffffffffu, inc, 31), &tot, s_w);
+  const int excl = wb + inc - (c0 + c1);
+  const int kk = min(k, tot);
   if (kk > 0 && excl < kk && kk <= excl + c0 + c1) {
     if (kk - excl <= c0) {
       *s_bin = b0;
@@ -141,47 +164,118 @@ __device__ int rank_bins(const uint32_t* hist, int nbins, int k, int4* s_warp, i
     }
   }
   __syncthreads();
-  return tot.x;
+  return tot;
 }
 
-// Phase 2: the selection, run by one CTA of kThreads threads.  keys/fl: [n_ctx] each,
-// in shared or global memory.
-__device__ void select_tail(const SelectArgs& a, uint32_t* keys, uint8_t* fl) {
-  __shared__ uint32_t hist[2048];
-  __shared__ int4 s_warp[kWarps + 1];
-  __shared__ int s_budget, s_bin, s_k;
+__device__ __forceinline__ bool eligible(uint32_t f) { return (f & kPool) && !(f & kKeep); }
+__device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xffu; }
+
+// fl[p] |= bit for p in [s, e), by one warp, eight reads in flight per lane.  Returns
+// (on every lane) whether a byte that gained the bit had `watch` set and not kKeep.
+__device__ __forceinline__ bool set_span_bit(uint8_t* fl, int s, int e, uint8_t bit, uint8_t watch) {
+  const int lane = threadIdx.x & 31;
+  bool seen = false;
+  for (int q = s + lane; q < e; q += 8 * 32) {
+    uint8_t f[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = q + 32 * j < e ? fl[q + 32 * j] : uint8_t(0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (q + 32 * j < e) {
+        fl[q + 32 * j] = f[j] | bit;
+        seen |= (f[j] & watch) && !(f[j] & kKeep);
+      }
+  }
+  return __any_sync(0xffffffffu, seen);
+}
+
+// Phase 2: the selection, run by one CTA of kThreads threads.  keys/fl: [round16(n_ctx)]
+// each, in shared or global memory (16-byte aligned).  hist: kBins shared counters;
+// phase1_hist: the control block's histogram (nullptr: no usable phase-1 histogram),
+// read and cleared here.
+__device__ void select_tail(const SelectArgs& a, uint32_t* keys, uint8_t* fl, bool in_smem,
+                            uint32_t* hist, unsigned* phase1_hist) {
+  __shared__ int s_w[kWarps + 1];
+  __shared__ int s_budget, s_bin, s_k, s_slow;
   __shared__ unsigned s_escmask;
+  __shared__ __align__(8) uint64_t bar[1];
+  __shared__ int s_abort;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n = a.n_ctx;
-
-  // 1. per-position state: keep = ~cached | sink (torch_engine.py:125)
-  for (int p = tid; p < n; p += kThreads) {
-    const uint8_t f = a.pos_flags[p];
-    uint8_t w = 0;
-    if (!(f & kInCached) || (f & kInSink)) w |= kKeep;
-    if (f & kInExact) w |= kExact;
-    if (f & kInCached) w |= kCached;
-    fl[p] = w;
-    keys[p] = kNotEligible;
-  }
+  const int nq = (n + 3) >> 2;  // quads of positions
+  const bool vec_in = ((reinterpret_cast<uintptr_t>(a.pos_flags) & 3u) == 0) &&
+                      ((reinterpret_cast<uintptr_t>(a.diff) & 15u) == 0);
+  // the phase-1 histogram, copied out and cleared for the next launch
+  if (phase1_hist)
+    for (int i = tid; i < kBins; i += kThreads) {
+      hist[i] = __ldcg(phase1_hist + i);
+      phase1_hist[i] = 0u;
+    }
   if (tid == 0) {
     s_budget = 0;
     s_escmask = 0u;
+    s_slow = phase1_hist ? 0 : 1;
   }
-  __syncthreads();
 
-  // 2. per chunk: rel over its span (positions never computed count as 0, as in the
-  // reference's zero-initialised buffers), escalation keeps the span whole, the
-  // budgets of pooled chunks add up (torch_engine.py:128-140)
+  // 1. stage the inputs: with the keys in shared memory, diff lands in the key array
+  // and pos_flags in the flag array by bulk copies (one thread issues them; the rest of
+  // each array, under 16 bytes, by plain loads); otherwise they are read in step 3.
+  const bool staged = in_smem && ((reinterpret_cast<uintptr_t>(a.diff) & 15u) == 0) &&
+                      ((reinterpret_cast<uintptr_t>(a.pos_flags) & 15u) == 0);
+  if (staged) {
+    const uint32_t diff_bulk = uint32_t(n) * 4u / 16u * 16u, flag_bulk = uint32_t(n) / 16u * 16u;
+    if (tid == 0) {
+      s_abort = 0;
+      mbar_init(bar, 1);
+      fence_barrier_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+      fence_async_smem();  // earlier generic accesses to these bytes (phase 1's chunk table)
+      mbar_expect_tx(bar, diff_bulk + flag_bulk);
+      if (diff_bulk) bulk_load(keys, a.diff, diff_bulk, bar);
+      if (flag_bulk) bulk_load(fl, a.pos_flags, flag_bulk, bar);
+    }
+    for (int p = int(diff_bulk / 4) + tid; p < n; p += kThreads) keys[p] = __float_as_uint(__ldcg(a.diff + p));
+    for (int p = int(flag_bulk) + tid; p < n; p += kThreads) fl[p] = a.pos_flags[p];
+    const bool ok = mbar_wait(bar, 0, &s_abort, &g_err_word);
+    if (__syncthreads_or(!ok)) {
+      // the copy did not complete in time (mbar_wait recorded CKV_DEV_ERR_WAIT_TIMEOUT):
+      // one more bounded wait so that nothing is still writing this CTA's shared
+      // memory, then stop with the status set
+      const uint64_t t0 = global_ns();
+      while (!mbar_try_wait(bar, 0) && global_ns() - t0 < kWaitLimitNs) {
+      }
+      if (tid == 0) a.counts[5] = int(CKV_DEV_ERR_WAIT_TIMEOUT);
+      return;
+    }
+  }
+
+  // 2. per chunk: rel over its span (never-computed positions count as 0), escalation
+  // decided (its span is kept whole in step 4), the budgets of pooled chunks add up
+  // (torch_engine.py:128-140)
   for (int c = warp; c < a.n_chunks; c += kWarps) {
     const int32_t* m = a.meta + c * CKV_SEL_META_STRIDE;
     if (m[3]) continue;  // exact
     const int s = max(m[0], 0), e = min(m[0] + m[1], n);
     float sd = 0.f, sn = 0.f;
-    for (int p = s + lane; p < e; p += 32) {
-      if (fl[p] & kExact) continue;
-      sd += __ldcg(a.diff + p);
-      sn += __ldcg(a.norm + p);
+    for (int q = s + lane; q < e; q += 16 * 32) {
+      float dd[16], nn[16];
+      uint8_t ff[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int p = q + 32 * j;
+        const bool in = p < e;
+        ff[j] = in ? (staged ? fl[p] : a.pos_flags[p]) : uint8_t(kInExact);
+        dd[j] = in ? (staged ? __uint_as_float(keys[p]) : __ldcg(a.diff + p)) : 0.f;
+        nn[j] = in ? __ldcg(a.norm + p) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (ff[j] & kInExact) continue;
+        sd += dd[j];
+        sn += nn[j];
+      }
     }
     sd = warp_sum(sd);
     sn = warp_sum(sn);
@@ -191,106 +285,236 @@ __device__ void select_tail(const SelectArgs& a, uint32_t* keys, uint8_t* fl) {
       a.rel[c] = rel;
       if (esc && c < 32) atomicOr(&s_escmask, 1u << c);
       if (!esc && m[2] >= 0) atomicAdd(&s_budget, m[2]);
+      if (esc) s_slow = 1;  // phase 1 counted this span's rows as eligible
     }
-    // overlapping escalated spans set the same bit of a byte no other step changes now
-    if (esc)
-      for (int p = s + lane; p < e; p += 32) fl[p] |= kKeep;
   }
   __syncthreads();
 
-  // 3. eligible = pool & ~keep gets its score key (torch_engine.py:142-144)
+  // 3. per-position state: keep = ~cached | sink (torch_engine.py:125); the score key
+  // of every position (never-computed positions score 0, torch_engine.py:121-122).
+  // Four positions per lane, in place over the staged copy or from global memory.
+  for (int g0 = tid; g0 < nq; g0 += 4 * kThreads) {
+    uint32_t f4[4];
+    uint4 d4[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int g = g0 + u * kThreads, p = 4 * g;
+      f4[u] = 0u;
+      d4[u] = make_uint4(0u, 0u, 0u, 0u);
+      if (g >= nq) continue;
+      if (staged) {
+        f4[u] = *reinterpret_cast<const uint32_t*>(fl + p);
+        d4[u] = *reinterpret_cast<const uint4*>(keys + p);
+      } else if (vec_in && p + 3 < n) {
+        f4[u] = __ldcg(reinterpret_cast<const unsigned*>(a.pos_flags + p));
+        d4[u] = __ldcg(reinterpret_cast<const uint4*>(a.diff + p));
+      } else {
+        uint32_t* dd = reinterpret_cast<uint32_t*>(&d4[u]);
+        for (int i = 0; i < 4 && p + i < n; ++i) {
+          f4[u] |= uint32_t(a.pos_flags[p + i]) << (8 * i);
+          dd[i] = __float_as_uint(__ldcg(a.diff + p + i));
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int g = g0 + u * kThreads, p = 4 * g;
+      if (g >= nq) continue;
+      const uint32_t d[4] = {d4[u].x, d4[u].y, d4[u].z, d4[u].w};
+      uint32_t w = 0;
+      uint4 k;
+      uint32_t* kk = reinterpret_cast<uint32_t*>(&k);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t f = byte_of(f4[u], i);
+        uint32_t b = 0;
+        if (p + i < n) {
+          if (!(f & kInCached) || (f & kInSink)) b |= kKeep;
+          if (f & kInExact) b |= kExact;
+          if (f & kInCached) b |= kCached;
+        }
+        w |= b << (8 * i);
+        kk[i] = (p + i < n && !(f & kInExact)) ? score_key(__uint_as_float(d[i])) : 0u;
+      }
+      *reinterpret_cast<uint32_t*>(fl + p) = w;
+      *reinterpret_cast<uint4*>(keys + p) = k;
+    }
+  }
+  __syncthreads();
+
+  // 4. escalated spans are kept whole (torch_engine.py:133-135); overlapping escalated
+  // spans set the same bit of a byte that no other step changes now
+  if (a.has_thr)
+    for (int c = warp; c < a.n_chunks; c += kWarps) {
+      const int32_t* m = a.meta + c * CKV_SEL_META_STRIDE;
+      if (m[3] || !(double(a.rel[c]) > a.thr)) continue;
+      set_span_bit(fl, max(m[0], 0), min(m[0] + m[1], n), kKeep, 0);
+    }
+  __syncthreads();
+
+  // 5. pool = spans of pooled, non-escalated chunks (torch_engine.py:136-140)
   for (int c = warp; c < a.n_chunks; c += kWarps) {
     const int32_t* m = a.meta + c * CKV_SEL_META_STRIDE;
     if (m[3] || m[2] < 0) continue;
     if (a.has_thr && double(a.rel[c]) > a.thr) continue;  // escalated
     const int s = max(m[0], 0), e = min(m[0] + m[1], n);
-    for (int p = s + lane; p < e; p += 32) {
-      const uint8_t f = fl[p];
-      if (!(f & kKeep)) keys[p] = score_key((f & kExact) ? 0.f : __ldcg(a.diff + p));
-    }
+    // an exact position in the pool was never computed, so phase 1 did not count it
+    if (set_span_bit(fl, s, e, kPool, kExact) && lane == 0) s_slow = 1;
   }
   __syncthreads();
 
-  // 4. radix select of the budget-th largest key: bits [30:20], [19:9], [8:0]
-  for (int i = tid; i < 2048; i += kThreads) hist[i] = 0u;
-  __syncthreads();
-  for (int base = warp * 32; base < n; base += kThreads) {
-    const int p = base + lane;
-    const uint32_t key = p < n ? keys[p] : kNotEligible;
-    hist_add(hist, key >> 20, key != kNotEligible);
+  // 6. radix select of the budget-th largest eligible key (eligible = pool & ~keep,
+  // torch_engine.py:142-144): bits [30:20], [19:9], [8:0].  Passes walk this warp's
+  // block of quads (position order = block, quad, position in quad).
+  const int per_warp = (nq + kThreads - 1) / kThreads * 32;  // quads, a multiple of 32
+  const int g_lo = min(nq, warp * per_warp), g_hi = min(nq, g_lo + per_warp);
+  if (s_slow) {  // first level from the keys
+    for (int i = tid; i < kBins; i += kThreads) hist[i] = 0u;
+    __syncthreads();
+    for (int g0 = g_lo; g0 < g_hi; g0 += 32) {
+      const int g = g0 + lane;
+      uint4 k = make_uint4(0u, 0u, 0u, 0u);
+      uint32_t f = 0u;
+      if (g < g_hi) {
+        k = *reinterpret_cast<const uint4*>(keys + 4 * g);
+        f = *reinterpret_cast<const uint32_t*>(fl + 4 * g);
+      }
+      const uint32_t kk[4] = {k.x, k.y, k.z, k.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) hist_add(hist, kk[i] >> 20, eligible(byte_of(f, i)));
+    }
   }
   __syncthreads();
-  const int n_elig = rank_bins(hist, 2048, s_budget, s_warp, &s_bin, &s_k);
+  const int n_elig = rank_bins(hist, kBins, s_budget, s_w, &s_bin, &s_k);
   const int budget = min(s_budget, n_elig);
-  uint32_t thr = 0x80000000u;  // above every eligible key: nothing selected
+  uint32_t thr = 0x80000000u;  // above every key: nothing selected
   int take_eq = 0;
   if (budget > 0) {
     uint32_t prefix = uint32_t(s_bin) << 20;
-    for (int i = tid; i < 2048; i += kThreads) hist[i] = 0u;
-    __syncthreads();
-    for (int base = warp * 32; base < n; base += kThreads) {
-      const int p = base + lane;
-      const uint32_t key = p < n ? keys[p] : kNotEligible;
-      hist_add(hist, (key >> 9) & 0x7ffu, (key >> 20) == (prefix >> 20));
+    for (int level = 0; level < 2; ++level) {
+      const int shift = level == 0 ? 20 : 9;  // bits already fixed: [31:shift]
+      const int nbits = level == 0 ? 11 : 9;  // bits resolved now, below them
+      const int nbins = 1 << nbits;
+      for (int i = tid; i < nbins; i += kThreads) hist[i] = 0u;
+      __syncthreads();
+      for (int g0 = g_lo; g0 < g_hi; g0 += 32) {
+        const int g = g0 + lane;
+        uint4 k = make_uint4(0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu);
+        uint32_t f = 0u;
+        if (g < g_hi) {
+          k = *reinterpret_cast<const uint4*>(keys + 4 * g);
+          f = *reinterpret_cast<const uint32_t*>(fl + 4 * g);
+        }
+        const uint32_t kk[4] = {k.x, k.y, k.z, k.w};
+        bool any = false;
+        bool on[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          on[i] = (kk[i] >> shift) == (prefix >> shift) && eligible(byte_of(f, i));
+          any |= on[i];
+        }
+        if (__any_sync(0xffffffffu, any)) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            hist_add(hist, (kk[i] >> (shift - nbits)) & uint32_t(nbins - 1), on[i]);
+        }
+      }
+      __syncthreads();
+      rank_bins(hist, nbins, s_k, s_w, &s_bin, &s_k);
+      prefix |= uint32_t(s_bin) << (shift - nbits);
     }
-    __syncthreads();
-    rank_bins(hist, 2048, s_k, s_warp, &s_bin, &s_k);
-    prefix |= uint32_t(s_bin) << 9;
-    for (int i = tid; i < 512; i += kThreads) hist[i] = 0u;
-    __syncthreads();
-    for (int base = warp * 32; base < n; base += kThreads) {
-      const int p = base + lane;
-      const uint32_t key = p < n ? keys[p] : kNotEligible;
-      hist_add(hist, key & 0x1ffu, (key >> 9) == (prefix >> 9));
-    }
-    __syncthreads();
-    rank_bins(hist, 512, s_k, s_warp, &s_bin, &s_k);
-    thr = prefix | uint32_t(s_bin);
+    thr = prefix;
     take_eq = s_k;
   }
 
-  // 5. mark: keys above thr, then the first take_eq equal to it by position; compact
-  // (torch_engine.py:144-150).  Each thread owns one contiguous run of positions.
-  const int seg = (n + kThreads - 1) / kThreads;
-  const int p0 = min(n, tid * seg), p1 = min(n, p0 + seg);
-  int c_eq = 0;
-  if (take_eq > 0)
-    for (int p = p0; p < p1; ++p) c_eq += keys[p] == thr ? 1 : 0;
-  int4 tot;
-  int r = block_scan4(make_int4(c_eq, 0, 0, 0), &tot, s_warp).x;
-  int4 c = make_int4(0, 0, 0, 0);  // kept, exact, kept & cached, kept & exact
-  for (int p = p0; p < p1; ++p) {
-    const uint32_t key = keys[p];
-    uint8_t f = fl[p];
-    bool kept;
-    if (key != kNotEligible) {
-      kept = key > thr;
-      if (key == thr) kept = r++ < take_eq;
-    } else {
-      kept = (f & kKeep) != 0;
+  // 7. mark: keys above thr, then the first take_eq equal to it by position; compact
+  // (torch_engine.py:144-150).  Ranks inside a warp come from lane scans, across warps
+  // from one scan per count.
+  int tot = 0;
+  int eq_run = 0;
+  if (take_eq > 0) {
+    int cnt = 0;
+    for (int g = g_lo + lane; g < g_hi; g += 32) {
+      const uint4 k = *reinterpret_cast<const uint4*>(keys + 4 * g);
+      const uint32_t f = *reinterpret_cast<const uint32_t*>(fl + 4 * g);
+      const uint32_t kk[4] = {k.x, k.y, k.z, k.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) cnt += (kk[i] == thr && eligible(byte_of(f, i))) ? 1 : 0;
     }
-    if (kept) {
-      f |= kKept;
-      fl[p] = f;
-      ++c.x;
-      if (f & kCached) ++c.z;
-      if (f & kExact) ++c.w;
-    }
-    if (f & kExact) ++c.y;
+    eq_run = warp_bases(warp_sum_i(cnt), &tot, s_w);
   }
-  const int4 base = block_scan4(c, &tot, s_warp);
-  int out = base.x, ex = base.y;
-  for (int p = p0; p < p1; ++p) {
-    const uint8_t f = fl[p];
-    if (f & kKept) {
-      a.keep_abs[out] = p;
-      a.sel[out] = p - ex;
-      ++out;
+  int c_keep = 0, c_ex = 0, c_cached = 0, c_bad = 0;  // per lane
+  for (int g0 = g_lo; g0 < g_hi; g0 += 32) {
+    const int g = g0 + lane;
+    uint4 k = make_uint4(0u, 0u, 0u, 0u);
+    uint32_t f = 0u;
+    if (g < g_hi) {
+      k = *reinterpret_cast<const uint4*>(keys + 4 * g);
+      f = *reinterpret_cast<const uint32_t*>(fl + 4 * g);
     }
-    if (f & kExact) ++ex;
+    const uint32_t kk[4] = {k.x, k.y, k.z, k.w};
+    int n_eq = 0;
+    if (take_eq > 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) n_eq += (kk[i] == thr && eligible(byte_of(f, i))) ? 1 : 0;
+    }
+    const int inc = warp_incl(n_eq);
+    int r = eq_run + inc - n_eq;  // equal keys before this quad
+    eq_run += __shfl_sync(0xffffffffu, inc, 31);
+    uint32_t out = f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t b = byte_of(f, i);
+      bool kept;
+      if (eligible(b)) {
+        kept = kk[i] > thr;
+        if (kk[i] == thr) kept = (r++ < take_eq);
+      } else {
+        kept = (b & kKeep) != 0;
+      }
+      if (kept) {
+        out |= uint32_t(kKept) << (8 * i);
+        ++c_keep;
+        if (b & kCached) ++c_cached;
+        if (b & kExact) ++c_bad;
+      }
+      if (b & kExact) ++c_ex;
+    }
+    if (g < g_hi && out != f) *reinterpret_cast<uint32_t*>(fl + 4 * g) = out;
+  }
+  int n_sel, n_exact, sel_cached, bad;
+  int out_run = warp_bases(warp_sum_i(c_keep), &n_sel, s_w);
+  int ex_run = warp_bases(warp_sum_i(c_ex), &n_exact, s_w);
+  warp_bases(warp_sum_i(c_cached), &sel_cached, s_w);
+  warp_bases(warp_sum_i(c_bad), &bad, s_w);
+  for (int g0 = g_lo; g0 < g_hi; g0 += 32) {
+    const int g = g0 + lane;
+    const uint32_t f = g < g_hi ? *reinterpret_cast<const uint32_t*>(fl + 4 * g) : 0u;
+    int nk = 0, nx = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      nk += (byte_of(f, i) & kKept) ? 1 : 0;
+      nx += (byte_of(f, i) & kExact) ? 1 : 0;
+    }
+    const int inc = warp_incl(nk | (nx << 16));  // both counts fit 16 bits per step
+    int ik = out_run + (inc & 0xffff) - nk;
+    int ix = ex_run + (inc >> 16) - nx;
+    const int all = __shfl_sync(0xffffffffu, inc, 31);
+    out_run += all & 0xffff;
+    ex_run += all >> 16;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t b = byte_of(f, i);
+      const int p = 4 * g + i;
+      if (b & kKept) {
+        a.keep_abs[ik] = p;
+        a.sel[ik] = p - ix;
+        ++ik;
+      }
+      if (b & kExact) ++ix;
+    }
   }
   if (tid == 0) {
-    const int n_sel = tot.x, sel_cached = tot.z, bad = tot.w;
     a.counts[0] = n_sel;
     a.counts[1] = sel_cached;
     a.counts[2] = budget;
@@ -304,16 +528,17 @@ __device__ void select_tail(const SelectArgs& a, uint32_t* keys, uint8_t* fl) {
 }
 
 // Phase 1 for one active row i (one warp): diff[p], norm[p] for p = active[i].
-__device__ __forceinline__ void deviation_row(
+// Returns p (on every lane; -1 if the position is out of range) and *d_out = diff[p].
+__device__ __forceinline__ int deviation_row(
     int64_t i, const uint16_t* __restrict__ k_fresh, const uint16_t* __restrict__ v_fresh,
     int64_t fstride, const uint16_t* __restrict__ k_base, const uint16_t* __restrict__ v_base,
     const int32_t* __restrict__ active, int H, int D, const uint8_t* __restrict__ pos_flags,
-    int n_ctx, float* diff, float* norm) {
+    int n_ctx, float* diff, float* norm, float* d_out) {
   const int lane = threadIdx.x & 31;
   const int p = active[i];
   if (p < 0 || p >= n_ctx) {
     if (lane == 0) atomicOr(&g_err_word, CKV_DEV_ERR_POSITION_RANGE);
-    return;
+    return -1;
   }
   // the reference compares against a zero-initialised cache (torch_engine.py:97) that
   // only moved chunks fill, so a position no chunk covers compares against zeros
@@ -368,10 +593,13 @@ __device__ __forceinline__ void deviation_row(
   dv = warp_sum(dv);
   nk = warp_sum(nk);
   nv = warp_sum(nv);
+  const float d = dk + dv;
   if (lane == 0) {
-    diff[p] = dk + dv;
+    diff[p] = d;
     norm[p] = nk + nv;
   }
+  *d_out = d;
+  return p;
 }
 
 struct RowArgs {
@@ -390,28 +618,60 @@ struct RowArgs {
 };
 
 // This CTA's rows: a contiguous block of n_act / gridDim.x (+1) rows, a warp per row.
-__device__ __forceinline__ void deviation_rows(const RowArgs& r) {
-  const int warp = threadIdx.x >> 5;
+// With `hist` (and the chunk table `tab` of n_tab chunks in shared memory), rows that
+// are eligible unless their chunk escalates add their score's top bits to it.
+__device__ __forceinline__ void deviation_rows(const RowArgs& r, uint32_t* hist, const int4* tab,
+                                               int n_tab) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r0 = int64_t(blockIdx.x) * r.n_act / gridDim.x;
   const int64_t r1 = int64_t(blockIdx.x + 1) * r.n_act / gridDim.x;
-  for (int64_t i = r0 + warp; i < r1; i += kWarps)
-    deviation_row(i, r.k_fresh, r.v_fresh, r.fstride, r.k_base, r.v_base, r.active, r.H, r.D,
-                  r.pos_flags, r.n_ctx, r.diff, r.norm);
+  for (int64_t i = r0 + warp; i < r1; i += kWarps) {
+    float d;
+    const int p = deviation_row(i, r.k_fresh, r.v_fresh, r.fstride, r.k_base, r.v_base, r.active,
+                                r.H, r.D, r.pos_flags, r.n_ctx, r.diff, r.norm, &d);
+    if (hist == nullptr || p < 0) continue;
+    const uint8_t f = r.pos_flags[p];
+    if (!(f & kInCached) || (f & (kInSink | kInExact))) continue;
+    bool pooled = false;  // inside any chunk with a budget (torch_engine.py:136-140)
+    for (int c0 = 0; c0 < n_tab && !pooled; c0 += 32) {
+      bool in = false;
+      if (c0 + lane < n_tab) {
+        const int4 t = tab[c0 + lane];  // start, length, budget, exact
+        in = !t.w && t.z >= 0 && p >= t.x && p < t.x + t.y;
+      }
+      pooled = __any_sync(0xffffffffu, in);
+    }
+    if (pooled && lane == 0) atomicAdd(&hist[score_key(d) >> 20], 1u);
+  }
 }
 
 __global__ void __launch_bounds__(kThreads) deviation_scores_kernel(RowArgs r) {
-  deviation_rows(r);
+  deviation_rows(r, nullptr, nullptr, 0);
 }
 
-__global__ void __launch_bounds__(kThreads) deviation_select_kernel(RowArgs r, unsigned* counter,
+__global__ void __launch_bounds__(kThreads) deviation_select_kernel(RowArgs r, Control* ctl,
                                                                      SelectArgs sa) {
   extern __shared__ __align__(16) unsigned char dyn_smem[];
+  __shared__ uint32_t hist[kBins];
   __shared__ int s_last;
-  deviation_rows(r);
+  // phase 1: rows, with the first radix level's histogram when the chunk table fits
+  const bool with_hist = sa.n_chunks <= kPhase1Chunks;
+  int4* tab = reinterpret_cast<int4*>(dyn_smem);
+  if (with_hist) {
+    for (int i = threadIdx.x; i < kBins; i += kThreads) hist[i] = 0u;
+    for (int c = threadIdx.x; c < sa.n_chunks; c += kThreads)
+      tab[c] = make_int4(sa.meta[4 * c], sa.meta[4 * c + 1], sa.meta[4 * c + 2], sa.meta[4 * c + 3]);
+    __syncthreads();
+  }
+  deviation_rows(r, with_hist ? hist : nullptr, tab, with_hist ? sa.n_chunks : 0);
+  __syncthreads();
+  if (with_hist)
+    for (int i = threadIdx.x; i < kBins; i += kThreads)
+      if (hist[i]) atomicAdd(&ctl->hist[i], hist[i]);
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(counter, 1u);
+    const unsigned prev = atomicAdd(&ctl->ticket, 1u);
     s_last = (prev == gridDim.x - 1) ? 1 : 0;
   }
   __syncthreads();
@@ -419,17 +679,18 @@ __global__ void __launch_bounds__(kThreads) deviation_select_kernel(RowArgs r, u
   __threadfence();
   const bool in_smem = sa.n_ctx <= kSmemPositions;
   uint32_t* keys = in_smem ? reinterpret_cast<uint32_t*>(dyn_smem) : sa.keys_scratch;
-  uint8_t* fl = in_smem ? dyn_smem + 4 * size_t(sa.n_ctx) : sa.flags_scratch;
-  select_tail(sa, keys, fl);
-  if (threadIdx.x == 0) *counter = 0u;  // ready for the next launch
+  uint8_t* fl = in_smem ? dyn_smem + 4 * size_t(round16(sa.n_ctx)) : sa.flags_scratch;
+  select_tail(sa, keys, fl, in_smem, hist, with_hist ? ctl->hist : nullptr);
+  if (threadIdx.x == 0) ctl->ticket = 0u;  // ready for the next launch
 }
 
 __global__ void __launch_bounds__(kThreads) select_only_kernel(SelectArgs sa) {
   extern __shared__ __align__(16) unsigned char dyn_smem[];
+  __shared__ uint32_t hist[kBins];
   const bool in_smem = sa.n_ctx <= kSmemPositions;
   uint32_t* keys = in_smem ? reinterpret_cast<uint32_t*>(dyn_smem) : sa.keys_scratch;
-  uint8_t* fl = in_smem ? dyn_smem + 4 * size_t(sa.n_ctx) : sa.flags_scratch;
-  select_tail(sa, keys, fl);
+  uint8_t* fl = in_smem ? dyn_smem + 4 * size_t(round16(sa.n_ctx)) : sa.flags_scratch;
+  select_tail(sa, keys, fl, in_smem, hist, nullptr);
 }
 
 int check_select(const uint8_t* pos_flags, int n_ctx, const int32_t* meta, int n_chunks,
@@ -438,8 +699,8 @@ int check_select(const uint8_t* pos_flags, int n_ctx, const int32_t* meta, int n
               "selection: null pointer");
   CKV_REQUIRE(n_chunks == 0 || meta, "selection: null chunk table");
   CKV_REQUIRE(n_ctx > 0 && n_chunks >= 0, "selection: bad sizes");
-  CKV_REQUIRE((reinterpret_cast<uintptr_t>(scratch) & 3u) == 0,
-              "selection: scratch must be 4-byte aligned");
+  CKV_REQUIRE((reinterpret_cast<uintptr_t>(scratch) & 15u) == 0,
+              "selection: scratch must be 16-byte aligned");
   return CKV_OK;
 }
 
@@ -448,20 +709,26 @@ SelectArgs make_select_args(const float* diff, const float* norm, const uint8_t*
                             float* rel, int32_t* keep_abs, int32_t* sel, int32_t* counts,
                             uint8_t* scratch) {
   return SelectArgs{diff, norm, pos_flags, n_ctx, meta, n_chunks, has_thr, thr, rel, keep_abs,
-                    sel, counts, reinterpret_cast<uint32_t*>(scratch), scratch + 4 * size_t(n_ctx)};
+                    sel, counts, reinterpret_cast<uint32_t*>(scratch),
+                    scratch + 4 * size_t(round16(n_ctx))};
 }
 
-// Phase-1 grid: two 1024-thread CTAs per SM (every SM gets the same number of rows),
-// at most one CTA per row.
-int rows_grid(int n_act) { return std::max(1, std::min(n_act, 2 * num_sms())); }
+// Phase-1 grid: as many 1024-thread CTAs per SM as fit at once (two, or one when the
+// selection's shared memory is large), so every SM gets the same number of rows; at
+// most one CTA per row.
+int rows_grid(int n_act, int dyn_smem) {
+  const int per_sm = 2 * (dyn_smem + kStaticSmem + 1024) <= 228 * 1024 ? 2 : 1;
+  return std::max(1, std::min(n_act, per_sm * num_sms()));
+}
 
-int launch_fused(const RowArgs& r, unsigned* counter, const SelectArgs& sa, cudaStream_t st,
+int launch_fused(const RowArgs& r, void* control, const SelectArgs& sa, cudaStream_t st,
                  const char* name) {
-  const int dyn = dyn_smem_bytes(sa.n_ctx);
+  const int dyn = dyn_smem_bytes(sa.n_ctx, sa.n_chunks);
   if (int rc = set_smem_limit(reinterpret_cast<const void*>(deviation_select_kernel),
-                              dyn_smem_bytes(kSmemPositions)))
+                              dyn_smem_bytes(kSmemPositions, 0)))
     return rc;
-  deviation_select_kernel<<<rows_grid(r.n_act), kThreads, dyn, st>>>(r, counter, sa);
+  deviation_select_kernel<<<rows_grid(r.n_act, dyn), kThreads, dyn, st>>>(
+      r, static_cast<Control*>(control), sa);
   CKV_LAUNCH_CHECK(name);
   return CKV_OK;
 }
@@ -480,14 +747,15 @@ int ckv_deviation_select(const uint16_t* k_fresh, const uint16_t* v_fresh,
                          int n_chunks, int has_threshold, double escalate_threshold,
                          int n_kv_heads, int head_dim, float* diff, float* norm, float* rel,
                          int32_t* keep_abs, int32_t* sel, int32_t* counts, uint8_t* scratch,
-                         uint32_t* counter, ckv_stream_t stream) {
+                         void* control, ckv_stream_t stream) {
   if (int rc = check_select(pos_flags, n_ctx, sel_meta, n_chunks, rel, keep_abs, sel, counts,
                             scratch))
     return rc;
-  CKV_REQUIRE(k_fresh && v_fresh && k_base && v_base && active && diff && norm && counter,
+  CKV_REQUIRE(k_fresh && v_fresh && k_base && v_base && active && diff && norm && control,
               "ckv_deviation_select: null pointer");
-  CKV_REQUIRE(aligned16(k_fresh) && aligned16(v_fresh) && aligned16(k_base) && aligned16(v_base),
-              "ckv_deviation_select: K/V must be 16-byte aligned");
+  CKV_REQUIRE(aligned16(k_fresh) && aligned16(v_fresh) && aligned16(k_base) && aligned16(v_base) &&
+                  aligned16(control),
+              "ckv_deviation_select: K/V and the control block must be 16-byte aligned");
   CKV_REQUIRE(head_dim % 8 == 0 && fresh_row_stride % 8 == 0 && n_kv_heads > 0,
               "ckv_deviation_select: head_dim and row stride must be multiples of 8");
   CKV_REQUIRE(n_act > 0 && n_act <= n_ctx, "ckv_deviation_select: n_act %d out of range", n_act);
@@ -496,7 +764,7 @@ int ckv_deviation_select(const uint16_t* k_fresh, const uint16_t* v_fresh,
   const SelectArgs sa = make_select_args(diff, norm, pos_flags, n_ctx, sel_meta, n_chunks,
                                          has_threshold, escalate_threshold, rel, keep_abs, sel,
                                          counts, scratch);
-  return launch_fused(r, counter, sa, as_stream(stream), "ckv_deviation_select");
+  return launch_fused(r, control, sa, as_stream(stream), "ckv_deviation_select");
 }
 
 int ckv_deviation_scores(const uint16_t* k_fresh, const uint16_t* v_fresh,
@@ -515,7 +783,7 @@ int ckv_deviation_scores(const uint16_t* k_fresh, const uint16_t* v_fresh,
   if (n_act == 0) return CKV_OK;
   const RowArgs r{k_fresh, v_fresh, fresh_row_stride, k_base, v_base, active, n_act,
                   n_kv_heads, head_dim, pos_flags, n_ctx, diff, norm};
-  deviation_scores_kernel<<<rows_grid(n_act), kThreads, 0, as_stream(stream)>>>(r);
+  deviation_scores_kernel<<<rows_grid(n_act, 0), kThreads, 0, as_stream(stream)>>>(r);
   CKV_LAUNCH_CHECK("ckv_deviation_scores");
   return CKV_OK;
 }
@@ -532,9 +800,10 @@ int ckv_select_from_scores(const float* diff, const float* norm, const uint8_t* 
                                          has_threshold, escalate_threshold, rel, keep_abs, sel,
                                          counts, scratch);
   if (int rc = set_smem_limit(reinterpret_cast<const void*>(select_only_kernel),
-                              dyn_smem_bytes(kSmemPositions)))
+                              dyn_smem_bytes(kSmemPositions, 0)))
     return rc;
-  select_only_kernel<<<1, kThreads, dyn_smem_bytes(n_ctx), as_stream(stream)>>>(sa);
+  const int dyn = n_ctx <= kSmemPositions ? 5 * round16(n_ctx) : 0;
+  select_only_kernel<<<1, kThreads, dyn, as_stream(stream)>>>(sa);
   CKV_LAUNCH_CHECK("ckv_select_from_scores");
   return CKV_OK;
 }
@@ -548,27 +817,26 @@ int ckv_select_from_scores(const float* diff, const float* norm, const uint8_t* 
 // already own: a serving loop whose device memory is entirely carved up by its
 // own arena or caching allocator (a cudaMalloc there would synchronise the GPU
 // or break its memory accounting), or a plain C/FFI host that has the input and
-// output buffers but no allocator to make the selection's two scratch buffers
-// with.  For them the scratch lives here, in one file-scope device array that
+// output buffers but no allocator to make the selection's scratch and control
+// block with.  For them both live here, in one file-scope device array that
 // every GPU which loads the library keeps until the process exits:
-//   bytes [0, 4)                                 the last-CTA ticket counter
-//   bytes [256, 256 + 5 * CKV_NOALLOC_MAX_CTX)   the selection's per-position keys
-//                                                and flags (phase 2 uses them only
-//                                                when n_ctx exceeds what it keeps
-//                                                in shared memory)
+//   bytes [0, CKV_SELECT_CONTROL_BYTES)  the control block (ticket counter and the
+//                                        phase-1 histogram)
+//   then 5 * CKV_NOALLOC_MAX_CTX bytes   the selection's per-position keys and
+//                                        flags (phase 2 uses them only when n_ctx
+//                                        exceeds what it keeps in shared memory)
 // Its device address is looked up once per device (cudaGetSymbolAddress, on the
 // first call made while that device is current).  Every call shares the array:
-// the counter is cleared with an async memset on the caller's stream before
-// each launch and the keys and flags are rewritten in full, but two calls that
-// overlap on the GPU (different streams, no ordering between them) race on it.
+// the control block is cleared with an async memset on the caller's stream
+// before each launch and the keys and flags are rewritten in full, but two calls
+// that overlap on the GPU (different streams, no ordering between them) race on it.
 #include <atomic>
 
 namespace ckv {
 namespace {
 
-constexpr int kNoAllocScratchOffset = 256;
 static __device__ __align__(256) unsigned char
-    g_noalloc_scratch[kNoAllocScratchOffset + 5 * CKV_NOALLOC_MAX_CTX];
+    g_noalloc_scratch[CKV_SELECT_CONTROL_BYTES + 5 * CKV_NOALLOC_MAX_CTX];
 
 constexpr int kNoAllocMaxDevices = 64;
 
@@ -614,8 +882,8 @@ extern "C" int ckv_deviation_select_noalloc(
               n_ctx, CKV_NOALLOC_MAX_CTX);
   unsigned char* scratch = nullptr;
   if (int rc = noalloc_scratch(&scratch)) return rc;
-  uint32_t* counter = reinterpret_cast<uint32_t*>(scratch);
-  uint8_t* select_scratch = scratch + kNoAllocScratchOffset;
+  unsigned char* control = scratch;
+  uint8_t* select_scratch = scratch + CKV_SELECT_CONTROL_BYTES;
   if (int rc = check_select(pos_flags, n_ctx, sel_meta, n_chunks, rel, keep_abs, sel, counts,
                             select_scratch))
     return rc;
@@ -627,10 +895,11 @@ extern "C" int ckv_deviation_select_noalloc(
               "ckv_deviation_select_noalloc: head_dim and row stride must be multiples of 8");
   CKV_REQUIRE(n_act > 0 && n_act <= n_ctx, "ckv_deviation_select_noalloc: n_act %d out of range",
               n_act);
-  // the ticket counter must start at zero; a memset is a copy, not an allocation
-  cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(uint32_t), as_stream(stream));
+  // the control block must start at zero; a memset is a copy, not an allocation
+  cudaError_t e = cudaMemsetAsync(control, 0, CKV_SELECT_CONTROL_BYTES, as_stream(stream));
   if (e != cudaSuccess) {
-    set_error("ckv_deviation_select_noalloc: clearing the counter failed: %s", cudaGetErrorString(e));
+    set_error("ckv_deviation_select_noalloc: clearing the control block failed: %s",
+              cudaGetErrorString(e));
     return CKV_ERR_CUDA;
   }
   const RowArgs r{k_fresh, v_fresh, fresh_row_stride, k_base, v_base, active, n_act,
@@ -638,5 +907,5 @@ extern "C" int ckv_deviation_select_noalloc(
   const SelectArgs sa = make_select_args(diff, norm, pos_flags, n_ctx, sel_meta, n_chunks,
                                          has_threshold, escalate_threshold, rel, keep_abs, sel,
                                          counts, select_scratch);
-  return launch_fused(r, counter, sa, as_stream(stream), "ckv_deviation_select_noalloc");
+  return launch_fused(r, control, sa, as_stream(stream), "ckv_deviation_select_noalloc");
 }

@@ -344,6 +344,8 @@ class TorchEngine:
                 torch.cuda.current_stream().synchronize()
                 counts = hv[:8].numpy().copy()
                 rel = hv[8:8 + n_ch].view(torch.float32).numpy().astype(np.float64)
+                if counts[5] & 0x1:  # CKV_DEV_ERR_WAIT_TIMEOUT: a bounded device wait ran out
+                    raise RuntimeError("layer-1 selection: a device wait ran out (see ckv_get_device_error)")
                 if counts[5]:
                     raise AssertionError("selected a token that was never computed")
                 M = int(counts[0])

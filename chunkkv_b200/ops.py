@@ -16,7 +16,12 @@ BF16 = torch.bfloat16
 PAGE_TOKENS = 16
 META_STRIDE = 8
 SEL_META_STRIDE = 4
-SELECT_SCRATCH_PER_POSITION = 5  # bytes of selection scratch per position (CKV_SELECT_SCRATCH_BYTES)
+SELECT_CONTROL_BYTES = 8448  # CKV_SELECT_CONTROL_BYTES: ticket + first-level histogram
+
+
+def select_scratch_bytes(n_ctx: int) -> int:
+    """CKV_SELECT_SCRATCH_BYTES: a score key and a flag byte per position (rounded to 16)."""
+    return 5 * ((n_ctx + 15) // 16 * 16)
 
 
 class LaunchTimer:
@@ -187,7 +192,7 @@ def _fresh_rows(k_fresh: torch.Tensor, v_fresh: torch.Tensor, rows: int, H: int,
 
 
 def _select_ws(ws: "SelectWorkspace", n_ctx: int, n_chunks: int) -> None:
-    if ws.keep_abs.numel() < n_ctx or ws.diff.numel() < n_ctx or ws.scratch.numel() < SELECT_SCRATCH_PER_POSITION * n_ctx or ws.rel.numel() < n_chunks:
+    if ws.keep_abs.numel() < n_ctx or ws.diff.numel() < n_ctx or ws.scratch.numel() < select_scratch_bytes(n_ctx) or ws.rel.numel() < n_chunks:
         raise ValueError(f"selection workspace too small for {n_ctx} positions and {n_chunks} chunks")
 
 
@@ -302,7 +307,7 @@ def deviation_select(k_fresh: torch.Tensor, v_fresh: torch.Tensor, k_base: torch
               _ptr(v_base), _ptr(active), active.numel(), _ptr(pos_flags), n_ctx, _ptr(sel_meta),
               sel_meta.shape[0], int(threshold is not None), float(threshold or 0.0), H, D,
               _ptr(ws.diff), _ptr(ws.norm), _ptr(ws.rel), _ptr(ws.keep_abs), _ptr(ws.sel),
-              _ptr(ws.counts), _ptr(ws.scratch), _ptr(ws.counter), _stream())
+              _ptr(ws.counts), _ptr(ws.scratch), _ptr(ws.control), _stream())
 
 
 def deviation_scores(k_fresh: torch.Tensor, v_fresh: torch.Tensor, k_base: torch.Tensor,
@@ -356,8 +361,9 @@ class SelectWorkspace:
         self.counts = torch.zeros(8, **i32)
         # per position: a 4-byte score key and a flag byte (used by the selection when
         # n_ctx is larger than what it keeps in shared memory)
-        self.scratch = torch.zeros(SELECT_SCRATCH_PER_POSITION * n_ctx, dtype=torch.uint8, device=device)
-        self.counter = torch.zeros(1, **i32)
+        self.scratch = torch.zeros(select_scratch_bytes(n_ctx), dtype=torch.uint8, device=device)
+        # ticket counter and first-level histogram: zero now, left zero by every launch
+        self.control = torch.zeros(SELECT_CONTROL_BYTES // 4, **i32)
 
 
 def apply_selection(ws: SelectWorkspace, max_rows: int, h_in, h_out, x_in, x_out, k_fresh, v_fresh,

@@ -143,13 +143,16 @@ CKV_API int ckv_pages_write(uint16_t* pool, int64_t n_pages, const int32_t* page
  *   status (0 ok), n_keep_fresh, reserved.
  * The threshold is compared in double, as the reference compares the Python float
  * rel (torch_engine.py:132-134).
- * Scratch: CKV_SELECT_SCRATCH_BYTES(n_ctx) bytes, 4-byte aligned (a score key and
+ * Scratch: CKV_SELECT_SCRATCH_BYTES(n_ctx) bytes, 16-byte aligned (a score key and
  * a flag byte per position; the selection uses it only when n_ctx is larger than
- * what it keeps in shared memory, 20480 positions); counter: one uint32 that must
- * be zero before the first call (the kernel leaves it zero).  Calls that share a
- * counter or scratch must not overlap on the GPU. */
+ * what it keeps in shared memory, 43008 positions).  control: CKV_SELECT_CONTROL_BYTES
+ * bytes, 16-byte aligned (the last-CTA ticket and the first radix level's histogram,
+ * which every CTA adds its rows to); it must be zero before the first call and every
+ * call leaves it zero (zero it again after a device error).  Calls that share a
+ * control block or scratch must not overlap on the GPU. */
 #define CKV_SEL_META_STRIDE 4
-#define CKV_SELECT_SCRATCH_BYTES(n_ctx) (5 * (size_t)(n_ctx))
+#define CKV_SELECT_SCRATCH_BYTES(n_ctx) (5 * (((size_t)(n_ctx) + 15) / 16 * 16))
+#define CKV_SELECT_CONTROL_BYTES 8448
 CKV_API int ckv_deviation_select(const uint16_t* k_fresh, const uint16_t* v_fresh,
                          int64_t fresh_row_stride, const uint16_t* k_base,
                          const uint16_t* v_base, const int32_t* active, int n_act,
@@ -157,15 +160,15 @@ CKV_API int ckv_deviation_select(const uint16_t* k_fresh, const uint16_t* v_fres
                          int n_chunks, int has_threshold, double escalate_threshold,
                          int n_kv_heads, int head_dim, float* diff, float* norm, float* rel,
                          int32_t* keep_abs, int32_t* sel, int32_t* counts, uint8_t* scratch,
-                         uint32_t* counter, ckv_stream_t stream);
+                         void* control, ckv_stream_t stream);
 
 /* Allocation-free variant of ckv_deviation_select — no counterpart in the
  * reference.  For callers that can pass their inputs and outputs but cannot
  * provide (allocate) the selection's scratch: its per-position keys and flags and
- * its ticket counter live in a static device array inside the library, held by every GPU that
- * loads it until process exit (256 + 5 * CKV_NOALLOC_MAX_CTX bytes, 320 KiB).
- * Same arguments and results as ckv_deviation_select without `scratch` and
- * `counter`; n_ctx must be at most
+ * its control block live in a static device array inside the library, held by every GPU that
+ * loads it until process exit (CKV_SELECT_CONTROL_BYTES + 5 * CKV_NOALLOC_MAX_CTX
+ * bytes, 328 KiB).  Same arguments and results as ckv_deviation_select without
+ * `scratch` and `control`; n_ctx must be at most
  * CKV_NOALLOC_MAX_CTX (else CKV_ERR_ARG).  The first call on a device looks up
  * the array's device address; make that first call before any stream capture.
  * Calls share the array: calls that overlap on the GPU race. */

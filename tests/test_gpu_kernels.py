@@ -325,7 +325,7 @@ def test_deviation_select_fused_matches_formula_and_selection():
     np.testing.assert_array_equal(ws.keep_abs[:n_sel].cpu().numpy(), ref["keep_abs"].numpy())
     # the ticket counter is back at zero: a second launch works the same
     ops.deviation_select(kf, vf, Kb, Vb, active, flags, meta, None, ws)
-    assert int(ws.counts[0]) == n_sel and int(ws.counter[0]) == 0
+    assert int(ws.counts[0]) == n_sel and not ws.control.any()
     # scores only, per head group (tensor-parallel ranks): the group sums are the fused
     # kernel's scores, and the selection from them is the fused kernel's selection
     parts = []

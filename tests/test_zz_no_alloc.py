@@ -57,7 +57,7 @@ def _noalloc(x, o, thr=None):
     s = torch.cuda.current_stream().cuda_stream
     p = lambda t: t.data_ptr()  # noqa: E731
     _lib.call("ckv_deviation_select_noalloc", p(x["kf"]), p(x["vf"]), x["kf"].stride(0), p(x["Kb"]),
-              p(x["Vb"]), p(x["active"]), x["N"], p(x["flags"]), x["N"], p(x["meta"]), x["meta"].shape[0],
+              p(x["Vb"]), p(x["active"]), x["active"].numel(), p(x["flags"]), x["N"], p(x["meta"]), x["meta"].shape[0],
               int(thr is not None), float(thr or 0.0), x["H"], x["D"], p(o["diff"]), p(o["norm"]),
               p(o["rel"]), p(o["keep_abs"]), p(o["sel"]), p(o["counts"]), s)
 
