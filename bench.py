@@ -1056,10 +1056,10 @@ def run_policies(args):
 
 def run_micro(args):
     """Config 2: the bandwidth-bound kernels at the 7B KV shape (H = 4, D = 128), 28 layers,
-    8 chunks x 256 tokens, Delta uniform in [-4096, 4096].  Each kernel runs on two sets of
-    inputs used alternately, so consecutive launches never find their data in L2; GB/s are
-    the algorithmic bytes (read + write) over the device time per launch (CUDA events
-    around a CUDA graph of the launches)."""
+    8 chunks x 256 tokens, Delta uniform in [-4096, 4096].  Each kernel runs on enough sets
+    of inputs AND outputs, used in turn, that neither are still in L2 when their turn
+    comes again; GB/s are the algorithmic bytes (read + write) over the device time per
+    launch (CUDA events around a CUDA graph of the launches)."""
     import torch
 
     from chunkkv_b200 import ops
@@ -1102,17 +1102,30 @@ def run_micro(args):
         gbs = nbytes / (ms * 1e-3) / 1e9
         return {"ms": round(ms, 4), "bytes": int(nbytes), "gbs": round(gbs, 1), "frac_hbm": round(gbs / pk["hbm_gbs"], 4)}
 
+    def sets_for(nbytes):
+        """Input/output sets used in turn so that, between two uses of one set, the
+        other sets move at least three times the L2 (126 MB): neither the inputs nor
+        the outputs of a launch are still in L2 when their turn comes again."""
+        return max(2, -(-3 * 126_000_000 // int(nbytes)) + 1)
+
     out = {}
     # re-RoPE by Delta (TorchEngine.shift_keys), all chunks of all layers in one launch
-    keys = [torch.randn((L * n_ch, H, cl, D), generator=g, device=dev).to(bf) for _ in range(2)]
+    rr_bytes = 2.0 * L * n_ch * H * cl * D * 2
+    ns = sets_for(rr_bytes)
+    keys = [torch.randn((L * n_ch, H, cl, D), generator=g, device=dev).to(bf) for _ in range(ns)]
     shifted = [torch.empty_like(k) for k in keys]
     # context, not this library's kernel: a plain device-to-device copy of the same bytes
-    out["reference_copy_same_bytes"] = timed(lambda i: shifted[i % 2].copy_(keys[i % 2]), 2.0 * keys[0].numel() * 2)
-    out["rerope_shift_keys"] = timed(lambda i: ops.shift_keys(keys[i % 2], deltas[0], inv, out=shifted[i % 2]),
-                                     2.0 * keys[0].numel() * 2)
+    out["reference_copy_same_bytes"] = timed(lambda i: shifted[i % ns].copy_(keys[i % ns]), rr_bytes)
+    out["rerope_shift_keys"] = timed(lambda i: ops.shift_keys(keys[i % ns], deltas[0], inv, out=shifted[i % ns]),
+                                     rr_bytes)
+    out["rerope_shift_keys"]["sets"] = ns
+    del keys, shifted
+    torch.cuda.empty_cache()
     # paged gather of K (re-roped) and V for all layers, chunks placed at shifted positions
     n_pages = T // PAGE_TOKENS
-    pools = [PagePool(L, H, D, n_pages, dev) for _ in range(2)]
+    g_bytes = 2.0 * 2 * L * H * T * D * 2
+    ng = sets_for(g_bytes)
+    pools = [PagePool(L, H, D, n_pages, dev) for _ in range(ng)]
     for pool in pools:
         pool.pages.normal_(generator=g)
     table = torch.arange(n_pages, dtype=torch.int32, device=dev)
@@ -1120,20 +1133,32 @@ def run_micro(args):
     rng.shuffle(order)
     meta = torch.tensor([[c * cl // PAGE_TOKENS, cl, order[c] * cl, deltas[c], 0, L, 0, 0] for c in range(n_ch)],
                         dtype=torch.int32, device=dev)
-    kall = [torch.empty((L, H, T, D), dtype=bf, device=dev) for _ in range(2)]
+    kall = [torch.empty((L, H, T, D), dtype=bf, device=dev) for _ in range(ng)]
     vall = [torch.empty_like(k) for k in kall]
-    out["gather_paged"] = timed(lambda i: ops.blend_gather_paged(pools[i % 2].pages, table, meta, inv, kall[i % 2],
-                                                                 vall[i % 2], 0, L),
-                                2.0 * 2 * L * H * T * D * 2)
-    # store insert (write-back): one chunk of 256 tokens, all layers, from a result cache
-    ids = torch.arange(cl // PAGE_TOKENS, dtype=torch.int32, device=dev)
-    kp = [torch.tensor([kall[b][li].data_ptr() for li in range(L)], dtype=torch.int64).view(torch.uint64).to(dev)
-          for b in range(2)]
-    vp = [torch.tensor([vall[b][li].data_ptr() for li in range(L)], dtype=torch.int64).view(torch.uint64).to(dev)
-          for b in range(2)]
-    out["scatter_pages_write"] = timed(lambda i: ops.pages_write(pools[i % 2].pages, ids, cl, kp[i % 2], vp[i % 2],
-                                                                 T * D),
-                                       2.0 * 2 * L * H * cl * D * 2)
+    out["gather_paged"] = timed(lambda i: ops.blend_gather_paged(pools[i % ng].pages, table, meta, inv, kall[i % ng],
+                                                                 vall[i % ng], 0, L), g_bytes)
+    out["gather_paged"]["sets"] = ng
+    # store insert (write-back): one chunk of 256 tokens, all layers, from a result cache;
+    # every set reads another chunk of a gathered cache and writes other pages
+    w_bytes = 2.0 * 2 * L * H * cl * D * 2
+    nw = min(ng * n_ch, sets_for(w_bytes))
+    big = PagePool(L, H, D, nw * (cl // PAGE_TOKENS), dev)
+    ids = [torch.arange(w * (cl // PAGE_TOKENS), (w + 1) * (cl // PAGE_TOKENS), dtype=torch.int32, device=dev)
+           for w in range(nw)]
+
+    def src_ptrs(w, kv):
+        b, c = divmod(w, n_ch)
+        t = (kall if kv == 0 else vall)[b]
+        return torch.tensor([t[li, :, c * cl:].data_ptr() for li in range(L)],
+                            dtype=torch.int64).view(torch.uint64).to(dev)
+
+    kp = [src_ptrs(w, 0) for w in range(nw)]
+    vp = [src_ptrs(w, 1) for w in range(nw)]
+    out["scatter_pages_write"] = timed(lambda i: ops.pages_write(big.pages, ids[i % nw], cl, kp[i % nw], vp[i % nw],
+                                                                 T * D), w_bytes)
+    out["scatter_pages_write"]["sets"] = nw
+    del pools, kall, vall, big
+    torch.cuda.empty_cache()
     # layer-1 deviation + pooled top-k: fresh = cached + noise on 20 % of tokens
     # (16 input sets used in turn: 8 MiB per launch would otherwise stay in L2)
     n_sets = 16

@@ -28,6 +28,8 @@ SIGNATURES: dict[str, list] = {
     "ckv_rope_table": [_p, _i32, _i32, _p, _p],
     "ckv_shift_keys": [_p, _p, _i64, _i32, _i32, _i32, _p, _p],
     "ckv_apply_rope": [_p, _p, _i64, _i32, _i32, _i32, _p, _p, _p],
+    "ckv_shift_keys_f32": [_p, _p, _i64, _i32, _i32, _i32, _p, _p],
+    "ckv_apply_rope_f32": [_p, _p, _i64, _i32, _i32, _i32, _p, _p, _p],
     "ckv_blend_gather_paged": [_p, _i64, _p, _p, _i32, _p, _i32, _p, _p, _i32, _i32, _i32, _i32, _i32,
                                _i32, _p],
     "ckv_blend_gather_dense": [_p, _p, _p, _i32, _p, _i32, _p, _p, _i32, _i32, _i32, _i32, _i32, _p],

@@ -169,6 +169,54 @@ __global__ void rope_rows_kernel(const uint16_t* __restrict__ src, uint16_t* __r
   }
 }
 
+// fp32 rows (torch_engine.py:46-51 with x.dtype float32: the result stays fp32):
+// dst[row] = rotate(src[row], cs(pos(row))), four rotary pairs per item as two float4,
+// pos = delta (shift) or positions[row % seq]; dims past rot copied.
+__global__ void rope_rows_f32_kernel(const float* __restrict__ src, float* __restrict__ dst, int64_t rows,
+                                     int head_dim, int rot, int delta, const int32_t* __restrict__ positions,
+                                     int seq, const float* __restrict__ inv_freq) {
+  const int n_pair = rot / 8;
+  const int n_copy = (head_dim - rot) / 4;
+  const int per_row = n_pair + n_copy;
+  const int64_t total = rows * per_row;
+  for (int64_t it = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; it < total;
+       it += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = it / per_row;
+    const int item = int(it - r * per_row);
+    const float* s = src + r * head_dim;
+    float* d = dst + r * head_dim;
+    if (item < n_pair) {
+      const int j = item * 4;
+      const float p = positions ? float(positions[r % seq]) : float(delta);
+      const float4 a4 = *reinterpret_cast<const float4*>(s + j);
+      const float4 b4 = *reinterpret_cast<const float4*>(s + j + rot / 2);
+      const float a[4] = {a4.x, a4.y, a4.z, a4.w}, b[4] = {b4.x, b4.y, b4.z, b4.w};
+      float o1[4], o2[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 cs = rope_cs(p, inv_freq[j + e]);
+        o1[e] = __fsub_rn(__fmul_rn(a[e], cs.x), __fmul_rn(b[e], cs.y));
+        o2[e] = __fadd_rn(__fmul_rn(a[e], cs.y), __fmul_rn(b[e], cs.x));
+      }
+      *reinterpret_cast<float4*>(d + j) = make_float4(o1[0], o1[1], o1[2], o1[3]);
+      *reinterpret_cast<float4*>(d + j + rot / 2) = make_float4(o2[0], o2[1], o2[2], o2[3]);
+    } else {
+      const int off = rot + (item - n_pair) * 4;
+      *reinterpret_cast<float4*>(d + off) = *reinterpret_cast<const float4*>(s + off);
+    }
+  }
+}
+
+int launch_rope_f32(const float* src, float* dst, int64_t rows, int head_dim, int rot, int delta,
+                    const int32_t* positions, int seq, const float* inv_freq, cudaStream_t st,
+                    const char* name) {
+  const int64_t items = rows * (rot / 8 + (head_dim - rot) / 4);
+  const int grid = static_cast<int>(std::min<int64_t>((items + 255) / 256, 16 * num_sms()));
+  rope_rows_f32_kernel<<<grid, 256, 0, st>>>(src, dst, rows, head_dim, rot, delta, positions, seq, inv_freq);
+  CKV_LAUNCH_CHECK(name);
+  return CKV_OK;
+}
+
 // One CTA column (blockIdx.y) per chunk; warps stride over the chunk's units.
 // Unit u -> (block b, head h, kv, layer l), block fastest so consecutive warps write
 // consecutive 4 KiB pieces of the same (layer, K|V, head) plane of the blended cache
@@ -365,6 +413,36 @@ int ckv_apply_rope(const uint16_t* src, uint16_t* dst, int64_t batch_heads, int 
                                                         positions, seq, inv_freq);
   CKV_LAUNCH_CHECK("ckv_apply_rope");
   return CKV_OK;
+}
+
+int ckv_shift_keys_f32(const float* src, float* dst, int64_t rows, int head_dim, int rot_dims, int delta,
+                       const float* inv_freq, ckv_stream_t stream) {
+  CKV_REQUIRE(src && dst && inv_freq, "ckv_shift_keys_f32: null pointer");
+  CKV_REQUIRE(aligned16(src) && aligned16(dst), "ckv_shift_keys_f32: pointers must be 16-byte aligned");
+  if (int rc = check_rot(head_dim, rot_dims)) return rc;
+  if (rows <= 0) return CKV_OK;
+  if (delta == 0) {
+    if (src != dst && cudaMemcpyAsync(dst, src, rows * head_dim * 4, cudaMemcpyDeviceToDevice,
+                                      as_stream(stream)) != cudaSuccess) {
+      set_error("ckv_shift_keys_f32: copy failed");
+      return CKV_ERR_CUDA;
+    }
+    return CKV_OK;
+  }
+  return launch_rope_f32(src, dst, rows, head_dim, rot_dims, delta, nullptr, 1, inv_freq, as_stream(stream),
+                         "ckv_shift_keys_f32");
+}
+
+int ckv_apply_rope_f32(const float* src, float* dst, int64_t batch_heads, int seq, int head_dim, int rot_dims,
+                       const int32_t* positions, const float* inv_freq, ckv_stream_t stream) {
+  CKV_REQUIRE(src && dst && inv_freq && positions, "ckv_apply_rope_f32: null pointer");
+  CKV_REQUIRE(aligned16(src) && aligned16(dst), "ckv_apply_rope_f32: pointers must be 16-byte aligned");
+  if (int rc = check_rot(head_dim, rot_dims)) return rc;
+  CKV_REQUIRE(seq >= 0 && batch_heads >= 0, "ckv_apply_rope_f32: bad sizes");
+  const int64_t rows = batch_heads * seq;
+  if (rows == 0) return CKV_OK;
+  return launch_rope_f32(src, dst, rows, head_dim, rot_dims, 0, positions, seq, inv_freq, as_stream(stream),
+                         "ckv_apply_rope_f32");
 }
 
 static int gather_common(const int32_t* chunk_meta, int n_chunks, const float* inv_freq, int rot,

@@ -133,10 +133,12 @@ class TorchEngine:
         return m <= ops.GEMV_NORM_MAX_ROWS and self.shape.hidden <= ops.GEMV_NORM_MAX_K
 
     def shift_keys(self, keys: torch.Tensor, delta: int) -> torch.Tensor:
-        """Re-RoPE post-RoPE keys (1, H, L, D) by `delta` (torch_engine.py:56-59)."""
+        """Re-RoPE post-RoPE keys (1, H, L, D) by `delta` (torch_engine.py:56-59): rotated
+        in fp32 and returned in the keys' dtype (bf16 or fp32; other dtypes raise
+        NotImplementedError), on this engine's device."""
         if delta == 0:
             return keys
-        k = keys.to(device=self.device, dtype=torch.bfloat16).contiguous()
+        k = keys.to(device=self.device).contiguous()
         return ops.shift_keys(k, delta, self.inv_freq)
 
     def _chunk_tensors(self, chunk, li: int, kv: int) -> torch.Tensor:

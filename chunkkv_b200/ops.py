@@ -206,25 +206,40 @@ def rope_table(inv_freq: torch.Tensor, max_pos: int) -> torch.Tensor:
     return out
 
 
+# rotation entry point per key dtype: the reference rotates in fp32 and returns the
+# input dtype (torch_engine.py:46-51), so bf16 keys come back bf16 and fp32 keys fp32
+_ROPE_DTYPES = {torch.bfloat16: "", torch.float32: "_f32"}
+
+
+def _rope_suffix(t: torch.Tensor, what: str) -> str:
+    if t.dtype not in _ROPE_DTYPES:
+        raise NotImplementedError(f"{what}: dtype {t.dtype} is not supported (bfloat16 and float32 are)")
+    return _ROPE_DTYPES[t.dtype]
+
+
 def shift_keys(keys: torch.Tensor, delta: int, inv_freq: torch.Tensor, rot_dims: int | None = None,
                out: torch.Tensor | None = None) -> torch.Tensor:
-    """Rotate post-RoPE keys (..., L, D) by `delta` positions (new tensor unless `out`)."""
+    """Rotate post-RoPE keys (..., L, D) by `delta` positions (new tensor unless `out`),
+    in fp32, returned in the keys' dtype (bf16 or fp32)."""
+    sfx = _rope_suffix(keys, "shift_keys")
     _cuda(keys, inv_freq)
-    _bf16(keys)
     _contig(keys)
     D = keys.shape[-1]
     rot = D if rot_dims is None else rot_dims
     out = torch.empty_like(keys) if out is None else out
-    _run("ckv_shift_keys", _ptr(keys), _ptr(out), keys.numel() // D, D, rot, int(delta),
-              _ptr(inv_freq), _stream())
+    if out.dtype != keys.dtype or out.shape != keys.shape or not out.is_contiguous():
+        raise ValueError("shift_keys: out must be a contiguous tensor of the keys' shape and dtype")
+    _run("ckv_shift_keys" + sfx, _ptr(keys), _ptr(out), keys.numel() // D, D, rot, int(delta),
+         _ptr(inv_freq), _stream())
     return out
 
 
 def apply_rope(x: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor,
                rot_dims: int | None = None) -> torch.Tensor:
-    """RoPE of x (..., L, D) at int positions (L,)."""
+    """RoPE of x (..., L, D) at int positions (L,), in fp32, returned in x's dtype
+    (bf16 or fp32)."""
+    sfx = _rope_suffix(x, "apply_rope")
     _cuda(x, positions, inv_freq)
-    _bf16(x)
     _contig(x)
     D, L = x.shape[-1], x.shape[-2]
     pos = positions.to(torch.int32).contiguous()
@@ -232,8 +247,8 @@ def apply_rope(x: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor,
         raise ValueError(f"positions has {pos.numel()} entries for sequence length {L}")
     out = torch.empty_like(x)
     rot = D if rot_dims is None else rot_dims
-    _run("ckv_apply_rope", _ptr(x), _ptr(out), x.numel() // (D * L) if L else 0, L, D, rot,
-              _ptr(pos), _ptr(inv_freq), _stream())
+    _run("ckv_apply_rope" + sfx, _ptr(x), _ptr(out), x.numel() // (D * L) if L else 0, L, D, rot,
+         _ptr(pos), _ptr(inv_freq), _stream())
     return out
 
 

@@ -56,19 +56,19 @@ def _check(spec: RopeSpec, x: torch.Tensor) -> None:
 
 
 def apply_rope(x: torch.Tensor, positions: torch.Tensor, spec: RopeSpec) -> torch.Tensor:
-    """RoPE of x (B, H, L, D) at arbitrary (possibly non-contiguous) positions (L,)."""
+    """RoPE of x (B, H, L, D) at arbitrary (possibly non-contiguous) positions (L,),
+    rotated in fp32 and returned in x's dtype (bf16 or fp32; others raise
+    NotImplementedError), as rerope.py:36-53 does."""
     _check(spec, x)
-    xb = x.to(torch.bfloat16).contiguous()
     pos = torch.as_tensor(positions, device=x.device)
-    out = ops.apply_rope(xb, pos, _inv_freq(spec, x.device), rot_dims=spec.dims)
-    return out.to(x.dtype)
+    return ops.apply_rope(x.contiguous(), pos, _inv_freq(spec, x.device), rot_dims=spec.dims)
 
 
 def shift_keys(keys: torch.Tensor, delta: int, spec: RopeSpec) -> torch.Tensor:
-    """Move already-rotated keys (B, H, L, D) by `delta` positions; delta 0 returns `keys` itself."""
+    """Move already-rotated keys (B, H, L, D) by `delta` positions, rotated in fp32 and
+    returned in the keys' dtype (bf16 or fp32; others raise NotImplementedError);
+    delta 0 returns `keys` itself (rerope.py:56-61)."""
     if delta == 0:
         return keys
     _check(spec, keys)
-    kb = keys.to(torch.bfloat16).contiguous()
-    out = ops.shift_keys(kb, int(delta), _inv_freq(spec, keys.device), rot_dims=spec.dims)
-    return out.to(keys.dtype)
+    return ops.shift_keys(keys.contiguous(), int(delta), _inv_freq(spec, keys.device), rot_dims=spec.dims)

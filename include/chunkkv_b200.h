@@ -82,6 +82,15 @@ CKV_API int ckv_apply_rope(const uint16_t* src, uint16_t* dst, int64_t batch_hea
                    int head_dim, int rot_dims, const int32_t* positions,
                    const float* inv_freq, ckv_stream_t stream);
 
+/* fp32 forms of the two above, for fp32 keys: the reference rotates in fp32 and
+ * returns the input dtype (torch_engine.py:46-51, 56-59; rerope.py:36-61), so fp32
+ * keys stay fp32.  src/dst: fp32 rows, 16-byte aligned; same layout and pairs. */
+CKV_API int ckv_shift_keys_f32(const float* src, float* dst, int64_t rows, int head_dim, int rot_dims,
+                               int delta, const float* inv_freq, ckv_stream_t stream);
+CKV_API int ckv_apply_rope_f32(const float* src, float* dst, int64_t batch_heads, int seq, int head_dim,
+                               int rot_dims, const int32_t* positions, const float* inv_freq,
+                               ckv_stream_t stream);
+
 /* ---- gather of moved chunks into the blended cache -------------------------
  * Replaces base_kv (torch_engine.py:96-103) for ALL layers in one launch:
  * for every chunk c and layer l in [max(layer_lo, meta.layer_begin), min(layer_hi, meta.layer_end)),

@@ -96,6 +96,56 @@ def test_apply_rope_matches_reference_rope():
     assert (out.float() != ref.float()).float().mean() < 1e-3
 
 
+@pytest.mark.parametrize("D", [64, 128, 256])
+def test_fp32_keys_stay_fp32(D):
+    """The reference rotates in fp32 and returns the input dtype (torch_engine.py:46-51,
+    56-59; rerope.py:36-61): fp32 keys come back fp32, rotated with fp32 rounding.  The
+    only difference from the torch restatement is the ulp of cos/sin, so the bar is
+    fp32-sized: max |err| <= 4e-6 x max |ref|."""
+    from chunkkv_b200.scheduler import rerope
+
+    g = torch.Generator(device=DEV).manual_seed(5)
+    k = torch.randn((1, 4, 300, D), generator=g, device=DEV)
+    inv = inv_freq(D)
+    for delta in (1, -37, 4096, -16384):
+        ref = torch_rotate(k, (delta * inv)[None, :].expand(k.shape[-2], -1))
+        out = ops.shift_keys(k, delta, inv)
+        assert out.dtype == torch.float32 and rel_err(out, ref) <= 4e-6, delta
+    pos = torch.randperm(30000, device=DEV)[:300].sort().values
+    ref = torch_rotate(k, pos.float()[:, None] * inv[None, :])
+    out = ops.apply_rope(k, pos, inv)
+    assert out.dtype == torch.float32 and rel_err(out, ref) <= 4e-6
+    # the scheduler API (RopeSpec) keeps the dtype of its input too
+    spec = rerope.RopeSpec(dims=D, base=1e6)
+    sk = rerope.shift_keys(k, 77, spec)
+    assert sk.dtype == torch.float32
+    assert rel_err(sk, torch_rotate(k, (77 * inv)[None, :].expand(k.shape[-2], -1))) <= 4e-6
+    kb = k.to(BF)
+    assert rerope.shift_keys(kb, 77, spec).dtype == BF and rerope.apply_rope(kb, pos, spec).dtype == BF
+    assert rerope.apply_rope(k, pos, spec).dtype == torch.float32
+    # a round trip in fp32 returns the keys to fp32 accuracy
+    back = ops.shift_keys(ops.shift_keys(k, 1234, inv), -1234, inv)
+    assert rel_err(back, k) <= 1e-5
+    with pytest.raises(NotImplementedError):
+        ops.shift_keys(k.half(), 3, inv)
+
+
+def test_engine_shift_keys_keeps_dtype():
+    """TorchEngine.shift_keys (torch_engine.py:56-59) returns the input dtype."""
+    from chunkkv_b200.engine.torch_engine import TorchEngine
+    from chunkkv_b200.engine.weights import SHAPES, random_packed
+
+    eng = TorchEngine.from_packed(random_packed(SHAPES["tiny"], seed=0, device=DEV))
+    k32 = torch.randn((1, eng.n_kv, 50, eng.head_dim), device=DEV)
+    out = eng.shift_keys(k32, 11)
+    assert out.dtype == torch.float32
+    ref = torch_rotate(k32, (11 * eng.inv_freq)[None, :].expand(50, -1))
+    assert rel_err(out, ref) <= 4e-6
+    assert eng.shift_keys(k32.to(BF), 11).dtype == BF
+    with pytest.raises(NotImplementedError):
+        eng.shift_keys(k32.half(), 11)
+
+
 def test_partial_rotary_dims_copy_tail():
     D, rot = 128, 64
     x = torch.randn((1, 2, 40, D), device=DEV).to(BF)
