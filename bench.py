@@ -60,7 +60,6 @@ def parse():
     ap.add_argument("--chunks", type=int, default=None)
     ap.add_argument("--chunk-len", type=int, default=512)
     ap.add_argument("--query-len", type=int, default=128)
-    ap.add_argument("--cpu-layers", type=int, default=3, help="layers the CPU sample executes")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--extra-ratios", default="0.30,0.50", help="also time these ratios (TTFT only)")
     ap.add_argument("--kernel-case", choices=["swiglu", "oproj", "down", "qkv", "attention", "gather", "deviation",
@@ -189,102 +188,87 @@ class ClockSampler:
 
 # -------------------------------------------------------------- CPU sample
 class CpuSample:
-    """The reference algorithm (oracle port of torch_engine.py) on the host cores.
-
-    Bounded sample: the same request on a truncated model of `cpu_layers` layers
-    (layer 0 on every token, layer 1 with the deviation and selection, then one
-    recompute layer); the time of layers 2..L-1 is extrapolated from the
-    measured layer-2 time.  fp32 (the host has no fast bf16 matmul path).
-    Weight values are a tiled random block (timing only)."""
+    """The reference algorithm (oracle port of torch_engine.py:80-178) on the host cores,
+    on the bench's own request: every layer of the model, seed-0 random weights, the
+    chunks' cached K/V at N(0, 1) scale.  It computes in the dtype the host multiplies
+    fastest, bf16 (the reference's deployment dtype) when the host has native bf16
+    matrix units, else fp32.  One call of `run_once` is one whole prefill with the
+    first-token log-probs; nothing is extrapolated."""
 
     def __init__(self, args, shape):
         import torch
 
         from chunkkv_b200.engine.base import BlendConfig, ChunkKV, Placement
-        from chunkkv_b200.engine.weights import param_shapes
+        from chunkkv_b200.engine.weights import random_state_dict
         from oracle.blend_oracle import OracleEngine
 
         torch.set_num_threads(os.cpu_count() or 1)
         self.shape = shape
-        self.nl = nl = max(3, args.cpu_layers)
-        small = shape.truncated(nl)
-        g = torch.Generator().manual_seed(0)
-        block = torch.randn(1 << 20, generator=g) * 0.02
-
-        def fill(*shp, scale=1.0):
-            n = 1
-            for x in shp:
-                n *= x
-            reps_ = (n + block.numel() - 1) // block.numel()
-            return (block.repeat(reps_)[:n] * scale).view(*shp).clone()
-
-        sd = {}
-        for name, shp in param_shapes(small):
-            if name.endswith("norm.weight"):
-                sd[name] = torch.ones(shp)
-            else:
-                sd[name] = fill(*shp, scale=50.0 if "embed" in name else 1.0)
-        self.eng = OracleEngine(small, sd, dtype=torch.float32)
+        self.dtype = self._fastest_dtype()
+        # seed-0 random weights, drawn where it is fastest (the GPU when there is one:
+        # setup, not timed), held on the host
+        gen_dev = "cuda" if torch.cuda.is_available() else "cpu"
+        sd = random_state_dict(shape, seed=0, dtype=torch.bfloat16, device=gen_dev)
+        sd = {k: v.to("cpu", self.dtype) for k, v in sd.items()}
+        self.eng = OracleEngine(shape, sd, dtype=self.dtype)
+        del sd
         chunks, order, query = make_request(shape.vocab, args.chunks, args.chunk_len, args.query_len, 0)
-        H, D = shape.n_kv, shape.head_dim
+        H, D, L = shape.n_kv, shape.head_dim, shape.n_layers
+        g = torch.Generator().manual_seed(1)
         tokens, pl = [], []
-        for c in order:
-            ck = ChunkKV([fill(1, H, args.chunk_len, D, scale=50.0) for _ in range(nl)],
-                         [fill(1, H, args.chunk_len, D, scale=50.0) for _ in range(nl)], c * args.chunk_len)
+        for c in order:  # cached K/V of N(0, 1) scale, like post-RoPE keys and values
+            ck = ChunkKV([torch.randn((1, H, args.chunk_len, D), generator=g).to(self.dtype) for _ in range(L)],
+                         [torch.randn((1, H, args.chunk_len, D), generator=g).to(self.dtype) for _ in range(L)],
+                         c * args.chunk_len)
             pl.append(Placement(ck, len(tokens)))
             tokens += chunks[c]
         self.tokens, self.pl = tokens + query, pl
+        self.ratio = args.ratio
         self.cfg = BlendConfig(recompute_ratio=args.ratio, n_sink=args.n_sink)
         self.threads = torch.get_num_threads()
 
+    @staticmethod
+    def _fastest_dtype():
+        import torch
+
+        a = torch.randn(1024, 2048)
+        best, best_t = torch.float32, float("inf")
+        for dt in (torch.float32, torch.bfloat16):
+            x, w = a.to(dt), a.to(dt)
+            torch.nn.functional.linear(x, w)
+            t0 = time.perf_counter()
+            for _ in range(3):
+                torch.nn.functional.linear(x, w)
+            t = time.perf_counter() - t0
+            if t < best_t:
+                best, best_t = dt, t
+        return best
+
     def run_once(self) -> float:
-        """Estimated full-depth TTFT in seconds."""
+        """Seconds of one blend prefill with its first-token log-probs."""
         t0 = time.perf_counter()
         res = self.eng.prefill(self.tokens, self.pl, self.cfg)
         self.eng.last_logprobs(res)
-        total = time.perf_counter() - t0
-        lt = res.layer_times
-        self.fixed = (total - sum(lt)) + lt[0] + lt[1]  # embedding, layers 0-1, logits
-        self.keep_abs = res.keep_abs
-        return self.fixed + (self.shape.n_layers - 2) * lt[2]
-
-    def run_layer(self) -> float:
-        """Seconds of one recompute layer (layer 2) of the same request: the selected rows
-        through RMSNorm, QKV + RoPE, the moved chunks' re-roped K/V, masked attention,
-        o_proj and the MLP, as the oracle port's layer loop does them.  run_once first."""
-        import torch
-
-        e, li, N = self.eng, 2, len(self.tokens)
-        active = self.keep_abs
-        g = torch.Generator().manual_seed(li)
-        h = torch.randn((1, len(active), self.shape.hidden), generator=g)
-        ar = torch.arange(N)
-        t0 = time.perf_counter()
-        x = e._rms(h, e._lw(li, "input_layernorm.weight"))
-        q, k, v = e._qkv(li, x, active)
-        K = torch.zeros((1, e.n_kv, N, e.head_dim))
-        V = torch.zeros_like(K)
-        for p in self.pl:
-            end = p.start + p.chunk.length
-            K[:, :, p.start:end] = e.shift_keys(p.chunk.keys[li], p.start - p.chunk.start)
-            V[:, :, p.start:end] = p.chunk.values[li]
-        K[:, :, active] = k
-        V[:, :, active] = v
-        e._attend(li, h, q, K, V, active[:, None] >= ar[None, :])
+        self.n_selected = int(len(res.keep_abs))
         return time.perf_counter() - t0
 
+    @property
+    def dtype_name(self) -> str:
+        return "bf16" if str(self.dtype).endswith("bfloat16") else "f32"
+
     def describe(self, reps: int) -> str:
-        return (f"oracle port of TorchEngine.prefill on the host CPU, fp32, same request shape "
-                f"(N={len(self.tokens)}, 15% recompute); {self.nl} of {self.shape.n_layers} layers executed, "
-                f"layers 2..{self.shape.n_layers - 1} extrapolated from the measured layer-2 time; "
-                f"median of {reps}")
+        return (f"oracle port of TorchEngine.prefill (timed equal to the reference's own on a shared CPU "
+                f"request) on the host CPU, {self.dtype_name}, all {self.shape.n_layers} layers of the same "
+                f"request (N={len(self.tokens)}, {self.ratio:.0%} recompute, {self.n_selected} rows recomputed "
+                f"past layer 1), seed-0 random weights; median of {reps} prefills after one warm-up")
 
 
 def cpu_sample(args, shape, reps: int = 2) -> dict:
     s = CpuSample(args, shape)
+    s.run_once()  # warm-up
     t = statistics.median(s.run_once() for _ in range(reps))
     return {"value": round(len(s.tokens) / t, 2), "unit": "tokens/s", "cores": s.threads, "kind": "port",
-            "ttft_ms": round(t * 1e3, 1), "sample": s.describe(reps)}
+            "dtype": s.dtype_name, "ttft_ms": round(t * 1e3, 1), "sample": s.describe(reps)}
 
 
 # ------------------------------------------------------------------ ours
@@ -1255,37 +1239,33 @@ def run_decode(args):
 
 
 def run_reference(args):
-    """CPU reference arm: the oracle port of the reference path on the host cores.
-
-    One full prefill of the truncated 3-layer model (warm-up) measures the fixed part
-    (embedding, layer 0 on every token, layer 1 with the selection, logits) and the
-    selection; then every step is one recompute layer of the same request, so the run
-    stays bounded for any --steps.  TTFT = fixed part + (L - 2) x median layer time."""
+    """CPU reference arm: the oracle port of the reference path on the host cores, one
+    whole prefill of the bench's request per step (all layers, nothing extrapolated).
+    At most `--warmup` (capped at 2) warm-up prefills, then `--steps` timed ones, cut
+    short once about two minutes of timed prefills have run; the line says how many."""
     if int(os.environ.get("RANK", "0")) != 0:
         return
     from chunkkv_b200.engine.weights import SHAPES
 
     shape = SHAPES[args.shape]
     s = CpuSample(args, shape)
-    s.run_once()
-    for _ in range(args.warmup):
-        s.run_layer()
+    for _ in range(max(1, min(args.warmup, 2))):
+        s.run_once()
+    times = []
     t0 = time.perf_counter()
-    layer = [s.run_layer() for _ in range(args.steps)]
-    wall = time.perf_counter() - t0
-    ttft = s.fixed + (shape.n_layers - 2) * statistics.median(layer)
+    for _ in range(args.steps):
+        times.append(s.run_once())
+        if time.perf_counter() - t0 > 120.0:
+            break
+    ttft = statistics.median(times)
     v = len(s.tokens) / ttft
-    sample = (f"oracle port of TorchEngine.prefill on the host CPU, fp32, same request shape (N={len(s.tokens)}, "
-              f"{args.ratio:.0%} recompute): embedding, layers 0-1 and logits measured once on a 3-layer "
-              f"truncation; each step is one recompute layer ({len(s.keep_abs)} selected rows); "
-              f"TTFT = fixed part + {shape.n_layers - 2} x median layer time")
-    cb = {"value": round(v, 2), "unit": "tokens/s", "cores": s.threads, "kind": "port",
-          "ttft_ms": round(ttft * 1e3, 1), "sample": sample}
+    cb = {"value": round(v, 2), "unit": "tokens/s", "cores": s.threads, "kind": "port", "dtype": s.dtype_name,
+          "ttft_ms": round(ttft * 1e3, 1), "sample": s.describe(len(times))}
     out = {"impl": "reference", "metric": METRIC, "value": round(v, 2), "unit": "tokens/s",
-           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-           "ms_per_step": round(1e3 * wall / max(1, args.steps), 1), "higher_is_better": True, "scaling": "weak",
-           "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-           "config": {"workload": "BASELINE config 3 request on the host CPU (bounded sample, see cpu_baseline)",
+           "n_gpus": args.gpus, "steps": len(times), "steps_requested": args.steps, "warmup": args.warmup,
+           "ms_per_step": round(1e3 * statistics.mean(times), 1), "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": s.dtype_name, "data": "synthetic",
+           "config": {"workload": "BASELINE config 3 request on the host CPU (every layer, see cpu_baseline)",
                       "model": f"{args.shape} architecture", "tokens": len(s.tokens)},
            "cpu_baseline": cb,
            "e2e": {"value": round(v, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
