@@ -126,7 +126,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap tmQ, const int32_t* __restrict__ positions,
                         uint16_t* __restrict__ out, int M, int Hq, int Hk, int n_ctx, float scale_log2,
                         int tps, int max_splits, int blocks, unsigned* __restrict__ sched,
-                        uint16_t* __restrict__ part_o, float2* __restrict__ part_ml) {
+                        float* __restrict__ part_o, float2* __restrict__ part_ml) {
   using C = Cfg<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -583,11 +583,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
       };
-      // O / l in bf16: the output row, or, for one slice of the keys, a partial that the
-      // combine kernel merges with the slice's (max, sum)
-      {
+      if (cur.n_split > 1) {
+        // one slice of the keys: unnormalised O with its (max, sum), merged by the combine kernel
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 32) {
+          float o[32];
+          tmem_ld32(obuf + c, o);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint32_t v[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(o[16 * h + e]);
+            flush(v, reinterpret_cast<uint8_t*>(part_o), 4, (c + 16 * h) * 4);
+          }
+        }
+        if (row.valid) {
+          const int64_t prow = int64_t((cur.rb * Hk + cur.hk) * max_splits + cur.split) * (NQ * BM) + w * BM + r;
+          part_ml[prow] = make_float2(m, l);
+        }
+      } else {
         const float inv = l > 0.f ? 1.0f / l : 0.f;
-        uint8_t* base = reinterpret_cast<uint8_t*>(cur.n_split > 1 ? part_o : out);
 #pragma unroll 1
         for (int c = 0; c < HD; c += 32) {
           float o[32];
@@ -595,12 +610,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t v[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) v[e] = pack_bf2(o[2 * e] * inv, o[2 * e + 1] * inv);
-          flush(v, base, 2, c * 2);
+          flush(v, reinterpret_cast<uint8_t*>(out), 2, c * 2);
         }
-      }
-      if (cur.n_split > 1 && row.valid) {
-        const int64_t prow = int64_t((cur.rb * Hk + cur.hk) * max_splits + cur.split) * (NQ * BM) + w * BM + r;
-        part_ml[prow] = make_float2(m, l);
       }
       // O has been read: the next item's first P V (which overwrites it) is issued only
       // after this warpgroup's next p_full
@@ -618,16 +629,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Merge the key splits of the row blocks that were split: with O_s / l_s the slice's
-// normalised partial (bf16), O = sum_s 2^(m_s - M) l_s (O_s / l_s) / sum_s 2^(m_s - M) l_s,
-// M = max_s m_s (all in the log2 domain of the kernel).  One warp per packed row; lane
-// s reads split s's (m, l), then each lane sums HD/32 consecutive columns over the
-// splits.  Rows of unsplit blocks were written directly.
+// Merge the key splits of the row blocks that were split: O = sum_s 2^(m_s - M) O_s /
+// sum_s 2^(m_s - M) l_s with M = max_s m_s (all in the log2 domain of the kernel).
+// One warp per packed row; lane s reads split s's (m, l), each lane then sums its
+// HD/32 columns over the splits.  Rows of unsplit blocks were written directly.
 constexpr int kCombineWarps = 8;
 template <int HD>
 __global__ void __launch_bounds__(kCombineWarps * 32) attention_combine_kernel(
     const int32_t* __restrict__ positions, uint16_t* __restrict__ out, int M, int Hq, int Hk, int n_ctx,
-    int tps, int max_splits, const uint16_t* __restrict__ part_o, const float2* __restrict__ part_ml) {
+    int tps, int max_splits, const float* __restrict__ part_o, const float2* __restrict__ part_ml) {
   const int G = Hq / Hk;
   const int T = BM / G;
   constexpr int kChunks = NQ * BM / kCombineWarps;  // CTAs per (row block, KV head)
@@ -653,42 +663,24 @@ __global__ void __launch_bounds__(kCombineWarps * 32) attention_combine_kernel(
   float mmax = ml.x;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, o));
-  const float wl = lane < n_split ? exp2f(ml.x - mmax) * ml.y : 0.f;  // the slice's weight
-  float L = wl;
+  const float wgt = lane < n_split ? exp2f(ml.x - mmax) : 0.f;
+  float L = wgt * ml.y;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-  constexpr int PER = HD / 32;  // consecutive columns per lane: 4 (HD 128) or 2 (HD 64)
-  float acc[PER];
+  float acc[HD / 32];
 #pragma unroll
-  for (int i = 0; i < PER; ++i) acc[i] = 0.f;
+  for (int i = 0; i < HD / 32; ++i) acc[i] = 0.f;
 #pragma unroll 4
   for (int sp = 0; sp < n_split; ++sp) {
-    const float ws = __shfl_sync(0xffffffffu, wl, sp);
-    const uint16_t* po = part_o + (base + sp * stride) * HD + PER * lane;
-    uint32_t u[PER / 2];
-    if constexpr (PER == 4) {
-      const uint2 x = *reinterpret_cast<const uint2*>(po);
-      u[0] = x.x;
-      u[1] = x.y;
-    } else {
-      u[0] = *reinterpret_cast<const uint32_t*>(po);
-    }
+    const float ws = __shfl_sync(0xffffffffu, wgt, sp);
+    const float* po = part_o + (base + sp * stride) * HD + lane;
 #pragma unroll
-    for (int i = 0; i < PER / 2; ++i) {
-      acc[2 * i] = fmaf(ws, lo_bf(u[i]), acc[2 * i]);
-      acc[2 * i + 1] = fmaf(ws, hi_bf(u[i]), acc[2 * i + 1]);
-    }
+    for (int i = 0; i < HD / 32; ++i) acc[i] = fmaf(ws, po[32 * i], acc[i]);
   }
   const float inv = L > 0.f ? 1.0f / L : 0.f;
-  uint16_t* orow = out + (int64_t(t0 + tt) * Hq + hk * G + g) * HD + PER * lane;
-  uint32_t v[PER / 2];
+  uint16_t* orow = out + (int64_t(t0 + tt) * Hq + hk * G + g) * HD;
 #pragma unroll
-  for (int i = 0; i < PER / 2; ++i) v[i] = pack_bf2(acc[2 * i] * inv, acc[2 * i + 1] * inv);
-  if constexpr (PER == 4) {
-    *reinterpret_cast<uint2*>(orow) = make_uint2(v[0], v[1]);
-  } else {
-    *reinterpret_cast<uint32_t*>(orow) = v[0];
-  }
+  for (int i = 0; i < HD / 32; ++i) orow[lane + 32 * i] = f2bf(acc[i] * inv);
 }
 
 // Key-split plan: split only when the unsplit grid leaves SMs idle.
@@ -701,7 +693,7 @@ struct SplitPlan {
 constexpr int64_t kSchedBytes = 256;
 // Fixed cost of one item, in key-tile times, for the persistent kernel: its first S
 // MMA and the epilogue are only partly hidden behind the neighbouring items; a split
-// item also writes its partial O (bf16, normalised) and (max, sum).
+// item also writes its fp32 partial O.
 constexpr double kItemCost = 0.7;
 constexpr double kSplitItemCost = 1.0;
 // Estimated makespan, in key-tile times, of a split plan: the list-scheduling estimate
@@ -723,7 +715,7 @@ double plan_cost(int blocks, int Hk, int HD, int n_ctx, int tps, int sms) {
     max_item = std::max(max_item, std::min(kt, tps));
   }
   total *= Hk;
-  const double combine = split ? double(items_all) * Hk * NQ * BM * (HD * 2 + 8) / 14.3e6 : 0.0;
+  const double combine = split ? double(items_all) * Hk * NQ * BM * (HD * 4 + 8) / 14.3e6 : 0.0;
   return total / sms + 0.5 * (max_item + cta_cost) + combine;
 }
 
@@ -762,7 +754,7 @@ SplitPlan plan_splits(int M, int Hq, int Hk, int HD, int n_ctx) {
   if (best > 0.90 * unsplit) best_tps = max_kt;
   p.tps = best_tps;
   p.max_splits = ceil_div(max_kt, p.tps);
-  p.bytes = p.max_splits > 1 ? int64_t(p.blocks) * Hk * p.max_splits * NQ * BM * (int64_t(HD) * 2 + 8) : 0;
+  p.bytes = p.max_splits > 1 ? int64_t(p.blocks) * Hk * p.max_splits * NQ * BM * (int64_t(HD) * 4 + 8) : 0;
   std::lock_guard<std::mutex> lock(mu);
   if (cache.size() < 256) cache.push_back({Key{M, Hq, Hk, HD, n_ctx, sms}, p});
   return p;
@@ -1087,8 +1079,8 @@ int launch(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int3
     p.tps = ceil_div(n_ctx, BN);
     p.max_splits = 1;
   }
-  uint16_t* part_o = p.max_splits > 1 ? reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(workspace) + kSchedBytes)
-                                      : nullptr;
+  float* part_o = p.max_splits > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kSchedBytes)
+                                   : nullptr;
   float2* part_ml = p.max_splits > 1
                         ? reinterpret_cast<float2*>(part_o + int64_t(p.blocks) * Hk * p.max_splits * NQ * BM * HD)
                         : nullptr;

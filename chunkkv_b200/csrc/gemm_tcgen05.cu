@@ -7,13 +7,14 @@
 //              k/v written straight into the blended cache       (torch_engine.py:155-156)
 //
 // D = A B^T with A = x [M][K] and B = W [N][K], both K-major.  One persistent CTA
-// per SM, 6 warps:
+// per SM, 10 warps:
 //   warp 0      TMA producer (one thread): A 128x64 and B 256x64 tiles, 128B swizzle,
 //               4-stage ring guarded by full/empty mbarriers;
 //   warp 1      TMEM owner + MMA issuer (one thread): tcgen05.mma kind::f16,
 //               M=128 N=256 K=16 per instruction, fp32 accumulators in TMEM;
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes
-//               32*(w%4)..+31 = tile rows), fused math, stores.
+//   warps 2..9  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes
+//               32*(w%4)..+31 = tile rows; warps w and w+4 take the two halves of the
+//               tile's columns), fused math, stores.
 // Two 256-column accumulators (all 512 TMEM columns) let the epilogue of one tile
 // overlap the main loop of the next.  Tiles are visited M-fastest so CTAs that
 // run together share the same weight tile through L2.
@@ -28,7 +29,10 @@ namespace ckv {
 namespace {
 
 constexpr int BM = 128, BK = 64, UMMA_K = 16;
-constexpr int kThreads = 192;
+// warp 0 TMA, warp 1 MMA, warps 2..9 epilogue: two warps per TMEM lane quadrant, each
+// taking one half of the tile's columns
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr uint32_t A_BYTES = BM * BK * 2;  // 16 KiB
 constexpr uint32_t TMEM_COLS = 512;        // two accumulators of up to 256 columns
 
@@ -79,12 +83,24 @@ __device__ __forceinline__ void store8(uint16_t* dst, const float* v) {
   *reinterpret_cast<uint4*>(dst) = w;
 }
 
-// ---- epilogues: one thread = one tile row; all lanes execute the TMEM loads.
+// ---- epilogues: one thread = one tile row; all lanes execute the TMEM loads.  `part`
+// (0 or 1) selects which half of the tile's 32-column chunks (or heads) this warp does.
+template <int BN>
+__device__ __forceinline__ int chunk_lo(int part) {
+  constexpr int n = (BN + 31) / 32;
+  return part == 0 ? 0 : 32 * ((n + 1) / 2);
+}
+template <int BN>
+__device__ __forceinline__ int chunk_hi(int part) {
+  constexpr int n = (BN + 31) / 32;
+  return part == 0 ? 32 * ((n + 1) / 2) : 32 * n;
+}
+
 template <int BN>
 __device__ __forceinline__ void epi_store(uint32_t tacc, int row, int M, int n0, int N,
-                                          const EpiParams& ep) {
+                                          const EpiParams& ep, int part) {
 #pragma unroll 1
-  for (int c = 0; c < BN; c += 32) {
+  for (int c = chunk_lo<BN>(part); c < chunk_hi<BN>(part); c += 32) {
     float v[32];
     tmem_ld32(tacc + c, v);
     if (row >= M) continue;
@@ -105,9 +121,9 @@ __device__ __forceinline__ void epi_store(uint32_t tacc, int row, int M, int n0,
 
 template <int BN>
 __device__ __forceinline__ void epi_resid(uint32_t tacc, int row, int M, int n0, int N,
-                                          const EpiParams& ep) {
+                                          const EpiParams& ep, int part) {
 #pragma unroll 1
-  for (int c = 0; c < BN; c += 32) {
+  for (int c = chunk_lo<BN>(part); c < chunk_hi<BN>(part); c += 32) {
     float v[32];
     tmem_ld32(tacc + c, v);
     if (row >= M) continue;
@@ -132,10 +148,10 @@ __device__ __forceinline__ void epi_resid(uint32_t tacc, int row, int M, int n0,
 // Tile = 128 gate columns then the 128 matching up columns (interleaved weight).
 template <int BN>
 __device__ __forceinline__ void epi_swiglu(uint32_t tacc, int row, int M, int n0, int N,
-                                           const EpiParams& ep) {
+                                           const EpiParams& ep, int part) {
   const int out0 = n0 / 2;
 #pragma unroll 1
-  for (int c = 0; c < BN / 2; c += 32) {
+  for (int c = chunk_lo<BN / 2>(part); c < chunk_hi<BN / 2>(part); c += 32) {
     float g[32], u[32];
     tmem_ld32(tacc + c, g);
     tmem_ld32(tacc + BN / 2 + c, u);
@@ -155,7 +171,7 @@ __device__ __forceinline__ void epi_swiglu(uint32_t tacc, int row, int M, int n0
 
 template <int BN, int HD>
 __device__ __forceinline__ void epi_qkv(uint32_t tacc, int row, int M, int n0, int N,
-                                        const EpiParams& ep) {
+                                        const EpiParams& ep, int part) {
   constexpr int HALF = HD / 2;
   const int Hq = ep.n_q_heads, Hk = ep.n_kv_heads;
   int pos = 0;
@@ -168,8 +184,9 @@ __device__ __forceinline__ void epi_qkv(uint32_t tacc, int row, int M, int n0, i
       ok = false;
     }
   }
+  constexpr int kHeads = BN / HD;  // heads per tile, split between the two parts
 #pragma unroll 1
-  for (int hh = 0; hh < BN / HD; ++hh) {
+  for (int hh = part * ((kHeads + 1) / 2); hh < (part == 0 ? (kHeads + 1) / 2 : kHeads); ++hh) {
     if (n0 + hh * HD >= N) break;  // warp-uniform
     const int gcol = ep.col_begin + n0 + hh * HD;
     const int head = gcol / HD;
@@ -231,12 +248,12 @@ __device__ __forceinline__ void epi_qkv(uint32_t tacc, int row, int M, int n0, i
 
 template <int EPI, int HD, int BN>
 __device__ __forceinline__ void run_epilogue(uint32_t tacc, int row, int M, int n0, int N,
-                                             const EpiParams& ep) {
-  if constexpr (EPI == EPI_STORE) epi_store<BN>(tacc, row, M, n0, N, ep);
-  else if constexpr (EPI == EPI_RESID) epi_resid<BN>(tacc, row, M, n0, N, ep);
-  else if constexpr (EPI == EPI_SWIGLU) epi_swiglu<BN>(tacc, row, M, n0, N, ep);
-  else if constexpr (EPI == EPI_PARTIAL) epi_store<BN>(tacc, row, M, n0, N, ep);
-  else epi_qkv<BN, HD>(tacc, row, M, n0, N, ep);
+                                             const EpiParams& ep, int part) {
+  if constexpr (EPI == EPI_STORE) epi_store<BN>(tacc, row, M, n0, N, ep, part);
+  else if constexpr (EPI == EPI_RESID) epi_resid<BN>(tacc, row, M, n0, N, ep, part);
+  else if constexpr (EPI == EPI_SWIGLU) epi_swiglu<BN>(tacc, row, M, n0, N, ep, part);
+  else if constexpr (EPI == EPI_PARTIAL) epi_store<BN>(tacc, row, M, n0, N, ep, part);
+  else epi_qkv<BN, HD>(tacc, row, M, n0, N, ep, part);
 }
 
 // Bounded wait that ignores the abort flag (used only while draining).
@@ -279,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
+      mbar_init(&tempty[a], kEpiWarps);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
     *abort = 0;
@@ -355,7 +372,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    const int sub = warp & 3;  // TMEM sub-partition this warp may access
+    const int sub = warp & 3;             // TMEM sub-partition this warp may access
+    const int part = (warp - 2) / 4;      // which half of the tile's columns
     int tcount = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tcount) {
       const int acc = tcount & 1;
@@ -365,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int mt = tile % m_tiles, nt = tile / m_tiles;
       const int row = mt * BM + sub * 32 + lane;
       const uint32_t tacc = tmem_base + (uint32_t(sub * 32) << 16) + acc * 256;
-      run_epilogue<EPI, HD, BN>(tacc, row, M, nt * BN, N, ep);
+      run_epilogue<EPI, HD, BN>(tacc, row, M, nt * BN, N, ep, part);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
