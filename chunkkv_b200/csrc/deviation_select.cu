@@ -1,42 +1,52 @@
 // Layer-1 K/V deviation + pooled top-k selection (torch_engine.py:117-153).
 //
-// One launch.  Phase 1 (every CTA, a balanced block of active rows each, one
-// warp per row with all of the row's loads in flight):
+// One launch, in clusters of kCluster CTAs.  Phase 1 (every CTA, a balanced block of
+// active rows each, one warp per row with all of the row's loads in flight):
 //   diff = sum_{h,d} fp32(bf16(k - K))^2 + sum fp32(bf16(v - V))^2   (torch_engine.py:118-119)
 //   norm = sum fp32(k)^2 + sum fp32(v)^2                             (torch_engine.py:120)
-// and, for rows that are eligible unless their chunk escalates (cached, not a
-// sink, inside a pooled chunk), a shared-memory histogram of the top 11 bits of
-// the score, added into a global histogram in the control block.
-// Phase 2 (the last CTA to finish, found with an atomic ticket — no waiting):
+// and, for rows that are eligible unless their chunk escalates (cached, not a sink,
+// inside a pooled chunk), a shared-memory histogram of the top 11 bits of the score,
+// added into a global histogram in the control block.
+// Phase 2 (the last cluster to finish, found with an atomic ticket — no waiting): the
+// cluster's CTAs each hold one contiguous slice of the positions (a score key and a
+// flag byte per position, in shared memory) and exchange what crosses slices through
+// distributed shared memory, between hardware cluster barriers:
 //   per-chunk rel = sum diff / sum norm over the chunk span           (torch_engine.py:132)
+//     (each CTA sums its slice, the slice sums are added in rank order)
 //   keep = ~cached | sink | escalated spans; pool = pooled spans     (torch_engine.py:125-140)
 //   budget = min(sum of per-chunk budgets, |pool & ~keep|)          (torch_engine.py:139,142)
-//   top-`budget` eligible positions by diff: a three-level radix select
-//   (11, 11 and 9 bits) on the fp32 bit pattern of diff >= 0 — the first
-//   level's histogram is phase 1's unless a chunk escalated, an exact position
-//   lies in the pool, or there was no phase 1 (selection from given scores);
-//   equal scores: lower position first — the reference's argsort leaves that
-//   order undefined, torch_engine.py:144
-//   keep_abs = ascending kept positions, sel = index in the active list (146-150).
-// Phase 2 keeps one 4-byte score key and one flag byte per position in shared
-// memory when n_ctx <= kSmemPositions, otherwise in the caller's scratch, and
-// walks them four positions per lane at a time.
+//   top-`budget` eligible positions by diff: a three-level radix select (11, 11 and 9
+//     bits) on the fp32 bit pattern of diff >= 0, each level's histogram the sum of the
+//     slices' (the first level's is phase 1's unless a chunk escalated, an exact
+//     position lies in the pool, or there was no phase 1); equal scores: lower
+//     position first — the reference's argsort leaves that order undefined,
+//     torch_engine.py:144
+//   keep_abs = ascending kept positions, sel = index in the active list (146-150),
+//     each slice at the offset the lower slices' counts give.
 #include "ckv_common.cuh"
 
 CKV_DEFINE_ERR_WORD(select)
+
+#include <cooperative_groups.h>
+
+#include <mutex>
+
+namespace cg = cooperative_groups;
 
 namespace ckv {
 namespace {
 
 constexpr int kThreads = 1024;
 constexpr int kWarps = kThreads / 32;
-// positions whose keys and flags phase 2 holds in shared memory (5 bytes each: 210 KiB
-// at the limit, beside about 9 KiB of static shared memory)
-constexpr int kSmemPositions = 43008;
-constexpr int kStaticSmem = 10 * 1024;  // bound on the kernels' static shared memory
+constexpr int kCluster = 8;  // CTAs of one cluster; the last cluster runs the selection
+// positions of one CTA's slice held in shared memory (5 bytes each), beside the
+// chunk partials (8 bytes per chunk) and about 17 KiB of static shared memory
+constexpr int kSmemSlice = 35328;
+constexpr int kMaxChunks = 4096;        // chunk table the selection takes
 // chunk tables up to this size are copied to shared memory for phase 1's histogram
 constexpr int kPhase1Chunks = 1024;
 constexpr int kBins = 2048;  // first radix level: score bits [30:20]
+constexpr int kVals = 8;     // per-CTA scalars exchanged between the cluster's CTAs
 
 // pos_flags input bits
 constexpr uint8_t kInCached = 1, kInSink = 2, kInExact = 4;
@@ -65,17 +75,20 @@ struct SelectArgs {
   int32_t* keep_abs;
   int32_t* sel;
   int32_t* counts;
-  uint32_t* keys_scratch;   // [round16(n_ctx)] used when n_ctx > kSmemPositions
+  uint32_t* keys_scratch;   // [round16(n_ctx)] used when a slice exceeds kSmemSlice
   uint8_t* flags_scratch;   // [round16(n_ctx)]
 };
 
 __host__ __device__ constexpr int round16(int n) { return (n + 15) / 16 * 16; }
-// dynamic shared memory of the fused kernel: phase 1's copy of the chunk table, later
-// phase 2's keys and flags (when they fit) in the same bytes
+// positions per CTA slice (a multiple of 16, so every slice starts 64-byte aligned)
+__host__ __device__ constexpr int slice_len(int n_ctx) { return round16((n_ctx + kCluster - 1) / kCluster); }
+__host__ __device__ constexpr bool slice_in_smem(int n_ctx) { return slice_len(n_ctx) <= kSmemSlice; }
+// dynamic shared memory: the slice's keys and flags (when they fit), then the chunk
+// partials; phase 1's copy of the chunk table shares the same bytes
 __host__ __device__ constexpr int dyn_smem_bytes(int n_ctx, int n_chunks) {
-  return (n_ctx <= kSmemPositions ? 5 * round16(n_ctx) : 0) >
+  return (slice_in_smem(n_ctx) ? 5 * slice_len(n_ctx) : 0) + 16 * ((n_chunks + 1) / 2) >
                  16 * (n_chunks < kPhase1Chunks ? n_chunks : kPhase1Chunks)
-             ? (n_ctx <= kSmemPositions ? 5 * round16(n_ctx) : 0)
+             ? (slice_in_smem(n_ctx) ? 5 * slice_len(n_ctx) : 0) + 16 * ((n_chunks + 1) / 2)
              : 16 * (n_chunks < kPhase1Chunks ? n_chunks : kPhase1Chunks);
 }
 
@@ -101,7 +114,7 @@ __device__ __forceinline__ int warp_incl(int v) {
 }
 
 // Exclusive scan over the kWarps warps of one int per warp (lane 0's value counts);
-// returns the warp's base, *total the block sum.  All kThreads threads call it.
+// returns the warp's base, *total the CTA sum.  All kThreads threads call it.
 __device__ int warp_bases(int v, int* total, int* s_w) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (lane == 0) s_w[warp] = v;
@@ -143,10 +156,10 @@ __device__ __forceinline__ void hist_add(uint32_t* hist, uint32_t bin, bool on) 
   }
 }
 
-// Bins of `hist` (nbins = 2048 or 512) ranked from the top.  Returns the number of
-// keys counted; for k' = min(k, that number) > 0, *s_bin and *s_k receive the bin that
-// holds the k'-th largest key and the key's rank inside that bin.
-__device__ int rank_bins(const uint32_t* hist, int nbins, int k, int* s_w, int* s_bin, int* s_k) {
+// Bins ranked from the top of this CTA's `hist` (nbins = 2048 or 512).  Returns the
+// number of keys counted; for k' = min(k, that number) > 0, *s_bin and *s_k receive the
+// bin that holds the k'-th largest key and the key's rank inside that bin.
+__device__ int rank_bins_local(const uint32_t* hist, int nbins, int k, int* s_w, int* s_bin, int* s_k) {
   const int b0 = nbins - 1 - 2 * int(threadIdx.x), b1 = b0 - 1;
   const int c0 = b0 >= 0 ? int(hist[b0]) : 0, c1 = b1 >= 0 ? int(hist[b1]) : 0;
   const int inc = warp_incl(c0 + c1);
@@ -167,13 +180,46 @@ __device__ int rank_bins(const uint32_t* hist, int nbins, int k, int* s_w, int* 
   return tot;
 }
 
+struct Rank {
+  int bin, k, total;
+};
+
+// The same over the sum of the cluster's CTAs' histograms: rank 0 adds the CTAs'
+// counts into its own `hist` (remote reads of the other CTAs' shared memory) and ranks
+// them; after a cluster barrier every CTA reads rank 0's answer.  Called by every CTA,
+// after a cluster barrier that follows the last update of any `hist`.
+__device__ Rank rank_bins_cluster(cg::cluster_group& cluster, uint32_t* hist, int nbins, int k, int* s_w,
+                                  Rank* s_rank) {
+  if (cluster.block_rank() == 0) {
+    for (int b = threadIdx.x; b < nbins; b += kThreads) {
+      uint32_t c = hist[b];
+#pragma unroll
+      for (int r = 1; r < kCluster; ++r) c += cluster.map_shared_rank(hist, r)[b];
+      hist[b] = c;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      s_rank->bin = 0;
+      s_rank->k = 0;
+    }
+    const int tot = rank_bins_local(hist, nbins, k, s_w, &s_rank->bin, &s_rank->k);
+    if (threadIdx.x == 0) s_rank->total = tot;
+  }
+  cluster.sync();
+  return *cluster.map_shared_rank(s_rank, 0);
+}
+
 __device__ __forceinline__ bool eligible(uint32_t f) { return (f & kPool) && !(f & kKeep); }
 __device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xffu; }
 
-// fl[p] |= bit for p in [s, e), by one warp, eight reads in flight per lane.  Returns
-// (on every lane) whether a byte that gained the bit had `watch` set and not kKeep.
-__device__ __forceinline__ bool set_span_bit(uint8_t* fl, int s, int e, uint8_t bit, uint8_t watch) {
+// fl[p - lo] |= bit for p in [s, e) ∩ [lo, hi), by one warp, eight reads in flight per
+// lane.  Returns (on every lane) whether a byte that gained the bit had `watch` set and
+// not kKeep.
+__device__ __forceinline__ bool set_span_bit(uint8_t* fl, int lo, int hi, int s, int e, uint8_t bit,
+                                             uint8_t watch) {
   const int lane = threadIdx.x & 31;
+  s = max(s, lo) - lo;
+  e = min(e, hi) - lo;
   bool seen = false;
   for (int q = s + lane; q < e; q += 8 * 32) {
     uint8_t f[8];
@@ -189,186 +235,172 @@ __device__ __forceinline__ bool set_span_bit(uint8_t* fl, int s, int e, uint8_t 
   return __any_sync(0xffffffffu, seen);
 }
 
-// Phase 2: the selection, run by one CTA of kThreads threads.  keys/fl: [round16(n_ctx)]
-// each, in shared or global memory (16-byte aligned).  hist: kBins shared counters;
-// phase1_hist: the control block's histogram (nullptr: no usable phase-1 histogram),
-// read and cleared here.
-__device__ void select_tail(const SelectArgs& a, uint32_t* keys, uint8_t* fl, bool in_smem,
-                            uint32_t* hist, unsigned* phase1_hist) {
-  __shared__ int s_w[kWarps + 1];
-  __shared__ int s_budget, s_bin, s_k, s_slow;
-  __shared__ unsigned s_escmask;
-  __shared__ __align__(8) uint64_t bar[1];
-  __shared__ int s_abort;
+struct TailShared {
+  int w[kWarps + 1];
+  int vals[kVals];  // exchanged: [0] exact position in the pool, [1] equal keys,
+                    // [2] kept, [3] exact, [4] kept & cached, [5] kept & exact
+  int budget, bin, k, slow;
+  Rank rank;  // rank 0's answer of a cluster-wide ranking
+  unsigned escmask;
+  unsigned esc[kMaxChunks / 32];
+};
+
+// Phase 2: the selection, by the kCluster CTAs of one cluster (kThreads threads each).
+// keys/fl: this CTA's slice [rank * S, rank * S + S) of the positions, in shared or
+// global memory (16-byte aligned); part: n_chunks float2 in shared memory; hist: kBins
+// shared counters; phase1_hist: the control block's histogram (nullptr: none usable),
+// read by every CTA and cleared by rank 0.
+__device__ void select_tail(cg::cluster_group& cluster, const SelectArgs& a, uint32_t* keys, uint8_t* fl,
+                            float2* part, uint32_t* hist, unsigned* phase1_hist) {
+  __shared__ TailShared t;
+  __shared__ uint32_t hist2[kBins];  // the second level's counters
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int rank = int(cluster.block_rank());
   const int n = a.n_ctx;
-  const int nq = (n + 3) >> 2;  // quads of positions
-  const bool vec_in = ((reinterpret_cast<uintptr_t>(a.pos_flags) & 3u) == 0) &&
-                      ((reinterpret_cast<uintptr_t>(a.diff) & 15u) == 0);
-  // the phase-1 histogram, copied out and cleared for the next launch
+  const int S = slice_len(n);
+  const int lo = min(n, rank * S), hi = min(n, lo + S);
+  const int nl = hi - lo;            // positions of this slice
+  const int nq = (nl + 3) >> 2;      // quads of them
+
   if (phase1_hist)
-    for (int i = tid; i < kBins; i += kThreads) {
-      hist[i] = __ldcg(phase1_hist + i);
-      phase1_hist[i] = 0u;
-    }
+    for (int i = tid; i < kBins; i += kThreads) hist[i] = __ldcg(phase1_hist + i);
   if (tid == 0) {
-    s_budget = 0;
-    s_escmask = 0u;
-    s_slow = phase1_hist ? 0 : 1;
+    t.budget = 0;
+    t.escmask = 0u;
+    t.slow = phase1_hist ? 0 : 1;
   }
+  for (int i = tid; i < kMaxChunks / 32; i += kThreads) t.esc[i] = 0u;
+  for (int i = tid; i < kVals; i += kThreads) t.vals[i] = 0;
 
-  // 1. stage the inputs: with the keys in shared memory, diff lands in the key array
-  // and pos_flags in the flag array by bulk copies (one thread issues them; the rest of
-  // each array, under 16 bytes, by plain loads); otherwise they are read in step 3.
-  const bool staged = in_smem && ((reinterpret_cast<uintptr_t>(a.diff) & 15u) == 0) &&
-                      ((reinterpret_cast<uintptr_t>(a.pos_flags) & 15u) == 0);
-  if (staged) {
-    const uint32_t diff_bulk = uint32_t(n) * 4u / 16u * 16u, flag_bulk = uint32_t(n) / 16u * 16u;
-    if (tid == 0) {
-      s_abort = 0;
-      mbar_init(bar, 1);
-      fence_barrier_init();
-    }
-    __syncthreads();
-    if (tid == 0) {
-      fence_async_smem();  // earlier generic accesses to these bytes (phase 1's chunk table)
-      mbar_expect_tx(bar, diff_bulk + flag_bulk);
-      if (diff_bulk) bulk_load(keys, a.diff, diff_bulk, bar);
-      if (flag_bulk) bulk_load(fl, a.pos_flags, flag_bulk, bar);
-    }
-    for (int p = int(diff_bulk / 4) + tid; p < n; p += kThreads) keys[p] = __float_as_uint(__ldcg(a.diff + p));
-    for (int p = int(flag_bulk) + tid; p < n; p += kThreads) fl[p] = a.pos_flags[p];
-    const bool ok = mbar_wait(bar, 0, &s_abort, &g_err_word);
-    if (__syncthreads_or(!ok)) {
-      // the copy did not complete in time (mbar_wait recorded CKV_DEV_ERR_WAIT_TIMEOUT):
-      // one more bounded wait so that nothing is still writing this CTA's shared
-      // memory, then stop with the status set
-      const uint64_t t0 = global_ns();
-      while (!mbar_try_wait(bar, 0) && global_ns() - t0 < kWaitLimitNs) {
+  // 1. this slice's raw flags and scores (torch_engine.py:121-122: positions never
+  // computed score 0), four positions per lane, vector loads where the inputs allow
+  const bool vec_in = ((reinterpret_cast<uintptr_t>(a.pos_flags + lo) & 3u) == 0) &&
+                      ((reinterpret_cast<uintptr_t>(a.diff + lo) & 15u) == 0);
+  for (int g = tid; g < nq; g += kThreads) {
+    const int p = lo + 4 * g;
+    uint32_t f4 = 0u;
+    uint4 d4 = make_uint4(0u, 0u, 0u, 0u);
+    if (vec_in && p + 3 < hi) {
+      f4 = __ldcg(reinterpret_cast<const unsigned*>(a.pos_flags + p));
+      d4 = __ldcg(reinterpret_cast<const uint4*>(a.diff + p));
+    } else {
+      uint32_t* dd = reinterpret_cast<uint32_t*>(&d4);
+      for (int i = 0; i < 4 && p + i < hi; ++i) {
+        f4 |= uint32_t(a.pos_flags[p + i]) << (8 * i);
+        dd[i] = __float_as_uint(__ldcg(a.diff + p + i));
       }
-      if (tid == 0) a.counts[5] = int(CKV_DEV_ERR_WAIT_TIMEOUT);
-      return;
     }
+    *reinterpret_cast<uint32_t*>(fl + 4 * g) = f4;  // raw pos_flags for now
+    *reinterpret_cast<uint4*>(keys + 4 * g) = d4;   // raw diff bits for now
   }
+  __syncthreads();
 
-  // 2. per chunk: rel over its span (never-computed positions count as 0), escalation
-  // decided (its span is kept whole in step 4), the budgets of pooled chunks add up
-  // (torch_engine.py:128-140)
+  // 2. per chunk, this slice's share of its span: (sum diff, sum norm) over the
+  // positions that were computed (torch_engine.py:128-132)
   for (int c = warp; c < a.n_chunks; c += kWarps) {
+    const int32_t* m = a.meta + c * CKV_SEL_META_STRIDE;
+    const int s = max(m[0], lo), e = min(m[0] + m[1], hi);
+    float sd = 0.f, sn = 0.f;
+    if (!m[3]) {
+      for (int q = s + lane; q < e; q += 8 * 32) {
+        float dd[8], nn[8];
+        bool use[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int p = q + 32 * j;
+          use[j] = p < e && !(fl[p - lo] & kInExact);
+          dd[j] = use[j] ? __uint_as_float(keys[p - lo]) : 0.f;
+          nn[j] = use[j] ? __ldcg(a.norm + p) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          sd += dd[j];
+          sn += nn[j];
+        }
+      }
+      sd = warp_sum(sd);
+      sn = warp_sum(sn);
+    }
+    if (lane == 0) part[c] = make_float2(sd, sn);
+  }
+  cluster.sync();  // every slice's partials are written
+  if (phase1_hist && rank == 0)  // every CTA has its copy: clear it for the next launch
+    for (int i = tid; i < kBins; i += kThreads) phase1_hist[i] = 0u;
+
+  // 3. rel of every chunk from the slices' partials in rank order; escalation, budget
+  // (torch_engine.py:128-140) — the same values in every CTA
+  for (int c = tid; c < a.n_chunks; c += kThreads) {
     const int32_t* m = a.meta + c * CKV_SEL_META_STRIDE;
     if (m[3]) continue;  // exact
-    const int s = max(m[0], 0), e = min(m[0] + m[1], n);
     float sd = 0.f, sn = 0.f;
-    for (int q = s + lane; q < e; q += 16 * 32) {
-      float dd[16], nn[16];
-      uint8_t ff[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int p = q + 32 * j;
-        const bool in = p < e;
-        ff[j] = in ? (staged ? fl[p] : a.pos_flags[p]) : uint8_t(kInExact);
-        dd[j] = in ? (staged ? __uint_as_float(keys[p]) : __ldcg(a.diff + p)) : 0.f;
-        nn[j] = in ? __ldcg(a.norm + p) : 0.f;
-      }
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        if (ff[j] & kInExact) continue;
-        sd += dd[j];
-        sn += nn[j];
-      }
+    for (int r = 0; r < kCluster; ++r) {
+      const float2 v = cluster.map_shared_rank(part, r)[c];
+      sd += v.x;
+      sn += v.y;
     }
-    sd = warp_sum(sd);
-    sn = warp_sum(sn);
     const float rel = __fdiv_rn(sd, sn);
     const bool esc = a.has_thr && (double(rel) > a.thr);
-    if (lane == 0) {
-      a.rel[c] = rel;
-      if (esc && c < 32) atomicOr(&s_escmask, 1u << c);
-      if (!esc && m[2] >= 0) atomicAdd(&s_budget, m[2]);
-      if (esc) s_slow = 1;  // phase 1 counted this span's rows as eligible
+    if (rank == 0) a.rel[c] = rel;
+    if (esc) {
+      atomicOr(&t.esc[c >> 5], 1u << (c & 31));
+      if (c < 32) atomicOr(&t.escmask, 1u << c);
+      t.slow = 1;  // phase 1 counted the span's rows as eligible
+    } else if (m[2] >= 0) {
+      atomicAdd(&t.budget, m[2]);
     }
+  }
+
+  // 4. per-position state: keep = ~cached | sink (torch_engine.py:125), the score key
+  for (int g = tid; g < nq; g += kThreads) {
+    const uint32_t f4 = *reinterpret_cast<const uint32_t*>(fl + 4 * g);
+    const uint4 d4 = *reinterpret_cast<const uint4*>(keys + 4 * g);
+    const uint32_t d[4] = {d4.x, d4.y, d4.z, d4.w};
+    uint32_t w = 0;
+    uint4 k;
+    uint32_t* kk = reinterpret_cast<uint32_t*>(&k);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t f = byte_of(f4, i);
+      const bool in = 4 * g + i < nl;
+      uint32_t b = 0;
+      if (in) {
+        if (!(f & kInCached) || (f & kInSink)) b |= kKeep;
+        if (f & kInExact) b |= kExact;
+        if (f & kInCached) b |= kCached;
+      }
+      w |= b << (8 * i);
+      kk[i] = (in && !(f & kInExact)) ? score_key(__uint_as_float(d[i])) : 0u;
+    }
+    *reinterpret_cast<uint32_t*>(fl + 4 * g) = w;
+    *reinterpret_cast<uint4*>(keys + 4 * g) = k;
   }
   __syncthreads();
 
-  // 3. per-position state: keep = ~cached | sink (torch_engine.py:125); the score key
-  // of every position (never-computed positions score 0, torch_engine.py:121-122).
-  // Four positions per lane, in place over the staged copy or from global memory.
-  for (int g0 = tid; g0 < nq; g0 += 4 * kThreads) {
-    uint32_t f4[4];
-    uint4 d4[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int g = g0 + u * kThreads, p = 4 * g;
-      f4[u] = 0u;
-      d4[u] = make_uint4(0u, 0u, 0u, 0u);
-      if (g >= nq) continue;
-      if (staged) {
-        f4[u] = *reinterpret_cast<const uint32_t*>(fl + p);
-        d4[u] = *reinterpret_cast<const uint4*>(keys + p);
-      } else if (vec_in && p + 3 < n) {
-        f4[u] = __ldcg(reinterpret_cast<const unsigned*>(a.pos_flags + p));
-        d4[u] = __ldcg(reinterpret_cast<const uint4*>(a.diff + p));
-      } else {
-        uint32_t* dd = reinterpret_cast<uint32_t*>(&d4[u]);
-        for (int i = 0; i < 4 && p + i < n; ++i) {
-          f4[u] |= uint32_t(a.pos_flags[p + i]) << (8 * i);
-          dd[i] = __float_as_uint(__ldcg(a.diff + p + i));
-        }
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int g = g0 + u * kThreads, p = 4 * g;
-      if (g >= nq) continue;
-      const uint32_t d[4] = {d4[u].x, d4[u].y, d4[u].z, d4[u].w};
-      uint32_t w = 0;
-      uint4 k;
-      uint32_t* kk = reinterpret_cast<uint32_t*>(&k);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint32_t f = byte_of(f4[u], i);
-        uint32_t b = 0;
-        if (p + i < n) {
-          if (!(f & kInCached) || (f & kInSink)) b |= kKeep;
-          if (f & kInExact) b |= kExact;
-          if (f & kInCached) b |= kCached;
-        }
-        w |= b << (8 * i);
-        kk[i] = (p + i < n && !(f & kInExact)) ? score_key(__uint_as_float(d[i])) : 0u;
-      }
-      *reinterpret_cast<uint32_t*>(fl + p) = w;
-      *reinterpret_cast<uint4*>(keys + p) = k;
-    }
-  }
-  __syncthreads();
-
-  // 4. escalated spans are kept whole (torch_engine.py:133-135); overlapping escalated
-  // spans set the same bit of a byte that no other step changes now
-  if (a.has_thr)
-    for (int c = warp; c < a.n_chunks; c += kWarps) {
-      const int32_t* m = a.meta + c * CKV_SEL_META_STRIDE;
-      if (m[3] || !(double(a.rel[c]) > a.thr)) continue;
-      set_span_bit(fl, max(m[0], 0), min(m[0] + m[1], n), kKeep, 0);
-    }
-  __syncthreads();
-
-  // 5. pool = spans of pooled, non-escalated chunks (torch_engine.py:136-140)
+  // 5. escalated spans kept whole (torch_engine.py:133-135), then pool = spans of
+  // pooled, non-escalated chunks (136-140); an exact position in the pool was never
+  // computed, so phase 1 did not count it
   for (int c = warp; c < a.n_chunks; c += kWarps) {
     const int32_t* m = a.meta + c * CKV_SEL_META_STRIDE;
-    if (m[3] || m[2] < 0) continue;
-    if (a.has_thr && double(a.rel[c]) > a.thr) continue;  // escalated
-    const int s = max(m[0], 0), e = min(m[0] + m[1], n);
-    // an exact position in the pool was never computed, so phase 1 did not count it
-    if (set_span_bit(fl, s, e, kPool, kExact) && lane == 0) s_slow = 1;
+    if (!m[3] && (t.esc[c >> 5] >> (c & 31)) & 1u) set_span_bit(fl, lo, hi, m[0], m[0] + m[1], kKeep, 0);
   }
   __syncthreads();
+  for (int c = warp; c < a.n_chunks; c += kWarps) {
+    const int32_t* m = a.meta + c * CKV_SEL_META_STRIDE;
+    if (m[3] || m[2] < 0 || ((t.esc[c >> 5] >> (c & 31)) & 1u)) continue;
+    if (set_span_bit(fl, lo, hi, m[0], m[0] + m[1], kPool, kExact) && lane == 0) t.vals[0] = 1;
+  }
+  cluster.sync();  // every slice's flags are final; vals[0] of every CTA written
+  int slow = t.slow;
+  for (int r = 0; r < kCluster; ++r) slow |= cluster.map_shared_rank(&t.vals[0], r)[0];
 
   // 6. radix select of the budget-th largest eligible key (eligible = pool & ~keep,
-  // torch_engine.py:142-144): bits [30:20], [19:9], [8:0].  Passes walk this warp's
-  // block of quads (position order = block, quad, position in quad).
+  // torch_engine.py:142-144): bits [30:20], [19:9], [8:0].  Each CTA walks its slice in
+  // warp blocks of quads; the histograms are summed over the CTAs.
   const int per_warp = (nq + kThreads - 1) / kThreads * 32;  // quads, a multiple of 32
   const int g_lo = min(nq, warp * per_warp), g_hi = min(nq, g_lo + per_warp);
-  if (s_slow) {  // first level from the keys
+  int n_elig, bin1, k1;
+  if (slow) {  // first level from the keys
     for (int i = tid; i < kBins; i += kThreads) hist[i] = 0u;
     __syncthreads();
     for (int g0 = g_lo; g0 < g_hi; g0 += 32) {
@@ -383,19 +415,34 @@ __device__ void select_tail(const SelectArgs& a, uint32_t* keys, uint8_t* fl, bo
 #pragma unroll
       for (int i = 0; i < 4; ++i) hist_add(hist, kk[i] >> 20, eligible(byte_of(f, i)));
     }
+    cluster.sync();
+    const Rank rr = rank_bins_cluster(cluster, hist, kBins, t.budget, t.w, &t.rank);
+    n_elig = rr.total;
+    bin1 = rr.bin;
+    k1 = rr.k;
+  } else {  // phase 1's histogram, the same in every CTA
+    if (tid == 0) {
+      t.bin = 0;
+      t.k = 0;
+    }
+    n_elig = rank_bins_local(hist, kBins, t.budget, t.w, &t.bin, &t.k);
+    bin1 = t.bin;
+    k1 = t.k;
   }
-  __syncthreads();
-  const int n_elig = rank_bins(hist, kBins, s_budget, s_w, &s_bin, &s_k);
-  const int budget = min(s_budget, n_elig);
+  const int budget = min(t.budget, n_elig);
   uint32_t thr = 0x80000000u;  // above every key: nothing selected
   int take_eq = 0;
   if (budget > 0) {
-    uint32_t prefix = uint32_t(s_bin) << 20;
+    uint32_t prefix = uint32_t(bin1) << 20;
+    int k_level = k1;
     for (int level = 0; level < 2; ++level) {
       const int shift = level == 0 ? 20 : 9;  // bits already fixed: [31:shift]
       const int nbits = level == 0 ? 11 : 9;  // bits resolved now, below them
       const int nbins = 1 << nbits;
-      for (int i = tid; i < nbins; i += kThreads) hist[i] = 0u;
+      // levels alternate between two arrays: the one cleared here was last read before
+      // the previous level's cluster barriers, so no CTA can still be reading it
+      uint32_t* h = level == 0 ? hist2 : hist;
+      for (int i = tid; i < nbins; i += kThreads) h[i] = 0u;
       __syncthreads();
       for (int g0 = g_lo; g0 < g_hi; g0 += 32) {
         const int g = g0 + lane;
@@ -416,20 +463,21 @@ __device__ void select_tail(const SelectArgs& a, uint32_t* keys, uint8_t* fl, bo
         if (__any_sync(0xffffffffu, any)) {
 #pragma unroll
           for (int i = 0; i < 4; ++i)
-            hist_add(hist, (kk[i] >> (shift - nbits)) & uint32_t(nbins - 1), on[i]);
+            hist_add(h, (kk[i] >> (shift - nbits)) & uint32_t(nbins - 1), on[i]);
         }
       }
-      __syncthreads();
-      rank_bins(hist, nbins, s_k, s_w, &s_bin, &s_k);
-      prefix |= uint32_t(s_bin) << (shift - nbits);
+      cluster.sync();  // every CTA's histogram of this level is complete
+      const Rank rr = rank_bins_cluster(cluster, h, nbins, k_level, t.w, &t.rank);
+      prefix |= uint32_t(rr.bin) << (shift - nbits);
+      k_level = rr.k;
     }
     thr = prefix;
-    take_eq = s_k;
+    take_eq = k_level;
   }
 
   // 7. mark: keys above thr, then the first take_eq equal to it by position; compact
   // (torch_engine.py:144-150).  Ranks inside a warp come from lane scans, across warps
-  // from one scan per count.
+  // from one scan per count, across CTAs from the lower slices' counts.
   int tot = 0;
   int eq_run = 0;
   if (take_eq > 0) {
@@ -441,8 +489,12 @@ __device__ void select_tail(const SelectArgs& a, uint32_t* keys, uint8_t* fl, bo
 #pragma unroll
       for (int i = 0; i < 4; ++i) cnt += (kk[i] == thr && eligible(byte_of(f, i))) ? 1 : 0;
     }
-    eq_run = warp_bases(warp_sum_i(cnt), &tot, s_w);
+    eq_run = warp_bases(warp_sum_i(cnt), &tot, t.w);
+    if (tid == 0) t.vals[1] = tot;
   }
+  cluster.sync();  // equal-key counts of every slice
+  if (take_eq > 0)
+    for (int r = 0; r < rank; ++r) eq_run += cluster.map_shared_rank(&t.vals[1], r)[0];
   int c_keep = 0, c_ex = 0, c_cached = 0, c_bad = 0;  // per lane
   for (int g0 = g_lo; g0 < g_hi; g0 += 32) {
     const int g = g0 + lane;
@@ -482,11 +534,29 @@ __device__ void select_tail(const SelectArgs& a, uint32_t* keys, uint8_t* fl, bo
     }
     if (g < g_hi && out != f) *reinterpret_cast<uint32_t*>(fl + 4 * g) = out;
   }
-  int n_sel, n_exact, sel_cached, bad;
-  int out_run = warp_bases(warp_sum_i(c_keep), &n_sel, s_w);
-  int ex_run = warp_bases(warp_sum_i(c_ex), &n_exact, s_w);
-  warp_bases(warp_sum_i(c_cached), &sel_cached, s_w);
-  warp_bases(warp_sum_i(c_bad), &bad, s_w);
+  int k_tot, x_tot, ch_tot, bad_tot;
+  int out_run = warp_bases(warp_sum_i(c_keep), &k_tot, t.w);
+  int ex_run = warp_bases(warp_sum_i(c_ex), &x_tot, t.w);
+  warp_bases(warp_sum_i(c_cached), &ch_tot, t.w);
+  warp_bases(warp_sum_i(c_bad), &bad_tot, t.w);
+  if (tid == 0) {
+    t.vals[2] = k_tot;
+    t.vals[3] = x_tot;
+    t.vals[4] = ch_tot;
+    t.vals[5] = bad_tot;
+  }
+  cluster.sync();  // kept / exact counts of every slice
+  int n_sel = 0, sel_cached = 0, bad = 0;
+  for (int r = 0; r < kCluster; ++r) {
+    const int* v = cluster.map_shared_rank(t.vals, r);
+    if (r < rank) {
+      out_run += v[2];
+      ex_run += v[3];
+    }
+    n_sel += v[2];
+    sel_cached += v[4];
+    bad += v[5];
+  }
   for (int g0 = g_lo; g0 < g_hi; g0 += 32) {
     const int g = g0 + lane;
     const uint32_t f = g < g_hi ? *reinterpret_cast<const uint32_t*>(fl + 4 * g) : 0u;
@@ -505,7 +575,7 @@ __device__ void select_tail(const SelectArgs& a, uint32_t* keys, uint8_t* fl, bo
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const uint32_t b = byte_of(f, i);
-      const int p = 4 * g + i;
+      const int p = lo + 4 * g + i;
       if (b & kKept) {
         a.keep_abs[ik] = p;
         a.sel[ik] = p - ix;
@@ -514,17 +584,18 @@ __device__ void select_tail(const SelectArgs& a, uint32_t* keys, uint8_t* fl, bo
       if (b & kExact) ++ix;
     }
   }
-  if (tid == 0) {
+  if (rank == 0 && tid == 0) {
     a.counts[0] = n_sel;
     a.counts[1] = sel_cached;
     a.counts[2] = budget;
     a.counts[3] = n_elig;
-    a.counts[4] = int(s_escmask);
+    a.counts[4] = int(t.escmask);
     a.counts[5] = bad ? int(CKV_DEV_ERR_SELECT_UNCOMPUTED) : 0;
     a.counts[6] = n_sel - sel_cached;
     a.counts[7] = 0;
     if (bad) atomicOr(&g_err_word, CKV_DEV_ERR_SELECT_UNCOMPUTED);
   }
+  cluster.sync();  // no CTA leaves while another may still read its shared memory
 }
 
 // Phase 1 for one active row i (one warp): diff[p], norm[p] for p = active[i].
@@ -649,11 +720,35 @@ __global__ void __launch_bounds__(kThreads) deviation_scores_kernel(RowArgs r) {
   deviation_rows(r, nullptr, nullptr, 0);
 }
 
+// The tail's per-CTA arrays: keys and flags of this CTA's slice (shared memory, or the
+// caller's scratch when the slice is too long), then the chunk partials.
+struct TailArrays {
+  uint32_t* keys;
+  uint8_t* fl;
+  float2* part;
+};
+__device__ __forceinline__ TailArrays tail_arrays(const SelectArgs& sa, unsigned char* dyn, int rank) {
+  const int S = slice_len(sa.n_ctx);
+  TailArrays t;
+  if (slice_in_smem(sa.n_ctx)) {
+    t.keys = reinterpret_cast<uint32_t*>(dyn);
+    t.fl = dyn + 4 * size_t(S);
+    t.part = reinterpret_cast<float2*>(dyn + 5 * size_t(S));
+  } else {
+    t.keys = sa.keys_scratch + size_t(rank) * S;
+    t.fl = sa.flags_scratch + size_t(rank) * S;
+    t.part = reinterpret_cast<float2*>(dyn);
+  }
+  return t;
+}
+
+// Launched in clusters of kCluster CTAs (grid a multiple of kCluster).
 __global__ void __launch_bounds__(kThreads) deviation_select_kernel(RowArgs r, Control* ctl,
                                                                      SelectArgs sa) {
   extern __shared__ __align__(16) unsigned char dyn_smem[];
   __shared__ uint32_t hist[kBins];
   __shared__ int s_last;
+  cg::cluster_group cluster = cg::this_cluster();
   // phase 1: rows, with the first radix level's histogram when the chunk table fits
   const bool with_hist = sa.n_chunks <= kPhase1Chunks;
   int4* tab = reinterpret_cast<int4*>(dyn_smem);
@@ -669,28 +764,28 @@ __global__ void __launch_bounds__(kThreads) deviation_select_kernel(RowArgs r, C
     for (int i = threadIdx.x; i < kBins; i += kThreads)
       if (hist[i]) atomicAdd(&ctl->hist[i], hist[i]);
   __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
+  cluster.sync();  // the cluster's rows and histogram shares are all written
+  const int rank = int(cluster.block_rank());
+  if (rank == 0 && threadIdx.x == 0) {
     const unsigned prev = atomicAdd(&ctl->ticket, 1u);
-    s_last = (prev == gridDim.x - 1) ? 1 : 0;
+    const int last = (prev == gridDim.x / kCluster - 1) ? 1 : 0;
+    for (int q = 0; q < kCluster; ++q) *cluster.map_shared_rank(&s_last, q) = last;
   }
-  __syncthreads();
-  if (!s_last) return;
+  cluster.sync();
+  if (!s_last) return;  // every CTA of the cluster leaves together
   __threadfence();
-  const bool in_smem = sa.n_ctx <= kSmemPositions;
-  uint32_t* keys = in_smem ? reinterpret_cast<uint32_t*>(dyn_smem) : sa.keys_scratch;
-  uint8_t* fl = in_smem ? dyn_smem + 4 * size_t(round16(sa.n_ctx)) : sa.flags_scratch;
-  select_tail(sa, keys, fl, in_smem, hist, with_hist ? ctl->hist : nullptr);
-  if (threadIdx.x == 0) ctl->ticket = 0u;  // ready for the next launch
+  const TailArrays ta = tail_arrays(sa, dyn_smem, rank);
+  select_tail(cluster, sa, ta.keys, ta.fl, ta.part, hist, with_hist ? ctl->hist : nullptr);
+  if (rank == 0 && threadIdx.x == 0) ctl->ticket = 0u;  // ready for the next launch
 }
 
+// One cluster of kCluster CTAs.
 __global__ void __launch_bounds__(kThreads) select_only_kernel(SelectArgs sa) {
   extern __shared__ __align__(16) unsigned char dyn_smem[];
   __shared__ uint32_t hist[kBins];
-  const bool in_smem = sa.n_ctx <= kSmemPositions;
-  uint32_t* keys = in_smem ? reinterpret_cast<uint32_t*>(dyn_smem) : sa.keys_scratch;
-  uint8_t* fl = in_smem ? dyn_smem + 4 * size_t(round16(sa.n_ctx)) : sa.flags_scratch;
-  select_tail(sa, keys, fl, in_smem, hist, nullptr);
+  cg::cluster_group cluster = cg::this_cluster();
+  const TailArrays ta = tail_arrays(sa, dyn_smem, int(cluster.block_rank()));
+  select_tail(cluster, sa, ta.keys, ta.fl, ta.part, hist, nullptr);
 }
 
 int check_select(const uint8_t* pos_flags, int n_ctx, const int32_t* meta, int n_chunks,
@@ -699,6 +794,7 @@ int check_select(const uint8_t* pos_flags, int n_ctx, const int32_t* meta, int n
               "selection: null pointer");
   CKV_REQUIRE(n_chunks == 0 || meta, "selection: null chunk table");
   CKV_REQUIRE(n_ctx > 0 && n_chunks >= 0, "selection: bad sizes");
+  CKV_REQUIRE(n_chunks <= kMaxChunks, "selection: %d chunks (at most %d)", n_chunks, kMaxChunks);
   CKV_REQUIRE((reinterpret_cast<uintptr_t>(scratch) & 15u) == 0,
               "selection: scratch must be 16-byte aligned");
   return CKV_OK;
@@ -713,22 +809,76 @@ SelectArgs make_select_args(const float* diff, const float* norm, const uint8_t*
                     scratch + 4 * size_t(round16(n_ctx))};
 }
 
-// Phase-1 grid: as many 1024-thread CTAs per SM as fit at once (two, or one when the
-// selection's shared memory is large), so every SM gets the same number of rows; at
-// most one CTA per row.
-int rows_grid(int n_act, int dyn_smem) {
-  const int per_sm = 2 * (dyn_smem + kStaticSmem + 1024) <= 228 * 1024 ? 2 : 1;
-  return std::max(1, std::min(n_act, per_sm * num_sms()));
+cudaLaunchConfig_t cluster_config(int grid, int dyn, cudaStream_t st, cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = dyn;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+// Clusters of the fused kernel that are resident at once for a dynamic shared memory
+// size (queried once per device and size); 0 if the query fails.
+int resident_clusters(int dyn) {
+  struct Entry {
+    int dev, dyn, clusters;
+  };
+  static std::mutex mu;
+  static Entry cache[64];
+  static int n_cache = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < n_cache; ++i)
+      if (cache[i].dev == dev && cache[i].dyn == dyn) return cache[i].clusters;
+  }
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = cluster_config(kCluster * num_sms(), dyn, nullptr, attr);
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, deviation_select_kernel, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    clusters = 0;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (n_cache < 64) cache[n_cache++] = {dev, dyn, clusters};
+  return clusters;
+}
+
+// Phase-1 grid without clusters (scores only): two 1024-thread CTAs per SM, every SM
+// the same number of rows; at most one CTA per row.
+int rows_grid(int n_act) { return std::max(1, std::min(n_act, 2 * num_sms())); }
+
+// Fused grid: as many whole clusters as are resident at once (so every CTA starts at
+// once and every SM gets the same number of rows), at most one CTA per row, at least
+// one cluster.
+int fused_grid(int n_act, int dyn) {
+  int clusters = resident_clusters(dyn);
+  if (clusters <= 0) clusters = num_sms() / kCluster;
+  clusters = std::min(clusters, std::max(1, n_act / kCluster));
+  return kCluster * std::max(1, clusters);
 }
 
 int launch_fused(const RowArgs& r, void* control, const SelectArgs& sa, cudaStream_t st,
                  const char* name) {
   const int dyn = dyn_smem_bytes(sa.n_ctx, sa.n_chunks);
   if (int rc = set_smem_limit(reinterpret_cast<const void*>(deviation_select_kernel),
-                              dyn_smem_bytes(kSmemPositions, 0)))
+                              dyn_smem_bytes(kCluster * kSmemSlice, kMaxChunks)))
     return rc;
-  deviation_select_kernel<<<rows_grid(r.n_act, dyn), kThreads, dyn, st>>>(
-      r, static_cast<Control*>(control), sa);
+  cudaLaunchAttribute attr[1];
+  const cudaLaunchConfig_t cfg = cluster_config(fused_grid(r.n_act, dyn), dyn, st, attr);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, deviation_select_kernel, r, static_cast<Control*>(control), sa);
+  if (e != cudaSuccess) {
+    set_error("%s: launch failed: %s", name, cudaGetErrorString(e));
+    return CKV_ERR_CUDA;
+  }
   CKV_LAUNCH_CHECK(name);
   return CKV_OK;
 }
@@ -783,7 +933,7 @@ int ckv_deviation_scores(const uint16_t* k_fresh, const uint16_t* v_fresh,
   if (n_act == 0) return CKV_OK;
   const RowArgs r{k_fresh, v_fresh, fresh_row_stride, k_base, v_base, active, n_act,
                   n_kv_heads, head_dim, pos_flags, n_ctx, diff, norm};
-  deviation_scores_kernel<<<rows_grid(n_act, 0), kThreads, 0, as_stream(stream)>>>(r);
+  deviation_scores_kernel<<<rows_grid(n_act), kThreads, 0, as_stream(stream)>>>(r);
   CKV_LAUNCH_CHECK("ckv_deviation_scores");
   return CKV_OK;
 }
@@ -800,10 +950,15 @@ int ckv_select_from_scores(const float* diff, const float* norm, const uint8_t* 
                                          has_threshold, escalate_threshold, rel, keep_abs, sel,
                                          counts, scratch);
   if (int rc = set_smem_limit(reinterpret_cast<const void*>(select_only_kernel),
-                              dyn_smem_bytes(kSmemPositions, 0)))
+                              dyn_smem_bytes(kCluster * kSmemSlice, kMaxChunks)))
     return rc;
-  const int dyn = n_ctx <= kSmemPositions ? 5 * round16(n_ctx) : 0;
-  select_only_kernel<<<1, kThreads, dyn, as_stream(stream)>>>(sa);
+  cudaLaunchAttribute attr[1];
+  const cudaLaunchConfig_t cfg = cluster_config(kCluster, dyn_smem_bytes(n_ctx, n_chunks), as_stream(stream), attr);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, select_only_kernel, sa);
+  if (e != cudaSuccess) {
+    set_error("ckv_select_from_scores: launch failed: %s", cudaGetErrorString(e));
+    return CKV_ERR_CUDA;
+  }
   CKV_LAUNCH_CHECK("ckv_select_from_scores");
   return CKV_OK;
 }

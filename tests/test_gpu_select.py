@@ -10,8 +10,9 @@ positions, budget, eligible count and recomputed-cached count:
   ckv_select_from_scores  - the selection alone, from given fp32 scores
   ckv_deviation_select    - phase 1 scores from K/V, then the same selection
 
-n_ctx covers both homes of the per-position keys: shared memory (n_ctx <= 43008)
-and the caller's scratch (above it).
+n_ctx covers both homes of the per-position keys: the shared memory of the eight
+CTAs of the selecting cluster (slices of up to 35328 positions, n_ctx <= 282624) and
+the caller's scratch (above it).
 """
 
 from __future__ import annotations
@@ -128,13 +129,15 @@ CASES = [
     (1, 300, 3, False, 0.5),
     (2, 5248, 10, False, 0.8),
     (3, 5248, 10, True, 0.3),
-    (4, 43008, 40, False, 0.8),   # the largest n_ctx held in shared memory
-    (5, 43009, 40, True, 0.5),    # the smallest in the caller's scratch
-    (6, 32896, 64, False, 0.0),   # config 5's request length
+    (4, 282624, 300, False, 0.8),  # the largest n_ctx held in shared memory
+    (5, 282625, 300, True, 0.5),   # the smallest in the caller's scratch
+    (6, 32896, 64, False, 0.0),    # config 5's request length
     (7, 32896, 64, True, 0.9),
-    (10, 20480, 40, False, 0.8),  # two CTAs per SM still fit up to here
+    (10, 20480, 40, False, 0.8),
     (8, 65536, 128, False, 0.6),
-    (9, 1000, 200, True, 0.2),    # more chunks than warps in the CTA
+    (9, 1000, 200, True, 0.2),     # more chunks than warps in the CTA
+    (11, 65536, 4096, False, 0.4),  # the largest chunk table
+    (12, 37, 3, False, 0.5),       # fewer positions than CTAs x 16: empty slices
 ]
 
 
