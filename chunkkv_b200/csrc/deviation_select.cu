@@ -36,8 +36,11 @@ namespace cg = cooperative_groups;
 namespace ckv {
 namespace {
 
-constexpr int kThreads = 1024;
+// 512 threads: two CTAs fit on an SM (64 registers each), so an 8-CTA cluster packs
+// into four SMs and the resident clusters cover every SM
+constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
+static_assert(kWarps <= 32, "one warp scans the warp totals");
 constexpr int kCluster = 8;  // CTAs of one cluster; the last cluster runs the selection
 // positions of one CTA's slice held in shared memory (5 bytes each), beside the
 // chunk partials (8 bytes per chunk) and about 17 KiB of static shared memory
@@ -120,10 +123,10 @@ __device__ int warp_bases(int v, int* total, int* s_w) {
   if (lane == 0) s_w[warp] = v;
   __syncthreads();
   if (warp == 0) {
-    const int x = s_w[lane];  // kWarps == 32
+    const int x = lane < kWarps ? s_w[lane] : 0;
     const int inc = warp_incl(x);
-    s_w[lane] = inc - x;
-    if (lane == 31) s_w[kWarps] = inc;
+    if (lane < kWarps) s_w[lane] = inc - x;
+    if (lane == kWarps - 1) s_w[kWarps] = inc;
   }
   __syncthreads();
   const int base = s_w[warp];
@@ -156,24 +159,30 @@ __device__ __forceinline__ void hist_add(uint32_t* hist, uint32_t bin, bool on) 
   }
 }
 
-// Bins ranked from the top of this CTA's `hist` (nbins = 2048 or 512).  Returns the
-// number of keys counted; for k' = min(k, that number) > 0, *s_bin and *s_k receive the
-// bin that holds the k'-th largest key and the key's rank inside that bin.
+// Bins ranked from the top of this CTA's `hist` (nbins = 2048 or 512, a multiple of
+// kThreads): thread t takes the nbins / kThreads bins that follow, from the top, the
+// t * nbins / kThreads highest.  Returns the number of keys counted; for
+// k' = min(k, that number) > 0, *s_bin and *s_k receive the bin that holds the k'-th
+// largest key and the key's rank inside that bin.
 __device__ int rank_bins_local(const uint32_t* hist, int nbins, int k, int* s_w, int* s_bin, int* s_k) {
-  const int b0 = nbins - 1 - 2 * int(threadIdx.x), b1 = b0 - 1;
-  const int c0 = b0 >= 0 ? int(hist[b0]) : 0, c1 = b1 >= 0 ? int(hist[b1]) : 0;
-  const int inc = warp_incl(c0 + c1);
+  const int per = nbins / kThreads;  // 4 or 1
+  const int top = nbins - 1 - per * int(threadIdx.x);
+  int mine = 0;
+  for (int i = 0; i < per; ++i) mine += int(hist[top - i]);
+  const int inc = warp_incl(mine);
   int tot;
   const int wb = warp_bases(__shfl_sync(0xffffffffu, inc, 31), &tot, s_w);
-  const int excl = wb + inc - (c0 + c1);
+  int excl = wb + inc - mine;
   const int kk = min(k, tot);
-  if (kk > 0 && excl < kk && kk <= excl + c0 + c1) {
-    if (kk - excl <= c0) {
-      *s_bin = b0;
-      *s_k = kk - excl;
-    } else {
-      *s_bin = b1;
-      *s_k = kk - excl - c0;
+  if (kk > 0 && excl < kk && kk <= excl + mine) {
+    for (int i = 0; i < per; ++i) {
+      const int c = int(hist[top - i]);
+      if (kk - excl <= c) {
+        *s_bin = top - i;
+        *s_k = kk - excl;
+        break;
+      }
+      excl += c;
     }
   }
   __syncthreads();
@@ -852,9 +861,30 @@ int resident_clusters(int dyn) {
   return clusters;
 }
 
-// Phase-1 grid without clusters (scores only): two 1024-thread CTAs per SM, every SM
-// the same number of rows; at most one CTA per row.
-int rows_grid(int n_act) { return std::max(1, std::min(n_act, 2 * num_sms())); }
+// Phase-1 grid without clusters (scores only): every resident CTA of the device (queried
+// once per device), so every SM gets the same number of rows; at most one CTA per row.
+int rows_grid(int n_act) {
+  static std::mutex mu;
+  static int per_sm[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int blocks = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64) blocks = per_sm[dev];
+  }
+  if (blocks <= 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, deviation_scores_kernel, kThreads, 0) !=
+            cudaSuccess ||
+        blocks <= 0) {
+      cudaGetLastError();
+      blocks = 2;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64) per_sm[dev] = blocks;
+  }
+  return std::max(1, std::min(n_act, blocks * num_sms()));
+}
 
 // Fused grid: as many whole clusters as are resident at once (so every CTA starts at
 // once and every SM gets the same number of rows), at most one CTA per row, at least
