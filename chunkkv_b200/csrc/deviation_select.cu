@@ -193,18 +193,38 @@ struct Rank {
   int bin, k, total;
 };
 
+// 16 bytes of CTA `rank`'s shared memory at the address that `p` has in this CTA.
+__device__ __forceinline__ uint4 ld_cluster_v4(const void* p, unsigned rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+  uint4 v;
+  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(a));
+  return v;
+}
+
 // The same over the sum of the cluster's CTAs' histograms: rank 0 adds the CTAs'
-// counts into its own `hist` (remote reads of the other CTAs' shared memory) and ranks
-// them; after a cluster barrier every CTA reads rank 0's answer.  Called by every CTA,
-// after a cluster barrier that follows the last update of any `hist`.
+// counts into its own `hist` (one 16-byte remote read per CTA and four bins, all in
+// flight at once) and ranks them; after a cluster barrier every CTA reads rank 0's
+// answer.  Called by every CTA, after a cluster barrier that follows the last update
+// of any `hist`.
 __device__ Rank rank_bins_cluster(cg::cluster_group& cluster, uint32_t* hist, int nbins, int k, int* s_w,
                                   Rank* s_rank) {
   if (cluster.block_rank() == 0) {
-    for (int b = threadIdx.x; b < nbins; b += kThreads) {
-      uint32_t c = hist[b];
+    for (int q = threadIdx.x; q < nbins / 4; q += kThreads) {
+      uint4 v[kCluster];
 #pragma unroll
-      for (int r = 1; r < kCluster; ++r) c += cluster.map_shared_rank(hist, r)[b];
-      hist[b] = c;
+      for (int r = 0; r < kCluster; ++r) v[r] = ld_cluster_v4(hist + 4 * q, unsigned(r));
+      uint4 c = v[0];
+#pragma unroll
+      for (int r = 1; r < kCluster; ++r) {
+        c.x += v[r].x;
+        c.y += v[r].y;
+        c.z += v[r].z;
+        c.w += v[r].w;
+      }
+      *reinterpret_cast<uint4*>(hist + 4 * q) = c;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -262,7 +282,7 @@ struct TailShared {
 __device__ void select_tail(cg::cluster_group& cluster, const SelectArgs& a, uint32_t* keys, uint8_t* fl,
                             float2* part, uint32_t* hist, unsigned* phase1_hist) {
   __shared__ TailShared t;
-  __shared__ uint32_t hist2[kBins];  // the second level's counters
+  __shared__ __align__(16) uint32_t hist2[kBins];  // the second level's counters
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int rank = int(cluster.block_rank());
   const int n = a.n_ctx;
@@ -755,7 +775,7 @@ __device__ __forceinline__ TailArrays tail_arrays(const SelectArgs& sa, unsigned
 __global__ void __launch_bounds__(kThreads) deviation_select_kernel(RowArgs r, Control* ctl,
                                                                      SelectArgs sa) {
   extern __shared__ __align__(16) unsigned char dyn_smem[];
-  __shared__ uint32_t hist[kBins];
+  __shared__ __align__(16) uint32_t hist[kBins];
   __shared__ int s_last;
   cg::cluster_group cluster = cg::this_cluster();
   // phase 1: rows, with the first radix level's histogram when the chunk table fits
@@ -791,7 +811,7 @@ __global__ void __launch_bounds__(kThreads) deviation_select_kernel(RowArgs r, C
 // One cluster of kCluster CTAs.
 __global__ void __launch_bounds__(kThreads) select_only_kernel(SelectArgs sa) {
   extern __shared__ __align__(16) unsigned char dyn_smem[];
-  __shared__ uint32_t hist[kBins];
+  __shared__ __align__(16) uint32_t hist[kBins];
   cg::cluster_group cluster = cg::this_cluster();
   const TailArrays ta = tail_arrays(sa, dyn_smem, int(cluster.block_rank()));
   select_tail(cluster, sa, ta.keys, ta.fl, ta.part, hist, nullptr);
