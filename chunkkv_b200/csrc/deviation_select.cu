@@ -42,19 +42,19 @@ constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 static_assert(kWarps <= 32, "one warp scans the warp totals");
 constexpr int kCluster = 8;  // CTAs of one cluster; the last cluster runs the selection
-// positions of one CTA's slice held in shared memory (5 bytes each), beside the
-// chunk partials (8 bytes per chunk) and about 17 KiB of static shared memory
-constexpr int kSmemSlice = 35328;
+// positions of one CTA's slice held in shared memory (9 bytes each: key, flags and
+// norm), beside the chunk partials (8 bytes per chunk) and about 17 KiB of static
+// shared memory
+constexpr int kSmemSlice = 20128;
 constexpr int kMaxChunks = 4096;        // chunk table the selection takes
 // chunk tables up to this size are copied to shared memory for phase 1's histogram
 constexpr int kPhase1Chunks = 1024;
 constexpr int kBins = 2048;  // first radix level: score bits [30:20]
-constexpr int kVals = 8;     // per-CTA scalars exchanged between the cluster's CTAs
 
 // pos_flags input bits
 constexpr uint8_t kInCached = 1, kInSink = 2, kInExact = 4;
 // working flag bits
-constexpr uint8_t kKeep = 1, kExact = 2, kCached = 4, kPool = 8, kKept = 0x80;
+constexpr uint8_t kKeep = 1, kExact = 2, kCached = 4, kPool = 8;
 
 // Control block (global, CKV_SELECT_CONTROL_BYTES): ticket counter, then the phase-1
 // histogram.  Zero before the first launch; every launch leaves it zero.
@@ -86,12 +86,12 @@ __host__ __device__ constexpr int round16(int n) { return (n + 15) / 16 * 16; }
 // positions per CTA slice (a multiple of 16, so every slice starts 64-byte aligned)
 __host__ __device__ constexpr int slice_len(int n_ctx) { return round16((n_ctx + kCluster - 1) / kCluster); }
 __host__ __device__ constexpr bool slice_in_smem(int n_ctx) { return slice_len(n_ctx) <= kSmemSlice; }
-// dynamic shared memory: the slice's keys and flags (when they fit), then the chunk
-// partials; phase 1's copy of the chunk table shares the same bytes
+// dynamic shared memory: the slice's keys, flags and norms (when they fit), then the
+// chunk partials; phase 1's copy of the chunk table shares the same bytes
 __host__ __device__ constexpr int dyn_smem_bytes(int n_ctx, int n_chunks) {
-  return (slice_in_smem(n_ctx) ? 5 * slice_len(n_ctx) : 0) + 16 * ((n_chunks + 1) / 2) >
+  return (slice_in_smem(n_ctx) ? 9 * slice_len(n_ctx) : 0) + 16 * ((n_chunks + 1) / 2) >
                  16 * (n_chunks < kPhase1Chunks ? n_chunks : kPhase1Chunks)
-             ? (slice_in_smem(n_ctx) ? 5 * slice_len(n_ctx) : 0) + 16 * ((n_chunks + 1) / 2)
+             ? (slice_in_smem(n_ctx) ? 9 * slice_len(n_ctx) : 0) + 16 * ((n_chunks + 1) / 2)
              : 16 * (n_chunks < kPhase1Chunks ? n_chunks : kPhase1Chunks);
 }
 
@@ -193,49 +193,74 @@ struct Rank {
   int bin, k, total;
 };
 
-// 16 bytes of CTA `rank`'s shared memory at the address that `p` has in this CTA.
-__device__ __forceinline__ uint4 ld_cluster_v4(const void* p, unsigned rank) {
+// Distributed shared memory: CTA `rank`'s copy of the shared variable at `p`.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, unsigned rank) {
   uint32_t a;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+  return a;
+}
+__device__ __forceinline__ uint4 ld_cluster_v4(const void* p, unsigned rank) {
   uint4 v;
   asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(a));
+               : "r"(cluster_addr(p, rank)));
   return v;
 }
+__device__ __forceinline__ float2 ld_cluster_f2(const void* p, unsigned rank) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(cluster_addr(p, rank)));
+  return v;
+}
+__device__ __forceinline__ int ld_cluster_i32(const void* p, unsigned rank) {
+  int v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(cluster_addr(p, rank)));
+  return v;
+}
+// A cluster barrier in two halves: arrive (release) once this CTA's shared values that
+// the others read are written, or once its reads of theirs are done; wait (acquire)
+// before relying on the others.  Local work between the two hides the barrier.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 
-// The same over the sum of the cluster's CTAs' histograms: rank 0 adds the CTAs'
-// counts into its own `hist` (one 16-byte remote read per CTA and four bins, all in
-// flight at once) and ranks them; after a cluster barrier every CTA reads rank 0's
-// answer.  Called by every CTA, after a cluster barrier that follows the last update
-// of any `hist`.
-__device__ Rank rank_bins_cluster(cg::cluster_group& cluster, uint32_t* hist, int nbins, int k, int* s_w,
-                                  Rank* s_rank) {
-  if (cluster.block_rank() == 0) {
-    for (int q = threadIdx.x; q < nbins / 4; q += kThreads) {
-      uint4 v[kCluster];
+// The cluster-wide ranking of a level: every CTA sums the kCluster CTAs' copies of `h`
+// itself (thread t: bins [nbins - 4t - 4, nbins - 4t), one 16-byte remote read per CTA,
+// all in flight at once) and ranks the sums from the top, so no CTA waits for another
+// one's answer.  Called by every thread after a cluster barrier that follows the last
+// update of any copy; *s_bin and *s_k as in rank_bins_local.
+__device__ int rank_bins_merged(const uint32_t* h, int nbins, int k, int* s_w, int* s_bin, int* s_k) {
+  const int t = threadIdx.x;
+  uint32_t c[4] = {0u, 0u, 0u, 0u};  // highest bin first
+  if (4 * t < nbins) {
+    const uint32_t* q = h + nbins - 4 * (t + 1);
+    uint4 v[kCluster];
 #pragma unroll
-      for (int r = 0; r < kCluster; ++r) v[r] = ld_cluster_v4(hist + 4 * q, unsigned(r));
-      uint4 c = v[0];
+    for (int r = 0; r < kCluster; ++r) v[r] = ld_cluster_v4(q, unsigned(r));
 #pragma unroll
-      for (int r = 1; r < kCluster; ++r) {
-        c.x += v[r].x;
-        c.y += v[r].y;
-        c.z += v[r].z;
-        c.w += v[r].w;
-      }
-      *reinterpret_cast<uint4*>(hist + 4 * q) = c;
+    for (int r = 0; r < kCluster; ++r) {
+      c[0] += v[r].w;
+      c[1] += v[r].z;
+      c[2] += v[r].y;
+      c[3] += v[r].x;
     }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      s_rank->bin = 0;
-      s_rank->k = 0;
-    }
-    const int tot = rank_bins_local(hist, nbins, k, s_w, &s_rank->bin, &s_rank->k);
-    if (threadIdx.x == 0) s_rank->total = tot;
   }
-  cluster.sync();
-  return *cluster.map_shared_rank(s_rank, 0);
+  const int mine = int(c[0] + c[1] + c[2] + c[3]);
+  const int inc = warp_incl(mine);
+  int tot;
+  const int wb = warp_bases(__shfl_sync(0xffffffffu, inc, 31), &tot, s_w);
+  int excl = wb + inc - mine;
+  const int kk = min(k, tot);
+  if (kk > 0 && excl < kk && kk <= excl + mine) {
+    for (int i = 0; i < 4; ++i) {
+      if (kk - excl <= int(c[i])) {
+        *s_bin = nbins - 1 - 4 * t - i;
+        *s_k = kk - excl;
+        break;
+      }
+      excl += int(c[i]);
+    }
+  }
+  __syncthreads();
+  return tot;
 }
 
 __device__ __forceinline__ bool eligible(uint32_t f) { return (f & kPool) && !(f & kKeep); }
@@ -264,23 +289,65 @@ __device__ __forceinline__ bool set_span_bit(uint8_t* fl, int lo, int hi, int s,
   return __any_sync(0xffffffffu, seen);
 }
 
+// Row c of the chunk table: start, length, budget, exact.
+__device__ __forceinline__ int4 chunk_row(const int32_t* meta, int c) {
+  const int32_t* m = meta + c * CKV_SEL_META_STRIDE;
+  return make_int4(m[0], m[1], m[2], m[3]);
+}
+
 struct TailShared {
   int w[kWarps + 1];
-  int vals[kVals];  // exchanged: [0] exact position in the pool, [1] equal keys,
-                    // [2] kept, [3] exact, [4] kept & cached, [5] kept & exact
+  int wc[4][kWarps];  // per warp of the final pass: eligible keys above thr, equal to it,
+                      // other kept positions, exact positions
+  int wp[2][kWarps];  // exclusive prefixes over the warps of wc[1] and wc[3]
+  __align__(16) int tot[4];  // this CTA's sums of wc, read by the others
+  int base[3];               // eq keys, kept and exact positions of the lower slices
+  int n_sel;
+  int x5;  // an exact position of this slice lies in the pool
   int budget, bin, k, slow;
-  Rank rank;  // rank 0's answer of a cluster-wide ranking
   unsigned escmask;
   unsigned esc[kMaxChunks / 32];
 };
 
+// One radix level's counts of this CTA's slice into its own `h` (cleared here): eligible
+// keys whose bits [31:shift] equal prefix's, binned by the nbits below them.
+__device__ __forceinline__ void count_level(uint32_t* h, const uint32_t* keys, const uint8_t* fl, int g_lo,
+                                            int g_hi, uint32_t prefix, int shift, int nbits) {
+  const int lane = threadIdx.x & 31;
+  const int nbins = 1 << nbits;
+  for (int i = threadIdx.x; i < nbins; i += kThreads) h[i] = 0u;
+  __syncthreads();
+  for (int g0 = g_lo; g0 < g_hi; g0 += 32) {
+    const int g = g0 + lane;
+    uint4 k = make_uint4(0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu);
+    uint32_t f = 0u;
+    if (g < g_hi) {
+      k = *reinterpret_cast<const uint4*>(keys + 4 * g);
+      f = *reinterpret_cast<const uint32_t*>(fl + 4 * g);
+    }
+    const uint32_t kk[4] = {k.x, k.y, k.z, k.w};
+    bool any = false;
+    bool on[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      on[i] = (kk[i] >> shift) == (prefix >> shift) && eligible(byte_of(f, i));
+      any |= on[i];
+    }
+    if (__any_sync(0xffffffffu, any)) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) hist_add(h, (kk[i] >> (shift - nbits)) & uint32_t(nbins - 1), on[i]);
+    }
+  }
+}
+
 // Phase 2: the selection, by the kCluster CTAs of one cluster (kThreads threads each).
 // keys/fl: this CTA's slice [rank * S, rank * S + S) of the positions, in shared or
-// global memory (16-byte aligned); part: n_chunks float2 in shared memory; hist: kBins
+// global memory (16-byte aligned); nrm: the slice's norms staged in shared memory, or
+// nullptr (read from global memory); part: n_chunks float2 in shared memory; hist: kBins
 // shared counters; phase1_hist: the control block's histogram (nullptr: none usable),
 // read by every CTA and cleared by rank 0.
 __device__ void select_tail(cg::cluster_group& cluster, const SelectArgs& a, uint32_t* keys, uint8_t* fl,
-                            float2* part, uint32_t* hist, unsigned* phase1_hist) {
+                            float* nrm, float2* part, uint32_t* hist, unsigned* phase1_hist) {
   __shared__ TailShared t;
   __shared__ __align__(16) uint32_t hist2[kBins];  // the second level's counters
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -297,90 +364,102 @@ __device__ void select_tail(cg::cluster_group& cluster, const SelectArgs& a, uin
     t.budget = 0;
     t.escmask = 0u;
     t.slow = phase1_hist ? 0 : 1;
+    t.x5 = 0;
+    if (rank == 0) {  // the counts every CTA adds to (step 8)
+      a.counts[1] = 0;
+      a.counts[5] = 0;
+      a.counts[6] = 0;
+    }
   }
   for (int i = tid; i < kMaxChunks / 32; i += kThreads) t.esc[i] = 0u;
-  for (int i = tid; i < kVals; i += kThreads) t.vals[i] = 0;
 
-  // 1. this slice's raw flags and scores (torch_engine.py:121-122: positions never
-  // computed score 0), four positions per lane, vector loads where the inputs allow
+  // 1. this slice's raw flags, scores and norms (torch_engine.py:121-122: positions
+  // never computed score 0), four positions per lane and four quads per thread in
+  // flight, vector loads where the inputs allow
   const bool vec_in = ((reinterpret_cast<uintptr_t>(a.pos_flags + lo) & 3u) == 0) &&
-                      ((reinterpret_cast<uintptr_t>(a.diff + lo) & 15u) == 0);
-  for (int g = tid; g < nq; g += kThreads) {
-    const int p = lo + 4 * g;
-    uint32_t f4 = 0u;
-    uint4 d4 = make_uint4(0u, 0u, 0u, 0u);
-    if (vec_in && p + 3 < hi) {
-      f4 = __ldcg(reinterpret_cast<const unsigned*>(a.pos_flags + p));
-      d4 = __ldcg(reinterpret_cast<const uint4*>(a.diff + p));
-    } else {
-      uint32_t* dd = reinterpret_cast<uint32_t*>(&d4);
-      for (int i = 0; i < 4 && p + i < hi; ++i) {
-        f4 |= uint32_t(a.pos_flags[p + i]) << (8 * i);
-        dd[i] = __float_as_uint(__ldcg(a.diff + p + i));
+                      ((reinterpret_cast<uintptr_t>(a.diff + lo) & 15u) == 0) &&
+                      ((reinterpret_cast<uintptr_t>(a.norm + lo) & 15u) == 0);
+  for (int g0 = tid; g0 < nq; g0 += 4 * kThreads) {
+    uint32_t f4[4];
+    uint4 d4[4];
+    float4 n4[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int g = g0 + u * kThreads;
+      const int p = lo + 4 * g;
+      f4[u] = 0u;
+      d4[u] = make_uint4(0u, 0u, 0u, 0u);
+      n4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (g < nq) {
+        if (vec_in && p + 3 < hi) {
+          f4[u] = __ldcg(reinterpret_cast<const unsigned*>(a.pos_flags + p));
+          d4[u] = __ldcg(reinterpret_cast<const uint4*>(a.diff + p));
+          if (nrm) n4[u] = __ldcg(reinterpret_cast<const float4*>(a.norm + p));
+        } else {
+          uint32_t* dd = reinterpret_cast<uint32_t*>(&d4[u]);
+          float* nn = reinterpret_cast<float*>(&n4[u]);
+          for (int i = 0; i < 4 && p + i < hi; ++i) {
+            f4[u] |= uint32_t(a.pos_flags[p + i]) << (8 * i);
+            dd[i] = __float_as_uint(__ldcg(a.diff + p + i));
+            if (nrm) nn[i] = __ldcg(a.norm + p + i);
+          }
+        }
       }
     }
-    *reinterpret_cast<uint32_t*>(fl + 4 * g) = f4;  // raw pos_flags for now
-    *reinterpret_cast<uint4*>(keys + 4 * g) = d4;   // raw diff bits for now
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int g = g0 + u * kThreads;
+      if (g < nq) {
+        *reinterpret_cast<uint32_t*>(fl + 4 * g) = f4[u];  // raw pos_flags for now
+        *reinterpret_cast<uint4*>(keys + 4 * g) = d4[u];   // raw diff bits for now
+        if (nrm) *reinterpret_cast<float4*>(nrm + 4 * g) = n4[u];
+      }
+    }
   }
   __syncthreads();
 
   // 2. per chunk, this slice's share of its span: (sum diff, sum norm) over the
-  // positions that were computed (torch_engine.py:128-132)
-  for (int c = warp; c < a.n_chunks; c += kWarps) {
-    const int32_t* m = a.meta + c * CKV_SEL_META_STRIDE;
-    const int s = max(m[0], lo), e = min(m[0] + m[1], hi);
-    float sd = 0.f, sn = 0.f;
-    if (!m[3]) {
+  // positions that were computed (torch_engine.py:128-132).  Warp w takes chunks w,
+  // w + kWarps, ...; lane j fetches the table row of the warp's j-th chunk, so one
+  // round of loads covers 32 chunks per warp.
+  for (int c0 = 0; c0 < a.n_chunks; c0 += 32 * kWarps) {
+    const int c = c0 + warp + kWarps * lane;
+    const int4 m = c < a.n_chunks ? chunk_row(a.meta, c) : make_int4(0, 0, -1, 1);
+    const bool span = c < a.n_chunks && !m.w && max(m.x, lo) < min(m.x + m.y, hi);
+    if (c < a.n_chunks && !span) part[c] = make_float2(0.f, 0.f);
+    unsigned todo = __ballot_sync(0xffffffffu, span);
+    while (todo) {
+      const int j = __ffs(todo) - 1;
+      todo &= todo - 1;
+      const int ms = __shfl_sync(0xffffffffu, m.x, j), ml = __shfl_sync(0xffffffffu, m.y, j);
+      const int s = max(ms, lo), e = min(ms + ml, hi);
+      float sd = 0.f, sn = 0.f;
       for (int q = s + lane; q < e; q += 8 * 32) {
         float dd[8], nn[8];
         bool use[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int p = q + 32 * j;
-          use[j] = p < e && !(fl[p - lo] & kInExact);
-          dd[j] = use[j] ? __uint_as_float(keys[p - lo]) : 0.f;
-          nn[j] = use[j] ? __ldcg(a.norm + p) : 0.f;
+        for (int i = 0; i < 8; ++i) {
+          const int p = q + 32 * i;
+          use[i] = p < e && !(fl[p - lo] & kInExact);
+          dd[i] = use[i] ? __uint_as_float(keys[p - lo]) : 0.f;
+          nn[i] = use[i] ? (nrm ? nrm[p - lo] : __ldcg(a.norm + p)) : 0.f;
         }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          sd += dd[j];
-          sn += nn[j];
+        for (int i = 0; i < 8; ++i) {
+          sd += dd[i];
+          sn += nn[i];
         }
       }
       sd = warp_sum(sd);
       sn = warp_sum(sn);
-    }
-    if (lane == 0) part[c] = make_float2(sd, sn);
-  }
-  cluster.sync();  // every slice's partials are written
-  if (phase1_hist && rank == 0)  // every CTA has its copy: clear it for the next launch
-    for (int i = tid; i < kBins; i += kThreads) phase1_hist[i] = 0u;
-
-  // 3. rel of every chunk from the slices' partials in rank order; escalation, budget
-  // (torch_engine.py:128-140) — the same values in every CTA
-  for (int c = tid; c < a.n_chunks; c += kThreads) {
-    const int32_t* m = a.meta + c * CKV_SEL_META_STRIDE;
-    if (m[3]) continue;  // exact
-    float sd = 0.f, sn = 0.f;
-#pragma unroll
-    for (int r = 0; r < kCluster; ++r) {
-      const float2 v = cluster.map_shared_rank(part, r)[c];
-      sd += v.x;
-      sn += v.y;
-    }
-    const float rel = __fdiv_rn(sd, sn);
-    const bool esc = a.has_thr && (double(rel) > a.thr);
-    if (rank == 0) a.rel[c] = rel;
-    if (esc) {
-      atomicOr(&t.esc[c >> 5], 1u << (c & 31));
-      if (c < 32) atomicOr(&t.escmask, 1u << c);
-      t.slow = 1;  // phase 1 counted the span's rows as eligible
-    } else if (m[2] >= 0) {
-      atomicAdd(&t.budget, m[2]);
+      if (lane == 0) part[c0 + warp + kWarps * j] = make_float2(sd, sn);
     }
   }
+  __syncthreads();  // partials written; the raw values are read
+  cluster_arrive();
 
-  // 4. per-position state: keep = ~cached | sink (torch_engine.py:125), the score key
+  // 4. (under the barrier) per-position state: keep = ~cached | sink
+  // (torch_engine.py:125), the score key
   for (int g = tid; g < nq; g += kThreads) {
     const uint32_t f4 = *reinterpret_cast<const uint32_t*>(fl + 4 * g);
     const uint4 d4 = *reinterpret_cast<const uint4*>(keys + 4 * g);
@@ -404,52 +483,72 @@ __device__ void select_tail(cg::cluster_group& cluster, const SelectArgs& a, uin
     *reinterpret_cast<uint32_t*>(fl + 4 * g) = w;
     *reinterpret_cast<uint4*>(keys + 4 * g) = k;
   }
+  cluster_wait();  // every slice's partials are written
+  if (phase1_hist && rank == 0)  // every CTA has its copy: clear it for the next launch
+    for (int i = tid; i < kBins; i += kThreads) phase1_hist[i] = 0u;
+
+  // 3. rel of every chunk from the slices' partials in rank order; escalation, budget
+  // (torch_engine.py:128-140) — the same values in every CTA
+  for (int c = tid; c < a.n_chunks; c += kThreads) {
+    const int4 m = chunk_row(a.meta, c);
+    if (m.w) continue;  // exact
+    float2 v[kCluster];
+#pragma unroll
+    for (int r = 0; r < kCluster; ++r) v[r] = ld_cluster_f2(part + c, unsigned(r));
+    float sd = 0.f, sn = 0.f;
+#pragma unroll
+    for (int r = 0; r < kCluster; ++r) {
+      sd += v[r].x;
+      sn += v[r].y;
+    }
+    const float rel = __fdiv_rn(sd, sn);
+    const bool esc = a.has_thr && (double(rel) > a.thr);
+    if (rank == 0) a.rel[c] = rel;
+    if (esc) {
+      atomicOr(&t.esc[c >> 5], 1u << (c & 31));
+      if (c < 32) atomicOr(&t.escmask, 1u << c);
+      t.slow = 1;  // phase 1 counted the span's rows as eligible
+    } else if (m.z >= 0) {
+      atomicAdd(&t.budget, m.z);
+    }
+  }
   __syncthreads();
 
   // 5. escalated spans kept whole (torch_engine.py:133-135), then pool = spans of
   // pooled, non-escalated chunks (136-140); an exact position in the pool was never
   // computed, so phase 1 did not count it
-  for (int c = warp; c < a.n_chunks; c += kWarps) {
-    const int32_t* m = a.meta + c * CKV_SEL_META_STRIDE;
-    if (!m[3] && (t.esc[c >> 5] >> (c & 31)) & 1u) set_span_bit(fl, lo, hi, m[0], m[0] + m[1], kKeep, 0);
+  for (int pass = 0; pass < 2; ++pass) {
+    for (int c0 = 0; c0 < a.n_chunks; c0 += 32 * kWarps) {
+      const int c = c0 + warp + kWarps * lane;
+      const int4 m = c < a.n_chunks ? chunk_row(a.meta, c) : make_int4(0, 0, -1, 1);
+      const bool esc = c < a.n_chunks && ((t.esc[c >> 5] >> (c & 31)) & 1u);
+      const bool go = c < a.n_chunks && !m.w && max(m.x, lo) < min(m.x + m.y, hi) &&
+                      (pass == 0 ? esc : (!esc && m.z >= 0));
+      unsigned todo = __ballot_sync(0xffffffffu, go);
+      while (todo) {
+        const int j = __ffs(todo) - 1;
+        todo &= todo - 1;
+        const int ms = __shfl_sync(0xffffffffu, m.x, j), ml = __shfl_sync(0xffffffffu, m.y, j);
+        if (pass == 0) {
+          set_span_bit(fl, lo, hi, ms, ms + ml, kKeep, 0);
+        } else if (set_span_bit(fl, lo, hi, ms, ms + ml, kPool, kExact) && lane == 0) {
+          t.x5 = 1;
+        }
+      }
+    }
+    __syncthreads();
   }
-  __syncthreads();
-  for (int c = warp; c < a.n_chunks; c += kWarps) {
-    const int32_t* m = a.meta + c * CKV_SEL_META_STRIDE;
-    if (m[3] || m[2] < 0 || ((t.esc[c >> 5] >> (c & 31)) & 1u)) continue;
-    if (set_span_bit(fl, lo, hi, m[0], m[0] + m[1], kPool, kExact) && lane == 0) t.vals[0] = 1;
-  }
-  cluster.sync();  // every slice's flags are final; vals[0] of every CTA written
-  int slow = t.slow;
-  for (int r = 0; r < kCluster; ++r) slow |= cluster.map_shared_rank(&t.vals[0], r)[0];
+  cluster_arrive();  // every slice's flags are final; x5 of every CTA written
 
   // 6. radix select of the budget-th largest eligible key (eligible = pool & ~keep,
-  // torch_engine.py:142-144): bits [30:20], [19:9], [8:0].  Each CTA walks its slice in
-  // warp blocks of quads; the histograms are summed over the CTAs.
+  // torch_engine.py:142-144): bits [30:20], [19:9], [8:0].  Each CTA counts its slice
+  // in warp blocks of quads; the counts of a level are summed over the CTAs.  Under the
+  // barrier: phase 1's histogram (the same in every CTA) gives the first level and this
+  // slice's second-level counts start, unless escalation already rules phase 1 out.
   const int per_warp = (nq + kThreads - 1) / kThreads * 32;  // quads, a multiple of 32
   const int g_lo = min(nq, warp * per_warp), g_hi = min(nq, g_lo + per_warp);
-  int n_elig, bin1, k1;
-  if (slow) {  // first level from the keys
-    for (int i = tid; i < kBins; i += kThreads) hist[i] = 0u;
-    __syncthreads();
-    for (int g0 = g_lo; g0 < g_hi; g0 += 32) {
-      const int g = g0 + lane;
-      uint4 k = make_uint4(0u, 0u, 0u, 0u);
-      uint32_t f = 0u;
-      if (g < g_hi) {
-        k = *reinterpret_cast<const uint4*>(keys + 4 * g);
-        f = *reinterpret_cast<const uint32_t*>(fl + 4 * g);
-      }
-      const uint32_t kk[4] = {k.x, k.y, k.z, k.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) hist_add(hist, kk[i] >> 20, eligible(byte_of(f, i)));
-    }
-    cluster.sync();
-    const Rank rr = rank_bins_cluster(cluster, hist, kBins, t.budget, t.w, &t.rank);
-    n_elig = rr.total;
-    bin1 = rr.bin;
-    k1 = rr.k;
-  } else {  // phase 1's histogram, the same in every CTA
+  int n_elig = 0, bin1 = 0, k1 = 0;
+  if (!t.slow) {
     if (tid == 0) {
       t.bin = 0;
       t.k = 0;
@@ -457,74 +556,125 @@ __device__ void select_tail(cg::cluster_group& cluster, const SelectArgs& a, uin
     n_elig = rank_bins_local(hist, kBins, t.budget, t.w, &t.bin, &t.k);
     bin1 = t.bin;
     k1 = t.k;
+    if (min(t.budget, n_elig) > 0) count_level(hist2, keys, fl, g_lo, g_hi, uint32_t(bin1) << 20, 20, 11);
+  }
+  cluster_wait();
+  int slow = t.slow;
+  for (int r = 0; r < kCluster; ++r) slow |= ld_cluster_i32(&t.x5, unsigned(r));
+  if (slow) {  // first level from the keys (phase 1's histogram misses positions)
+    if (tid == 0) {
+      t.bin = 0;
+      t.k = 0;
+    }
+    count_level(hist, keys, fl, g_lo, g_hi, 0u, 31, 11);
+    cluster.sync();
+    n_elig = rank_bins_merged(hist, kBins, t.budget, t.w, &t.bin, &t.k);
+    bin1 = t.bin;
+    k1 = t.k;
+    if (min(t.budget, n_elig) > 0) count_level(hist2, keys, fl, g_lo, g_hi, uint32_t(bin1) << 20, 20, 11);
   }
   const int budget = min(t.budget, n_elig);
   uint32_t thr = 0x80000000u;  // above every key: nothing selected
   int take_eq = 0;
-  if (budget > 0) {
+  if (budget > 0) {  // the same in every CTA
     uint32_t prefix = uint32_t(bin1) << 20;
-    int k_level = k1;
-    for (int level = 0; level < 2; ++level) {
-      const int shift = level == 0 ? 20 : 9;  // bits already fixed: [31:shift]
-      const int nbits = level == 0 ? 11 : 9;  // bits resolved now, below them
-      const int nbins = 1 << nbits;
-      // levels alternate between two arrays: the one cleared here was last read before
-      // the previous level's cluster barriers, so no CTA can still be reading it
-      uint32_t* h = level == 0 ? hist2 : hist;
-      for (int i = tid; i < nbins; i += kThreads) h[i] = 0u;
-      __syncthreads();
-      for (int g0 = g_lo; g0 < g_hi; g0 += 32) {
-        const int g = g0 + lane;
-        uint4 k = make_uint4(0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu);
-        uint32_t f = 0u;
-        if (g < g_hi) {
-          k = *reinterpret_cast<const uint4*>(keys + 4 * g);
-          f = *reinterpret_cast<const uint32_t*>(fl + 4 * g);
-        }
-        const uint32_t kk[4] = {k.x, k.y, k.z, k.w};
-        bool any = false;
-        bool on[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          on[i] = (kk[i] >> shift) == (prefix >> shift) && eligible(byte_of(f, i));
-          any |= on[i];
-        }
-        if (__any_sync(0xffffffffu, any)) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            hist_add(h, (kk[i] >> (shift - nbits)) & uint32_t(nbins - 1), on[i]);
-        }
-      }
-      cluster.sync();  // every CTA's histogram of this level is complete
-      const Rank rr = rank_bins_cluster(cluster, h, nbins, k_level, t.w, &t.rank);
-      prefix |= uint32_t(rr.bin) << (shift - nbits);
-      k_level = rr.k;
+    // second level: bits [19:9] from hist2 (counted above)
+    cluster.sync();
+    if (tid == 0) {
+      t.bin = 0;
+      t.k = 0;
     }
-    thr = prefix;
-    take_eq = k_level;
+    rank_bins_merged(hist2, kBins, k1, t.w, &t.bin, &t.k);
+    prefix |= uint32_t(t.bin) << 9;
+    const int k2 = t.k;
+    // third level: bits [8:0] into hist, which no CTA reads any more (every CTA passed
+    // the barrier above after its last read of the others' hist)
+    count_level(hist, keys, fl, g_lo, g_hi, prefix, 9, 9);
+    cluster.sync();
+    if (tid == 0) {
+      t.bin = 0;
+      t.k = 0;
+    }
+    rank_bins_merged(hist, 512, k2, t.w, &t.bin, &t.k);
+    thr = prefix | uint32_t(t.bin);
+    take_eq = t.k;
   }
 
-  // 7. mark: keys above thr, then the first take_eq equal to it by position; compact
-  // (torch_engine.py:144-150).  Ranks inside a warp come from lane scans, across warps
-  // from one scan per count, across CTAs from the lower slices' counts.
-  int tot = 0;
-  int eq_run = 0;
-  if (take_eq > 0) {
-    int cnt = 0;
+  // 7. counts over the slice, per warp: eligible keys above thr and equal to it, other
+  // kept positions, exact positions; one exchange gives every CTA the lower slices'
+  // totals (torch_engine.py:144-150: the first take_eq equal keys by position are kept)
+  {
+    int c[4] = {0, 0, 0, 0};
     for (int g = g_lo + lane; g < g_hi; g += 32) {
       const uint4 k = *reinterpret_cast<const uint4*>(keys + 4 * g);
       const uint32_t f = *reinterpret_cast<const uint32_t*>(fl + 4 * g);
       const uint32_t kk[4] = {k.x, k.y, k.z, k.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) cnt += (kk[i] == thr && eligible(byte_of(f, i))) ? 1 : 0;
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t b = byte_of(f, i);
+        if (eligible(b)) {
+          c[0] += kk[i] > thr ? 1 : 0;
+          c[1] += kk[i] == thr ? 1 : 0;
+        } else {
+          c[2] += (b & kKeep) ? 1 : 0;
+        }
+        c[3] += (b & kExact) ? 1 : 0;
+      }
     }
-    eq_run = warp_bases(warp_sum_i(cnt), &tot, t.w);
-    if (tid == 0) t.vals[1] = tot;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int s = warp_sum_i(c[j]);
+      if (lane == 0) t.wc[j][warp] = s;
+    }
   }
-  cluster.sync();  // equal-key counts of every slice
-  if (take_eq > 0)
-    for (int r = 0; r < rank; ++r) eq_run += cluster.map_shared_rank(&t.vals[1], r)[0];
-  int c_keep = 0, c_ex = 0, c_cached = 0, c_bad = 0;  // per lane
+  __syncthreads();
+  if (warp == 0) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int x = lane < kWarps ? t.wc[j][lane] : 0;
+      const int inc = warp_incl(x);
+      if (j == 1 && lane < kWarps) t.wp[0][lane] = inc - x;
+      if (j == 3 && lane < kWarps) t.wp[1][lane] = inc - x;
+      if (lane == 31) t.tot[j] = inc;
+    }
+  }
+  __syncthreads();
+  cluster.sync();  // every CTA's totals
+  if (warp == 0) {
+    int4 v = make_int4(0, 0, 0, 0);
+    if (lane < kCluster) {
+      const uint4 u = ld_cluster_v4(t.tot, unsigned(lane));
+      v = make_int4(int(u.x), int(u.y), int(u.z), int(u.w));
+    }
+    const int eq_incl = warp_incl(v.y);
+    const int eq_before = eq_incl - v.y;  // equal keys of the lower slices
+    const int taken = lane < kCluster ? max(0, min(take_eq - eq_before, v.y)) : 0;
+    const int kept = v.x + v.z + taken;
+    const int kept_incl = warp_incl(kept), ex_incl = warp_incl(v.w);
+    if (lane == rank) {
+      t.base[0] = eq_before;
+      t.base[1] = kept_incl - kept;
+      t.base[2] = ex_incl - v.w;
+    }
+    if (lane == 31) t.n_sel = kept_incl;
+  }
+  __syncthreads();
+  cluster_arrive();  // the others' totals are read; the wait comes before leaving
+
+  // 8. mark and compact: keys above thr, then the first take_eq equal to it by position;
+  // kept positions in order (keep_abs) and their index among the computed ones (sel)
+  int eq_run = t.base[0] + t.wp[0][warp];
+  int ex_run = t.base[2] + t.wp[1][warp];
+  int out_run = t.base[1];
+  {
+    int before = 0;  // kept positions of the lower warps of this CTA
+    if (lane < warp) {
+      const int eb = t.base[0] + t.wp[0][lane];
+      before = t.wc[0][lane] + t.wc[2][lane] + max(0, min(take_eq - eb, t.wc[1][lane]));
+    }
+    out_run += warp_sum_i(before);
+  }
+  int c_keep = 0, c_cached = 0, c_bad = 0;  // per lane
   for (int g0 = g_lo; g0 < g_hi; g0 += 32) {
     const int g = g0 + lane;
     uint4 k = make_uint4(0u, 0u, 0u, 0u);
@@ -535,14 +685,13 @@ __device__ void select_tail(cg::cluster_group& cluster, const SelectArgs& a, uin
     }
     const uint32_t kk[4] = {k.x, k.y, k.z, k.w};
     int n_eq = 0;
-    if (take_eq > 0) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) n_eq += (kk[i] == thr && eligible(byte_of(f, i))) ? 1 : 0;
-    }
+    for (int i = 0; i < 4; ++i) n_eq += (kk[i] == thr && eligible(byte_of(f, i))) ? 1 : 0;
     const int inc = warp_incl(n_eq);
     int r = eq_run + inc - n_eq;  // equal keys before this quad
     eq_run += __shfl_sync(0xffffffffu, inc, 31);
-    uint32_t out = f;
+    uint32_t kept4 = 0u;
+    int nk = 0, nx = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const uint32_t b = byte_of(f, i);
@@ -554,77 +703,50 @@ __device__ void select_tail(cg::cluster_group& cluster, const SelectArgs& a, uin
         kept = (b & kKeep) != 0;
       }
       if (kept) {
-        out |= uint32_t(kKept) << (8 * i);
-        ++c_keep;
+        kept4 |= 1u << i;
+        ++nk;
         if (b & kCached) ++c_cached;
         if (b & kExact) ++c_bad;
       }
-      if (b & kExact) ++c_ex;
+      if (b & kExact) ++nx;
     }
-    if (g < g_hi && out != f) *reinterpret_cast<uint32_t*>(fl + 4 * g) = out;
-  }
-  int k_tot, x_tot, ch_tot, bad_tot;
-  int out_run = warp_bases(warp_sum_i(c_keep), &k_tot, t.w);
-  int ex_run = warp_bases(warp_sum_i(c_ex), &x_tot, t.w);
-  warp_bases(warp_sum_i(c_cached), &ch_tot, t.w);
-  warp_bases(warp_sum_i(c_bad), &bad_tot, t.w);
-  if (tid == 0) {
-    t.vals[2] = k_tot;
-    t.vals[3] = x_tot;
-    t.vals[4] = ch_tot;
-    t.vals[5] = bad_tot;
-  }
-  cluster.sync();  // kept / exact counts of every slice
-  int n_sel = 0, sel_cached = 0, bad = 0;
-  for (int r = 0; r < kCluster; ++r) {
-    const int* v = cluster.map_shared_rank(t.vals, r);
-    if (r < rank) {
-      out_run += v[2];
-      ex_run += v[3];
-    }
-    n_sel += v[2];
-    sel_cached += v[4];
-    bad += v[5];
-  }
-  for (int g0 = g_lo; g0 < g_hi; g0 += 32) {
-    const int g = g0 + lane;
-    const uint32_t f = g < g_hi ? *reinterpret_cast<const uint32_t*>(fl + 4 * g) : 0u;
-    int nk = 0, nx = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      nk += (byte_of(f, i) & kKept) ? 1 : 0;
-      nx += (byte_of(f, i) & kExact) ? 1 : 0;
-    }
-    const int inc = warp_incl(nk | (nx << 16));  // both counts fit 16 bits per step
-    int ik = out_run + (inc & 0xffff) - nk;
-    int ix = ex_run + (inc >> 16) - nx;
-    const int all = __shfl_sync(0xffffffffu, inc, 31);
+    c_keep += nk;
+    const int inc2 = warp_incl(nk | (nx << 16));  // both counts fit 16 bits per step
+    int ik = out_run + (inc2 & 0xffff) - nk;
+    int ix = ex_run + (inc2 >> 16) - nx;
+    const int all = __shfl_sync(0xffffffffu, inc2, 31);
     out_run += all & 0xffff;
     ex_run += all >> 16;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint32_t b = byte_of(f, i);
       const int p = lo + 4 * g + i;
-      if (b & kKept) {
+      if ((kept4 >> i) & 1u) {
         a.keep_abs[ik] = p;
         a.sel[ik] = p - ix;
         ++ik;
       }
-      if (b & kExact) ++ix;
+      if ((byte_of(f, i) & kExact)) ++ix;
+    }
+  }
+  c_keep = warp_sum_i(c_keep);
+  c_cached = warp_sum_i(c_cached);
+  c_bad = warp_sum_i(c_bad);
+  if (lane == 0) {
+    if (c_cached) atomicAdd(&a.counts[1], c_cached);
+    if (c_keep - c_cached) atomicAdd(&a.counts[6], c_keep - c_cached);
+    if (c_bad) {
+      atomicOr(&a.counts[5], int(CKV_DEV_ERR_SELECT_UNCOMPUTED));
+      atomicOr(&g_err_word, CKV_DEV_ERR_SELECT_UNCOMPUTED);
     }
   }
   if (rank == 0 && tid == 0) {
-    a.counts[0] = n_sel;
-    a.counts[1] = sel_cached;
+    a.counts[0] = t.n_sel;
     a.counts[2] = budget;
     a.counts[3] = n_elig;
     a.counts[4] = int(t.escmask);
-    a.counts[5] = bad ? int(CKV_DEV_ERR_SELECT_UNCOMPUTED) : 0;
-    a.counts[6] = n_sel - sel_cached;
     a.counts[7] = 0;
-    if (bad) atomicOr(&g_err_word, CKV_DEV_ERR_SELECT_UNCOMPUTED);
   }
-  cluster.sync();  // no CTA leaves while another may still read its shared memory
+  cluster_wait();  // no CTA leaves while another may still read its shared memory
 }
 
 // Phase 1 for one active row i (one warp): diff[p], norm[p] for p = active[i].
@@ -749,11 +871,13 @@ __global__ void __launch_bounds__(kThreads) deviation_scores_kernel(RowArgs r) {
   deviation_rows(r, nullptr, nullptr, 0);
 }
 
-// The tail's per-CTA arrays: keys and flags of this CTA's slice (shared memory, or the
-// caller's scratch when the slice is too long), then the chunk partials.
+// The tail's per-CTA arrays: keys, flags and norms of this CTA's slice (shared memory;
+// keys and flags in the caller's scratch and norms read in place when the slice is too
+// long), then the chunk partials.
 struct TailArrays {
   uint32_t* keys;
   uint8_t* fl;
+  float* nrm;
   float2* part;
 };
 __device__ __forceinline__ TailArrays tail_arrays(const SelectArgs& sa, unsigned char* dyn, int rank) {
@@ -762,10 +886,12 @@ __device__ __forceinline__ TailArrays tail_arrays(const SelectArgs& sa, unsigned
   if (slice_in_smem(sa.n_ctx)) {
     t.keys = reinterpret_cast<uint32_t*>(dyn);
     t.fl = dyn + 4 * size_t(S);
-    t.part = reinterpret_cast<float2*>(dyn + 5 * size_t(S));
+    t.nrm = reinterpret_cast<float*>(dyn + 5 * size_t(S));
+    t.part = reinterpret_cast<float2*>(dyn + 9 * size_t(S));
   } else {
     t.keys = sa.keys_scratch + size_t(rank) * S;
     t.fl = sa.flags_scratch + size_t(rank) * S;
+    t.nrm = nullptr;
     t.part = reinterpret_cast<float2*>(dyn);
   }
   return t;
@@ -804,7 +930,7 @@ __global__ void __launch_bounds__(kThreads) deviation_select_kernel(RowArgs r, C
   if (!s_last) return;  // every CTA of the cluster leaves together
   __threadfence();
   const TailArrays ta = tail_arrays(sa, dyn_smem, rank);
-  select_tail(cluster, sa, ta.keys, ta.fl, ta.part, hist, with_hist ? ctl->hist : nullptr);
+  select_tail(cluster, sa, ta.keys, ta.fl, ta.nrm, ta.part, hist, with_hist ? ctl->hist : nullptr);
   if (rank == 0 && threadIdx.x == 0) ctl->ticket = 0u;  // ready for the next launch
 }
 
@@ -814,7 +940,7 @@ __global__ void __launch_bounds__(kThreads) select_only_kernel(SelectArgs sa) {
   __shared__ __align__(16) uint32_t hist[kBins];
   cg::cluster_group cluster = cg::this_cluster();
   const TailArrays ta = tail_arrays(sa, dyn_smem, int(cluster.block_rank()));
-  select_tail(cluster, sa, ta.keys, ta.fl, ta.part, hist, nullptr);
+  select_tail(cluster, sa, ta.keys, ta.fl, ta.nrm, ta.part, hist, nullptr);
 }
 
 int check_select(const uint8_t* pos_flags, int n_ctx, const int32_t* meta, int n_chunks,

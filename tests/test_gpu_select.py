@@ -11,7 +11,7 @@ positions, budget, eligible count and recomputed-cached count:
   ckv_deviation_select    - phase 1 scores from K/V, then the same selection
 
 n_ctx covers both homes of the per-position keys: the shared memory of the eight
-CTAs of the selecting cluster (slices of up to 35328 positions, n_ctx <= 282624) and
+CTAs of the selecting cluster (slices of up to 20128 positions, n_ctx <= 161024) and
 the caller's scratch (above it).
 """
 
@@ -129,8 +129,8 @@ CASES = [
     (1, 300, 3, False, 0.5),
     (2, 5248, 10, False, 0.8),
     (3, 5248, 10, True, 0.3),
-    (4, 282624, 300, False, 0.8),  # the largest n_ctx held in shared memory
-    (5, 282625, 300, True, 0.5),   # the smallest in the caller's scratch
+    (4, 161024, 300, False, 0.8),  # the largest n_ctx held in shared memory
+    (5, 161025, 300, True, 0.5),   # the smallest in the caller's scratch
     (6, 32896, 64, False, 0.0),    # config 5's request length
     (7, 32896, 64, True, 0.9),
     (10, 20480, 40, False, 0.8),
