@@ -21,6 +21,9 @@
 //
 // Every mbarrier wait is bounded (ckv::mbar_wait); a wait that runs out sets
 // CKV_DEV_ERR_WAIT_TIMEOUT, the CTA drains what it issued and frees its TMEM.
+#include <algorithm>
+#include <mutex>
+
 #include "ckv_common.cuh"
 
 CKV_DEFINE_ERR_WORD(gemm)
@@ -411,6 +414,192 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---- the same GEMM on CTA pairs.  A cluster of two CTAs (the two SMs of a TPC) owns a
+// 256 x BN tile: CTA r loads rows [128r, 128r + 128) of A and rows [r BN/2, (r+1) BN/2)
+// of B into its own shared memory, and CTA 0 issues tcgen05.mma.cta_group::2 (M = 256),
+// which reads both CTAs' operands and leaves rows 128r.. of the accumulator in CTA r's
+// TMEM.  Per SM and k-step the shared memory takes 32 KiB of loads and serves 32 KiB to
+// the tensor core, against 48 + 48 KiB for a one-SM 128 x 256 tile: the one-SM kernel's
+// k-loop is bound by shared-memory bandwidth, this one by the tensor core.
+//   full[s]    CTA 0 only: CTA 0's expect_tx for both CTAs' bytes; both CTAs' copies
+//              complete on it (loads without multicast)
+//   empty[s]   both CTAs: the pair MMA's commit arrives on both
+//   tfull[a]   both CTAs: accumulator a is complete (commit to both)
+//   tempty[a]  CTA 0 only: 2 x kEpiWarps arrivals, the peer's from across the pair
+template <int BN, int ST>
+struct PCfg {
+  static constexpr int BNH = BN / 2;  // B rows per CTA
+  static_assert(BN % 16 == 0 && BN <= 256 && BNH % 8 == 0, "BN");
+  static constexpr uint32_t B_BYTES = BNH * BK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;  // one CTA's share of a stage
+  static constexpr int STAGES = ST;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+  static_assert(SMEM_BYTES <= 227 * 1024, "stages do not fit in shared memory");
+  static_assert(B_BYTES % 1024 == 0, "B stages must keep the 1024-byte swizzle alignment");
+  static constexpr uint32_t IDESC = umma_idesc_bf16(2 * BM, BN);
+};
+
+template <int EPI, int HD, int BN, int ST>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     int M, int N, int K, EpiParams ep) {
+  using C = PCfg<BN, ST>;
+  constexpr uint32_t B_BYTES = C::B_BYTES, STAGE_BYTES = C::STAGE_BYTES, IDESC = C::IDESC;
+  constexpr int STAGES = C::STAGES, BNH = C::BNH;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint32_t rank;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+  const int m_tiles = (M + 2 * BM - 1) / (2 * BM);
+  const int n_tiles = (N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int num_kb = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * kEpiWarps);  // every epilogue warp of both CTAs
+    }
+    mbar_init(drain, 1);
+    *abort = 0;
+    fence_barrier_init();
+    fence_async_smem();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  // both CTAs' barriers are initialised before either CTA's copies or arrivals reach them
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += n_pairs) {
+        const int mt = tile % m_tiles, nt = tile / m_tiles;
+        const int ya = mt * 2 * BM + int(rank) * BM, yb = nt * BN + int(rank) * BNH;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort, &g_err_word)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_expect_tx(&full[s], 2 * STAGE_BYTES);
+          const uint32_t bar = cluster_smem_addr(&full[s], 0);
+          tma_load_2d_pair(sA + s * A_BYTES, &tmA, kb * BK, ya, bar);
+          tma_load_2d_pair(sB + s * B_BYTES, &tmB, kb * BK, yb, bar);
+        }
+      }
+      // CTA 0 lets the copies already issued (its own and the peer's) land before the
+      // pair goes away; the peer's copies complete on CTA 0's barriers, and the peer
+      // stays resident until the cluster barrier at the end
+      if (!ok && rank == 0)
+        for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
+          drain_wait(&full[j % STAGES], (j / STAGES) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      int it = 0, tcount = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += n_pairs, ++tcount) {
+        const int acc = tcount & 1;
+        const uint32_t use = tcount >> 1;
+        if (!mbar_wait(&tempty[acc], (use & 1) ^ 1, abort, &g_err_word)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * 256;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, abort, &g_err_word)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * A_BYTES);
+          const uint32_t b0 = smem_u32(sB + s * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k) {
+            const uint64_t ad = umma_desc_sw128(a0 + k * UMMA_K * 2);
+            const uint64_t bd = umma_desc_sw128(b0 + k * UMMA_K * 2);
+            tc_mma_f16_pair(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          tc_commit_pair(&empty[s]);
+        }
+        if (ok) tc_commit_pair(&tfull[acc]);
+      }
+      if (!ok) {  // wait for the MMAs already issued before TMEM is released
+        tc_commit_pair_local(drain);
+        drain_wait(drain, 0);
+      }
+    }
+  } else {
+    const int sub = warp & 3;
+    const int part = (warp - 2) / 4;
+    const uint32_t tempty0[2] = {cluster_smem_addr(&tempty[0], 0), cluster_smem_addr(&tempty[1], 0)};
+    int tcount = 0;
+    for (int tile = pair; tile < num_tiles; tile += n_pairs, ++tcount) {
+      const int acc = tcount & 1;
+      const uint32_t use = tcount >> 1;
+      if (!mbar_wait(&tfull[acc], use & 1, abort, &g_err_word)) break;
+      tc_fence_after();
+      const int mt = tile % m_tiles, nt = tile / m_tiles;
+      const int row = mt * 2 * BM + int(rank) * BM + sub * 32 + lane;
+      const uint32_t tacc = tmem_base + (uint32_t(sub * 32) << 16) + acc * 256;
+      run_epilogue<EPI, HD, BN>(tacc, row, M, nt * BN, N, ep, part);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty0[acc]);
+    }
+  }
+
+  if constexpr (EPI == EPI_PARTIAL) __threadfence_system();
+  tc_fence_before();
+  __syncthreads();
+  // neither CTA leaves (or frees TMEM) while the other may still signal its barriers,
+  // copy into its shared memory or run MMAs into its TMEM
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+  if constexpr (EPI == EPI_PARTIAL) {
+    if (threadIdx.x == 0) {
+      const unsigned t = atomicAdd(ep.push_ticket, 1u);
+      if (t == gridDim.x - 1) {
+        __threadfence_system();
+        for (int q = 0; q < ep.push_ranks; ++q)
+          red_release_sys_add(reinterpret_cast<unsigned*>(ep.push_flag[q]) + ep.push_rank, 1u);
+        *ep.push_ticket = 0u;
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- host side
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -476,10 +665,93 @@ int launch_bn(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, in
   return CKV_OK;
 }
 
+// CTA pairs of a pair kernel that are resident at once (queried once per kernel and
+// device); 0 when the query fails.
+int resident_pairs(const void* kern, int smem) {
+  struct Entry {
+    const void* kern;
+    int dev, pairs;
+  };
+  static std::mutex mu;
+  static Entry cache[64];
+  static int n_cache = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < n_cache; ++i)
+      if (cache[i].kern == kern && cache[i].dev == dev) return cache[i].pairs;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(2 * (num_sms() / 2));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int pairs = 0;
+  if (cudaOccupancyMaxActiveClusters(&pairs, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    pairs = 0;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (n_cache < 64) cache[n_cache++] = {kern, dev, pairs};
+  return pairs;
+}
+
+template <int EPI, int HD, int BN, int ST>
+int launch_pair_bn(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, int M, int N, int K,
+                   const EpiParams& ep, cudaStream_t stream, const char* name) {
+  CKV_REQUIRE(a && b, "%s: null operand", name);
+  CKV_REQUIRE(M >= 0 && N > 0 && K > 0, "%s: bad sizes m=%d n=%d k=%d", name, M, N, K);
+  CKV_REQUIRE(aligned16(a) && aligned16(b), "%s: operands must be 16-byte aligned", name);
+  CKV_REQUIRE(K % 8 == 0 && lda % 8 == 0 && ldb % 8 == 0,
+              "%s: k and row strides must be multiples of 8", name);
+  CKV_REQUIRE(N % 16 == 0, "%s: n=%d must be a multiple of 16", name, N);
+  if (M == 0) return CKV_OK;
+  CUtensorMap ma, mb;
+  if (int rc = make_map(&ma, a, M, K, lda, BM)) return rc;
+  if (int rc = make_map(&mb, b, N, K, ldb, BN / 2)) return rc;
+  auto kern = gemm_pair_kernel<EPI, HD, BN, ST>;
+  constexpr int smem = PCfg<BN, ST>::SMEM_BYTES;
+  if (int rc = set_smem_limit(reinterpret_cast<const void*>(kern), smem)) return rc;
+  const int tiles = ceil_div(M, 2 * BM) * ceil_div(N, BN);
+  int pairs = resident_pairs(reinterpret_cast<const void*>(kern), smem);
+  if (pairs <= 0) pairs = num_sms() / 2;
+  pairs = std::max(1, std::min(tiles, pairs));
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, ma, mb, M, N, K, ep) != cudaSuccess) {
+    set_error("%s: launch failed: %s", name, cudaGetErrorString(cudaGetLastError()));
+    return CKV_ERR_CUDA;
+  }
+  CKV_LAUNCH_CHECK(name);
+  return CKV_OK;
+}
+
 // Makespan of whole tiles, in column units: waves x tile width.
 int64_t makespan(int M, int N, int bn) {
   const int tiles = ceil_div(M, BM) * ceil_div(N, bn);
   return int64_t(ceil_div(tiles, num_sms())) * bn;
+}
+// The same for 256-row pair tiles on the SM pairs.
+int64_t makespan_pair(int M, int N, int bn) {
+  const int tiles = ceil_div(M, 2 * BM) * ceil_div(N, bn);
+  return int64_t(ceil_div(tiles, std::max(1, num_sms() / 2))) * bn;
 }
 
 // SwiGLU (interleaved 128-column blocks) and QKV (whole heads) tiles stay 256 wide;
@@ -487,6 +759,19 @@ int64_t makespan(int M, int N, int bn) {
 template <int EPI, int HD>
 int launch(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, int M, int N, int K,
            const EpiParams& ep, cudaStream_t stream, const char* name) {
+  // 256-row tiles on SM pairs when every pair gets two tiles or more (the k-loop then
+  // dominates, and the pair's lighter operand traffic pays); a single wave of tiles
+  // gains nothing from it (measured: o_proj at M = 938 slower, qkv and down_proj equal)
+  if (int64_t(ceil_div(M, 2 * BM)) * ceil_div(N, 256) >= 2 * int64_t(num_sms() / 2)) {
+    if constexpr (EPI == EPI_STORE || EPI == EPI_RESID || EPI == EPI_PARTIAL) {
+      const int64_t m256 = makespan_pair(M, N, 256), m224 = makespan_pair(M, N, 224),
+                    m208 = makespan_pair(M, N, 208);
+      if (m208 < m224 && m208 < m256)
+        return launch_pair_bn<EPI, HD, 208, 7>(a, lda, b, ldb, M, N, K, ep, stream, name);
+      if (m224 < m256) return launch_pair_bn<EPI, HD, 224, 7>(a, lda, b, ldb, M, N, K, ep, stream, name);
+    }
+    return launch_pair_bn<EPI, HD, 256, 6>(a, lda, b, ldb, M, N, K, ep, stream, name);
+  }
   if constexpr (EPI == EPI_STORE || EPI == EPI_RESID || EPI == EPI_PARTIAL) {
     if (M > 0) {
       const int64_t m256 = makespan(M, N, 256), m224 = makespan(M, N, 224), m208 = makespan(M, N, 208);
