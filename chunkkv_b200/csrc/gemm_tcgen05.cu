@@ -125,8 +125,26 @@ __device__ __forceinline__ void epi_store(uint32_t tacc, int row, int M, int n0,
 template <int BN>
 __device__ __forceinline__ void epi_resid(uint32_t tacc, int row, int M, int n0, int N,
                                           const EpiParams& ep, int part) {
-#pragma unroll 1
-  for (int c = chunk_lo<BN>(part); c < chunk_hi<BN>(part); c += 32) {
+  constexpr int kChunks = ((BN + 31) / 32 + 1) / 2;  // 32-column chunks per part (<= 4)
+  const int c_lo = chunk_lo<BN>(part), c_hi = chunk_hi<BN>(part);
+  // every residual vector of this thread's part of the row is requested before the first
+  // TMEM load, so one global round trip serves the whole part
+  uint4 hv[kChunks][4];
+#pragma unroll
+  for (int ci = 0; ci < kChunks; ++ci) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int c = c_lo + 32 * ci;
+      const int col = n0 + c + g * 8;
+      hv[ci][g] = make_uint4(0u, 0u, 0u, 0u);
+      if (row < M && c < c_hi && c + g * 8 < BN && col < N)
+        hv[ci][g] = *reinterpret_cast<const uint4*>(ep.out + int64_t(row) * ep.ldo + col);
+    }
+  }
+#pragma unroll
+  for (int ci = 0; ci < kChunks; ++ci) {
+    const int c = c_lo + 32 * ci;
+    if (c >= c_hi) break;  // warp-uniform
     float v[32];
     tmem_ld32(tacc + c, v);
     if (row >= M) continue;
@@ -134,16 +152,14 @@ __device__ __forceinline__ void epi_resid(uint32_t tacc, int row, int M, int n0,
     for (int g = 0; g < 4; ++g) {
       const int col = n0 + c + g * 8;
       if (c + g * 8 >= BN || col >= N) continue;
-      uint16_t* hp = ep.out + int64_t(row) * ep.ldo + col;
-      const uint4 hv = *reinterpret_cast<const uint4*>(hp);
-      const uint32_t* hw = reinterpret_cast<const uint32_t*>(&hv);
+      const uint32_t* hw = reinterpret_cast<const uint32_t*>(&hv[ci][g]);
       float o[8];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         o[2 * e] = __fadd_rn(lo_bf(hw[e]), bf16_round(v[g * 8 + 2 * e]));
         o[2 * e + 1] = __fadd_rn(hi_bf(hw[e]), bf16_round(v[g * 8 + 2 * e + 1]));
       }
-      store8(hp, o);
+      store8(ep.out + int64_t(row) * ep.ldo + col, o);
     }
   }
 }
