@@ -549,59 +549,78 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      // Stores go through this warp's staging tile: a lane holds one row (TMEM lane) of
-      // O, and a store whose 32 lanes hit 32 rows is replayed once per row.  So 16 words
-      // of each row (64 bytes: 32 bf16 outputs or 16 fp32 partials) are staged, then
-      // written four lanes per row, eight rows per instruction.  dst[k]: element offset
-      // (in out, or part_o when split) of the first column of this warp's row
-      // 8k + lane / 4, -1 for padding rows and rows past M.
-      int64_t dst[4];
-      {
-        const int t0 = cur.rb * NQ * T;
-        const int n_tok = min(NQ * T, M - t0);
-        const int64_t split_base = int64_t((cur.rb * Hk + cur.hk) * max_splits + cur.split) * (NQ * BM) + w * BM;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int rq = sub * 32 + 8 * k + (lane >> 2);
-          const int tq = rq / G, gq = rq - tq * G, ttq = w * T + tq;
-          const bool vq = rq < T * G && ttq < n_tok;
-          dst[k] = !vq ? -1
-                       : (cur.n_split > 1 ? (split_base + rq) * HD
-                                          : (int64_t(t0 + ttq) * Hq + cur.hk * G + gq) * HD);
-        }
-      }
       uint32_t* stg = s_stage + warp * (32 * kStageStride);
-      auto flush = [&](const uint32_t(&v)[16], uint8_t* base, int elem, int col_bytes) {
-        uint4* mine = reinterpret_cast<uint4*>(stg + lane * kStageStride);
-#pragma unroll
-        for (int qd = 0; qd < 4; ++qd) mine[qd] = make_uint4(v[4 * qd], v[4 * qd + 1], v[4 * qd + 2], v[4 * qd + 3]);
-        __syncwarp();
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint4 x = reinterpret_cast<const uint4*>(stg + (8 * k + (lane >> 2)) * kStageStride)[lane & 3];
-          if (dst[k] >= 0) *reinterpret_cast<uint4*>(base + dst[k] * elem + col_bytes + (lane & 3) * 16) = x;
-        }
-        __syncwarp();
-      };
       if (cur.n_split > 1) {
-        // one slice of the keys: unnormalised O with its (max, sum), merged by the combine kernel
+        // One slice of the keys: unnormalised O with its (max, sum), merged by the combine
+        // kernel.  The partials of a warpgroup are stored column-chunk-major (8 fp32
+        // columns of all 128 rows per chunk, the two 16-byte halves of row r swapped when
+        // bit 2 of r is set), so the warp's 32 rows of one chunk are 1 KiB of contiguous
+        // global memory.  Each chunk is staged in one of the warp's two 1 KiB buffers and
+        // written by a TMA bulk store; the staging of the next chunk overlaps it.  Plain
+        // per-lane stores of the same partials took about four times as long here.
+        const int64_t blk = (int64_t((cur.rb * Hk + cur.hk) * max_splits + cur.split) * NQ + w) * BM * HD;
+        float* gdst = part_o + blk + sub * 32 * 8;
+        uint8_t* stg8 = reinterpret_cast<uint8_t*>(stg);
+        const int swz = (lane >> 2) & 1;
+        int chunk = 0;
 #pragma unroll 1
         for (int c = 0; c < HD; c += 32) {
           float o[32];
           tmem_ld32(obuf + c, o);
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            uint32_t v[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(o[16 * h + e]);
-            flush(v, reinterpret_cast<uint8_t*>(part_o), 4, (c + 16 * h) * 4);
+          for (int h = 0; h < 4; ++h, ++chunk) {
+            uint8_t* buf = stg8 + (chunk & 1) * 1024;
+            if (chunk >= 2) {  // the store that last read this buffer has read it
+              if (lane == 0) bulk_wait_read<1>();
+              __syncwarp();
+            }
+            float4* mine = reinterpret_cast<float4*>(buf + lane * 32);
+            mine[swz] = make_float4(o[8 * h], o[8 * h + 1], o[8 * h + 2], o[8 * h + 3]);
+            mine[swz ^ 1] = make_float4(o[8 * h + 4], o[8 * h + 5], o[8 * h + 6], o[8 * h + 7]);
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              bulk_store(gdst + (c / 8 + h) * (BM * 8), buf, 1024);
+              bulk_commit();
+            }
           }
         }
+        if (lane == 0) bulk_wait_read<0>();  // both buffers free for the next epilogue
+        __syncwarp();
         if (row.valid) {
           const int64_t prow = int64_t((cur.rb * Hk + cur.hk) * max_splits + cur.split) * (NQ * BM) + w * BM + r;
           part_ml[prow] = make_float2(m, l);
         }
       } else {
+        // Stores go through this warp's staging tile: a lane holds one row (TMEM lane) of
+        // O, and a store whose 32 lanes hit 32 rows is replayed once per row.  So 16 words
+        // of each row (32 bf16 outputs) are staged, then written four lanes per row, eight
+        // rows per instruction.  dst[k]: element offset in out of the first column of this
+        // warp's row 8k + lane / 4, -1 for padding rows and rows past M.
+        int64_t dst[4];
+        {
+          const int t0 = cur.rb * NQ * T;
+          const int n_tok = min(NQ * T, M - t0);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int rq = sub * 32 + 8 * k + (lane >> 2);
+            const int tq = rq / G, gq = rq - tq * G, ttq = w * T + tq;
+            const bool vq = rq < T * G && ttq < n_tok;
+            dst[k] = !vq ? -1 : (int64_t(t0 + ttq) * Hq + cur.hk * G + gq) * HD;
+          }
+        }
+        auto flush = [&](const uint32_t(&v)[16], int col) {
+          uint4* mine = reinterpret_cast<uint4*>(stg + lane * kStageStride);
+#pragma unroll
+          for (int qd = 0; qd < 4; ++qd) mine[qd] = make_uint4(v[4 * qd], v[4 * qd + 1], v[4 * qd + 2], v[4 * qd + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint4 x = reinterpret_cast<const uint4*>(stg + (8 * k + (lane >> 2)) * kStageStride)[lane & 3];
+            if (dst[k] >= 0) *reinterpret_cast<uint4*>(out + dst[k] + col + (lane & 3) * 8) = x;
+          }
+          __syncwarp();
+        };
         const float inv = l > 0.f ? 1.0f / l : 0.f;
 #pragma unroll 1
         for (int c = 0; c < HD; c += 32) {
@@ -610,7 +629,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t v[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) v[e] = pack_bf2(o[2 * e] * inv, o[2 * e + 1] * inv);
-          flush(v, reinterpret_cast<uint8_t*>(out), 2, c * 2);
+          flush(v, c);
         }
       }
       // O has been read: the next item's first P V (which overwrites it) is issued only
@@ -619,6 +638,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       cur = nxt;
       row = nrow;
     }
+    // the split partials' bulk stores have written global memory before the CTA ends
+    if (lane == 0) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -632,7 +653,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Merge the key splits of the row blocks that were split: O = sum_s 2^(m_s - M) O_s /
 // sum_s 2^(m_s - M) l_s with M = max_s m_s (all in the log2 domain of the kernel).
 // One warp per packed row; lane s reads split s's (m, l), each lane then sums its
-// HD/32 columns over the splits.  Rows of unsplit blocks were written directly.
+// four columns over the splits.  Rows of unsplit blocks were written directly.
 constexpr int kCombineWarps = 8;
 template <int HD>
 __global__ void __launch_bounds__(kCombineWarps * 32) attention_combine_kernel(
@@ -667,20 +688,29 @@ __global__ void __launch_bounds__(kCombineWarps * 32) attention_combine_kernel(
   float L = wgt * ml.y;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-  float acc[HD / 32];
-#pragma unroll
-  for (int i = 0; i < HD / 32; ++i) acc[i] = 0.f;
+  // lane v < HD / 4 takes columns 4v .. 4v + 3: 16-byte half (v & 1) of 8-column chunk
+  // v >> 1, stored swapped with the other half when bit 2 of the row is set (the
+  // kernel's column-chunk-major partial layout)
+  const bool mine = lane < HD / 4;
+  const int off = (lane >> 1) * (BM * 8) + r * 8 + (((lane & 1) ^ ((r >> 2) & 1)) << 2);
+  const float* po = part_o + (int64_t((rb * Hk + hk) * max_splits) * NQ + w) * BM * HD + off;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
   for (int sp = 0; sp < n_split; ++sp) {
     const float ws = __shfl_sync(0xffffffffu, wgt, sp);
-    const float* po = part_o + (base + sp * stride) * HD + lane;
-#pragma unroll
-    for (int i = 0; i < HD / 32; ++i) acc[i] = fmaf(ws, po[32 * i], acc[i]);
+    if (mine) {
+      const float4 x = *reinterpret_cast<const float4*>(po + int64_t(sp) * NQ * BM * HD);
+      acc.x = fmaf(ws, x.x, acc.x);
+      acc.y = fmaf(ws, x.y, acc.y);
+      acc.z = fmaf(ws, x.z, acc.z);
+      acc.w = fmaf(ws, x.w, acc.w);
+    }
   }
   const float inv = L > 0.f ? 1.0f / L : 0.f;
   uint16_t* orow = out + (int64_t(t0 + tt) * Hq + hk * G + g) * HD;
-#pragma unroll
-  for (int i = 0; i < HD / 32; ++i) orow[lane + 32 * i] = f2bf(acc[i] * inv);
+  if (mine)
+    *reinterpret_cast<uint2*>(orow + 4 * lane) =
+        make_uint2(pack_bf2(acc.x * inv, acc.y * inv), pack_bf2(acc.z * inv, acc.w * inv));
 }
 
 // Key-split plan: split only when the unsplit grid leaves SMs idle.

@@ -173,6 +173,24 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, 
       ::"r"(smem_u32(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// Untiled bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from
+// this CTA's shared memory to global memory by the TMA unit, in the thread's current
+// bulk group.  The writing threads order their shared-memory stores before it with
+// fence_async_smem() and a barrier; the source may be rewritten only after
+// bulk_wait_read() has seen the group's reads finish.
+__device__ __forceinline__ void bulk_store(void* gmem_dst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+               ::"l"(gmem_dst), "r"(smem_u32(smem_src)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until at most N of this thread's bulk groups still read their shared-memory source
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// wait until all of this thread's bulk groups have completed (writes performed)
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // 2-D tiled bulk tensor load into this CTA's shared memory (no multicast).
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y,
