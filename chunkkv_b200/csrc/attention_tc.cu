@@ -199,6 +199,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // set-up done; q, the caches, the positions and the workspace belong to the kernels
+  // before (dependent launch)
+  pdl_wait();
+  pdl_launch_next();
 
   if (warp == kWarpTma) {
     // ------------------------------------------- item scheduler + TMA producer (one warp)
@@ -659,6 +663,8 @@ template <int HD>
 __global__ void __launch_bounds__(kCombineWarps * 32) attention_combine_kernel(
     const int32_t* __restrict__ positions, uint16_t* __restrict__ out, int M, int Hq, int Hk, int n_ctx,
     int tps, int max_splits, const float* __restrict__ part_o, const float2* __restrict__ part_ml) {
+  pdl_wait();  // the partials come from the attention kernel just before (dependent launch)
+  pdl_launch_next();
   const int G = Hq / Hk;
   const int T = BM / G;
   constexpr int kChunks = NQ * BM / kCombineWarps;  // CTAs per (row block, KV head)
@@ -1118,12 +1124,13 @@ int launch(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int3
   const int64_t n_slots = int64_t(p.blocks) * Hk * p.max_splits;
   CKV_REQUIRE(n_slots < (int64_t(1) << 31) - 4 * 1024 * 1024, "ckv_attention: too many work items");
   const int grid = int(std::min<int64_t>(n_slots, num_sms()));
-  kern<<<grid, kThreads, Cfg<HD>::SMEM, stream>>>(mk, mv, mq, positions, out, M, Hq, Hk, n_ctx, sl2, p.tps,
-                                                   p.max_splits, p.blocks, sched, part_o, part_ml);
+  launch_pdl(kern, dim3(grid), dim3(kThreads), Cfg<HD>::SMEM, stream, mk, mv, mq, positions, out, M, Hq, Hk,
+             n_ctx, sl2, p.tps, p.max_splits, p.blocks, sched, part_o, part_ml);
   CKV_LAUNCH_CHECK("ckv_attention");
   if (p.max_splits > 1) {
-    attention_combine_kernel<HD><<<dim3(p.blocks * (NQ * BM / kCombineWarps), Hk), kCombineWarps * 32, 0, stream>>>(
-        positions, out, M, Hq, Hk, n_ctx, p.tps, p.max_splits, part_o, part_ml);
+    launch_pdl(attention_combine_kernel<HD>, dim3(p.blocks * (NQ * BM / kCombineWarps), Hk),
+               dim3(kCombineWarps * 32), 0, stream, positions, out, M, Hq, Hk, n_ctx, p.tps, p.max_splits,
+               static_cast<const float*>(part_o), static_cast<const float2*>(part_ml));
     CKV_LAUNCH_CHECK("ckv_attention(combine)");
   }
   return CKV_OK;

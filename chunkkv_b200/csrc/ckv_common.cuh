@@ -13,6 +13,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <string>
+#include <utility>
 
 #include "../../include/chunkkv_b200.h"
 
@@ -49,6 +50,29 @@ inline int ceil_div(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) 
 int num_sms();                    // SM count of the current device (cached per device)
 int set_smem_limit(const void* kernel, int bytes);  // raises the dynamic smem cap once per device
 
+// Programmatic dependent launch: the kernels of one prefill layer (RMSNorm, the GEMMs,
+// attention and its combine) are launched with programmatic stream serialization, so a
+// kernel's CTAs are scheduled, set up their barriers, TMEM and descriptors while the
+// kernel before it in the stream is still running.  Every kernel launched this way calls
+// pdl_wait() before its first global-memory access (it returns once the previous kernel
+// has completed and its writes are visible), then pdl_launch_next() so that the kernel
+// after it may be scheduled in turn.  Launched without the attribute, both are no-ops.
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // Each translation unit owns one device error word (OR of CKV_DEV_ERR_* bits)
 // and a host reader that returns and clears it (after a device sync).
 #define CKV_DEFINE_ERR_WORD(tag)                                             \
@@ -77,6 +101,10 @@ __device__ __forceinline__ uint32_t pack_bf2(float a, float b) {
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
   return r;
 }
+
+// ------------------------------------------------ device: dependent launches
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_next() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ------------------------------------------------------------ device: timing
 __device__ __forceinline__ uint64_t global_ns() {

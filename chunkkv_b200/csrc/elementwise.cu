@@ -52,6 +52,8 @@ __global__ void __launch_bounds__(kRmsThreads) rmsnorm_kernel(uint16_t* __restri
                                                               uint16_t* __restrict__ y, int hidden,
                                                               float eps) {
   __shared__ float s_red[kRmsThreads / 32];
+  pdl_wait();  // h comes from the kernel before (dependent launch)
+  pdl_launch_next();
   const int row = blockIdx.x;
   uint4* xr = reinterpret_cast<uint4*>(x + int64_t(row) * hidden);
   const uint4* wr = reinterpret_cast<const uint4*>(w);
@@ -250,8 +252,8 @@ int ckv_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows, int
   CKV_REQUIRE(hidden <= kRmsThreads * 8 * kRmsVec, "ckv_rmsnorm: hidden %d above %d", hidden,
               kRmsThreads * 8 * kRmsVec);
   if (rows <= 0) return CKV_OK;
-  rmsnorm_kernel<false><<<rows, kRmsThreads, 0, as_stream(stream)>>>(const_cast<uint16_t*>(x),
-                                                                      nullptr, w, y, hidden, eps);
+  launch_pdl(rmsnorm_kernel<false>, dim3(rows), dim3(kRmsThreads), 0, as_stream(stream),
+             const_cast<uint16_t*>(x), static_cast<const uint16_t*>(nullptr), w, y, hidden, eps);
   CKV_LAUNCH_CHECK("ckv_rmsnorm");
   return CKV_OK;
 }
@@ -266,7 +268,8 @@ int ckv_add_rmsnorm(uint16_t* h, const uint16_t* delta, const uint16_t* w, uint1
               kRmsThreads * 8 * kRmsVec);
   CKV_REQUIRE(y != h && y != delta, "ckv_add_rmsnorm: y must not alias h or delta");
   if (rows <= 0) return CKV_OK;
-  rmsnorm_kernel<true><<<rows, kRmsThreads, 0, as_stream(stream)>>>(h, delta, w, y, hidden, eps);
+  launch_pdl(rmsnorm_kernel<true>, dim3(rows), dim3(kRmsThreads), 0, as_stream(stream), h, delta, w, y,
+             hidden, eps);
   CKV_LAUNCH_CHECK("ckv_add_rmsnorm");
   return CKV_OK;
 }

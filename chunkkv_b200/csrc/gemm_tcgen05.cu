@@ -329,6 +329,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // set-up done; the operands and the epilogue's inputs and outputs belong to the kernels
+  // before (dependent launch)
+  pdl_wait();
+  pdl_launch_next();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -507,6 +511,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // set-up done; the data belong to the kernels before (dependent launch)
+  pdl_launch_next();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -676,7 +682,7 @@ int launch_bn(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, in
   if (int rc = set_smem_limit(reinterpret_cast<const void*>(kern), GCfg<BN, ST>::SMEM_BYTES)) return rc;
   const int tiles = ceil_div(M, BM) * ceil_div(N, BN);
   const int grid = std::min(tiles, num_sms());
-  kern<<<grid, kThreads, GCfg<BN, ST>::SMEM_BYTES, stream>>>(ma, mb, M, N, K, ep);
+  launch_pdl(kern, dim3(grid), dim3(kThreads), GCfg<BN, ST>::SMEM_BYTES, stream, ma, mb, M, N, K, ep);
   CKV_LAUNCH_CHECK(name);
   return CKV_OK;
 }
@@ -740,7 +746,7 @@ int launch_pair_bn(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ld
   if (pairs <= 0) pairs = num_sms() / 2;
   pairs = std::max(1, std::min(tiles, pairs));
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cfg.gridDim = dim3(2 * pairs);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
@@ -749,8 +755,10 @@ int launch_pair_bn(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ld
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // dependent launch
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   if (cudaLaunchKernelEx(&cfg, kern, ma, mb, M, N, K, ep) != cudaSuccess) {
     set_error("%s: launch failed: %s", name, cudaGetErrorString(cudaGetLastError()));
     return CKV_ERR_CUDA;
