@@ -656,18 +656,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // Merge the key splits of the row blocks that were split: O = sum_s 2^(m_s - M) O_s /
 // sum_s 2^(m_s - M) l_s with M = max_s m_s (all in the log2 domain of the kernel).
-// One warp per packed row; lane s reads split s's (m, l), each lane then sums its
-// four columns over the splits.  Rows of unsplit blocks were written directly.
+// A warp takes kCombineRows packed rows; for each, lane s reads split s's (m, l), then
+// each lane sums its four columns over the splits, the loads of all its rows in flight
+// together (one wave of CTAs at the 7B shape).  Rows of unsplit blocks were written
+// directly.
 constexpr int kCombineWarps = 8;
+constexpr int kCombineRows = 4;
 template <int HD>
-__global__ void __launch_bounds__(kCombineWarps * 32) attention_combine_kernel(
+__global__ void __launch_bounds__(kCombineWarps * 32, 4) attention_combine_kernel(
     const int32_t* __restrict__ positions, uint16_t* __restrict__ out, int M, int Hq, int Hk, int n_ctx,
     int tps, int max_splits, const float* __restrict__ part_o, const float2* __restrict__ part_ml) {
   pdl_wait();  // the partials come from the attention kernel just before (dependent launch)
   pdl_launch_next();
+  constexpr int R = kCombineRows;
   const int G = Hq / Hk;
   const int T = BM / G;
-  constexpr int kChunks = NQ * BM / kCombineWarps;  // CTAs per (row block, KV head)
+  constexpr int kChunks = NQ * BM / (kCombineWarps * R);  // CTAs per (row block, KV head)
   const int rb = blockIdx.x / kChunks, chunk = blockIdx.x - rb * kChunks, hk = blockIdx.y;
   const int t0 = rb * NQ * T;
   const int n_tok = min(NQ * T, M - t0);
@@ -680,43 +684,59 @@ __global__ void __launch_bounds__(kCombineWarps * 32) attention_combine_kernel(
   const int n_split = ((s_max + BN) / BN + tps - 1) / tps;
   if (n_split <= 1) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int pr = chunk * kCombineWarps + warp;
-  const int w = pr / BM, r = pr - w * BM;
-  const int tr = r / G, g = r - tr * G, tt = w * T + tr;
-  if (r >= T * G || tt >= n_tok) return;
   const int64_t stride = NQ * BM;
-  const int64_t base = int64_t((rb * Hk + hk) * max_splits) * stride + pr;
-  const float2 ml = lane < n_split ? part_ml[base + lane * stride] : make_float2(-INFINITY, 0.f);
-  float mmax = ml.x;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, o));
-  const float wgt = lane < n_split ? exp2f(ml.x - mmax) : 0.f;
-  float L = wgt * ml.y;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  const int64_t blk = int64_t((rb * Hk + hk) * max_splits);
   // lane v < HD / 4 takes columns 4v .. 4v + 3: 16-byte half (v & 1) of 8-column chunk
   // v >> 1, stored swapped with the other half when bit 2 of the row is set (the
   // kernel's column-chunk-major partial layout)
   const bool mine = lane < HD / 4;
-  const int off = (lane >> 1) * (BM * 8) + r * 8 + (((lane & 1) ^ ((r >> 2) & 1)) << 2);
-  const float* po = part_o + (int64_t((rb * Hk + hk) * max_splits) * NQ + w) * BM * HD + off;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
+  float wgt[R], inv[R];
+  int off[R];
+  int64_t orow[R];
+  bool ok[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    const int pr = (chunk * kCombineWarps + warp) * R + i;
+    const int w = pr / BM, r = pr - w * BM;
+    const int tr = r / G, g = r - tr * G, tt = w * T + tr;
+    ok[i] = r < T * G && tt < n_tok;  // the same for the whole warp
+    const float2 ml =
+        ok[i] && lane < n_split ? part_ml[blk * stride + pr + lane * stride] : make_float2(-INFINITY, 0.f);
+    float mmax = ml.x;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, o));
+    wgt[i] = ok[i] && lane < n_split ? exp2f(ml.x - mmax) : 0.f;
+    float L = wgt[i] * ml.y;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    inv[i] = L > 0.f ? 1.0f / L : 0.f;
+    off[i] = w * (BM * HD) + (lane >> 1) * (BM * 8) + r * 8 + (((lane & 1) ^ ((r >> 2) & 1)) << 2);
+    orow[i] = (int64_t(t0 + tt) * Hq + hk * G + g) * HD;
+  }
+  const float* po = part_o + blk * NQ * BM * HD;
+  float4 acc[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 2
   for (int sp = 0; sp < n_split; ++sp) {
-    const float ws = __shfl_sync(0xffffffffu, wgt, sp);
-    if (mine) {
-      const float4 x = *reinterpret_cast<const float4*>(po + int64_t(sp) * NQ * BM * HD);
-      acc.x = fmaf(ws, x.x, acc.x);
-      acc.y = fmaf(ws, x.y, acc.y);
-      acc.z = fmaf(ws, x.z, acc.z);
-      acc.w = fmaf(ws, x.w, acc.w);
+    const float* ps = po + int64_t(sp) * NQ * BM * HD;
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      const float ws = __shfl_sync(0xffffffffu, wgt[i], sp);
+      if (mine && ok[i]) {
+        const float4 x = *reinterpret_cast<const float4*>(ps + off[i]);
+        acc[i].x = fmaf(ws, x.x, acc[i].x);
+        acc[i].y = fmaf(ws, x.y, acc[i].y);
+        acc[i].z = fmaf(ws, x.z, acc[i].z);
+        acc[i].w = fmaf(ws, x.w, acc[i].w);
+      }
     }
   }
-  const float inv = L > 0.f ? 1.0f / L : 0.f;
-  uint16_t* orow = out + (int64_t(t0 + tt) * Hq + hk * G + g) * HD;
-  if (mine)
-    *reinterpret_cast<uint2*>(orow + 4 * lane) =
-        make_uint2(pack_bf2(acc.x * inv, acc.y * inv), pack_bf2(acc.z * inv, acc.w * inv));
+#pragma unroll
+  for (int i = 0; i < R; ++i)
+    if (mine && ok[i])
+      *reinterpret_cast<uint2*>(out + orow[i] + 4 * lane) =
+          make_uint2(pack_bf2(acc[i].x * inv[i], acc[i].y * inv[i]), pack_bf2(acc[i].z * inv[i], acc[i].w * inv[i]));
 }
 
 // Key-split plan: split only when the unsplit grid leaves SMs idle.
@@ -1128,7 +1148,7 @@ int launch(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int3
              n_ctx, sl2, p.tps, p.max_splits, p.blocks, sched, part_o, part_ml);
   CKV_LAUNCH_CHECK("ckv_attention");
   if (p.max_splits > 1) {
-    launch_pdl(attention_combine_kernel<HD>, dim3(p.blocks * (NQ * BM / kCombineWarps), Hk),
+    launch_pdl(attention_combine_kernel<HD>, dim3(p.blocks * (NQ * BM / (kCombineWarps * kCombineRows)), Hk),
                dim3(kCombineWarps * 32), 0, stream, positions, out, M, Hq, Hk, n_ctx, p.tps, p.max_splits,
                static_cast<const float*>(part_o), static_cast<const float2*>(part_ml));
     CKV_LAUNCH_CHECK("ckv_attention(combine)");

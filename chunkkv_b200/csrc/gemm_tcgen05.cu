@@ -329,8 +329,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // set-up done; the operands and the epilogue's inputs and outputs belong to the kernels
-  // before (dependent launch)
+  // The weights are not written by the kernels before, so the weight tiles of the first
+  // stages are requested before the dependent-launch wait and arrive while the previous
+  // kernel ends; A and everything the epilogue touches wait for it.
+  int pre = 0;
+  if (warp == 0 && lane == 0 && int(blockIdx.x) < num_tiles) {
+    pre = min(STAGES, num_kb);
+    const int nt0 = int(blockIdx.x) / m_tiles;
+    for (int kb = 0; kb < pre; ++kb) {
+      mbar_expect_tx(&full[kb], STAGE_BYTES);
+      tma_load_2d(sB + kb * B_BYTES, &tmB, kb * BK, nt0 * BN, &full[kb]);
+    }
+  }
   pdl_wait();
   pdl_launch_next();
 
@@ -343,6 +353,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
+          if (it < pre) {  // weight tile already requested: the activation tile joins it
+            tma_load_2d(sA + s * A_BYTES, &tmA, kb * BK, mt * BM, &full[s]);
+            continue;
+          }
           if (!mbar_wait(&empty[s], ph ^ 1, abort, &g_err_word)) {
             ok = false;
             break;
@@ -511,7 +525,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  pdl_wait();  // set-up done; the data belong to the kernels before (dependent launch)
+  // the weight halves of the first stages go out before the dependent-launch wait (the
+  // weights are not written by the kernels before); A waits for the previous kernel
+  int pre = 0;
+  if (warp == 0 && lane == 0 && pair < num_tiles) {
+    pre = min(STAGES, num_kb);
+    const int yb0 = (pair / m_tiles) * BN + int(rank) * BNH;
+    for (int kb = 0; kb < pre; ++kb) {
+      if (rank == 0) mbar_expect_tx(&full[kb], 2 * STAGE_BYTES);
+      tma_load_2d_pair(sB + kb * B_BYTES, &tmB, kb * BK, yb0, cluster_smem_addr(&full[kb], 0));
+    }
+  }
+  pdl_wait();
   pdl_launch_next();
 
   if (warp == 0) {
@@ -524,12 +549,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
+          const uint32_t bar = cluster_smem_addr(&full[s], 0);
+          if (it < pre) {  // weight half already requested: the activation rows join it
+            tma_load_2d_pair(sA + s * A_BYTES, &tmA, kb * BK, ya, bar);
+            continue;
+          }
           if (!mbar_wait(&empty[s], ph ^ 1, abort, &g_err_word)) {
             ok = false;
             break;
           }
           if (rank == 0) mbar_expect_tx(&full[s], 2 * STAGE_BYTES);
-          const uint32_t bar = cluster_smem_addr(&full[s], 0);
           tma_load_2d_pair(sA + s * A_BYTES, &tmA, kb * BK, ya, bar);
           tma_load_2d_pair(sB + s * B_BYTES, &tmB, kb * BK, yb, bar);
         }
