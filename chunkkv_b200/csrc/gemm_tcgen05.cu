@@ -814,7 +814,7 @@ int launch(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, int M
            const EpiParams& ep, cudaStream_t stream, const char* name) {
   // 256-row tiles on SM pairs when every pair gets two tiles or more (the k-loop then
   // dominates, and the pair's lighter operand traffic pays); a single wave of tiles
-  // gains nothing from it (measured: o_proj at M = 938 slower, qkv and down_proj equal)
+  // mostly gains nothing from it (measured at M = 938: o_proj and qkv slower)
   if (int64_t(ceil_div(M, 2 * BM)) * ceil_div(N, 256) >= 2 * int64_t(num_sms() / 2)) {
     if constexpr (EPI == EPI_STORE || EPI == EPI_RESID || EPI == EPI_PARTIAL) {
       const int64_t m256 = makespan_pair(M, N, 256), m224 = makespan_pair(M, N, 224),
@@ -824,6 +824,12 @@ int launch(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, int M
       if (m224 < m256) return launch_pair_bn<EPI, HD, 224, 7>(a, lda, b, ldb, M, N, K, ep, stream, name);
     }
     return launch_pair_bn<EPI, HD, 256, 6>(a, lda, b, ldb, M, N, K, ep, stream, name);
+  }
+  // the residual GEMM with a long K loop (down_proj) is the exception: 256 x 256 pair
+  // tiles, fewer of them than SMs, measured 110 us against 114 us for 128 x 208 tiles on
+  // single SMs at M = 938, K = 18944 (same box)
+  if constexpr (EPI == EPI_RESID) {
+    if (K >= 8192 && M > BM) return launch_pair_bn<EPI, HD, 256, 6>(a, lda, b, ldb, M, N, K, ep, stream, name);
   }
   if constexpr (EPI == EPI_STORE || EPI == EPI_RESID || EPI == EPI_PARTIAL) {
     if (M > 0) {
