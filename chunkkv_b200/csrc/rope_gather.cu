@@ -125,6 +125,8 @@ __global__ void __launch_bounds__(256, 4) shift_rows_kernel(const uint16_t* __re
                                                          const float* __restrict__ inv_freq) {
   __shared__ float2 cs[kMaxHalf];
   __shared__ __align__(16) uint4 s_stage[kCopyWarps][kStageVec];
+  pdl_wait();  // the rows come from the kernel before (dependent launch)
+  pdl_launch_next();
   for (int j = threadIdx.x; j < rot / 2; j += blockDim.x) cs[j] = rope_cs(float(delta), inv_freq[j]);
   __syncthreads();
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -232,6 +234,8 @@ __global__ void __launch_bounds__(256, 4) blend_gather_kernel(
   __shared__ float2 cs[kMaxHalf];
   __shared__ int s_pages[kSmemPages];  // this chunk's page ids, so no unit waits on a table load
   __shared__ __align__(16) uint4 s_stage[kCopyWarps][kStageVec];  // plain (V, Δ = 0) units
+  pdl_wait();  // the chunk tables and pages come from the work before (dependent launch)
+  pdl_launch_next();
   const int32_t* meta = chunk_meta + blockIdx.y * CKV_META_STRIDE;
   const int table_off = meta[CKV_META_TABLE_OFFSET];
   const int length = meta[CKV_META_LENGTH];
@@ -317,6 +321,8 @@ __global__ void __launch_bounds__(256) pages_write_kernel(
     const uint64_t* __restrict__ k_ptrs, const uint64_t* __restrict__ v_ptrs, int64_t head_stride,
     int n_layers, int H, int D) {
   __shared__ __align__(16) uint4 s_stage[kCopyWarps][kStageVec];
+  pdl_wait();  // the chunk's K/V come from the kernels before (dependent launch)
+  pdl_launch_next();
   const int n_blocks = (length + kPage - 1) / kPage;
   const int64_t n_units = int64_t(n_blocks) * n_layers * 2 * H;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -392,8 +398,8 @@ int ckv_shift_keys(const uint16_t* src, uint16_t* dst, int64_t rows, int head_di
   }
   const int64_t units = (rows + kPage - 1) / kPage;
   const int grid = int(std::min<int64_t>((units + 7) / 8, 4 * num_sms()));
-  shift_rows_kernel<<<grid, 256, 0, as_stream(stream)>>>(src, dst, rows, head_dim, rot_dims, delta,
-                                                         inv_freq);
+  launch_pdl(shift_rows_kernel, dim3(grid), dim3(256), 0, as_stream(stream), src, dst, rows, head_dim, rot_dims,
+             delta, inv_freq);
   CKV_LAUNCH_CHECK("ckv_shift_keys");
   return CKV_OK;
 }
@@ -471,9 +477,10 @@ int ckv_blend_gather_paged(const uint16_t* pool, int64_t n_pages, const int32_t*
   CKV_REQUIRE(layer_hi <= n_layers, "ckv_blend_gather_paged: layer_hi > n_layers");
   if (n_chunks == 0 || layer_hi == layer_lo) return CKV_OK;
   const int gx = std::max(1, 4 * num_sms() / n_chunks);
-  blend_gather_kernel<true><<<dim3(gx, n_chunks), 256, 0, as_stream(stream)>>>(
-      pool, n_pages, page_table, nullptr, nullptr, chunk_meta, inv_freq, rot_dims, k_out, v_out,
-      layer_lo, layer_hi, n_layers, n_kv_heads, head_dim, n_ctx);
+  launch_pdl(blend_gather_kernel<true>, dim3(gx, n_chunks), dim3(256), 0, as_stream(stream), pool, n_pages,
+             page_table, static_cast<const uint64_t*>(nullptr), static_cast<const uint64_t*>(nullptr),
+             chunk_meta, inv_freq, rot_dims, k_out, v_out, layer_lo, layer_hi, n_layers, n_kv_heads, head_dim,
+             n_ctx);
   CKV_LAUNCH_CHECK("ckv_blend_gather_paged");
   return CKV_OK;
 }
@@ -489,9 +496,10 @@ int ckv_blend_gather_dense(const uint64_t* k_ptrs, const uint64_t* v_ptrs,
   CKV_REQUIRE(k_ptrs && v_ptrs, "ckv_blend_gather_dense: null pointer arrays");
   if (n_chunks == 0 || layer_hi == layer_lo) return CKV_OK;
   const int gx = std::max(1, 4 * num_sms() / n_chunks);
-  blend_gather_kernel<false><<<dim3(gx, n_chunks), 256, 0, as_stream(stream)>>>(
-      nullptr, 0, nullptr, k_ptrs, v_ptrs, chunk_meta, inv_freq, rot_dims, k_out, v_out, layer_lo,
-      layer_hi, /*n_layers=*/0, n_kv_heads, head_dim, n_ctx);
+  launch_pdl(blend_gather_kernel<false>, dim3(gx, n_chunks), dim3(256), 0, as_stream(stream),
+             static_cast<const uint16_t*>(nullptr), int64_t(0), static_cast<const int32_t*>(nullptr), k_ptrs,
+             v_ptrs, chunk_meta, inv_freq, rot_dims, k_out, v_out, layer_lo, layer_hi, /*n_layers=*/0,
+             n_kv_heads, head_dim, n_ctx);
   CKV_LAUNCH_CHECK("ckv_blend_gather_dense");
   return CKV_OK;
 }
@@ -507,9 +515,8 @@ int ckv_pages_write(uint16_t* pool, int64_t n_pages, const int32_t* page_ids, in
   if (length == 0) return CKV_OK;
   const int64_t units = int64_t(ceil_div(length, kPage)) * n_layers * 2 * n_kv_heads;
   const int grid = static_cast<int>(std::min<int64_t>((units + 7) / 8, 8 * num_sms()));
-  pages_write_kernel<<<grid, 256, 0, as_stream(stream)>>>(pool, n_pages, page_ids, length, k_ptrs,
-                                                          v_ptrs, head_stride, n_layers,
-                                                          n_kv_heads, head_dim);
+  launch_pdl(pages_write_kernel, dim3(grid), dim3(256), 0, as_stream(stream), pool, n_pages, page_ids, length,
+             k_ptrs, v_ptrs, head_stride, n_layers, n_kv_heads, head_dim);
   CKV_LAUNCH_CHECK("ckv_pages_write");
   return CKV_OK;
 }
