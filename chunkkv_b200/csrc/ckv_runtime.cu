@@ -32,10 +32,13 @@ int num_sms() {
 }
 
 int set_smem_limit(const void* kernel, int bytes) {
-  // One attribute call per (kernel, device); the table is small and append-only.
+  // One attribute call per (kernel, device) and size: the cap is raised when a launch needs
+  // more than the largest size set so far (kernels whose shared memory depends on the
+  // shape); the table is small and append-only.
   struct Entry {
     const void* k;
     int dev;
+    int bytes;
   };
   static Entry done[256];
   static int n_done = 0;
@@ -43,14 +46,19 @@ int set_smem_limit(const void* kernel, int bytes) {
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(mu);
+  Entry* hit = nullptr;
   for (int i = 0; i < n_done; ++i)
-    if (done[i].k == kernel && done[i].dev == dev) return 0;
+    if (done[i].k == kernel && done[i].dev == dev) hit = &done[i];
+  if (hit && hit->bytes >= bytes) return 0;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess) {
     set_error("cudaFuncSetAttribute(%d bytes): %s", bytes, cudaGetErrorString(e));
     return CKV_ERR_CUDA;
   }
-  if (n_done < 256) done[n_done++] = {kernel, dev};
+  if (hit)
+    hit->bytes = bytes;
+  else if (n_done < 256)
+    done[n_done++] = {kernel, dev, bytes};
   return 0;
 }
 

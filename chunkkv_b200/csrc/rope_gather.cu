@@ -315,6 +315,176 @@ __global__ void __launch_bounds__(256, 4) blend_gather_kernel(
   }
 }
 
+// Paged gather through a ring of TMA bulk copies.  A warp takes the same units as
+// blend_gather_kernel (16 tokens of one (layer, K|V, head), one or two page pieces) and
+// keeps kRing of them in its own shared-memory slots: its lane 0 loads unit k + kRing - 1
+// (cp.async.bulk from the page pool, completing on the slot's mbarrier) while unit k is
+// stored.  A plain unit (V, or K with delta = 0) goes back out by one bulk store from the
+// slot, so its bytes never pass through registers; a unit to re-rope is rotated in place
+// in the slot by the warp's lanes (the same fp32 rotation as rotate8) and then stored the
+// same way.  Every wait is bounded.
+constexpr int kRing = 3;
+__global__ void __launch_bounds__(256, 2) blend_gather_bulk_kernel(
+    const uint16_t* __restrict__ pool, int64_t n_pages, const int32_t* __restrict__ page_table,
+    const int32_t* __restrict__ chunk_meta, const float* __restrict__ inv_freq, int rot,
+    uint16_t* __restrict__ k_out, uint16_t* __restrict__ v_out, int layer_lo, int layer_hi, int n_layers,
+    int H, int D, int n_ctx) {
+  extern __shared__ __align__(128) uint8_t ring_raw[];
+  __shared__ float2 cs[kMaxHalf];
+  __shared__ int s_pages[kSmemPages];
+  __shared__ __align__(8) uint64_t bars[kCopyWarps][kRing];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t unit_bytes = uint32_t(kPage) * D * 2;  // one slot
+  uint8_t* ring = ring_raw + size_t(warp) * kRing * unit_bytes;
+  if (lane == 0)
+    for (int r = 0; r < kRing; ++r) mbar_init(&bars[warp][r], 1);
+  fence_barrier_init();
+  pdl_wait();  // the chunk tables and pages come from the work before (dependent launch)
+  pdl_launch_next();
+  const int32_t* meta = chunk_meta + blockIdx.y * CKV_META_STRIDE;
+  const int table_off = meta[CKV_META_TABLE_OFFSET];
+  const int length = meta[CKV_META_LENGTH];
+  const int dst_start = meta[CKV_META_DST_START];
+  const int delta = meta[CKV_META_DELTA];
+  const int lb = max(layer_lo, meta[CKV_META_LAYER_BEGIN]);
+  const int le = min(layer_hi, meta[CKV_META_LAYER_END]);
+  const int src_off = meta[CKV_META_SRC_OFFSET];
+  if (le <= lb || length <= 0) return;  // the whole CTA: nothing issued yet
+  const bool rotate = delta != 0;
+  if (rotate)
+    for (int j = threadIdx.x; j < rot / 2; j += blockDim.x) cs[j] = rope_cs(float(delta), inv_freq[j]);
+  const int n_slots = min(kSmemPages, (src_off + length + kPage - 1) / kPage);
+  for (int i = threadIdx.x; i < n_slots; i += blockDim.x) s_pages[i] = page_table[table_off + i];
+  __syncthreads();
+
+  const int nl = le - lb;
+  const int n_blocks = (length + kPage - 1) / kPage;
+  const int n_units = n_blocks * nl * 2 * H;  // < 2^31: checked on the host
+  const int64_t layer_elems = int64_t(H) * n_ctx * D;
+  const int first = blockIdx.x * kCopyWarps + warp, step = gridDim.x * kCopyWarps;
+  const int my_units = first < n_units ? (n_units - 1 - first) / step + 1 : 0;
+
+  // where unit k of this warp comes from (up to two page pieces) and goes to
+  struct Unit {
+    const uint16_t* src[2];
+    int rows[2];  // rows of each piece (0: none, or skipped for a bad page id)
+    int off[2];   // row offset of each piece in the unit (and in the slot)
+    int n;        // rows of the unit
+    uint16_t* dst;
+    bool rot;
+  };
+  auto unit = [&](int k) {
+    Unit x{{nullptr, nullptr}, {0, 0}, {0, 0}, 0, nullptr, false};
+    int t = first + k * step;
+    const int b = t % n_blocks;
+    t /= n_blocks;
+    const int h = t % H;
+    t /= H;
+    const int kv = t & 1;
+    t >>= 1;
+    const int l = lb + t;
+    const int r0 = b * kPage;
+    const int rows = min(kPage, length - r0);
+    const int dpos = dst_start + r0;
+    if (dpos < 0 || dpos + rows > n_ctx) {
+      if (lane == 0) atomicOr(&g_err_word, CKV_DEV_ERR_POSITION_RANGE);
+      return x;
+    }
+    x.dst = (kv ? v_out : k_out) + int64_t(l - layer_lo) * layer_elems + (int64_t(h) * n_ctx + dpos) * D;
+    x.rot = rotate && kv == 0;
+    int done = 0;
+    for (int piece = 0; piece < 2 && done < rows; ++piece) {
+      const int tok = src_off + r0 + done;
+      const int slot = tok / kPage, in_page = tok % kPage;
+      const int take = min(rows - done, kPage - in_page);
+      const int page = slot < kSmemPages ? s_pages[slot] : page_table[table_off + slot];
+      x.off[piece] = done;
+      if (page < 0 || page >= n_pages) {
+        if (lane == 0) atomicOr(&g_err_word, CKV_DEV_ERR_PAGE_RANGE);
+      } else {
+        x.src[piece] = pool + ((((int64_t(page) * n_layers + l) * 2 + kv) * H + h) * kPage + in_page) * D;
+        x.rows[piece] = take;
+      }
+      done += take;
+    }
+    x.n = rows;
+    return x;
+  };
+  // lane 0: the copies of unit k into slot k % kRing (pieces at their row offsets)
+  auto load = [&](int k, const Unit& x) {
+    uint64_t* bar = &bars[warp][k % kRing];
+    uint8_t* slot = ring + (k % kRing) * unit_bytes;
+    const uint32_t b0 = uint32_t(x.rows[0]) * D * 2, b1 = uint32_t(x.rows[1]) * D * 2;
+    if (b0 + b1 == 0) {
+      mbar_arrive(bar);  // nothing to copy: the slot's phase completes at once
+      return;
+    }
+    mbar_expect_tx(bar, b0 + b1);
+    if (b0) bulk_load(slot + uint32_t(x.off[0]) * D * 2, x.src[0], b0, bar);
+    if (b1) bulk_load(slot + uint32_t(x.off[1]) * D * 2, x.src[1], b1, bar);
+  };
+  if (lane == 0)
+    for (int k = 0; k < kRing - 1 && k < my_units; ++k) load(k, unit(k));
+  for (int k = 0; k < my_units; ++k) {
+    const Unit x = unit(k);
+    uint8_t* slot = ring + (k % kRing) * unit_bytes;
+    // this unit's copies have landed (every lane waits: the lanes read the slot)
+    const uint64_t t0 = global_ns();
+    bool ok = true;
+    while (!mbar_try_wait(&bars[warp][k % kRing], (k / kRing) & 1))
+      if (global_ns() - t0 > kWaitLimitNs) {
+        ok = false;
+        break;
+      }
+    if (!__all_sync(0xffffffffu, ok)) {
+      if (lane == 0) {
+        atomicOr(&g_err_word, CKV_DEV_ERR_WAIT_TIMEOUT);
+        // let the copies already issued (units k .. k + kRing - 2) land before the CTA goes
+        for (int j = k; j < k + kRing - 1 && j < my_units; ++j) {
+          const uint64_t t1 = global_ns();
+          while (!mbar_try_wait(&bars[warp][j % kRing], (j / kRing) & 1))
+            if (global_ns() - t1 > kWaitLimitNs) break;
+        }
+      }
+      break;
+    }
+    const int rows = x.n;
+    if (x.rot && rows > 0) {
+      // rotate in place: lane takes rotary pairs (vectors p and p + rot / 16 of a row) and
+      // writes them back to the same slot positions
+      uint4* st = reinterpret_cast<uint4*>(slot);
+      const int vec_row = D / 8, n_pair = rot / 16;
+      for (int it = lane; it < kPage * n_pair; it += 32) {
+        const int r = it / n_pair, item = it - r * n_pair;
+        if (r >= rows) break;
+        const int base = r * vec_row;
+        uint4 v1 = st[base + item], v2 = st[base + item + n_pair];
+        rotate8(v1, v2, cs + item * 8);
+        st[base + item] = v1;
+        st[base + item + n_pair] = v2;
+      }
+      fence_async_smem();
+    }
+    __syncwarp();
+    if (lane == 0) {
+      // the slot's rows out to the blended cache (per piece: a skipped piece keeps dst
+      // untouched), then the copies of unit k + kRing - 1 into the slot unit k - 1 used
+#pragma unroll
+      for (int piece = 0; piece < 2; ++piece)
+        if (x.rows[piece])
+          bulk_store(x.dst + int64_t(x.off[piece]) * D, slot + uint32_t(x.off[piece]) * D * 2,
+                     uint32_t(x.rows[piece]) * D * 2);
+      bulk_commit();
+      if (k + kRing - 1 < my_units) {
+        bulk_wait_read<1>();  // the store of unit k - 1 has read its slot
+        load(k + kRing - 1, unit(k + kRing - 1));
+      }
+    }
+    __syncwarp();
+  }
+  if (lane == 0) bulk_wait_all();  // the stores have written the cache before the CTA ends
+}
+
 // Dense (H, >=length, D) per-layer sources -> pages.
 __global__ void __launch_bounds__(256) pages_write_kernel(
     uint16_t* __restrict__ pool, int64_t n_pages, const int32_t* __restrict__ page_ids, int length,
@@ -476,11 +646,14 @@ int ckv_blend_gather_paged(const uint16_t* pool, int64_t n_pages, const int32_t*
   CKV_REQUIRE(pool && page_table && aligned16(pool), "ckv_blend_gather_paged: bad pool/page table");
   CKV_REQUIRE(layer_hi <= n_layers, "ckv_blend_gather_paged: layer_hi > n_layers");
   if (n_chunks == 0 || layer_hi == layer_lo) return CKV_OK;
-  const int gx = std::max(1, 4 * num_sms() / n_chunks);
-  launch_pdl(blend_gather_kernel<true>, dim3(gx, n_chunks), dim3(256), 0, as_stream(stream), pool, n_pages,
-             page_table, static_cast<const uint64_t*>(nullptr), static_cast<const uint64_t*>(nullptr),
-             chunk_meta, inv_freq, rot_dims, k_out, v_out, layer_lo, layer_hi, n_layers, n_kv_heads, head_dim,
-             n_ctx);
+  // the TMA ring: kRing slots of one 16-token unit per warp (96 KiB per CTA at head_dim
+  // 128, two CTAs per SM)
+  const int smem = kCopyWarps * kRing * kPage * head_dim * 2;
+  if (int rc = set_smem_limit(reinterpret_cast<const void*>(blend_gather_bulk_kernel), smem)) return rc;
+  const int gx = std::max(1, 2 * num_sms() / n_chunks);
+  launch_pdl(blend_gather_bulk_kernel, dim3(gx, n_chunks), dim3(256), smem, as_stream(stream), pool, n_pages,
+             page_table, chunk_meta, inv_freq, rot_dims, k_out, v_out, layer_lo, layer_hi, n_layers, n_kv_heads,
+             head_dim, n_ctx);
   CKV_LAUNCH_CHECK("ckv_blend_gather_paged");
   return CKV_OK;
 }
