@@ -352,6 +352,11 @@ class TorchEngine:
                     raise AssertionError("selected a token that was never computed")
                 M = int(counts[0])
                 selected_cached = int(counts[1])
+                h, x = h2, x2
+                active = ws.keep_abs[:M]
+                # the GPU waits on this host: launch the next kernel first, then the bookkeeping
+                if M:
+                    ops.qkv_rope(x, lw.w_qkv, lw.b_qkv, M, 0, Hq * D, Hq, H, D, active, rope_tab, q_out=q)
                 active_host = hv[8 + n_ch:8 + n_ch + M].numpy().copy()
                 self.last_d2h_bytes = 4 * (8 + n_ch + N)
                 thr = config.escalate_threshold
@@ -360,11 +365,7 @@ class TorchEngine:
                         continue
                     chunk_stats.append({"start": p.start, "length": p.chunk.length, "rel_dev": float(r),
                                         "escalated": thr is not None and float(r) > thr})
-                h, x = h2, x2
-                active = ws.keep_abs[:M]
                 attn_flops = 4.0 * Hq * D * float((active_host.astype(np.int64) + 1).sum())
-                if M:
-                    ops.qkv_rope(x, lw.w_qkv, lw.b_qkv, M, 0, Hq * D, Hq, H, D, active, rope_tab, q_out=q)
             else:
                 ops.qkv_rope(x, lw.w_qkv, lw.b_qkv, M, 0, qkv_cols, Hq, H, D, active, rope_tab, q_out=q,
                              k_cache=K_all[li], v_cache=V_all[li])
