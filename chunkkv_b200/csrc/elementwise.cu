@@ -1,12 +1,16 @@
 // Bandwidth-bound pieces of the recompute: embedding rows, RMSNorm, the
 // shrink-to-selection copy/scatter, the small-m lm_head projection and the
-// final log-softmax.  All 16-byte vectorised, one warp (or CTA) per row.
+// final log-softmax (one 8-CTA cluster per row).  Row copies are 16-byte vectorised, one warp or CTA per row.
+#include <cooperative_groups.h>
+
 #include "ckv_common.cuh"
 
 CKV_DEFINE_ERR_WORD(elementwise)
 
 namespace ckv {
 namespace {
+
+namespace cg = cooperative_groups;
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -191,38 +195,59 @@ __global__ void __launch_bounds__(256) gemv_kernel(const uint16_t* __restrict__ 
   }
 }
 
-// log_softmax of one row (float math, bf16 input) — one CTA of 1024 threads.
-__global__ void __launch_bounds__(1024) log_softmax_kernel(const uint16_t* __restrict__ x, int n,
-                                                           float* __restrict__ out) {
-  __shared__ float s_red[32];
-  __shared__ float s_val;
+// log_softmax of one row (float math, bf16 input) on one cluster of kLsmCtas CTAs.
+// CTA r owns the contiguous slice [r * per, (r + 1) * per) of the row.  Each CTA
+// publishes its slice's max, then its slice's sum of exp(x - max), in its own shared
+// memory; every CTA reads the kLsmCtas partials through distributed shared memory and
+// combines them in rank order, so all CTAs hold the same max and log-sum-exp and the
+// result does not depend on timing.  The third pass writes (x - max) - lse.
+constexpr int kLsmCtas = 8;
+constexpr int kLsmThreads = 1024;
+__device__ __forceinline__ float lsm_block_reduce(float v, bool is_max, float* s_red) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = is_max ? warp_max(v) : warp_sum(v);
+  if (lane == 0) s_red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float t = s_red[lane];  // kLsmThreads / 32 == 32 partials
+    t = is_max ? warp_max(t) : warp_sum(t);
+    if (lane == 0) s_red[32] = t;
+  }
+  __syncthreads();
+  const float r = s_red[32];
+  __syncthreads();  // s_red is reused by the next reduction
+  return r;
+}
+__global__ void __cluster_dims__(kLsmCtas, 1, 1) __launch_bounds__(kLsmThreads)
+    log_softmax_kernel(const uint16_t* __restrict__ x, int n, float* __restrict__ out) {
+  static_assert(kLsmThreads == 1024, "lsm_block_reduce assumes 32 warps");
+  __shared__ float s_red[33];
+  __shared__ float s_part[2];  // this CTA's slice max, then its slice sum
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = int(cluster.block_rank());
+  const int per = (n + kLsmCtas - 1) / kLsmCtas;
+  const int lo = min(n, rank * per), hi = min(n, lo + per);
   float mx = -INFINITY;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) mx = fmaxf(mx, bf2f(x[i]));
-  mx = warp_max(mx);
-  if (lane == 0) s_red[warp] = mx;
-  __syncthreads();
-  if (warp == 0) {
-    float t = lane < (blockDim.x >> 5) ? s_red[lane] : -INFINITY;
-    t = warp_max(t);
-    if (lane == 0) s_val = t;
-  }
-  __syncthreads();
-  mx = s_val;
-  __syncthreads();
+  for (int i = lo + int(threadIdx.x); i < hi; i += kLsmThreads) mx = fmaxf(mx, bf2f(x[i]));
+  mx = lsm_block_reduce(mx, true, s_red);
+  if (threadIdx.x == 0) s_part[0] = mx;
+  cluster.sync();
+  float gmax = -INFINITY;
+#pragma unroll
+  for (int q = 0; q < kLsmCtas; ++q) gmax = fmaxf(gmax, cluster.map_shared_rank(s_part, q)[0]);
   float sum = 0.f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) sum += expf(bf2f(x[i]) - mx);
-  sum = warp_sum(sum);
-  if (lane == 0) s_red[warp] = sum;
-  __syncthreads();
-  if (warp == 0) {
-    float t = lane < (blockDim.x >> 5) ? s_red[lane] : 0.f;
-    t = warp_sum(t);
-    if (lane == 0) s_val = logf(t);
-  }
-  __syncthreads();
-  const float lse = s_val;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = (bf2f(x[i]) - mx) - lse;
+  for (int i = lo + int(threadIdx.x); i < hi; i += kLsmThreads) sum += expf(bf2f(x[i]) - gmax);
+  sum = lsm_block_reduce(sum, false, s_red);
+  if (threadIdx.x == 0) s_part[1] = sum;
+  cluster.sync();
+  float total = 0.f;
+#pragma unroll
+  for (int q = 0; q < kLsmCtas; ++q) total += cluster.map_shared_rank(s_part, q)[1];
+  const float lse = logf(total);
+  // No CTA may leave while another still reads its s_part: arrive now, wait at the end.
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  for (int i = lo + int(threadIdx.x); i < hi; i += kLsmThreads) out[i] = (bf2f(x[i]) - gmax) - lse;
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 }  // namespace
@@ -320,7 +345,7 @@ int ckv_gemv(const uint16_t* x, const uint16_t* w, uint16_t* out, int m, int n, 
 
 int ckv_log_softmax(const uint16_t* logits, int n, float* out, ckv_stream_t stream) {
   CKV_REQUIRE(logits && out && n > 0, "ckv_log_softmax: bad arguments");
-  log_softmax_kernel<<<1, 1024, 0, as_stream(stream)>>>(logits, n, out);
+  log_softmax_kernel<<<kLsmCtas, kLsmThreads, 0, as_stream(stream)>>>(logits, n, out);
   CKV_LAUNCH_CHECK("ckv_log_softmax");
   return CKV_OK;
 }

@@ -741,6 +741,9 @@ def test_rmsnorm_embed_gemv_log_softmax():
         xx = x[:mm].contiguous()
         lo = ops.gemv(xx, E)
         assert rel_err(lo, xx.float() @ E.float().T) <= 1e-2
-    row = (torch.randn(vocab, device=DEV) * 5).to(BF)
-    lp = ops.log_softmax(row)
-    torch.testing.assert_close(lp, torch.log_softmax(row.float(), -1), rtol=1e-5, atol=1e-5)
+    # the row is split over an 8-CTA cluster: sizes with empty and ragged slices, the 7B vocab
+    for n in (vocab, 1, 5, 9, 8191, 152064):
+        row = (torch.randn(n, device=DEV) * 5).to(BF)
+        lp = ops.log_softmax(row)
+        torch.testing.assert_close(lp, torch.log_softmax(row.float(), -1), rtol=1e-5, atol=1e-5)
+        assert torch.equal(lp, ops.log_softmax(row)), "the cluster's combine must be deterministic"
