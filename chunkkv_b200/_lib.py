@@ -67,6 +67,7 @@ SIGNATURES: dict[str, list] = {
     "ckv_attention": [_p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _i32, _f32, _p, _i64, _p],
     "ckv_gemv": [_p, _p, _p, _i32, _i32, _i32, _p],
     "ckv_log_softmax": [_p, _i32, _p, _p],
+    "ckv_greedy_next": [_p, _i32, _p, _p, _p],
 }
 _RESTYPES = {"ckv_version": C.c_char_p, "ckv_last_error": C.c_char_p, "ckv_attention_workspace_size": C.c_int64}
 

@@ -250,6 +250,89 @@ __global__ void __cluster_dims__(kLsmCtas, 1, 1) __launch_bounds__(kLsmThreads)
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// Greedy next token of the decode loop (logits[-1].argmax() and pos += 1,
+// torch_engine.py:185,196-197): the argmax of one bf16 logits row on one cluster of
+// kLsmCtas CTAs, each reducing one contiguous slice.  Order: NaN above every number
+// (torch.argmax propagates NaN), then the larger value, and on equal values the lower
+// index, so the result is torch.argmax's.  Rank 0 merges the slices' winners in rank
+// order, writes the token id and, when `pos` is given, advances the decode position by
+// one, so a replayed decode step needs no further kernel for either.
+__device__ __forceinline__ bool argmax_better(float av, int ai, float bv, int bi) {
+  const bool an = av != av, bn = bv != bv;
+  if (an != bn) return an;
+  if (!an && av != bv) return av > bv;
+  return ai < bi;
+}
+__global__ void __cluster_dims__(kLsmCtas, 1, 1) __launch_bounds__(kLsmThreads)
+    greedy_next_kernel(const uint16_t* __restrict__ x, int n, int32_t* __restrict__ tok,
+                       int32_t* __restrict__ pos) {
+  __shared__ float s_v[32];
+  __shared__ int s_i[32];
+  __shared__ float s_pv;  // this CTA's winner
+  __shared__ int s_pi;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = int(cluster.block_rank());
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int per = (n + kLsmCtas - 1) / kLsmCtas;
+  const int lo = min(n, rank * per), hi = min(n, lo + per);
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = lo + int(threadIdx.x); i < hi; i += kLsmThreads) {
+    const float v = bf2f(x[i]);
+    if (argmax_better(v, i, bv, bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (argmax_better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if (lane == 0) {
+    s_v[warp] = bv;
+    s_i[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    bv = s_v[lane];  // kLsmThreads / 32 == 32 warps
+    bi = s_i[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (argmax_better(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      s_pv = bv;
+      s_pi = bi;
+    }
+  }
+  cluster.sync();
+  if (rank == 0 && threadIdx.x == 0) {
+    float v = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int q = 0; q < kLsmCtas; ++q) {
+      const float qv = *cluster.map_shared_rank(&s_pv, q);
+      const int qi = *cluster.map_shared_rank(&s_pi, q);
+      if (argmax_better(qv, qi, v, idx)) {
+        v = qv;
+        idx = qi;
+      }
+    }
+    tok[0] = idx;
+    if (pos) pos[0] += 1;
+  }
+  cluster.sync();  // no CTA leaves while rank 0 still reads its winner
+}
+
 }  // namespace
 }  // namespace ckv
 
@@ -340,6 +423,13 @@ int ckv_gemv(const uint16_t* x, const uint16_t* w, uint16_t* out, int m, int n, 
 #undef CKV_GEMV_CASE
   }
   CKV_LAUNCH_CHECK("ckv_gemv");
+  return CKV_OK;
+}
+
+int ckv_greedy_next(const uint16_t* logits, int n, int32_t* token, int32_t* position, ckv_stream_t stream) {
+  CKV_REQUIRE(logits && token && n > 0, "ckv_greedy_next: bad arguments");
+  greedy_next_kernel<<<kLsmCtas, kLsmThreads, 0, as_stream(stream)>>>(logits, n, token, position);
+  CKV_LAUNCH_CHECK("ckv_greedy_next");
   return CKV_OK;
 }
 

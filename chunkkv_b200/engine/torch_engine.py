@@ -455,8 +455,7 @@ class TorchEngine:
                 x_ready = self._block_tail(li, attn, h, x, act, part, 1, exch, 0)
             last = x if x_ready else ops.rmsnorm(h, self.w.norm, s.rms_eps, out=xf)
             ops.gemv(last, self.w.lm_head, out=logits)
-            tok.copy_(torch.argmax(logits[0]).view(1))
-            posd.add_(1)
+            ops.greedy_next(logits[0], tok, posd)  # argmax into tok, posd += 1
 
         graph = None
         use_graph = self.tp is None and ops._TIMER is None

@@ -668,6 +668,19 @@ def gemv_qkv_rope(x: torch.Tensor, w_qkv: torch.Tensor, b_qkv: torch.Tensor, Hq:
         _run("ckv_gemv_qkv_rope_rmsnorm", _ptr(x), _ptr(norm_w), float(eps), *args, **work)
 
 
+def greedy_next(row: torch.Tensor, token: torch.Tensor, position: torch.Tensor | None = None) -> torch.Tensor:
+    """token[0] = argmax of the bf16 logits `row` (torch.argmax's order: NaN first, ties to
+    the lower index); with `position`, position[0] += 1 in the same launch (the greedy
+    decode step of torch_engine.py:196-197).  Both are int32 device tensors."""
+    _buf("row", row, 1)
+    _buf("token", token, 1, dtype=torch.int32)
+    if position is not None:
+        _buf("position", position, 1, dtype=torch.int32)
+    _cuda(row, token, position)
+    _run("ckv_greedy_next", _ptr(row), row.numel(), _ptr(token), _ptr(position), _stream())
+    return token
+
+
 def log_softmax(row: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     _buf("row", row, 0)
     if out is not None:

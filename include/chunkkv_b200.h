@@ -367,6 +367,12 @@ CKV_API int ckv_attention(const uint16_t* q, const uint16_t* k_cache, const uint
 CKV_API int ckv_gemv(const uint16_t* x, const uint16_t* w, uint16_t* out, int m, int n, int k,
              ckv_stream_t stream);
 
+/* Greedy next token of the decode loop (TorchEngine.generate, torch_engine.py:185,196-197):
+ * token[0] = argmax of one bf16 logits row (NaN first, then the largest value, ties to the
+ * lower index, as torch.argmax), and, when position is not NULL, position[0] += 1. */
+CKV_API int ckv_greedy_next(const uint16_t* logits, int n, int32_t* token, int32_t* position,
+                            ckv_stream_t stream);
+
 /* log_softmax of one bf16 row into fp32 (TorchEngine.last_logprobs, torch_engine.py:200-201). */
 CKV_API int ckv_log_softmax(const uint16_t* logits, int n, float* out, ckv_stream_t stream);
 

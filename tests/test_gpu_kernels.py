@@ -747,3 +747,24 @@ def test_rmsnorm_embed_gemv_log_softmax():
         lp = ops.log_softmax(row)
         torch.testing.assert_close(lp, torch.log_softmax(row.float(), -1), rtol=1e-5, atol=1e-5)
         assert torch.equal(lp, ops.log_softmax(row)), "the cluster's combine must be deterministic"
+
+
+def test_greedy_next_is_torch_argmax_and_advances_the_position():
+    g = torch.Generator(device=DEV).manual_seed(7)
+    tok = torch.zeros(1, dtype=torch.int32, device=DEV)
+    pos = torch.full((1,), 41, dtype=torch.int32, device=DEV)
+    rows = [(torch.randn(n, generator=g, device=DEV) * 4).to(BF) for n in (1, 5, 9, 5000, 152064)]
+    tied = torch.randint(0, 3, (152064,), generator=g, device=DEV).to(BF)  # the max repeats ~50k times
+    rows.append(tied)
+    late = torch.full((152064,), -3.0, device=DEV).to(BF)
+    late[-1] = 2.0  # the winner in the last slice
+    rows.append(late)
+    nan = rows[3].clone()
+    nan[[17, 4000]] = float("nan")  # torch.argmax returns the first NaN
+    rows.append(nan)
+    for i, row in enumerate(rows):
+        ops.greedy_next(row, tok, pos)
+        assert int(tok) == int(torch.argmax(row)), i
+        assert int(pos) == 42 + i
+    ops.greedy_next(rows[0], tok)  # no position: only the token is written
+    assert int(tok) == 0 and int(pos) == 41 + len(rows)
