@@ -89,6 +89,9 @@ def test_ops_check_shapes_before_launching():
         (lambda: ops.embed(w, torch.zeros(4, dtype=torch.int64), None, x), "int32"),
         (lambda: ops.embed(w, torch.zeros(3, dtype=i32), None, x), "tokens"),
         (lambda: ops.log_softmax(x[0], out=torch.zeros(64, dtype=bf)), "float32"),
+        (lambda: ops.greedy_next(x[0], torch.zeros(1, dtype=torch.int64)), "int32"),
+        (lambda: ops.greedy_next(x[0], torch.zeros(1, dtype=i32), torch.zeros(0, dtype=i32)), "position"),
+        (lambda: ops.greedy_next(x[0].float(), torch.zeros(1, dtype=i32)), "bfloat16"),
     ]
     # attention: q [m, Hq, D], caches [H, n_ctx, D], positions int32 [m]
     q, K = torch.zeros((3, 4, 16), dtype=bf), torch.zeros((2, 40, 16), dtype=bf)
