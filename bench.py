@@ -32,6 +32,13 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# Per-kernel times (the `kernels` table and the roofline): a second pass of the same steps
+# with a CUDA-event pair around every launch, each pair preceded by a device sleep so that
+# the launch is already queued when its start event runs.
+KERNEL_GATE_US = 50.0
+KERNEL_TIMING = (f"CUDA-event pair around each launch in a second pass of the same steps; a "
+                 f"{KERNEL_GATE_US:.0f} us device sleep before each pair keeps the host's submission "
+                 f"time out of it (no dependent-launch overlap inside a pair)")
 METRIC = "blend-prefill tokens/s (Qwen2.5-7B shape, 10x512 shuffled cached chunks + 128-token query)"
 
 
@@ -356,8 +363,9 @@ def run_ours(args):
     stats = res.stats
 
     # ---- the same K steps again with an event pair around every launch: per-kernel
-    # times for the roofline and the launch count (not part of the timed value)
-    with ops.LaunchTimer() as timer:
+    # times for the roofline and the launch count (not part of the timed value).  A device
+    # sleep before each pair keeps the GPU from waiting on the host inside the pair.
+    with ops.LaunchTimer(gate_us=KERNEL_GATE_US) as timer:
         for i in range(args.steps):
             step()
         torch.cuda.synchronize()
@@ -422,7 +430,8 @@ def run_ours(args):
     roof = dominant_roofline(timer, pk, pk_kind, shape)
     roof["gemm_family"] = {"kernels": "qkv+rope, o_proj+residual, gate/up+swiglu, down+residual",
                            "achieved": round(g_fl / (g_ms * 1e-3) / 1e12, 1) if g_ms else 0.0,
-                           "frac": round(g_fl / (g_ms * 1e-3) / 1e12 / pk["bf16_tflops_sustained"], 4)
+                           "frac": round(g_fl / (g_ms * 1e-3) / 1e12 / roof["peak"], 4) if g_ms else 0.0,
+                           "frac_sustained": round(g_fl / (g_ms * 1e-3) / 1e12 / pk["bf16_tflops_sustained"], 4)
                            if g_ms else 0.0,
                            "frac_burst": round(g_fl / (g_ms * 1e-3) / 1e12 / pk["bf16_tflops"], 4) if g_ms else 0.0,
                            "share_of_busy": round(g_ms / busy, 4) if busy else 0.0}
@@ -460,7 +469,7 @@ def run_ours(args):
                 "ttft_ms_p50": round(statistics.median(e2e_ms), 3),
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                 "api": "TorchEngine.prefill(list[int], placements from the paged store) + last_logprobs"},
-        "roofline": roof, "kernels": kernels, "gpu_launches": int(launches),
+        "roofline": roof, "kernels": kernels, "kernel_timing": KERNEL_TIMING, "gpu_launches": int(launches),
         "gpu_busy_ms_per_step": round(busy / args.steps, 3),
         "clocks": clk.summary(),
     }
@@ -500,13 +509,16 @@ def dominant_roofline(timer, pk, pk_kind, shape):
     ms = statistics.mean(times)
     achieved = flops / (ms * 1e-3) / 1e12
     m_rows = round(flops / (4.0 * shape.inter * shape.hidden))
+    # A launch timed after a device sleep runs alone, like the short cuBLAS run of the burst
+    # peak, so that is its denominator; without the sleep the launches run back to back
+    # inside the step, like the sustained run.
+    key = "bf16_tflops" if getattr(timer, "gate_cycles", 0) else "bf16_tflops_sustained"
     return {"kernel": "ckv_linear_swiglu (tcgen05 gate/up GEMM + SwiGLU epilogue), layers >= 1",
-            "bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops_sustained"],
-            "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops_sustained"], 4),
-            "peak_source": f"{pk_kind} bf16_tflops_sustained",
-            # the same against the burst peak (a short cuBLAS run at full clocks), since the
-            # sustained figure was measured at a lower SM clock than a prefill step runs at
+            "bound": "tensor", "achieved": round(achieved, 1), "peak": pk[key],
+            "unit": "TFLOP/s", "frac": round(achieved / pk[key], 4), "peak_source": f"{pk_kind} {key}",
             "peak_burst": pk["bf16_tflops"], "frac_burst": round(achieved / pk["bf16_tflops"], 4),
+            "peak_sustained": pk["bf16_tflops_sustained"],
+            "frac_sustained": round(achieved / pk["bf16_tflops_sustained"], 4),
             "peak_sustained_sm_mhz": pk.get("sustained_sm_mhz"),
             "launches": len(times), "rows": m_rows,
             "flops_per_launch": round(flops), "ms_per_launch": round(ms, 4),

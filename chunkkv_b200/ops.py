@@ -29,9 +29,14 @@ class LaunchTimer:
     while installed (``with LaunchTimer() as t: ...``), with the launch's algorithmic
     work (FLOPs and HBM bytes) for roofline accounting."""
 
-    def __init__(self):
+    def __init__(self, gate_us: float = 0.0):
         self.records: list[tuple[str, float, float, torch.cuda.Event, torch.cuda.Event]] = []
         self.kernels: dict[str, int] = {}  # device kernels launched per entry point
+        # With gate_us > 0 the stream first runs a device sleep of about gate_us (SM cycles
+        # counted at the top clock, so longer at lower clocks) before each timed launch: the
+        # launch is queued behind it, and its event pair then measures the kernel rather
+        # than the host's time to submit it.
+        self.gate_cycles = int(gate_us * 1965)
 
     def __enter__(self):
         global _TIMER
@@ -67,6 +72,8 @@ def _run(name: str, *args, flops: float = 0.0, nbytes: float = 0.0, kernels: int
         return
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    if t.gate_cycles:
+        torch.cuda._sleep(t.gate_cycles)
     e0.record()
     _lib.call(name, *args)
     e1.record()
